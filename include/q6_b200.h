@@ -1,0 +1,139 @@
+/*
+ * q6_b200.h - C ABI of the B200 (sm_100a) q6 affine linear / image-FF MLP library.
+ *
+ * Weight format (MLX affine, bits = 6): for a linear with N outputs and K
+ * inputs,
+ *   w       uint32 [N, K*6/32]  6-bit codes, code k of row n in bits [6k, 6k+6)
+ *                               of the row's little-endian word stream
+ *   scales  bf16   [N, K/gs]    per-group scale
+ *   qbiases bf16   [N, K/gs]    per-group bias, so  W[n,k] = scale*q + qbias
+ *   bias    bf16   [N]          optional output bias
+ * bf16 tensors are passed as uint16_t bit patterns.  All pointers are device
+ * pointers, rows are dense (row stride = row length).  Calls are
+ * stream-ordered on `stream` (a cudaStream_t; 0 = legacy default stream),
+ * never synchronise, allocate no device memory, and are safe to issue from
+ * several host threads on different streams.
+ *
+ * Every entry point returns 0 (Q6_OK) or a q6_status code; argument checks
+ * happen before anything is launched.
+ */
+#ifndef Q6_B200_H
+#define Q6_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define Q6_API __attribute__((visibility("default")))
+#else
+#define Q6_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* q6_stream_t; /* identical to cudaStream_t */
+
+enum q6_status {
+    Q6_OK = 0,
+    Q6_ERR_INVALID_ARGUMENT = 1, /* null pointer or non-positive size        */
+    Q6_ERR_SHAPE = 2,            /* K not a multiple of 16 or of group_size   */
+    Q6_ERR_GROUP_SIZE = 3,       /* group_size not in {32, 64, 128}           */
+    Q6_ERR_ALIGNMENT = 4,        /* pointer not aligned as the path requires  */
+    Q6_ERR_UNSUPPORTED = 5,      /* requested path cannot run this problem    */
+    Q6_ERR_CUDA = 6,             /* a CUDA runtime call failed                */
+    Q6_ERR_DEVICE = 7,           /* a kernel raised the device error word     */
+    Q6_ERR_WORKSPACE = 8         /* workspace missing or too small            */
+};
+
+/* Epilogue flags (bit set). */
+enum q6_epilogue {
+    Q6_EPI_NONE = 0,
+    Q6_EPI_GELU = 1 /* GELU-tanh after the bias (mlx nn.gelu_approx) */
+};
+
+/* Kernel path for q6_linear_bf16 (Q6_PATH_AUTO picks one). */
+enum q6_path {
+    Q6_PATH_AUTO = 0,
+    Q6_PATH_SIMT = 1,   /* CUDA-core kernel, fp32 dequantised weights   */
+    Q6_PATH_TENSOR = 2  /* tcgen05 kernel, bf16 dequantised weights     */
+};
+
+/*
+ * Dense bf16 weights from packed q6: out[n,k] = bf16_rn(fp32(scale)*q + fp32(qbias)).
+ * Replaces `dequantize_linear` / mx.dequantize(mode="affine")
+ * (shardedit_mlx/q6_metal_mlp.py:143-154).  out: uint16 [N, K].
+ */
+Q6_API int q6_dequantize_bf16(const uint32_t* w, const uint16_t* scales, const uint16_t* qbiases,
+                       uint16_t* out, int64_t N, int64_t K, int group_size, q6_stream_t stream);
+
+/*
+ * y = epi(x @ dequant(W)^T)      x bf16 [M, K], y bf16 [M, N]
+ * epi: + bias[n] (if bias), GELU (if flags & Q6_EPI_GELU), then
+ *      y = residual[m,n] + gate[n] * value  (each term only if its pointer is non-null).
+ * LoRA (lora_a bf16 [K, r], lora_b bf16 [r, N], both non-null): the value gains
+ *      lora_scale * ((x @ lora_a) @ lora_b) before the bias; needs
+ *      q6_linear_workspace_bytes(M, r) bytes of workspace.
+ * Replaces `affine_q6_qmm_t` (shardedit_mlx/q6_metal_mlp.py:157-204), its tiled
+ * and simdgroup twins (q6_steel_mlp.py:163-220, q6_simdgroup_mlp.py:133-181),
+ * the stock `mx.quantized_matmul(x, w, scales, biases, transpose=True,
+ * group_size, bits=6)` + bias call (benchmarks/benchmark_qwen_gemm.py:188-200),
+ * the LoRA-additive linear (dense_img_ff_window.py:48-60) and the block's
+ * residual gate `x + gate * ff(x)` (benchmarks/profile_qwen_block.py:294-301).
+ */
+Q6_API int q6_linear_bf16(const uint16_t* x, const uint32_t* w, const uint16_t* scales,
+                   const uint16_t* qbiases, const uint16_t* bias, const uint16_t* residual,
+                   const uint16_t* gate, const uint16_t* lora_a, const uint16_t* lora_b,
+                   float lora_scale, int lora_rank, uint16_t* y, int64_t M, int64_t N, int64_t K,
+                   int group_size, int flags, int path, void* workspace, size_t workspace_bytes,
+                   q6_stream_t stream);
+
+/* Workspace q6_linear_bf16 needs for a LoRA rank r at M tokens (0 without LoRA). */
+Q6_API size_t q6_linear_workspace_bytes(int64_t M, int lora_rank);
+
+/*
+ * fp32 activations in and out, fp32 dequantised weights (no bf16 rounding):
+ * the dtype=float32 use of `affine_q6_qmm_t` (q6_metal_mlp.py:157-204) that the
+ * reference's fp32 tests check against a dense fp32 matmul.
+ * Bias / residual / gate stay bf16 as in the weight files.
+ */
+Q6_API int q6_linear_f32(const float* x, const uint32_t* w, const uint16_t* scales,
+                  const uint16_t* qbiases, const uint16_t* bias, float* y, int64_t M, int64_t N,
+                  int64_t K, int group_size, int flags, q6_stream_t stream);
+
+/*
+ * Image feed-forward MLP  y = fc2(gelu(fc1(x)))  [+ residual/gate epilogue]:
+ *   x bf16 [M, D]; fc1: D -> H (+ bias, GELU); fc2: H -> D (+ bias); y bf16 [M, D].
+ * The bf16 hidden [M, H] lives in the caller's workspace
+ * (q6_mlp_workspace_bytes(M, H) bytes).
+ * Replaces `fused_q6_mlp` (shardedit_mlx/q6_metal_mlp.py:207-215) and the
+ * QwenFeedForward `img_ff(x)` call it stands in for (dense_img_ff_window.py:62-67).
+ */
+Q6_API int q6_mlp_bf16(const uint16_t* x, const uint32_t* w1, const uint16_t* scales1,
+                const uint16_t* qbiases1, const uint16_t* bias1, const uint32_t* w2,
+                const uint16_t* scales2, const uint16_t* qbiases2, const uint16_t* bias2,
+                const uint16_t* residual, const uint16_t* gate, uint16_t* y, int64_t M, int64_t D,
+                int64_t H, int group_size, void* workspace, size_t workspace_bytes,
+                q6_stream_t stream);
+
+Q6_API size_t q6_mlp_workspace_bytes(int64_t M, int64_t H);
+
+/* Device error word (0 = none).  Reading it synchronises the current device. */
+Q6_API int q6_get_device_error(int* code);
+Q6_API int q6_clear_device_error(void);
+
+/* Path the last q6_linear_bf16 / q6_mlp_bf16 call on this host thread launched. */
+Q6_API int q6_last_path(void);
+
+/* Token tile (MMA N) the tensor path would use for an M x N problem. */
+Q6_API int q6_tensor_token_tile(int64_t M, int64_t N);
+
+Q6_API const char* q6_status_string(int status);
+Q6_API int q6_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* Q6_B200_H */

@@ -1,0 +1,101 @@
+// Exact register-level unpacking of MLX affine 6-bit codes.
+//
+// Layout (shardedit_mlx/q6_metal_mlp.py:28-40): code j of a row occupies bits
+// [6j, 6j+6) of the row's little-endian uint32 stream, so every 16 codes fill
+// exactly three words w0, w1, w2 and codes 5 and 10 straddle a word boundary.
+//
+// Conversion: a code sitting at bit position P of a word is turned into an
+// fp32 value by splicing the masked word into the mantissa of 2^(23-P), which
+// gives exactly 2^(23-P) + q; subtracting 2^(23-P) again is exact.  One LOP3
+// per code plus one packed add and one packed FMA per code pair, then
+//   w = fma(q, scale, bias)            (fp32, rounded once; scale*q is exact)
+// and, for the tensor-core operand, bf16_rn(w) two at a time.  This is the
+// same value as the reference's `scale * float(code) + qbias`
+// (q6_metal_mlp.py:42-54) followed by round-to-nearest-even to bf16.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+namespace q6 {
+
+template <int P>
+__device__ __forceinline__ float code_spliced(uint32_t v) {
+    static_assert(P >= 0 && P <= 17, "code must sit in the low 23 mantissa bits");
+    constexpr uint32_t kMask = 0x3Fu << P;
+    constexpr uint32_t kExp = (127u + 23u - P) << 23;
+    return __uint_as_float((v & kMask) | kExp);
+}
+
+template <int P>
+__device__ __forceinline__ constexpr float code_offset() {
+    return static_cast<float>(1u << (23 - P));
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// Dequantise one code pair given as spliced values with their offsets.
+template <int PA, int PB>
+__device__ __forceinline__ float2 pair_f32(float a_spliced, float b_spliced, float2 s2, float2 b2) {
+    const float2 v = make_float2(a_spliced, b_spliced);
+    const float2 off = make_float2(-code_offset<PA>(), -code_offset<PB>());
+    const float2 q = __fadd2_rn(v, off);  // exact integer codes
+    return __ffma2_rn(q, s2, b2);         // s*q + b, one rounding
+}
+
+// Sixteen codes (three packed words) -> sixteen fp32 weights.
+__device__ __forceinline__ void dequant16_f32(uint32_t w0, uint32_t w1, uint32_t w2, float s, float b,
+                                              float (&out)[16]) {
+    const uint32_t t0 = w0 >> 12, t1 = w1 >> 12, t2 = w2 >> 12;
+    const uint32_t f5 = __funnelshift_r(w0, w1, 30);
+    const uint32_t f10 = __funnelshift_r(w1, w2, 28);
+    const float2 s2 = make_float2(s, s), b2 = make_float2(b, b);
+    float2 r;
+    r = pair_f32<0, 6>(code_spliced<0>(w0), code_spliced<6>(w0), s2, b2);
+    out[0] = r.x; out[1] = r.y;
+    r = pair_f32<12, 6>(code_spliced<12>(w0), code_spliced<6>(t0), s2, b2);
+    out[2] = r.x; out[3] = r.y;
+    r = pair_f32<12, 0>(code_spliced<12>(t0), code_spliced<0>(f5), s2, b2);
+    out[4] = r.x; out[5] = r.y;
+    r = pair_f32<4, 10>(code_spliced<4>(w1), code_spliced<10>(w1), s2, b2);
+    out[6] = r.x; out[7] = r.y;
+    r = pair_f32<16, 10>(code_spliced<16>(w1), code_spliced<10>(t1), s2, b2);
+    out[8] = r.x; out[9] = r.y;
+    r = pair_f32<0, 2>(code_spliced<0>(f10), code_spliced<2>(w2), s2, b2);
+    out[10] = r.x; out[11] = r.y;
+    r = pair_f32<8, 14>(code_spliced<8>(w2), code_spliced<14>(w2), s2, b2);
+    out[12] = r.x; out[13] = r.y;
+    r = pair_f32<8, 14>(code_spliced<8>(t2), code_spliced<14>(t2), s2, b2);
+    out[14] = r.x; out[15] = r.y;
+}
+
+// Sixteen codes -> eight bf16x2 words (low half = even code).
+__device__ __forceinline__ void dequant16_bf16x2(uint32_t w0, uint32_t w1, uint32_t w2, float s, float b,
+                                                 uint32_t* out) {
+    const uint32_t t0 = w0 >> 12, t1 = w1 >> 12, t2 = w2 >> 12;
+    const uint32_t f5 = __funnelshift_r(w0, w1, 30);
+    const uint32_t f10 = __funnelshift_r(w1, w2, 28);
+    const float2 s2 = make_float2(s, s), b2 = make_float2(b, b);
+    float2 r;
+    r = pair_f32<0, 6>(code_spliced<0>(w0), code_spliced<6>(w0), s2, b2);
+    out[0] = pack_bf16x2(r.x, r.y);
+    r = pair_f32<12, 6>(code_spliced<12>(w0), code_spliced<6>(t0), s2, b2);
+    out[1] = pack_bf16x2(r.x, r.y);
+    r = pair_f32<12, 0>(code_spliced<12>(t0), code_spliced<0>(f5), s2, b2);
+    out[2] = pack_bf16x2(r.x, r.y);
+    r = pair_f32<4, 10>(code_spliced<4>(w1), code_spliced<10>(w1), s2, b2);
+    out[3] = pack_bf16x2(r.x, r.y);
+    r = pair_f32<16, 10>(code_spliced<16>(w1), code_spliced<10>(t1), s2, b2);
+    out[4] = pack_bf16x2(r.x, r.y);
+    r = pair_f32<0, 2>(code_spliced<0>(f10), code_spliced<2>(w2), s2, b2);
+    out[5] = pack_bf16x2(r.x, r.y);
+    r = pair_f32<8, 14>(code_spliced<8>(w2), code_spliced<14>(w2), s2, b2);
+    out[6] = pack_bf16x2(r.x, r.y);
+    r = pair_f32<8, 14>(code_spliced<8>(t2), code_spliced<14>(t2), s2, b2);
+    out[7] = pack_bf16x2(r.x, r.y);
+}
+
+}  // namespace q6

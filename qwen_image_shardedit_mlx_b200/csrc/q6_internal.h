@@ -1,0 +1,52 @@
+// Host-side interfaces between the C ABI (q6_capi.cu) and the kernel launchers.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "q6_b200.h"
+
+namespace q6 {
+
+// Operands of one q6 linear, y = epilogue(x @ dequant(W)^T).
+struct LinearArgs {
+    const void* x;          // [M, K] bf16 (or fp32 for the fp32 path), row-major
+    const uint32_t* w;      // [N, K*6/32] packed codes
+    const uint16_t* scales; // [N, K/gs] bf16
+    const uint16_t* qbiases;// [N, K/gs] bf16
+    const uint16_t* bias;   // [N] bf16 or null
+    const uint16_t* residual;  // [M, N] bf16 or null
+    const uint16_t* gate;      // [N] bf16 or null
+    void* y;                // [M, N] bf16 (fp32 for the fp32 path)
+    int64_t M, N, K;
+    int group_size;
+    int flags;              // Q6_EPI_* bits
+};
+
+// Path selection recorded for tests and benchmarks.
+enum class Path : int { kNone = 0, kSimt = 1, kTensor = 2 };
+
+int launch_dequantize(const uint32_t* w, const uint16_t* scales, const uint16_t* qbiases,
+                      uint16_t* out, int64_t N, int64_t K, int group_size, cudaStream_t stream);
+
+// CUDA-core path: any shape the format allows, bf16 or fp32 activations,
+// fp32 (un-rounded) dequantised weights.
+int launch_linear_simt(const LinearArgs& a, bool f32_io, cudaStream_t stream);
+
+// tcgen05 path: bf16 activations, bf16-dequantised weights, fp32 accumulate.
+// Requires K % 64 == 0 and 16-byte aligned x / w rows.
+int launch_linear_tc(const LinearArgs& a, int token_tile, cudaStream_t stream);
+
+// Token tile the tensor-core path picks for an (M, N) problem.
+int choose_token_tile(int64_t M, int64_t N);
+
+bool tc_supported(const LinearArgs& a);
+
+int device_sm_count();
+
+// Per-translation-unit device error words (value, optionally cleared; -1 on
+// a failed copy).
+int error_word_simt(bool clear);
+int error_word_tc(bool clear);
+
+}  // namespace q6

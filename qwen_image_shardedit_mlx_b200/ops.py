@@ -1,0 +1,227 @@
+"""Torch-facing q6 ops; every call goes through the C ABI of libq6b200.so.
+
+Tensors must live on a CUDA device.  Launches are ordered on the current torch
+stream of that device; nothing here synchronises.  Output buffers are
+allocated with torch (the library itself never allocates).
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from qwen_image_shardedit_mlx_b200 import _lib
+
+GROUP_SIZES = (32, 64, 128)
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _as_u32(weight: torch.Tensor) -> torch.Tensor:
+    if weight.dtype not in (torch.uint32, torch.int32):
+        raise ValueError(f"expected packed uint32 weight, got {weight.dtype}")
+    return weight
+
+
+def _require_cuda(*tensors: torch.Tensor | None) -> torch.device:
+    dev = None
+    for t in tensors:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise RuntimeError("q6 ops run on CUDA tensors only (the library has no CPU path)")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise ValueError("all tensors must be on the same device")
+    assert dev is not None
+    return dev
+
+
+def _bf16_vec(t: torch.Tensor | None, n: int, name: str) -> torch.Tensor | None:
+    if t is None:
+        return None
+    t = t.reshape(-1)
+    if t.numel() != n:
+        raise ValueError(f"{name} must hold {n} values, got {t.numel()}")
+    return t.to(torch.bfloat16).contiguous()
+
+
+def check_q6_weights(weight: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor, group_size: int) -> tuple[int, int]:
+    """Validate the MLX q6 triplet; returns (N, K)."""
+
+    _as_u32(weight)
+    if group_size not in GROUP_SIZES:
+        raise ValueError(f"group_size must be one of {GROUP_SIZES}, got {group_size}")
+    if weight.dim() != 2:
+        raise ValueError(f"packed weight must be 2-D, got shape {tuple(weight.shape)}")
+    n = int(weight.shape[0])
+    if (int(weight.shape[1]) * 32) % 6:
+        raise ValueError(f"packed width {weight.shape[1]} is not a whole number of 6-bit codes")
+    k = int(weight.shape[1]) * 32 // 6
+    if k % group_size:
+        raise ValueError(f"in_features {k} is not a multiple of group_size {group_size}")
+    expect = (n, k // group_size)
+    if tuple(scales.shape) != expect or tuple(biases.shape) != expect:
+        raise ValueError(f"scales/biases must be {expect}, got {tuple(scales.shape)} / {tuple(biases.shape)}")
+    return n, k
+
+
+def q6_dequantize(weight: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor, group_size: int = 64) -> torch.Tensor:
+    """Dense bf16 [N, K] = bf16_rn(scale * q + bias) (MLX affine dequantisation)."""
+
+    n, k = check_q6_weights(weight, scales, biases, group_size)
+    dev = _require_cuda(weight, scales, biases)
+    out = torch.empty((n, k), dtype=torch.bfloat16, device=dev)
+    st = _lib.lib().q6_dequantize_bf16(
+        weight.contiguous().data_ptr(),
+        scales.to(torch.bfloat16).contiguous().data_ptr(),
+        biases.to(torch.bfloat16).contiguous().data_ptr(),
+        out.data_ptr(), n, k, group_size, _stream(dev),
+    )
+    _lib.check(st, "q6_dequantize_bf16")
+    return out
+
+
+def q6_linear(
+    x: torch.Tensor,
+    weight: torch.Tensor,
+    scales: torch.Tensor,
+    biases: torch.Tensor,
+    bias: torch.Tensor | None = None,
+    *,
+    group_size: int = 64,
+    apply_gelu: bool = False,
+    residual: torch.Tensor | None = None,
+    gate: torch.Tensor | None = None,
+    lora: tuple[torch.Tensor, torch.Tensor, float] | None = None,
+    path: str = "auto",
+    out: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """y = epilogue(x @ dequant(W)^T) for x [..., K]; returns [..., N].
+
+    bf16 x runs the tensor-core path (bf16-dequantised weights, fp32
+    accumulation) or, for a handful of rows, the CUDA-core path; fp32 x runs
+    the CUDA-core path with fp32 weights and returns fp32.
+    Epilogue order: + bias, GELU, then residual + gate * value.
+    """
+
+    n, k = check_q6_weights(weight, scales, biases, group_size)
+    if x.shape[-1] != k:
+        raise ValueError(f"x in_features {x.shape[-1]} != weight in_features {k}")
+    dev = _require_cuda(x, weight, scales, biases, bias, residual, gate)
+    leading = tuple(x.shape[:-1])
+    flat = x.reshape(-1, k)
+    m = int(flat.shape[0])
+    if m == 0:
+        return torch.empty(leading + (n,), dtype=x.dtype, device=dev)
+    flags = _lib.Q6_EPI_GELU if apply_gelu else _lib.Q6_EPI_NONE
+    sc = scales.to(torch.bfloat16).contiguous()
+    qb = biases.to(torch.bfloat16).contiguous()
+    bias_t = _bf16_vec(bias, n, "bias")
+    gate_t = _bf16_vec(gate, n, "gate")
+    w = weight.contiguous()
+    stream = _stream(dev)
+    if flat.dtype == torch.float32:
+        if residual is not None or gate is not None or lora is not None:
+            raise ValueError("the fp32 path supports bias and GELU only")
+        xf = flat.contiguous()
+        y = out if out is not None else torch.empty((m, n), dtype=torch.float32, device=dev)
+        st = _lib.lib().q6_linear_f32(
+            xf.data_ptr(), w.data_ptr(), sc.data_ptr(), qb.data_ptr(), _ptr(bias_t), y.data_ptr(),
+            m, n, k, group_size, flags, stream,
+        )
+        _lib.check(st, "q6_linear_f32")
+        return y.reshape(leading + (n,))
+    if flat.dtype != torch.bfloat16:
+        flat = flat.to(torch.bfloat16)
+    xb = flat.contiguous()
+    res_t = None
+    if residual is not None:
+        res_t = residual.reshape(m, n).to(torch.bfloat16).contiguous()
+    la = lb = None
+    lscale, rank = 0.0, 0
+    workspace = None
+    if lora is not None:
+        a, b, lscale = lora
+        rank = int(a.shape[-1])
+        la = a.to(torch.bfloat16).contiguous()
+        lb = b.to(torch.bfloat16).contiguous()
+        if tuple(la.shape) != (k, rank) or tuple(lb.shape) != (rank, n):
+            raise ValueError(f"LoRA A must be ({k}, r) and B (r, {n}); got {tuple(la.shape)}, {tuple(lb.shape)}")
+        nbytes = int(_lib.lib().q6_linear_workspace_bytes(m, rank))
+        workspace = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=dev)
+    y = out if out is not None else torch.empty((m, n), dtype=torch.bfloat16, device=dev)
+    st = _lib.lib().q6_linear_bf16(
+        xb.data_ptr(), w.data_ptr(), sc.data_ptr(), qb.data_ptr(), _ptr(bias_t), _ptr(res_t), _ptr(gate_t),
+        _ptr(la), _ptr(lb), float(lscale), rank, y.data_ptr(), m, n, k, group_size, flags,
+        _lib.PATHS[path], _ptr(workspace), 0 if workspace is None else workspace.numel(), stream,
+    )
+    _lib.check(st, "q6_linear_bf16")
+    return y.reshape(leading + (n,))
+
+
+def q6_mlp(
+    x: torch.Tensor,
+    w1: tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor | None],
+    w2: tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor | None],
+    *,
+    group_size: int = 64,
+    residual: torch.Tensor | None = None,
+    gate: torch.Tensor | None = None,
+    workspace: torch.Tensor | None = None,
+    out: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """fc2(gelu(fc1(x))) [+ residual + gate * .]; w1/w2 = (weight, scales, biases, bias)."""
+
+    h, d = check_q6_weights(w1[0], w1[1], w1[2], group_size)
+    d2, h2 = check_q6_weights(w2[0], w2[1], w2[2], group_size)
+    if (d2, h2) != (d, h):
+        raise ValueError(f"fc2 must map {h} -> {d}, got {h2} -> {d2}")
+    if x.shape[-1] != d:
+        raise ValueError(f"x features {x.shape[-1]} != {d}")
+    dev = _require_cuda(x, *w1[:3], *w2[:3])
+    leading = tuple(x.shape[:-1])
+    xb = x.reshape(-1, d).to(torch.bfloat16).contiguous()
+    m = int(xb.shape[0])
+    need = int(_lib.lib().q6_mlp_workspace_bytes(m, h))
+    if workspace is None or workspace.numel() * workspace.element_size() < need:
+        workspace = torch.empty(need, dtype=torch.uint8, device=dev)
+    y = out if out is not None else torch.empty((m, d), dtype=torch.bfloat16, device=dev)
+    res_t = None if residual is None else residual.reshape(m, d).to(torch.bfloat16).contiguous()
+    gate_t = _bf16_vec(gate, d, "gate")
+    b1 = _bf16_vec(w1[3], h, "fc1 bias")
+    b2 = _bf16_vec(w2[3], d, "fc2 bias")
+    st = _lib.lib().q6_mlp_bf16(
+        xb.data_ptr(),
+        w1[0].contiguous().data_ptr(), w1[1].to(torch.bfloat16).contiguous().data_ptr(),
+        w1[2].to(torch.bfloat16).contiguous().data_ptr(), _ptr(b1),
+        w2[0].contiguous().data_ptr(), w2[1].to(torch.bfloat16).contiguous().data_ptr(),
+        w2[2].to(torch.bfloat16).contiguous().data_ptr(), _ptr(b2),
+        _ptr(res_t), _ptr(gate_t), y.data_ptr(), m, d, h, group_size,
+        workspace.data_ptr(), workspace.numel() * workspace.element_size(), _stream(dev),
+    )
+    _lib.check(st, "q6_mlp_bf16")
+    return y.reshape(leading + (d,))
+
+
+def last_path() -> str:
+    code = _lib.lib().q6_last_path()
+    return {v: k for k, v in _lib.PATHS.items()}.get(code, "none")
+
+
+def device_error() -> int:
+    code = ctypes.c_int(0)
+    _lib.check(_lib.lib().q6_get_device_error(ctypes.byref(code)), "q6_get_device_error")
+    return int(code.value)
+
+
+def clear_device_error() -> None:
+    _lib.check(_lib.lib().q6_clear_device_error(), "q6_clear_device_error")

@@ -1,0 +1,227 @@
+"""Reference-compatible q6 linear / image-MLP surface, backed by the B200 kernels.
+
+Mirrors the names, argument meanings and errors of the reference module
+shardedit_mlx/q6_metal_mlp.py so callers can switch by import:
+
+=========================  =====================================================
+reference (file:line)      here
+=========================  =====================================================
+Q6LinearSpec :96-111       Q6LinearSpec (weight uint32 [N, K*6/32], scales and
+                           qbiases [N, K/gs], optional bias, group_size, bits)
+quantized_linear_spec      quantized_linear_spec(layer): bits must be 6 and the
+:114-134                   weight uint32, else ValueError
+DenseLinearWeights :137    DenseLinearWeights(weight [N, K], bias)
+dequantize_linear :143     dequantize_linear(spec, dtype=...) on the GPU kernel
+affine_q6_qmm_t :157-204   affine_q6_qmm_t(x, spec, apply_gelu=, dtype=): rank 2/3
+                           input, K check, leading dims kept, returns dtype
+fused_q6_mlp :207-215      fused_q6_mlp(hidden, mlp_in, mlp_out)
+dense_mlp :218-232         dense_mlp(hidden, mlp_in, mlp_out) on dense weights
+eager_q6_mlp :249-253      eager_q6_mlp(ff, hidden): mlp_in -> gelu -> mlp_out
+make_feed_forward_callables make_feed_forward_callables(ff, dtype=) ->
+:256-280                   (eager_q6, fused, dense_predequant)
+=========================  =====================================================
+
+One deliberate difference: the reference's spec widens scales/biases to fp32
+for its Metal kernel (:129-131).  Here they stay bf16 - the checkpoint dtype
+the C ABI reads - which carries exactly the same values.
+"""
+
+from __future__ import annotations
+
+from collections.abc import Callable
+from dataclasses import dataclass
+
+import torch
+import torch.nn.functional as F
+
+from qwen_image_shardedit_mlx_b200 import ops
+from qwen_image_shardedit_mlx_b200.quantize import quantize_affine_q6
+
+
+@dataclass(frozen=True)
+class Q6LinearSpec:
+    weight: torch.Tensor  # uint32 [N, K*bits/32]
+    scales: torch.Tensor  # bf16 [N, K/group_size]
+    qbiases: torch.Tensor  # bf16 [N, K/group_size]
+    bias: torch.Tensor | None  # [N]
+    group_size: int
+    bits: int
+
+    @property
+    def out_features(self) -> int:
+        return int(self.weight.shape[0])
+
+    @property
+    def in_features(self) -> int:
+        return int(self.weight.shape[1] * 32 // self.bits)
+
+
+class QuantizedLinear(torch.nn.Module):
+    """q6 linear layer holding MLX-layout tensors (weight, scales, biases, bias).
+
+    Same attribute names as mlx ``nn.QuantizedLinear``; calling it runs the
+    q6 kernel with the output bias fused into the epilogue.
+    """
+
+    def __init__(self, weight: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor,
+                 bias: torch.Tensor | None = None, *, group_size: int = 64, bits: int = 6) -> None:
+        super().__init__()
+        self.register_buffer("weight", weight)
+        self.register_buffer("scales", scales)
+        self.register_buffer("biases", biases)
+        self.register_buffer("bias", bias)
+        self.group_size = int(group_size)
+        self.bits = int(bits)
+        self.mode = "affine"
+
+    @classmethod
+    def from_linear(cls, linear: torch.nn.Linear, *, bits: int = 6, group_size: int = 64) -> "QuantizedLinear":
+        if bits != 6:
+            raise ValueError(f"only bits=6 is supported, got {bits}")
+        w, s, b = quantize_affine_q6(linear.weight.detach(), group_size)
+        bias = None if linear.bias is None else linear.bias.detach().to(torch.bfloat16)
+        return cls(w, s, b, bias, group_size=group_size, bits=bits)
+
+    @property
+    def in_features(self) -> int:
+        return int(self.weight.shape[1] * 32 // self.bits)
+
+    @property
+    def out_features(self) -> int:
+        return int(self.weight.shape[0])
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        return ops.q6_linear(x, self.weight, self.scales, self.biases, self.bias, group_size=self.group_size)
+
+
+def quantized_linear_spec(layer: torch.nn.Module) -> Q6LinearSpec:
+    """Extract packed affine q6 tensors from a QuantizedLinear-like module."""
+
+    weight = layer.weight
+    bits = int(layer.bits)
+    group_size = int(layer.group_size)
+    if bits != 6:
+        raise ValueError(f"only bits=6 is supported, got {bits}")
+    if weight.dtype not in (torch.uint32, torch.int32):
+        raise ValueError(f"expected packed uint32 weight, got {weight.dtype}")
+    bias = getattr(layer, "bias", None)
+    return Q6LinearSpec(
+        weight=weight,
+        scales=layer.scales.to(torch.bfloat16),
+        qbiases=layer.biases.to(torch.bfloat16),
+        bias=None if bias is None else bias.to(torch.bfloat16),
+        group_size=group_size,
+        bits=bits,
+    )
+
+
+@dataclass(frozen=True)
+class DenseLinearWeights:
+    weight: torch.Tensor  # [N, K]
+    bias: torch.Tensor | None
+
+
+def dequantize_linear(spec: Q6LinearSpec, *, dtype: torch.dtype = torch.bfloat16) -> DenseLinearWeights:
+    weight = ops.q6_dequantize(spec.weight, spec.scales, spec.qbiases, spec.group_size).to(dtype)
+    bias = None if spec.bias is None else spec.bias.to(dtype)
+    return DenseLinearWeights(weight=weight, bias=bias)
+
+
+def affine_q6_qmm_t(
+    x: torch.Tensor,
+    spec: Q6LinearSpec,
+    *,
+    apply_gelu: bool = False,
+    dtype: torch.dtype | None = None,
+) -> torch.Tensor:
+    """Affine q6 matmul, weight in Linear layout: act(x @ W.T + b)."""
+
+    if x.dim() not in (2, 3):
+        raise ValueError(f"expected x with rank 2 or 3, got shape {tuple(x.shape)}")
+    out_dtype = x.dtype if dtype is None else dtype
+    if x.shape[-1] != spec.in_features:
+        raise ValueError(f"x in_features {x.shape[-1]} != weight in_features {spec.in_features}")
+    xin = x.to(torch.float32) if out_dtype == torch.float32 else x.to(torch.bfloat16)
+    y = ops.q6_linear(xin, spec.weight, spec.scales, spec.qbiases, spec.bias,
+                      group_size=spec.group_size, apply_gelu=apply_gelu)
+    return y.to(out_dtype)
+
+
+def fused_q6_mlp(hidden: torch.Tensor, mlp_in: Q6LinearSpec, mlp_out: Q6LinearSpec) -> torch.Tensor:
+    """Image/text MLP: q6 mlp_in + GELU epilogue, then q6 mlp_out."""
+
+    if hidden.dtype == torch.float32:
+        mid = affine_q6_qmm_t(hidden, mlp_in, apply_gelu=True)
+        return affine_q6_qmm_t(mid, mlp_out, apply_gelu=False)
+    return ops.q6_mlp(
+        hidden,
+        (mlp_in.weight, mlp_in.scales, mlp_in.qbiases, mlp_in.bias),
+        (mlp_out.weight, mlp_out.scales, mlp_out.qbiases, mlp_out.bias),
+        group_size=mlp_in.group_size,
+    ).to(hidden.dtype)
+
+
+def dense_mlp(hidden: torch.Tensor, mlp_in: DenseLinearWeights, mlp_out: DenseLinearWeights) -> torch.Tensor:
+    """Dense Linear math with already-dequantised weights (library GEMM; an upper bound)."""
+
+    mid = hidden @ mlp_in.weight.T
+    if mlp_in.bias is not None:
+        mid = mid + mlp_in.bias
+    mid = F.gelu(mid, approximate="tanh")
+    out = mid @ mlp_out.weight.T
+    if mlp_out.bias is not None:
+        out = out + mlp_out.bias
+    return out
+
+
+def dense_mlp_from_q6(hidden: torch.Tensor, mlp_in: Q6LinearSpec, mlp_out: Q6LinearSpec) -> torch.Tensor:
+    """Dequantise each call, then dense math (diagnostic; includes the unpack cost)."""
+
+    return dense_mlp(hidden, dequantize_linear(mlp_in, dtype=hidden.dtype), dequantize_linear(mlp_out, dtype=hidden.dtype))
+
+
+def eager_q6_mlp(ff: torch.nn.Module, hidden: torch.Tensor) -> torch.Tensor:
+    hidden = ff.mlp_in(hidden)
+    hidden = F.gelu(hidden, approximate="tanh")
+    hidden = ff.mlp_out(hidden)
+    return hidden
+
+
+def make_feed_forward_callables(
+    ff: torch.nn.Module, *, dtype: torch.dtype = torch.bfloat16
+) -> tuple[Callable[[torch.Tensor], torch.Tensor], Callable[[torch.Tensor], torch.Tensor], Callable[[torch.Tensor], torch.Tensor]]:
+    """Return (eager_q6, fused_q6, dense_predequant) callables for one FF module."""
+
+    mlp_in = quantized_linear_spec(ff.mlp_in)
+    mlp_out = quantized_linear_spec(ff.mlp_out)
+    dense_in = dequantize_linear(mlp_in, dtype=dtype)
+    dense_out = dequantize_linear(mlp_out, dtype=dtype)
+    return (
+        lambda x, module=ff: eager_q6_mlp(module, x),
+        lambda x, a=mlp_in, b=mlp_out: fused_q6_mlp(x, a, b),
+        lambda x, a=dense_in, b=dense_out: dense_mlp(x, a, b),
+    )
+
+
+class QwenFeedForward(torch.nn.Module):
+    """``img_ff`` / ``txt_ff`` shaped module: mlp_in (D -> H), GELU-tanh, mlp_out (H -> D)."""
+
+    def __init__(self, mlp_in: QuantizedLinear, mlp_out: QuantizedLinear) -> None:
+        super().__init__()
+        self.mlp_in = mlp_in
+        self.mlp_out = mlp_out
+
+    @classmethod
+    def random(cls, dim: int = 3072, hidden: int = 12288, *, group_size: int = 64, std: float = 0.02,
+               bias_std: float = 0.01, generator: torch.Generator | None = None,
+               device: torch.device | str = "cuda") -> "QwenFeedForward":
+        def make(n: int, k: int) -> QuantizedLinear:
+            w = torch.randn((n, k), generator=generator, device=device) * std
+            q, s, b = quantize_affine_q6(w, group_size)
+            bias = (torch.randn((n,), generator=generator, device=device) * bias_std).to(torch.bfloat16)
+            return QuantizedLinear(q, s, b, bias, group_size=group_size)
+
+        return cls(make(hidden, dim), make(dim, hidden))
+
+    def forward(self, hidden: torch.Tensor) -> torch.Tensor:
+        return fused_q6_mlp(hidden, quantized_linear_spec(self.mlp_in), quantized_linear_spec(self.mlp_out))

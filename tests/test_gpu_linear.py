@@ -1,0 +1,217 @@
+"""GPU parity of the q6 kernels against the CPU oracle, through the C ABI.
+
+Bars:
+* dequantised weights: bit-exact vs bf16_rn(fp32(s)*q + fp32(b));
+* bf16 matmul outputs: max|err| <= 2e-2 * max|ref| and mean|err| <= 1e-3 * rms(ref)
+  against the oracle with the same weight precision (bf16 weights for the
+  tensor-core path, fp32 weights for the CUDA-core path);
+* against the reference kernel's own golden outputs (fp32 weights), the
+  tensor-core path meets max-abs-rel 2e-2 and the reference tests' own bar
+  of max|err| < 0.05 (tests/test_q6_metal_mlp.py:35-45);
+* fp32 path vs the fp32 golden: max|err| < 1e-5 (tests/test_q6_steel_mlp.py:13-33).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from qwen_image_shardedit_mlx_b200 import ops
+from tests.conftest import golden_case
+from tests.helpers import (
+    assert_close,
+    f32,
+    from_bits,
+    random_bf16,
+    random_weights,
+    to_bits,
+    u32_to_torch,
+    weights_to_torch,
+)
+
+pytestmark = pytest.mark.gpu
+
+BF16_GOLDEN = ["linear_bf16", "mlp_fc1", "mlp_fc2", "gs32", "gs128"]
+
+
+@pytest.fixture(autouse=True)
+def _no_device_error():
+    yield
+    assert ops.device_error() == 0
+
+
+@pytest.mark.parametrize("gs", [32, 64, 128])
+def test_dequantize_bit_exact(gs):
+    rng = np.random.default_rng(100 + gs)
+    w = random_weights(rng, 300, 3072, gs, bias=False)
+    wt, st, bt, _ = weights_to_torch(w)
+    dense = ops.q6_dequantize(wt, st, bt, gs)
+    torch.cuda.synchronize()
+    assert np.array_equal(to_bits(dense), oracle.dequantize(w.weight, w.scales, w.biases, gs, dtype="bf16"))
+
+
+def test_dequantize_bit_exact_extreme_scales():
+    # scales / biases spanning many binades, including values whose fp32 sum rounds
+    rng = np.random.default_rng(7)
+    n, k, gs = 64, 256, 64
+    codes = rng.integers(0, 64, size=(n, k), dtype=np.uint8)
+    packed = oracle.pack_q6(codes)
+    exps = rng.integers(-40, 20, size=(n, k // gs)).astype(np.float32)
+    scales = oracle.f32_to_bf16_bits((rng.uniform(1, 2, size=(n, k // gs)) * 2.0 ** exps).astype(np.float32))
+    biases = oracle.f32_to_bf16_bits((rng.uniform(-2, 2, size=(n, k // gs)) * 2.0 ** (exps + rng.integers(-10, 10, size=exps.shape))).astype(np.float32))
+    dense = ops.q6_dequantize(u32_to_torch(packed), from_bits(scales), from_bits(biases), gs)
+    torch.cuda.synchronize()
+    assert np.array_equal(to_bits(dense), oracle.c_dequant_bf16(packed, scales, biases, gs))
+
+
+@pytest.mark.parametrize("case", BF16_GOLDEN)
+@pytest.mark.parametrize("path", ["tensor", "simt"])
+def test_reference_golden_bf16(golden, case, path):
+    x, w, y, gelu = golden_case(golden, case)
+    wt, st, bt, bias = weights_to_torch(w)
+    got = ops.q6_linear(from_bits(x), wt, st, bt, bias, group_size=w.group_size, apply_gelu=gelu, path=path)
+    torch.cuda.synchronize()
+    assert ops.last_path() == path
+    ref = oracle.bf16_bits_to_f32(y)
+    assert float(np.abs(f32(got) - ref).max()) < 0.05
+    if path == "simt":
+        # same weight precision as the reference kernel: only summation order differs
+        assert_close(f32(got), ref, what=case)
+    else:
+        # bf16-dequantised weights: compare with the oracle of the same precision
+        xf = oracle.bf16_bits_to_f32(x)
+        assert_close(f32(got), oracle.linear(xf, w, apply_gelu=gelu, weight_dtype="bf16"), what=case)
+        assert_close(f32(got), ref, mean_abs_rel=4e-3, what=case + " vs fp32-weight golden")
+
+
+def test_reference_golden_f32(golden):
+    x, w, y, gelu = golden_case(golden, "linear_f32")
+    wt, st, bt, bias = weights_to_torch(w)
+    got = ops.q6_linear(torch.from_numpy(x).cuda(), wt, st, bt, bias, group_size=w.group_size)
+    torch.cuda.synchronize()
+    assert got.dtype == torch.float32
+    assert float(np.abs(f32(got) - y).max()) < 1e-5
+
+
+SHAPES = [
+    # (M, N, K, gs)
+    (5, 128, 64, 64),
+    (16, 384, 192, 32),
+    (17, 300, 256, 128),
+    (130, 640, 1024, 64),
+    (256, 3072, 3072, 64),
+    (333, 256, 12288, 64),
+    (1000, 96, 512, 32),
+]
+
+
+@pytest.mark.parametrize("m,n,k,gs", SHAPES)
+@pytest.mark.parametrize("epi", ["plain", "bias_gelu", "residual_gate"])
+def test_tensor_path_vs_oracle(m, n, k, gs, epi):
+    rng = np.random.default_rng(m * 7 + n * 3 + k)
+    w = random_weights(rng, n, k, gs, bias=epi != "plain")
+    x = random_bf16(rng, (m, k))
+    wt, st, bt, bias = weights_to_torch(w)
+    kwargs = {}
+    residual = gate = None
+    if epi == "residual_gate":
+        residual = random_bf16(rng, (m, n))
+        gate = random_bf16(rng, (n,), 0.5)
+        kwargs = dict(residual=from_bits(residual), gate=from_bits(gate))
+    got = ops.q6_linear(from_bits(x), wt, st, bt, bias, group_size=gs, apply_gelu=epi == "bias_gelu",
+                        path="tensor", **kwargs)
+    torch.cuda.synchronize()
+    ref = oracle.linear(
+        oracle.bf16_bits_to_f32(x), w, apply_gelu=epi == "bias_gelu", weight_dtype="bf16",
+        residual=None if residual is None else oracle.bf16_bits_to_f32(residual),
+        gate=None if gate is None else oracle.bf16_bits_to_f32(gate),
+    )
+    assert_close(f32(got), ref, what=f"{m}x{n}x{k} gs{gs} {epi}")
+
+
+@pytest.mark.parametrize("m,n,k", [(16, 128, 64), (5, 96, 256), (40, 200, 128), (200, 130, 192), (700, 256, 64)])
+@pytest.mark.parametrize("path", ["tensor", "simt"])
+def test_every_output_written(m, n, k, path):
+    """The output buffer starts as NaN; every element must be overwritten."""
+
+    rng = np.random.default_rng(m + n + k)
+    w = random_weights(rng, n, k, 64)
+    x = random_bf16(rng, (m, k))
+    wt, st, bt, bias = weights_to_torch(w)
+    out = torch.full((m, n), float("nan"), dtype=torch.bfloat16, device="cuda")
+    got = ops.q6_linear(from_bits(x), wt, st, bt, bias, group_size=64, path=path, out=out)
+    torch.cuda.synchronize()
+    assert got.data_ptr() == out.data_ptr()
+    assert bool(torch.isfinite(got).all())
+    ref = oracle.linear(oracle.bf16_bits_to_f32(x), w, weight_dtype="bf16" if path == "tensor" else "f32")
+    assert_close(f32(got), ref)
+
+
+@pytest.mark.parametrize("m", [1, 2, 3, 4, 7])
+def test_simt_path_small_m(m):
+    rng = np.random.default_rng(40 + m)
+    w = random_weights(rng, 1000, 3072, 64)
+    x = random_bf16(rng, (m, 3072))
+    wt, st, bt, bias = weights_to_torch(w)
+    got = ops.q6_linear(from_bits(x), wt, st, bt, bias, group_size=64, path="simt")
+    torch.cuda.synchronize()
+    ref = oracle.linear(oracle.bf16_bits_to_f32(x), w, weight_dtype="f32")
+    assert_close(f32(got), ref)
+
+
+def test_auto_path_choice():
+    rng = np.random.default_rng(1)
+    w = random_weights(rng, 256, 128, 64)
+    wt, st, bt, bias = weights_to_torch(w)
+    ops.q6_linear(from_bits(random_bf16(rng, (2, 128))), wt, st, bt, bias)
+    assert ops.last_path() == "simt"
+    ops.q6_linear(from_bits(random_bf16(rng, (64, 128))), wt, st, bt, bias)
+    assert ops.last_path() == "tensor"
+    torch.cuda.synchronize()
+
+
+def test_mlp_vs_oracle_fused_order():
+    rng = np.random.default_rng(21)
+    m, d, h = 300, 512, 2048
+    fc1 = random_weights(rng, h, d, 64)
+    fc2 = random_weights(rng, d, h, 64)
+    x = random_bf16(rng, (m, d))
+    y = ops.q6_mlp(from_bits(x), weights_to_torch(fc1), weights_to_torch(fc2), group_size=64)
+    torch.cuda.synchronize()
+    ref = oracle.fused_mlp(oracle.bf16_bits_to_f32(x), fc1, fc2)
+    assert_close(f32(y), ref)
+    eager = oracle.eager_mlp(oracle.bf16_bits_to_f32(x), fc1, fc2)
+    assert float(np.abs(f32(y) - eager).max()) < 0.05
+
+
+def test_mlp_image_ff_full_size_rows_sample():
+    """Config-2 shapes (3456 tokens, 3072 -> 12288 -> 3072): full run on the GPU,
+    oracle on a sample of rows (each output row depends only on its input row)."""
+
+    rng = np.random.default_rng(2)
+    m, d, h = 3456, 3072, 12288
+    fc1 = random_weights(rng, h, d, 64)
+    fc2 = random_weights(rng, d, h, 64)
+    x = random_bf16(rng, (m, d))
+    y = ops.q6_mlp(from_bits(x), weights_to_torch(fc1), weights_to_torch(fc2), group_size=64)
+    torch.cuda.synchronize()
+    rows = np.sort(rng.choice(m, size=48, replace=False))
+    rows[0], rows[-1] = 0, m - 1
+    ref = oracle.fused_mlp(oracle.bf16_bits_to_f32(x[rows]), fc1, fc2)
+    assert_close(f32(y)[rows], ref)
+
+
+def test_dropin_feed_forward_module():
+    from qwen_image_shardedit_mlx_b200 import QwenFeedForward, make_feed_forward_callables
+
+    g = torch.Generator(device="cuda").manual_seed(0)
+    ff = QwenFeedForward.random(256, 1024, generator=g)
+    x = torch.randn((1, 12, 256), generator=g, device="cuda").to(torch.bfloat16)
+    eager, fused, dense = make_feed_forward_callables(ff)
+    ye, yf, yd = eager(x), fused(x), dense(x)
+    assert yf.shape == (1, 12, 256) and yf.dtype == torch.bfloat16
+    assert float((ye.float() - yf.float()).abs().max()) < 0.05
+    assert float((yd.float() - yf.float()).abs().max()) < 0.05
+    assert torch.equal(ff(x), yf)
