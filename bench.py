@@ -1,0 +1,475 @@
+#!/usr/bin/env python3
+"""Benchmark of the q6 image feed-forward MLP (one Qwen-Image MMDiT block's img_ff).
+
+Workload (one step): x bf16 [3456, 3072] (1728 target + 1728 reference-image
+tokens of a 576x768 edit) -> q6 fc1 3072->12288 (+bias, GELU-tanh) -> q6 fc2
+12288->3072 (+bias), MLX affine 6-bit weights with group size 64, seeded
+synthetic N(0,1) activations and N(0,0.02) weights (no checkpoint exists here).
+4 * 3456 * 3072 * 12288 = 521.84 GFLOP per step.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One process per GPU (torchrun for N > 1).  The MLP is token-sharded: every
+rank runs its own 3456-token batch with replicated weights and no collective
+on the data path (weak scaling); the job value is all ranks' FLOPs over the
+slowest rank's device time.  Rank 0 prints one JSON line.
+
+--impl reference times the reference's own q6 kernel source
+(shardedit_mlx/q6_metal_mlp.py SOURCE_QMM_T, compiled for the host by
+oracle/build_ref.py) on the host cores, on a bounded token sample.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+TOKENS, DIM, HIDDEN, GROUP = 3456, 3072, 12288, 64
+FLOP_PER_STEP = 4 * TOKENS * DIM * HIDDEN  # two linears, 2*M*N*K each
+METRIC = "q6 img-FF MLP TFLOP/s & % bf16 peak at M=3456; q6 GEMV HBM GB/s; block ms 1/2/4/8 GPU"
+WORKLOAD = "fused image feed-forward MLP of one MMDiT block, q6 gs64 (3456 tokens, 3072->12288->3072)"
+L2_BYTES = 126 * 2**20
+
+
+def parse_args() -> argparse.Namespace:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the host-core baseline leg")
+    ap.add_argument("--no-gemv", action="store_true", help="skip the skinny-M GEMV side measurement")
+    return ap.parse_args()
+
+
+def measured_peaks() -> dict:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        data = json.loads(path.read_text())
+        return {"hbm_gbs": float(data["hbm_gbs"]), "bf16_tflops": float(data["bf16_tflops"]),
+                "bf16_tflops_sustained": float(data.get("bf16_tflops_sustained", data["bf16_tflops"])),
+                "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+def profiled_traffic() -> dict:
+    """Per-launch DRAM bytes of the dominant kernels from the committed ncu summary."""
+
+    path = ROOT / "profiles" / "dram_traffic.json"
+    if path.exists():
+        try:
+            return json.loads(path.read_text())
+        except (OSError, ValueError):
+            return {}
+    return {}
+
+
+class ClockSampler:
+    """SM clock and clock-event (throttle) reasons sampled through NVML from a
+    background thread every ~2 ms while the timed region runs (read-only; no
+    GPU setting is touched)."""
+
+    REASONS = {
+        "hw_slowdown": "nvmlClocksEventReasonHwSlowdown",
+        "hw_thermal_slowdown": "nvmlClocksEventReasonHwThermalSlowdown",
+        "sw_thermal_slowdown": "nvmlClocksEventReasonSwThermalSlowdown",
+        "sw_power_cap": "nvmlClocksEventReasonSwPowerCap",
+        "hw_power_brake_slowdown": "nvmlClocksEventReasonHwPowerBrakeSlowdown",
+    }
+
+    def __init__(self, gpu_index: int, period_s: float = 0.002) -> None:
+        self.gpu = gpu_index
+        self.period = period_s
+        self.samples: list[tuple[int, int, int]] = []
+        self._stop = None
+        self._thread = None
+        self._nvml = None
+        self._handle = None
+
+    def _sample(self) -> None:
+        nv = self._nvml
+        sm = nv.nvmlDeviceGetClockInfo(self._handle, nv.NVML_CLOCK_SM)
+        mx = nv.nvmlDeviceGetMaxClockInfo(self._handle, nv.NVML_CLOCK_SM)
+        rs = nv.nvmlDeviceGetCurrentClocksEventReasons(self._handle)
+        self.samples.append((sm, mx, rs))
+
+    def __enter__(self) -> "ClockSampler":
+        import threading
+
+        try:
+            import pynvml as nv
+
+            nv.nvmlInit()
+            self._nvml = nv
+            # NVML enumerates every GPU it can see; map the CUDA ordinal through its UUID.
+            import torch
+
+            uuid = getattr(torch.cuda.get_device_properties(self.gpu), "uuid", None)
+            try:
+                self._handle = nv.nvmlDeviceGetHandleByUUID(f"GPU-{uuid}") if uuid else None
+            except Exception:
+                self._handle = None
+            if self._handle is None:
+                self._handle = nv.nvmlDeviceGetHandleByIndex(self.gpu)
+            self._sample()
+        except Exception:
+            self._nvml = None
+            return self
+        self._stop = threading.Event()
+
+        def loop() -> None:
+            while not self._stop.is_set():
+                try:
+                    self._sample()
+                except Exception:
+                    return
+                self._stop.wait(self.period)
+
+        self._thread = threading.Thread(target=loop, daemon=True)
+        self._thread.start()
+        return self
+
+    def __exit__(self, *exc) -> None:
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join(timeout=5)
+            try:
+                self._sample()
+            except Exception:
+                pass
+        if self._nvml is not None:
+            try:
+                self._nvml.nvmlShutdown()
+            except Exception:
+                pass
+
+    def summary(self) -> dict:
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        reasons: set[str] = set()
+        nv = self._nvml
+        for _, _, rs in self.samples:
+            for name, const in self.REASONS.items():
+                bit = getattr(nv, const, 0) if nv is not None else 0
+                if bit and rs & bit:
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(s[0] for s in self.samples),
+                "sm_max_mhz": max(s[1] for s in self.samples), "reasons": sorted(reasons),
+                "samples": len(self.samples), "source": "nvml"}
+
+
+def dist_setup(args):
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(local)
+    return world, rank, local
+
+
+def barrier(world: int) -> None:
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(value: float, world: int) -> float:
+    if world == 1:
+        return value
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ----------------------------------------------------------------- our arm
+
+
+def make_weights(seed: int, device):
+    import torch
+
+    from qwen_image_shardedit_mlx_b200.quantize import random_q6
+
+    g = torch.Generator(device=device).manual_seed(seed)
+    w1 = random_q6(HIDDEN, DIM, group_size=GROUP, generator=g, device=device)
+    w2 = random_q6(DIM, HIDDEN, group_size=GROUP, generator=g, device=device)
+    b1 = (torch.randn(HIDDEN, generator=g, device=device) * 0.01).to(torch.bfloat16)
+    b2 = (torch.randn(DIM, generator=g, device=device) * 0.01).to(torch.bfloat16)
+    return (*w1, b1), (*w2, b2)
+
+
+def run_ours(args, world: int, rank: int, local: int) -> dict | None:
+    import torch
+
+    from qwen_image_shardedit_mlx_b200 import _lib, ops
+
+    dev = torch.device("cuda", local)
+    peaks = measured_peaks()
+    fc1, fc2 = make_weights(1234, dev)
+    g = torch.Generator(device=dev).manual_seed(4321 + rank)
+    x = torch.randn((TOKENS, DIM), generator=g, device=dev).to(torch.bfloat16)
+    hidden = torch.empty((TOKENS, HIDDEN), dtype=torch.bfloat16, device=dev)
+    y = torch.empty((TOKENS, DIM), dtype=torch.bfloat16, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    # Per-linear launches so each kernel can be timed on the launching stream.
+    def fc1_launch():
+        ops.q6_linear(x, fc1[0], fc1[1], fc1[2], fc1[3], group_size=GROUP, apply_gelu=True, out=hidden)
+
+    def fc2_launch():
+        ops.q6_linear(hidden, fc2[0], fc2[1], fc2[2], fc2[3], group_size=GROUP, out=y)
+
+    for _ in range(max(args.warmup, 3)):
+        fc1_launch()
+        fc2_launch()
+    torch.cuda.synchronize()
+
+    steps = args.steps
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(steps)]
+    barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for i in range(steps):
+            ev[i][0].record(stream)
+            fc1_launch()
+            ev[i][1].record(stream)
+            fc2_launch()
+            ev[i][2].record(stream)
+        end.record(stream)
+        torch.cuda.synchronize()
+    barrier(world)
+    local_ms = start.elapsed_time(end)
+    total_ms = max_over_ranks(local_ms, world)
+    fc1_ms = statistics.mean(ev[i][0].elapsed_time(ev[i][1]) for i in range(steps))
+    fc2_ms = statistics.mean(ev[i][1].elapsed_time(ev[i][2]) for i in range(steps))
+    assert ops.device_error() == 0, "device error word raised during the benchmark"
+
+    # ---- end to end through the public API, host buffers, copies inside the timed region
+    from qwen_image_shardedit_mlx_b200 import QuantizedLinear, QwenFeedForward
+
+    ff = QwenFeedForward(QuantizedLinear(*fc1[:3], fc1[3], group_size=GROUP),
+                         QuantizedLinear(*fc2[:3], fc2[3], group_size=GROUP))
+    x_host = x.cpu().pin_memory()
+    y_host = torch.empty((TOKENS, DIM), dtype=torch.bfloat16).pin_memory()
+    x_dev = torch.empty_like(x)
+    e2e_steps = max(3, min(steps, 20))
+    for _ in range(2):
+        x_dev.copy_(x_host, non_blocking=True)
+        y_host.copy_(ff(x_dev), non_blocking=True)
+    torch.cuda.synchronize()
+    barrier(world)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        x_dev.copy_(x_host, non_blocking=True)
+        y_host.copy_(ff(x_dev), non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1), world)
+
+    # ---- skinny-M GEMV side measurement (HBM-bound), rank 0 only
+    gemv = None
+    if rank == 0 and not args.no_gemv:
+        gemv = measure_gemv(dev, peaks)
+
+    if rank != 0:
+        return None
+    value = FLOP_PER_STEP * steps * world / (total_ms * 1e-3) / 1e12
+    dominant = ("fc2", fc2_ms) if fc2_ms >= fc1_ms else ("fc1", fc1_ms)
+    achieved = (FLOP_PER_STEP / 2) / (dominant[1] * 1e-3) / 1e12
+    traffic = profiled_traffic().get(dominant[0])
+    clock = clocks.summary()
+    line = {
+        "metric": METRIC,
+        "value": round(value, 2),
+        "unit": "TFLOP/s",
+        "n_gpus": world,
+        "steps": steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(total_ms / steps, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights quantised to MLX affine q6 gs64)",
+        "config": {
+            "workload": WORKLOAD,
+            "tokens_per_gpu": TOKENS,
+            "dim": DIM,
+            "hidden": HIDDEN,
+            "group_size": GROUP,
+            "global_batch_tokens": TOKENS * world,
+            "parallelism": f"token-sharded x{world}, weights replicated, no data-path collective",
+            "l2": "no flush: per-step working set ~190 MB (x 21 MB, codes+scales 61 MB, hidden 85 MB, y 21 MB) > 126 MB L2",
+            "token_tile": int(_lib.lib().q6_tensor_token_tile(TOKENS, HIDDEN)),
+        },
+        "fc1_ms": round(fc1_ms, 4),
+        "fc2_ms": round(fc2_ms, 4),
+        "pct_of_bf16_peak": round(100.0 * value / world / peaks["bf16_tflops"], 2),
+        "roofline": {
+            "bound": "tensor",
+            "kernel": f"q6_linear_tc ({dominant[0]}, 2*3456*3072*12288 FLOP per launch)",
+            "achieved": round(achieved, 2),
+            "peak": peaks["bf16_tflops"],
+            "unit": "TFLOP/s",
+            "frac": round(achieved / peaks["bf16_tflops"], 4),
+            "peak_source": f"{peaks['source']} (burst cuBLAS bf16)",
+            "traffic": traffic,
+        },
+        "e2e": {
+            "value": round(FLOP_PER_STEP * e2e_steps * world / (e2e_ms * 1e-3) / 1e12, 2),
+            "unit": "TFLOP/s",
+            "h2d_bytes_per_step": TOKENS * DIM * 2,
+            "d2h_bytes_per_step": TOKENS * DIM * 2,
+            "api": "QwenFeedForward(x) drop-in img_ff; pinned host x in, y out",
+        },
+        "gpu_launches": 2 * steps,
+        "clocks": clock,
+    }
+    if gemv is not None:
+        line["gemv"] = gemv
+    if not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline_port()
+    return line
+
+
+def measure_gemv(dev, peaks) -> dict:
+    """q6 GEMV at M=1 and M=16 (3072 -> 12288, gs64), rotating weight copies > L2."""
+
+    import torch
+
+    from qwen_image_shardedit_mlx_b200 import ops
+    from qwen_image_shardedit_mlx_b200.quantize import random_q6
+
+    n, k = 12288, 3072
+    g = torch.Generator(device=dev).manual_seed(77)
+    copies = []
+    per_copy = n * k * 6 // 8 + 2 * 2 * n * (k // GROUP)
+    count = max(8, int(4 * L2_BYTES // per_copy) + 1)
+    for _ in range(count):
+        copies.append(random_q6(n, k, group_size=GROUP, generator=g, device=dev))
+    out = {}
+    for m in (1, 16):
+        x = torch.randn((m, k), generator=g, device=dev).to(torch.bfloat16)
+        y = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
+
+        def launch(i):
+            w, s, b = copies[i % count]
+            ops.q6_linear(x, w, s, b, group_size=GROUP, out=y)
+
+        for i in range(count):
+            launch(i)
+        torch.cuda.synchronize()
+        reps = 4 * count
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(reps):
+            launch(i)
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / reps
+        nbytes = per_copy + 2 * m * (k + n)
+        gbs = nbytes / (us * 1e-6) / 1e9
+        out[f"m{m}"] = {"us": round(us, 2), "GB/s": round(gbs, 1), "frac_hbm": round(gbs / peaks["hbm_gbs"], 4),
+                        "path": ops.last_path(), "bytes": nbytes}
+    out["note"] = f"3072->12288 gs64, {count} rotating weight copies ({count * per_copy / 2**20:.0f} MB > L2), back-to-back launches"
+    return out
+
+
+# ------------------------------------------------------------ host baselines
+
+
+def cpu_baseline_port(budget_s: float = 12.0) -> dict:
+    """The oracle's torch-CPU restatement (dequantise, then matmul) on a token sample."""
+
+    import torch
+
+    from oracle.cpu_port import mlp_port_flops, time_mlp_port
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    tokens, seconds, steps = time_mlp_port(TOKENS, DIM, HIDDEN, GROUP, budget_s=budget_s)
+    flops = mlp_port_flops(tokens, DIM, HIDDEN) * steps
+    return {"value": round(flops / seconds / 1e12, 4), "unit": "TFLOP/s", "cores": torch.get_num_threads(),
+            "kind": "port",
+            "sample": f"{steps} step(s) of {tokens} tokens through fc1+GELU+fc2 (dequantise per call, torch bf16 matmul)"}
+
+
+def run_reference(args, world: int, rank: int) -> dict | None:
+    if rank != 0:
+        return None
+    from oracle.cpu_port import time_reference_kernel_mlp
+
+    res = time_reference_kernel_mlp(DIM, HIDDEN, GROUP, steps=args.steps, warmup=min(args.warmup, 1))
+    value = res["tflops"]
+    return {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": round(value, 6),
+        "unit": "TFLOP/s",
+        "n_gpus": world,
+        "steps": res["steps"],
+        "warmup": args.warmup,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic",
+        "config": {"workload": WORKLOAD, "tokens_per_step_sample": res["tokens"]},
+        "cpu_baseline": {"value": round(value, 6), "unit": "TFLOP/s", "cores": res["cores"], "kind": res["kind"],
+                         "sample": res["sample"]},
+        "e2e": {"value": round(value, 6), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main() -> int:
+    args = parse_args()
+    if args.impl == "reference":
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        line = run_reference(args, world, rank)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return 0
+    world, rank, local = dist_setup(args)
+    try:
+        line = run_ours(args, world, rank, local)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

@@ -9,22 +9,33 @@
 //     registers and write them straight into TMEM with tcgen05.st, so the
 //     dequantised tile never touches shared memory;
 //   * operand B (N = NT tokens) is the activation tile, TMA-loaded with
-//     128-byte swizzling into shared memory (K-major);
+//     128-byte swizzling into shared memory (K-major, two 64-wide boxes per
+//     stage);
 //   * the fp32 accumulator D (128 lanes x NT columns) sits in TMEM; epilogue
 //     warps read it with tcgen05.ld, add bias, apply GELU / residual gate and
 //     store bf16 rows of y.
 //
-// Warp roles (384 threads): warp 0 TMA producer, warp 1 MMA issuer, warp 2
-// TMEM allocator, warp 3 idle, warps 4-7 epilogue, warps 8-11 dequant.  The
-// CTA is persistent over (token tile, weight tile) pairs; accumulators are
-// double buffered when NT <= 192 so the epilogue of one tile overlaps the main
-// loop of the next.  Every mbarrier wait is bounded (q6_ptx.cuh).
+// One pipeline stage covers K = 128 (eight K=16 MMAs), which amortises the
+// per-stage synchronisation of the single MMA-issuing thread.  The activation
+// ring and the code ring are separate (codes are small, so their ring runs
+// deeper) and each has its own TMA producer thread.
+//
+// Warp roles: warp 0 activation producer, warp 1 MMA issuer, warp 2 TMEM
+// allocator, warp 3 code producer, warps 4-7 epilogue, warps 8.. dequant
+// (kDqSets sets of eight warps; set s takes the stages g % kDqSets == s and is
+// the only writer of TMEM A slot s and of the code slots of that parity - a
+// layout in which three sets rotating over two A slots showed rare corrupted
+// tiles at K = 12288, while one owner per slot never did).  The CTA is
+// persistent over (token tile, weight tile) pairs; accumulators are double
+// buffered when NT <= 192 so the epilogue of one tile overlaps the main loop of
+// the next.  Every mbarrier wait is bounded (q6_ptx.cuh).
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <mutex>
 
 #include "q6_dequant.cuh"
@@ -34,15 +45,26 @@
 namespace q6 {
 namespace {
 
-constexpr int kRows = 128;                       // weight rows per tile (MMA M)
-constexpr int kBK = 64;                          // K per pipeline stage
-constexpr int kCodeRowBytes = kBK * 6 / 8;       // 48 bytes of codes per row per stage
-constexpr int kCodeStageBytes = kRows * kCodeRowBytes;  // 6144
-constexpr int kCodeWordsPerStage = kBK * 6 / 32;        // 12
-constexpr int kAStages = 4;                      // TMEM ring of dequantised A tiles
-constexpr int kAColsPerStage = kBK / 2;          // bf16x2 per 32-bit column
-constexpr int kThreads = 384;
+constexpr int kRows = 128;                               // weight rows per tile (MMA M)
+constexpr int kBK = 128;                                 // K per pipeline stage
+constexpr int kBoxK = 64;                                // K per activation TMA box (128-byte swizzle span)
+constexpr int kCodeRowBytes = kBK * 6 / 8;               // 96 bytes of codes per row per stage
+constexpr int kCodeStageBytes = kRows * kCodeRowBytes;   // 12288
+constexpr int kCodeWordsPerStage = kBK * 6 / 32;         // 24
+constexpr int kAStages = 2;                              // TMEM ring of dequantised A tiles
+// "Stage g consumed by the MMA" barriers, one per stage modulo kADone.  A
+// dequant set moving from stage g - sets to stage g waits for stage g - 2; with
+// kADone a multiple of kAStages and >= kAStages + 3 no waiter can fall two
+// phases behind, for any set count up to 3.
+constexpr int kADone = 6;
+constexpr int kAColsPerStage = kBK / 2;                  // bf16x2 per 32-bit column
+constexpr int kControlThreads = 256;                     // warps 0-3 control, warps 4-7 epilogue
 constexpr int kSmemBudget = 227 * 1024;
+constexpr int kBarrierBytes = 512;
+
+constexpr int kDqWarpsPerSet = 8;                      // two warps per TMEM lane quarter
+
+__host__ __device__ constexpr int tc_threads(int dq_sets) { return kControlThreads + 32 * kDqWarpsPerSet * dq_sets; }
 
 constexpr int pow2_at_least(int v) {
     int p = 32;
@@ -50,22 +72,25 @@ constexpr int pow2_at_least(int v) {
     return p;
 }
 
+constexpr int clampi(int v, int lo, int hi) { return v < lo ? lo : (v > hi ? hi : v); }
+
 template <int NT>
 struct Cfg {
     static_assert(NT % 16 == 0 && NT >= 16 && NT <= 256, "MMA N must be a multiple of 16 in [16, 256]");
     static constexpr int kNAcc = (2 * NT + kAStages * kAColsPerStage <= 512) ? 2 : 1;
-    static constexpr int kXStageBytes = NT * 128;  // NT rows of 64 bf16
-    static constexpr int kStageBytes = kXStageBytes + kCodeStageBytes;
-    static constexpr int kBarrierBytes = 256;
-    static constexpr int kStagesFit = (kSmemBudget - 1024 - kBarrierBytes) / kStageBytes;
-    static constexpr int kStages = kStagesFit > 8 ? 8 : kStagesFit;
-    static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kBarrierBytes;
+    static constexpr int kXBoxBytes = NT * 128;  // NT rows of 64 bf16
+    static constexpr int kXStageBytes = 2 * kXBoxBytes;
+    static constexpr int kUsable = kSmemBudget - 1024 - kBarrierBytes;
+    static constexpr int kXStages = clampi((kUsable * 2 / 3) / kXStageBytes, 2, 8);
+    // even, so that with two dequant sets every code slot belongs to one set
+    static constexpr int kCStages = clampi((kUsable - kXStages * kXStageBytes) / kCodeStageBytes, 2, 12) & ~1;
+    static constexpr int kSmemBytes = 1024 + kXStages * kXStageBytes + kCStages * kCodeStageBytes + kBarrierBytes;
     static constexpr int kAccCols = kNAcc * NT;
     static constexpr int kTmemCols = pow2_at_least(kAccCols + kAStages * kAColsPerStage);
     static constexpr uint32_t kIdesc = idesc_bf16_f32(kRows, NT);
-    static_assert(kStages >= 2, "need at least two pipeline stages");
+    static_assert(kSmemBytes <= kSmemBudget, "shared memory budget");
     static_assert(kTmemCols <= 512, "TMEM budget");
-    static_assert(kXStageBytes % 1024 == 0, "stage bases must stay 1024-byte aligned");
+    static_assert(kXBoxBytes % 1024 == 0, "activation boxes must stay 1024-byte aligned");
 };
 
 struct TcParams {
@@ -76,7 +101,7 @@ struct TcParams {
     const uint16_t* gate;
     uint16_t* y;
     int M, N, K, gs, groups, flags;
-    int tiles_n, num_tiles, k_stages;
+    int tiles_n, num_tiles, k_stages, last_ksteps;
 };
 
 __device__ __forceinline__ float bf16f(uint16_t v) { return __uint_as_float(static_cast<uint32_t>(v) << 16); }
@@ -87,21 +112,23 @@ __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatil
     return __all_sync(0xffffffffu, ok);
 }
 
-template <int NT>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int NT, int kDqSets>
+__global__ void __launch_bounds__(tc_threads(kDqSets), 1)
     q6_linear_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
                         const TcParams p) {
     using C = Cfg<NT>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* x_smem = smem;
-    uint8_t* c_smem = smem + C::kStages * C::kXStageBytes;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(c_smem + C::kStages * kCodeStageBytes);
-    uint64_t* full = bars;
-    uint64_t* empty = full + C::kStages;
-    uint64_t* a_full = empty + C::kStages;
-    uint64_t* a_empty = a_full + kAStages;
-    uint64_t* acc_full = a_empty + kAStages;
+    uint8_t* c_smem = smem + C::kXStages * C::kXStageBytes;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(c_smem + C::kCStages * kCodeStageBytes);
+    uint64_t* x_full = bars;
+    uint64_t* x_empty = x_full + C::kXStages;
+    uint64_t* c_full = x_empty + C::kXStages;
+    uint64_t* c_empty = c_full + C::kCStages;
+    uint64_t* a_full = c_empty + C::kCStages;
+    uint64_t* a_done = a_full + kAStages;  // ring of kADone "stage g consumed by the MMA" barriers
+    uint64_t* acc_full = a_done + kADone;
     uint64_t* acc_empty = acc_full + C::kNAcc;
     uint64_t* drain = acc_empty + C::kNAcc;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
@@ -111,14 +138,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int lane = threadIdx.x & 31;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < C::kStages; ++s) {
-            mbar_init(smem_u32(full + s), 1);
-            mbar_init(smem_u32(empty + s), 1 + 4);  // MMA commit + 4 dequant warps
+        for (int s = 0; s < C::kXStages; ++s) {
+            mbar_init(smem_u32(x_full + s), 1);
+            mbar_init(smem_u32(x_empty + s), 1);  // MMA commit
         }
-        for (int s = 0; s < kAStages; ++s) {
-            mbar_init(smem_u32(a_full + s), 4);
-            mbar_init(smem_u32(a_empty + s), 1);
+        for (int s = 0; s < C::kCStages; ++s) {
+            mbar_init(smem_u32(c_full + s), 1);
+            mbar_init(smem_u32(c_empty + s), kDqWarpsPerSet);  // the warps of the dequant set that read it
         }
+        for (int s = 0; s < kAStages; ++s) mbar_init(smem_u32(a_full + s), kDqWarpsPerSet);
+        for (int s = 0; s < kADone; ++s) mbar_init(smem_u32(a_done + s), 1);
         for (int s = 0; s < C::kNAcc; ++s) {
             mbar_init(smem_u32(acc_full + s), 1);
             mbar_init(smem_u32(acc_empty + s), 4);
@@ -137,81 +166,133 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tmem_base = *tmem_slot;
 
     if (warp == 0) {
-        // ------------------------------------------------ TMA producer
+        // ------------------------------------------------ activation producer
         if (lane == 0) {
             tma_prefetch_map(&tmap_x);
-            tma_prefetch_map(&tmap_w);
-            int stage = 0;
-            uint32_t phase = 0;
+            int s = 0;
+            uint32_t ph = 0;
             long issued = 0;
             bool ok = true;
             for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
                 const int mb = tile / p.tiles_n;
-                const int nb = tile - mb * p.tiles_n;
                 for (int ks = 0; ks < p.k_stages; ++ks) {
-                    if (!mbar_wait(smem_u32(empty + stage), phase ^ 1u, abort_flag, 1)) {
+                    if (!mbar_wait(smem_u32(x_empty + s), ph ^ 1u, abort_flag, 1)) {
                         ok = false;
                         break;
                     }
-                    const uint32_t fb = smem_u32(full + stage);
-                    mbar_arrive_expect_tx(fb, C::kStageBytes);
-                    tma_load_2d(smem_u32(x_smem + stage * C::kXStageBytes), &tmap_x, fb, ks * kBK, mb * NT);
-                    tma_load_2d(smem_u32(c_smem + stage * kCodeStageBytes), &tmap_w, fb,
-                                ks * kCodeWordsPerStage, nb * kRows);
+                    const uint32_t fb = smem_u32(x_full + s);
+                    const uint32_t dst = smem_u32(x_smem + s * C::kXStageBytes);
+                    mbar_arrive_expect_tx(fb, C::kXStageBytes);
+                    tma_load_2d(dst, &tmap_x, fb, ks * kBK, mb * NT);
+                    tma_load_2d(dst + C::kXBoxBytes, &tmap_x, fb, ks * kBK + kBoxK, mb * NT);
                     ++issued;
-                    if (++stage == C::kStages) {
-                        stage = 0;
-                        phase ^= 1u;
+                    if (++s == C::kXStages) {
+                        s = 0;
+                        ph ^= 1u;
                     }
                 }
             }
             // Every issued copy must land before this CTA may exit.
-            const long tail = issued < C::kStages ? issued : C::kStages;
+            const long tail = issued < C::kXStages ? issued : C::kXStages;
             for (long i = 0; i < tail; ++i) {
                 const long L = issued - 1 - i;
-                mbar_wait_drain(smem_u32(full + (L % C::kStages)), static_cast<uint32_t>((L / C::kStages) & 1));
+                mbar_wait_drain(smem_u32(x_full + (L % C::kXStages)), static_cast<uint32_t>((L / C::kXStages) & 1));
+            }
+        }
+    } else if (warp == 3) {
+        // ------------------------------------------------ code producer
+        if (lane == 0) {
+            tma_prefetch_map(&tmap_w);
+            int s = 0;
+            uint32_t ph = 0;
+            long issued = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+                const int nb = tile % p.tiles_n;
+                for (int ks = 0; ks < p.k_stages; ++ks) {
+                    if (!mbar_wait(smem_u32(c_empty + s), ph ^ 1u, abort_flag, 8)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t fb = smem_u32(c_full + s);
+                    mbar_arrive_expect_tx(fb, kCodeStageBytes);
+                    tma_load_2d(smem_u32(c_smem + s * kCodeStageBytes), &tmap_w, fb, ks * kCodeWordsPerStage,
+                                nb * kRows);
+                    ++issued;
+                    if (++s == C::kCStages) {
+                        s = 0;
+                        ph ^= 1u;
+                    }
+                }
+            }
+            const long tail = issued < C::kCStages ? issued : C::kCStages;
+            for (long i = 0; i < tail; ++i) {
+                const long L = issued - 1 - i;
+                mbar_wait_drain(smem_u32(c_full + (L % C::kCStages)), static_cast<uint32_t>((L / C::kCStages) & 1));
             }
         }
     } else if (warp == 1) {
         // ------------------------------------------------ MMA issuer
         if (lane == 0) {
-            int stage = 0, astage = 0, acc = 0;
-            uint32_t phase = 0, aphase = 0, accphase = 0;
+            int xs = 0, as = 0, acc = 0, gdone = 0;
+            uint32_t xph = 0, aph = 0, accph = 0;
             bool ok = true;
             for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
-                if (!mbar_wait(smem_u32(acc_empty + acc), accphase ^ 1u, abort_flag, 2)) break;
-                tc_fence_after();
+                if (!mbar_wait(smem_u32(acc_empty + acc), accph ^ 1u, abort_flag, 2)) break;
                 const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * NT);
+                if (!mbar_wait(smem_u32(x_full + xs), xph, abort_flag, 3) ||
+                    !mbar_wait(smem_u32(a_full + as), aph, abort_flag, 4))
+                    break;
+                tc_fence_after();
                 for (int ks = 0; ks < p.k_stages; ++ks) {
-                    if (!mbar_wait(smem_u32(full + stage), phase, abort_flag, 3) ||
-                        !mbar_wait(smem_u32(a_full + astage), aphase, abort_flag, 4)) {
+                    const bool last = ks + 1 == p.k_stages;
+                    const int nk = last ? p.last_ksteps : kBK / 16;  // 8, or 4 for a K % 128 == 64 tail
+                    const uint32_t a_tmem = tmem_base + static_cast<uint32_t>(C::kAccCols + as * kAColsPerStage);
+                    const uint32_t xb = smem_u32(x_smem + xs * C::kXStageBytes);
+                    const uint64_t bdesc0 = sdesc_kmajor_sw128(xb);
+                    const uint64_t bdesc1 = sdesc_kmajor_sw128(xb + C::kXBoxBytes);
+                    auto issue = [&](int kk) {
+                        const uint64_t bd = (kk < 4 ? bdesc0 : bdesc1) + static_cast<uint64_t>((kk & 3) * 2);
+                        mma_bf16_ts(d_tmem, a_tmem + kk * 8, bd, C::kIdesc, (ks | kk) != 0 ? 1u : 0u);
+                    };
+                    // All but the last two MMAs of this stage go first; the
+                    // next stage's barriers are then checked while those MMAs
+                    // keep the tensor pipe busy.
+                    if (nk == kBK / 16) {
+#pragma unroll
+                        for (int kk = 0; kk < kBK / 16 - 2; ++kk) issue(kk);
+                    } else {
+                        for (int kk = 0; kk < nk - 2; ++kk) issue(kk);
+                    }
+                    const int nxs = xs + 1 == C::kXStages ? 0 : xs + 1;
+                    const uint32_t nxph = xs + 1 == C::kXStages ? (xph ^ 1u) : xph;
+                    const int nas = as + 1 == kAStages ? 0 : as + 1;
+                    const uint32_t naph = as + 1 == kAStages ? (aph ^ 1u) : aph;
+                    bool next_ok = true;
+                    if (!last) {
+                        next_ok = mbar_wait(smem_u32(x_full + nxs), nxph, abort_flag, 3) &&
+                                  mbar_wait(smem_u32(a_full + nas), naph, abort_flag, 4);
+                    }
+                    issue(nk - 2);
+                    issue(nk - 1);
+                    tc_commit(smem_u32(x_empty + xs));
+                    tc_commit(smem_u32(a_done + gdone));
+                    if (++gdone == kADone) gdone = 0;
+                    xs = nxs;
+                    xph = nxph;
+                    as = nas;
+                    aph = naph;
+                    if (!next_ok) {
                         ok = false;
                         break;
                     }
-                    tc_fence_after();
-                    const uint32_t a_tmem = tmem_base + static_cast<uint32_t>(C::kAccCols + astage * kAColsPerStage);
-                    const uint64_t bdesc = sdesc_kmajor_sw128(smem_u32(x_smem + stage * C::kXStageBytes));
-#pragma unroll
-                    for (int kk = 0; kk < kBK / 16; ++kk) {
-                        mma_bf16_ts(d_tmem, a_tmem + kk * 8, bdesc + static_cast<uint64_t>(kk * 2), C::kIdesc,
-                                    (ks | kk) != 0 ? 1u : 0u);
-                    }
-                    tc_commit(smem_u32(empty + stage));
-                    tc_commit(smem_u32(a_empty + astage));
-                    if (++stage == C::kStages) {
-                        stage = 0;
-                        phase ^= 1u;
-                    }
-                    if (++astage == kAStages) {
-                        astage = 0;
-                        aphase ^= 1u;
-                    }
+                    if (!last) tc_fence_after();
                 }
                 if (!ok) break;
                 tc_commit(smem_u32(acc_full + acc));
                 if (++acc == C::kNAcc) {
                     acc = 0;
-                    accphase ^= 1u;
+                    accph ^= 1u;
                 }
             }
             // All issued MMAs complete before TMEM may be released.
@@ -224,8 +305,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         static_assert(NT % kChunk == 0, "token tile must be a multiple of the load width");
         const int q = warp & 3;
         const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
+        const bool gelu = (p.flags & Q6_EPI_GELU) != 0;
+        // Paired stores: lanes 2i and 2i+1 swap one value so that each writes a
+        // 32-bit word holding two adjacent output columns (even lane: token j,
+        // odd lane: token j+1).  Needs an even row length and 4-byte aligned y.
+        const bool paired = (p.N % 2 == 0) && ((reinterpret_cast<uintptr_t>(p.y) & 3) == 0);
+        const bool odd = (lane & 1) != 0;
         int acc = 0;
-        uint32_t accphase = 0;
+        uint32_t accph = 0;
         for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
             const int mb = tile / p.tiles_n;
             const int nb = tile - mb * p.tiles_n;
@@ -233,7 +320,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const bool n_ok = n < p.N;
             const float bias_n = (n_ok && p.bias) ? bf16f(p.bias[n]) : 0.0f;
             const float gate_n = (n_ok && p.gate) ? bf16f(p.gate[n]) : 1.0f;
-            if (!warp_wait(smem_u32(acc_full + acc), accphase, abort_flag, 5)) break;
+            if (!warp_wait(smem_u32(acc_full + acc), accph, abort_flag, 5)) break;
             tc_fence_after();
 #pragma unroll 1
             for (int c = 0; c < NT / kChunk; ++c) {
@@ -246,19 +333,29 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 tmem_wait_ld();
                 const int m0 = mb * NT + c * kChunk;
-                if (n_ok) {
 #pragma unroll
-                    for (int j = 0; j < kChunk; ++j) {
-                        const int m = m0 + j;
-                        if (m < p.M) {
-                            float val = __uint_as_float(v[j]) + bias_n;
-                            if (p.flags & Q6_EPI_GELU) val = gelu_tanh(val);
-                            if (p.gate) val *= gate_n;
-                            const size_t off = static_cast<size_t>(m) * p.N + n;
-                            if (p.residual) val += bf16f(p.residual[off]);
-                            __nv_bfloat16 h = __float2bfloat16_rn(val);
-                            p.y[off] = *reinterpret_cast<uint16_t*>(&h);
-                        }
+                for (int j = 0; j < kChunk; j += 2) {
+                    // tokens m0 + j (x) and m0 + j + 1 (y) of this lane's column n
+                    float2 val = make_float2(__uint_as_float(v[j]) + bias_n, __uint_as_float(v[j + 1]) + bias_n);
+                    if (gelu) val = gelu_tanh2(val);
+                    if (p.gate) val = __fmul2_rn(val, make_float2(gate_n, gate_n));
+                    if (p.residual && n_ok) {
+                        const size_t off = static_cast<size_t>(m0 + j) * p.N + n;
+                        if (m0 + j < p.M) val.x += bf16f(p.residual[off]);
+                        if (m0 + j + 1 < p.M) val.y += bf16f(p.residual[off + p.N]);
+                    }
+                    if (paired) {
+                        const float send = odd ? val.x : val.y;
+                        const float recv = __shfl_xor_sync(0xffffffffu, send, 1);
+                        const int row = m0 + j + (odd ? 1 : 0);
+                        const uint32_t word = odd ? pack_bf16x2(recv, val.y) : pack_bf16x2(val.x, recv);
+                        if (n_ok && row < p.M)
+                            *reinterpret_cast<uint32_t*>(p.y + static_cast<size_t>(row) * p.N + (n & ~1)) = word;
+                    } else if (n_ok) {
+                        const size_t off = static_cast<size_t>(m0 + j) * p.N + n;
+                        const uint32_t word = pack_bf16x2(val.x, val.y);
+                        if (m0 + j < p.M) p.y[off] = static_cast<uint16_t>(word & 0xFFFFu);
+                        if (m0 + j + 1 < p.M) p.y[off + p.N] = static_cast<uint16_t>(word >> 16);
                     }
                 }
             }
@@ -267,66 +364,86 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (lane == 0) mbar_arrive(smem_u32(acc_empty + acc));
             if (++acc == C::kNAcc) {
                 acc = 0;
-                accphase ^= 1u;
+                accph ^= 1u;
             }
         }
     } else if (warp >= 8) {
         // ------------------------------------------------ dequant -> TMEM
+        // Two sets of eight warps.  Set s takes the stages g with g % 2 == s,
+        // so it alone writes A slot s and code slots of its parity.  Within a
+        // set, warp (half h, lane quarter q) expands K half h of the stage
+        // (64 codes, TMEM columns 32h..32h+31) for the 32 weight rows of q.
+        const int dw = warp - 8;
+        const int set = dw >> 3;
+        const int half = (dw >> 2) & 1;
         const int q = warp & 3;
         const int r = q * 32 + lane;
         const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
-        int stage = 0, astage = 0;
-        uint32_t phase = 0, aphase = 0;
+        uint32_t gstage = 0;
         bool ok = true;
         for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
-            const int mb = tile / p.tiles_n;
-            const int nb = tile - mb * p.tiles_n;
+            const int nb = tile % p.tiles_n;
             const int n = nb * kRows + r;
             const bool n_ok = n < p.N;
             const uint16_t* srow = p.scales + static_cast<size_t>(n_ok ? n : 0) * p.groups;
             const uint16_t* brow = p.qbiases + static_cast<size_t>(n_ok ? n : 0) * p.groups;
-            for (int ks = 0; ks < p.k_stages; ++ks) {
-                const int k0 = ks * kBK;
-                const int g0 = k0 / p.gs;
-                const int g1 = (k0 + kBK / 2) / p.gs;
-                float s0 = 0.f, b0 = 0.f, s1 = 0.f, b1 = 0.f;
-                if (n_ok) {
-                    s0 = bf16f(__ldg(srow + g0));
-                    b0 = bf16f(__ldg(brow + g0));
-                    s1 = bf16f(__ldg(srow + g1));
-                    b1 = bf16f(__ldg(brow + g1));
+            // Scale and bias of the two 32-code quarters of this warp's K half
+            // of stage ks (a quarter never straddles a group: group sizes are
+            // multiples of 32).  Quarters beyond K (a K % 128 == 64 tail) read 0.
+            auto load_sb = [&](int ks, float (&sb)[4]) {
+#pragma unroll
+                for (int qq = 0; qq < 2; ++qq) {
+                    const int k = ks * kBK + half * 64 + qq * 32;
+                    const bool in = n_ok && k < p.K;
+                    const int g = in ? k / p.gs : 0;
+                    sb[2 * qq] = in ? bf16f(__ldg(srow + g)) : 0.0f;
+                    sb[2 * qq + 1] = in ? bf16f(__ldg(brow + g)) : 0.0f;
                 }
-                if (!warp_wait(smem_u32(full + stage), phase, abort_flag, 6)) {
+            };
+            const uint32_t g_base = gstage;
+            gstage += static_cast<uint32_t>(p.k_stages);
+            int ks = static_cast<int>((static_cast<uint32_t>(set) + kDqSets - g_base % kDqSets) % kDqSets);
+            // Prefetch one set-period ahead so the global-load latency hides behind a stage.
+            float sb_next[4];
+            if (ks < p.k_stages) load_sb(ks, sb_next);
+            for (; ks < p.k_stages; ks += kDqSets) {
+                const uint32_t g = g_base + static_cast<uint32_t>(ks);
+                const int cs = static_cast<int>(g % C::kCStages);
+                const uint32_t cph = (g / C::kCStages) & 1u;
+                const int as = static_cast<int>(g % kAStages);
+                float sb[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) sb[i] = sb_next[i];
+                if (ks + kDqSets < p.k_stages) load_sb(ks + kDqSets, sb_next);
+                if (!warp_wait(smem_u32(c_full + cs), cph, abort_flag, 6)) {
                     ok = false;
                     break;
                 }
-                const uint4* src = reinterpret_cast<const uint4*>(c_smem + stage * kCodeStageBytes + r * kCodeRowBytes);
+                const uint4* src =
+                    reinterpret_cast<const uint4*>(c_smem + cs * kCodeStageBytes + r * kCodeRowBytes) + half * 3;
                 const uint4 c0 = src[0], c1 = src[1], c2 = src[2];
                 __syncwarp();
-                if (lane == 0) mbar_arrive(smem_u32(empty + stage));
+                if (lane == 0) mbar_arrive(smem_u32(c_empty + cs));
                 uint32_t a[32];
-                dequant16_bf16x2(c0.x, c0.y, c0.z, s0, b0, a);
-                dequant16_bf16x2(c0.w, c1.x, c1.y, s0, b0, a + 8);
-                dequant16_bf16x2(c1.z, c1.w, c2.x, s1, b1, a + 16);
-                dequant16_bf16x2(c2.y, c2.z, c2.w, s1, b1, a + 24);
-                if (!warp_wait(smem_u32(a_empty + astage), aphase ^ 1u, abort_flag, 7)) {
-                    ok = false;
-                    break;
+                dequant16_bf16x2(c0.x, c0.y, c0.z, sb[0], sb[1], a);
+                dequant16_bf16x2(c0.w, c1.x, c1.y, sb[0], sb[1], a + 8);
+                dequant16_bf16x2(c1.z, c1.w, c2.x, sb[2], sb[3], a + 16);
+                dequant16_bf16x2(c2.y, c2.z, c2.w, sb[2], sb[3], a + 24);
+                // A slot `as` was last read by the MMA of stage g - kAStages.
+                if (g >= static_cast<uint32_t>(kAStages)) {
+                    const uint32_t prev = g - kAStages;
+                    if (!warp_wait(smem_u32(a_done + prev % kADone), (prev / kADone) & 1u, abort_flag, 7)) {
+                        ok = false;
+                        break;
+                    }
                 }
                 tc_fence_after();
-                tmem_st_32x32b_x32(tmem_base + lane_base + static_cast<uint32_t>(C::kAccCols + astage * kAColsPerStage), a);
+                tmem_st_32x32b_x32(
+                    tmem_base + lane_base + static_cast<uint32_t>(C::kAccCols + as * kAColsPerStage + half * 32), a);
                 tmem_wait_st();
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(smem_u32(a_full + astage));
-                if (++stage == C::kStages) {
-                    stage = 0;
-                    phase ^= 1u;
-                }
-                if (++astage == kAStages) {
-                    astage = 0;
-                    aphase ^= 1u;
-                }
+                if (lane == 0) mbar_arrive(smem_u32(a_full + as));
             }
         }
     }
@@ -355,12 +472,10 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     return fn;
 }
 
-bool make_map_2d(CUtensorMap* map, CUtensorMapDataType dtype, int elem_bytes, const void* base, uint64_t inner,
-                 uint64_t outer, uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer,
-                 CUtensorMapSwizzle swizzle) {
+bool make_map_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t inner, uint64_t outer,
+                 uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swizzle) {
     auto fn = encode_fn();
     if (!fn) return false;
-    (void)elem_bytes;
     const cuuint64_t dims[2] = {inner, outer};
     const cuuint64_t strides[1] = {row_bytes};
     const cuuint32_t box[2] = {box_inner, box_outer};
@@ -371,25 +486,25 @@ bool make_map_2d(CUtensorMap* map, CUtensorMapDataType dtype, int elem_bytes, co
     return r == CUDA_SUCCESS;
 }
 
-template <int NT>
+template <int NT, int kDqSets>
 int launch_tc(const LinearArgs& a, cudaStream_t stream) {
     using C = Cfg<NT>;
     static int attr_set_for_device[64] = {0};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return Q6_ERR_CUDA;
     if (dev >= 0 && dev < 64 && !attr_set_for_device[dev]) {
-        if (cudaFuncSetAttribute(q6_linear_tc_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        if (cudaFuncSetAttribute(q6_linear_tc_kernel<NT, kDqSets>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  C::kSmemBytes) != cudaSuccess)
             return Q6_ERR_CUDA;
         attr_set_for_device[dev] = 1;
     }
     CUtensorMap tmap_x, tmap_w;
-    if (!make_map_2d(&tmap_x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.x, a.K, a.M, a.K * 2, kBK, NT,
+    if (!make_map_2d(&tmap_x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.x, a.K, a.M, a.K * 2, kBoxK, NT,
                      CU_TENSOR_MAP_SWIZZLE_128B))
         return Q6_ERR_CUDA;
     const uint64_t words = static_cast<uint64_t>(a.K) * 6 / 32;
-    if (!make_map_2d(&tmap_w, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, a.w, words, a.N, words * 4, kCodeWordsPerStage,
-                     kRows, CU_TENSOR_MAP_SWIZZLE_NONE))
+    if (!make_map_2d(&tmap_w, CU_TENSOR_MAP_DATA_TYPE_UINT32, a.w, words, a.N, words * 4, kCodeWordsPerStage, kRows,
+                     CU_TENSOR_MAP_SWIZZLE_NONE))
         return Q6_ERR_CUDA;
     TcParams p;
     p.scales = a.scales;
@@ -407,10 +522,32 @@ int launch_tc(const LinearArgs& a, cudaStream_t stream) {
     p.tiles_n = static_cast<int>((a.N + kRows - 1) / kRows);
     const int tiles_m = static_cast<int>((a.M + NT - 1) / NT);
     p.num_tiles = tiles_m * p.tiles_n;
-    p.k_stages = static_cast<int>(a.K / kBK);
+    p.k_stages = static_cast<int>((a.K + kBK - 1) / kBK);
+    p.last_ksteps = static_cast<int>((a.K - static_cast<int64_t>(p.k_stages - 1) * kBK) / 16);
     const int grid = std::min(p.num_tiles, device_sm_count());
-    q6_linear_tc_kernel<NT><<<grid, kThreads, C::kSmemBytes, stream>>>(tmap_x, tmap_w, p);
+    q6_linear_tc_kernel<NT, kDqSets><<<grid, tc_threads(kDqSets), C::kSmemBytes, stream>>>(tmap_x, tmap_w, p);
     return cudaGetLastError() == cudaSuccess ? Q6_OK : Q6_ERR_CUDA;
+}
+
+template <int NT>
+int launch_tc_sets(const LinearArgs& a, int dq_sets, cudaStream_t stream) {
+    switch (dq_sets) {
+        case 1: return launch_tc<NT, 1>(a, stream);
+        case 2: return launch_tc<NT, 2>(a, stream);
+        default: return Q6_ERR_UNSUPPORTED;
+    }
+}
+
+// Dequant warp sets per CTA.  Q6_TC_DQ_SETS (1 or 2) overrides the default for tuning.
+int dq_sets_for(int token_tile) {
+    static int env = -1;
+    if (env < 0) {
+        const char* v = std::getenv("Q6_TC_DQ_SETS");
+        env = (v && v[0] >= '1' && v[0] <= '2' && v[1] == 0) ? (v[0] - '0') : 0;
+    }
+    if (env > 0) return env;
+    (void)token_tile;
+    return 2;
 }
 
 }  // namespace
@@ -426,7 +563,7 @@ int error_word_tc(bool clear) {
 }
 
 bool tc_supported(const LinearArgs& a) {
-    if (a.K % kBK != 0) return false;
+    if (a.K % kBoxK != 0) return false;
     if (a.M > (int64_t(1) << 30) || a.N > (int64_t(1) << 30) || a.K > (int64_t(1) << 24)) return false;
     if (reinterpret_cast<uintptr_t>(a.x) % 16 != 0) return false;
     if (reinterpret_cast<uintptr_t>(a.w) % 16 != 0) return false;
@@ -434,6 +571,10 @@ bool tc_supported(const LinearArgs& a) {
 }
 
 int choose_token_tile(int64_t M, int64_t N) {
+    if (const char* v = std::getenv("Q6_TC_TOKEN_TILE")) {
+        const int t = std::atoi(v);
+        if (t == 16 || t == 32 || t == 64 || t == 128 || t == 192 || t == 256) return t;
+    }
     static const int kTiles[] = {256, 192, 128, 64, 32, 16};
     const int64_t sms = device_sm_count();
     const int64_t tiles_n = (N + kRows - 1) / kRows;
@@ -452,13 +593,14 @@ int choose_token_tile(int64_t M, int64_t N) {
 }
 
 int launch_linear_tc(const LinearArgs& a, int token_tile, cudaStream_t stream) {
+    const int sets = dq_sets_for(token_tile);
     switch (token_tile) {
-        case 256: return launch_tc<256>(a, stream);
-        case 192: return launch_tc<192>(a, stream);
-        case 128: return launch_tc<128>(a, stream);
-        case 64: return launch_tc<64>(a, stream);
-        case 32: return launch_tc<32>(a, stream);
-        case 16: return launch_tc<16>(a, stream);
+        case 256: return launch_tc_sets<256>(a, sets, stream);
+        case 192: return launch_tc_sets<192>(a, sets, stream);
+        case 128: return launch_tc_sets<128>(a, sets, stream);
+        case 64: return launch_tc_sets<64>(a, sets, stream);
+        case 32: return launch_tc_sets<32>(a, sets, stream);
+        case 16: return launch_tc_sets<16>(a, sets, stream);
         default: return Q6_ERR_UNSUPPORTED;
     }
 }

@@ -72,6 +72,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     return ok != 0;
 }
 
+// try_wait with a suspend-time hint: the thread may sleep up to `hint_ns`
+// inside the instruction and is woken when the phase completes, so waiting
+// warps do not spin on issue slots the dequant warps need.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred P;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 P, [%1], %2, %3;\n\t"
+        "selp.b32 %0, 1, 0, P;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+
 // Wait for the phase with the given parity to complete.  Gives up (returns
 // false) when the CTA-wide abort flag is raised or after kWaitLimitNs; in the
 // latter case it raises the abort flag and records `site` in g_device_error.
@@ -79,13 +94,15 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
                                           int site) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_timer_ns();
-    while (true) {
-        if (mbar_try_wait(bar, parity)) return true;
-        if (*abort_flag) return false;
-        if (global_timer_ns() - t0 > kWaitLimitNs) {
-            *abort_flag = 1;
-            record_error(site);
-            return false;
+    for (uint32_t i = 1;; ++i) {
+        if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
+        if ((i & 15u) == 0) {
+            if (*abort_flag) return false;
+            if (global_timer_ns() - t0 > kWaitLimitNs) {
+                *abort_flag = 1;
+                record_error(site);
+                return false;
+            }
         }
     }
 }
@@ -251,6 +268,21 @@ __device__ __forceinline__ float gelu_tanh(float x) {
     const float t = tanh_fast(inner);
 #endif
     return 0.5f * x * (1.0f + t);
+}
+
+// The same GELU on two values with packed fp32x2 arithmetic:
+// 0.5x + 0.5x * tanh(k (x + c x^3)).
+__device__ __forceinline__ float2 gelu_tanh2(float2 x) {
+    const float2 x3 = __fmul2_rn(__fmul2_rn(x, x), x);
+    const float2 inner = __fmul2_rn(make_float2(0.7978845608028654f, 0.7978845608028654f),
+                                    __ffma2_rn(make_float2(0.044715f, 0.044715f), x3, x));
+#if defined(Q6_PRECISE_GELU)
+    const float2 t = make_float2(tanhf(inner.x), tanhf(inner.y));
+#else
+    const float2 t = make_float2(tanh_fast(inner.x), tanh_fast(inner.y));
+#endif
+    const float2 h = __fmul2_rn(make_float2(0.5f, 0.5f), x);
+    return __ffma2_rn(h, t, h);
 }
 
 }  // namespace q6
