@@ -119,6 +119,26 @@ Q6_API int q6_mlp_bf16(const uint16_t* x, const uint32_t* w1, const uint16_t* sc
 
 Q6_API size_t q6_mlp_workspace_bytes(int64_t M, int64_t H);
 
+/*
+ * q6_mlp_bf16 for callers that cannot allocate device memory: the same fused
+ * MLP, but the bf16 hidden activations live in a library-owned static device
+ * array of 32 MiB per GPU (held by every GPU that loads the library until the
+ * process exits) instead of a caller workspace.  Fits M * H * 2 <= 32 MiB
+ * (1365 tokens at H = 12288); larger problems return Q6_ERR_WORKSPACE.
+ * The call allocates nothing.  Its first call on a device looks the array's
+ * address up once (make that first call before any stream capture).  All
+ * calls share the array: calls whose GPU work overlaps race and give wrong
+ * results, so order them on one stream.
+ * No counterpart in the reference: it exists for plugin hosts, FFI bindings
+ * and serving loops that receive only input/output pointers and must not call
+ * cudaMalloc.
+ */
+Q6_API int q6_mlp_bf16_noalloc(const uint16_t* x, const uint32_t* w1, const uint16_t* scales1,
+                               const uint16_t* qbiases1, const uint16_t* bias1, const uint32_t* w2,
+                               const uint16_t* scales2, const uint16_t* qbiases2, const uint16_t* bias2,
+                               const uint16_t* residual, const uint16_t* gate, uint16_t* y, int64_t M,
+                               int64_t D, int64_t H, int group_size, q6_stream_t stream);
+
 /* Device error word (0 = none).  Reading it synchronises the current device. */
 Q6_API int q6_get_device_error(int* code);
 Q6_API int q6_clear_device_error(void);

@@ -50,6 +50,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I, _P, _SZ, _P],
     ),
     "q6_mlp_workspace_bytes": (_SZ, [_I64, _I64]),
+    "q6_mlp_bf16_noalloc": (
+        _I,
+        [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I, _P],
+    ),
     "q6_get_device_error": (_I, [ctypes.POINTER(ctypes.c_int)]),
     "q6_clear_device_error": (_I, []),
     "q6_last_path": (_I, []),
