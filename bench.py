@@ -419,7 +419,7 @@ def cpu_baseline_port(budget_s: float = 12.0) -> dict:
     flops = mlp_port_flops(tokens, DIM, HIDDEN) * steps
     return {"value": round(flops / seconds / 1e12, 4), "unit": "TFLOP/s", "cores": torch.get_num_threads(),
             "kind": "port",
-            "sample": f"{steps} step(s) of {tokens} tokens through fc1+GELU+fc2 (dequantise per call, torch bf16 matmul)"}
+            "sample": f"{steps} step(s) of {tokens} tokens through fc1+GELU+fc2 (bf16 weights dequantised once before timing, torch bf16 matmul)"}
 
 
 def run_reference(args, world: int, rank: int) -> dict | None:
