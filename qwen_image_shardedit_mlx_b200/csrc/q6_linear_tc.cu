@@ -15,14 +15,21 @@
 //     warps read it with tcgen05.ld, add bias, apply GELU / residual gate and
 //     store bf16 rows of y.
 //
-// One pipeline stage covers K = 128 (eight K=16 MMAs), which amortises the
-// per-stage synchronisation of the single MMA-issuing thread.  The activation
-// ring and the code ring are separate (codes are small, so their ring runs
-// deeper) and each has its own TMA producer thread.
+// One pipeline stage covers K = 128 (eight K=16 MMAs).  The single thread that
+// issues the MMAs is on the critical path (each tcgen05.mma and
+// tcgen05.commit holds it for tens of cycles), so a stage costs it exactly one
+// barrier wait ("ready": activations landed and the A tile is in TMEM) and one
+// commit ("done": releases the activation slot and the TMEM A slot).
+//
+// Three TMA rings feed the stage: activations (one producer thread), packed
+// codes (a second producer thread, deeper ring since codes are small), and
+// scales / biases in chunks of 8 groups (issued by the code producer; each
+// chunk serves 2 to 8 stages).  Shapes whose scale rows are not 16-byte
+// aligned read scales with per-lane global loads instead.
 //
 // Warp roles: warp 0 activation producer, warp 1 MMA issuer, warp 2 TMEM
-// allocator, warp 3 code producer, warps 4-7 epilogue, warps 8.. dequant
-// (kDqSets sets of eight warps; set s takes the stages g % kDqSets == s and is
+// allocator, warp 3 code + scale producer, warps 4-7 epilogue, warps 8-23
+// dequant (two sets of eight warps; set s takes the stages g % 2 == s and is
 // the only writer of TMEM A slot s and of the code slots of that parity - a
 // layout in which three sets rotating over two A slots showed rare corrupted
 // tiles at K = 12288, while one owner per slot never did).  The CTA is
@@ -52,17 +59,32 @@ constexpr int kCodeRowBytes = kBK * 6 / 8;               // 96 bytes of codes pe
 constexpr int kCodeStageBytes = kRows * kCodeRowBytes;   // 12288
 constexpr int kCodeWordsPerStage = kBK * 6 / 32;         // 24
 constexpr int kAStages = 2;                              // TMEM ring of dequantised A tiles
-// "Stage g consumed by the MMA" barriers, one per stage modulo kADone.  A
-// dequant set moving from stage g - sets to stage g waits for stage g - 2; with
-// kADone a multiple of kAStages and >= kAStages + 3 no waiter can fall two
-// phases behind, for any set count up to 3.
-constexpr int kADone = 6;
+// Stage g is announced to the MMA issuer by one barrier, ready[g % kRing]
+// (the activation TMA bytes plus one arrival per dequant warp of the stage),
+// and handed back by one MMA commit, done[g % kRing], which frees both its
+// activation slot (g % kXStages) and its TMEM A slot (g % kAStages).  Every
+// agent that waits on done for stage g - d (d <= kRing) has already seen
+// stage g - d - 1 or earlier complete, and every agent that arrives on
+// ready for stage g has seen done(g - kRing) or later, so no wait or arrival
+// can be taken by a phase kRing stages away.
+constexpr int kRing = 8;
 constexpr int kAColsPerStage = kBK / 2;                  // bf16x2 per 32-bit column
 constexpr int kControlThreads = 256;                     // warps 0-3 control, warps 4-7 epilogue
 constexpr int kSmemBudget = 227 * 1024;
 constexpr int kBarrierBytes = 512;
 
 constexpr int kDqWarpsPerSet = 8;                      // two warps per TMEM lane quarter
+constexpr int kDqSets = 2;                              // set s dequantises the stages g % 2 == s
+constexpr int kDqWarps = kDqWarpsPerSet * kDqSets;
+
+// Scales and biases reach shared memory as TMA boxes of 8 groups (16 bytes,
+// the smallest TMA row) x 128 weight rows, one box each per chunk of 8
+// groups (2, 4 or 8 stages for group sizes 32, 64, 128), in a ring of two
+// chunk slots.
+constexpr int kSbGroups = 8;
+constexpr int kSbBoxBytes = kRows * kSbGroups * 2;     // 2048
+constexpr int kSbSlotBytes = 2 * kSbBoxBytes;          // scales box + biases box
+constexpr int kSbSlots = 2;
 
 __host__ __device__ constexpr int tc_threads(int dq_sets) { return kControlThreads + 32 * kDqWarpsPerSet * dq_sets; }
 
@@ -83,12 +105,15 @@ struct Cfg {
     static constexpr int kUsable = kSmemBudget - 1024 - kBarrierBytes;
     static constexpr int kXStages = clampi((kUsable * 2 / 3) / kXStageBytes, 2, 8);
     // even, so that with two dequant sets every code slot belongs to one set
-    static constexpr int kCStages = clampi((kUsable - kXStages * kXStageBytes) / kCodeStageBytes, 2, 12) & ~1;
-    static constexpr int kSmemBytes = 1024 + kXStages * kXStageBytes + kCStages * kCodeStageBytes + kBarrierBytes;
+    static constexpr int kCStages =
+        clampi((kUsable - kXStages * kXStageBytes - kSbSlots * kSbSlotBytes) / kCodeStageBytes, 2, 12) & ~1;
+    static constexpr int kSmemBytes = 1024 + kXStages * kXStageBytes + kCStages * kCodeStageBytes +
+                                      kSbSlots * kSbSlotBytes + kBarrierBytes;
     static constexpr int kAccCols = kNAcc * NT;
     static constexpr int kTmemCols = pow2_at_least(kAccCols + kAStages * kAColsPerStage);
     static constexpr uint32_t kIdesc = idesc_bf16_f32(kRows, NT);
     static_assert(kSmemBytes <= kSmemBudget, "shared memory budget");
+    static_assert(kXStages <= kRing && kRing % kAStages == 0, "stage barrier ring");
     static_assert(kTmemCols <= 512, "TMEM budget");
     static_assert(kXBoxBytes % 1024 == 0, "activation boxes must stay 1024-byte aligned");
 };
@@ -100,7 +125,8 @@ struct TcParams {
     const uint16_t* residual;
     const uint16_t* gate;
     uint16_t* y;
-    int M, N, K, gs, groups, flags;
+    int M, N, K, gs, gs_shift, groups, flags;
+    int sb_shift;  // log2(stages per 8-group chunk) when scales are TMA-staged
     int tiles_n, num_tiles, k_stages, last_ksteps;
 };
 
@@ -112,23 +138,25 @@ __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatil
     return __all_sync(0xffffffffu, ok);
 }
 
-template <int NT, int kDqSets>
+template <int NT, bool kSbTma>
 __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
     q6_linear_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
+                        const __grid_constant__ CUtensorMap tmap_s, const __grid_constant__ CUtensorMap tmap_b,
                         const TcParams p) {
     using C = Cfg<NT>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* x_smem = smem;
     uint8_t* c_smem = smem + C::kXStages * C::kXStageBytes;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(c_smem + C::kCStages * kCodeStageBytes);
-    uint64_t* x_full = bars;
-    uint64_t* x_empty = x_full + C::kXStages;
-    uint64_t* c_full = x_empty + C::kXStages;
+    uint8_t* sb_smem = c_smem + C::kCStages * kCodeStageBytes;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sb_smem + kSbSlots * kSbSlotBytes);
+    uint64_t* ready = bars;            // [kRing] activations landed + A tile in TMEM
+    uint64_t* done = ready + kRing;    // [kRing] MMAs of the stage retired
+    uint64_t* c_full = done + kRing;
     uint64_t* c_empty = c_full + C::kCStages;
-    uint64_t* a_full = c_empty + C::kCStages;
-    uint64_t* a_done = a_full + kAStages;  // ring of kADone "stage g consumed by the MMA" barriers
-    uint64_t* acc_full = a_done + kADone;
+    uint64_t* s_full = c_empty + C::kCStages;  // [kSbSlots] scale chunk landed
+    uint64_t* s_empty = s_full + kSbSlots;     // [kSbSlots] every dequant warp is done with it
+    uint64_t* acc_full = s_empty + kSbSlots;
     uint64_t* acc_empty = acc_full + C::kNAcc;
     uint64_t* drain = acc_empty + C::kNAcc;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
@@ -138,16 +166,18 @@ __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
     const int lane = threadIdx.x & 31;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < C::kXStages; ++s) {
-            mbar_init(smem_u32(x_full + s), 1);
-            mbar_init(smem_u32(x_empty + s), 1);  // MMA commit
+        for (int s = 0; s < kRing; ++s) {
+            mbar_init(smem_u32(ready + s), 1 + kDqWarpsPerSet);  // activation producer + dequant set
+            mbar_init(smem_u32(done + s), 1);                    // MMA commit
         }
         for (int s = 0; s < C::kCStages; ++s) {
             mbar_init(smem_u32(c_full + s), 1);
             mbar_init(smem_u32(c_empty + s), kDqWarpsPerSet);  // the warps of the dequant set that read it
         }
-        for (int s = 0; s < kAStages; ++s) mbar_init(smem_u32(a_full + s), kDqWarpsPerSet);
-        for (int s = 0; s < kADone; ++s) mbar_init(smem_u32(a_done + s), 1);
+        for (int s = 0; s < kSbSlots; ++s) {
+            mbar_init(smem_u32(s_full + s), 1);
+            mbar_init(smem_u32(s_empty + s), kDqWarps);
+        }
         for (int s = 0; s < C::kNAcc; ++s) {
             mbar_init(smem_u32(acc_full + s), 1);
             mbar_init(smem_u32(acc_empty + s), 4);
@@ -169,47 +199,72 @@ __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
         // ------------------------------------------------ activation producer
         if (lane == 0) {
             tma_prefetch_map(&tmap_x);
-            int s = 0;
-            uint32_t ph = 0;
-            long issued = 0;
+            uint32_t g = 0;  // stage counter over all tiles of this CTA
+            int s = 0;       // g % kXStages
             bool ok = true;
             for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
                 const int mb = tile / p.tiles_n;
-                for (int ks = 0; ks < p.k_stages; ++ks) {
-                    if (!mbar_wait(smem_u32(x_empty + s), ph ^ 1u, abort_flag, 1)) {
-                        ok = false;
-                        break;
+                for (int ks = 0; ks < p.k_stages; ++ks, ++g) {
+                    // x slot s was last read by the MMAs of stage g - kXStages.
+                    if (g >= static_cast<uint32_t>(C::kXStages)) {
+                        const uint32_t prev = g - C::kXStages;
+                        if (!mbar_wait(smem_u32(done + prev % kRing), (prev / kRing) & 1u, abort_flag, 1)) {
+                            ok = false;
+                            break;
+                        }
                     }
-                    const uint32_t fb = smem_u32(x_full + s);
+                    const uint32_t fb = smem_u32(ready + g % kRing);
                     const uint32_t dst = smem_u32(x_smem + s * C::kXStageBytes);
                     mbar_arrive_expect_tx(fb, C::kXStageBytes);
                     tma_load_2d(dst, &tmap_x, fb, ks * kBK, mb * NT);
                     tma_load_2d(dst + C::kXBoxBytes, &tmap_x, fb, ks * kBK + kBoxK, mb * NT);
-                    ++issued;
-                    if (++s == C::kXStages) {
-                        s = 0;
-                        ph ^= 1u;
-                    }
+                    if (++s == C::kXStages) s = 0;
                 }
             }
-            // Every issued copy must land before this CTA may exit.
-            const long tail = issued < C::kXStages ? issued : C::kXStages;
-            for (long i = 0; i < tail; ++i) {
-                const long L = issued - 1 - i;
-                mbar_wait_drain(smem_u32(x_full + (L % C::kXStages)), static_cast<uint32_t>((L / C::kXStages) & 1));
+            // Every issued copy must land before this CTA may exit: wait until
+            // the MMAs of the last stages retired (they read those copies).
+            const uint32_t tail = g < static_cast<uint32_t>(C::kXStages) ? g : C::kXStages;
+            for (uint32_t i = 0; i < tail; ++i) {
+                const uint32_t L = g - 1 - i;
+                mbar_wait_drain(smem_u32(done + L % kRing), (L / kRing) & 1u);
             }
         }
     } else if (warp == 3) {
         // ------------------------------------------------ code producer
         if (lane == 0) {
             tma_prefetch_map(&tmap_w);
+            if constexpr (kSbTma) {
+                tma_prefetch_map(&tmap_s);
+                tma_prefetch_map(&tmap_b);
+            }
             int s = 0;
             uint32_t ph = 0;
             long issued = 0;
+            int ss = 0;
+            uint32_t sph = 0;
+            long s_issued = 0;
             bool ok = true;
             for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
                 const int nb = tile % p.tiles_n;
                 for (int ks = 0; ks < p.k_stages; ++ks) {
+                    if (kSbTma && (ks & ((1 << p.sb_shift) - 1)) == 0) {
+                        // first stage of a chunk: its scales and biases
+                        if (!mbar_wait(smem_u32(s_empty + ss), sph ^ 1u, abort_flag, 9)) {
+                            ok = false;
+                            break;
+                        }
+                        const uint32_t fb = smem_u32(s_full + ss);
+                        const uint32_t dst = smem_u32(sb_smem + ss * kSbSlotBytes);
+                        const int gx = (ks >> p.sb_shift) * kSbGroups;
+                        mbar_arrive_expect_tx(fb, kSbSlotBytes);
+                        tma_load_2d(dst, &tmap_s, fb, gx, nb * kRows);
+                        tma_load_2d(dst + kSbBoxBytes, &tmap_b, fb, gx, nb * kRows);
+                        ++s_issued;
+                        if (++ss == kSbSlots) {
+                            ss = 0;
+                            sph ^= 1u;
+                        }
+                    }
                     if (!mbar_wait(smem_u32(c_empty + s), ph ^ 1u, abort_flag, 8)) {
                         ok = false;
                         break;
@@ -230,63 +285,56 @@ __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
                 const long L = issued - 1 - i;
                 mbar_wait_drain(smem_u32(c_full + (L % C::kCStages)), static_cast<uint32_t>((L / C::kCStages) & 1));
             }
+            const long s_tail = s_issued < kSbSlots ? s_issued : kSbSlots;
+            for (long i = 0; i < s_tail; ++i) {
+                const long L = s_issued - 1 - i;
+                mbar_wait_drain(smem_u32(s_full + (L % kSbSlots)), static_cast<uint32_t>((L / kSbSlots) & 1));
+            }
         }
     } else if (warp == 1) {
         // ------------------------------------------------ MMA issuer
+        // The issuing thread blocks for tens of cycles in every tcgen05.mma and
+        // tcgen05.commit, so its loop carries nothing else it can avoid: one
+        // wait, one fence, eight MMAs whose operand addresses are immediate
+        // offsets from per-stage bases, one commit.
         if (lane == 0) {
-            int xs = 0, as = 0, acc = 0, gdone = 0;
-            uint32_t xph = 0, aph = 0, accph = 0;
+            const uint64_t desc_base = sdesc_kmajor_sw128(smem_u32(x_smem));
+            const uint32_t desc_lo = static_cast<uint32_t>(desc_base);
+            const uint32_t desc_hi = static_cast<uint32_t>(desc_base >> 32);
+            const uint32_t a_base = tmem_base + static_cast<uint32_t>(C::kAccCols);
+            uint32_t g = 0;  // stage counter over all tiles of this CTA
+            int xs = 0, acc = 0;
+            uint32_t accph = 0;
             bool ok = true;
             for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
                 if (!mbar_wait(smem_u32(acc_empty + acc), accph ^ 1u, abort_flag, 2)) break;
                 const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * NT);
-                if (!mbar_wait(smem_u32(x_full + xs), xph, abort_flag, 3) ||
-                    !mbar_wait(smem_u32(a_full + as), aph, abort_flag, 4))
-                    break;
-                tc_fence_after();
-                for (int ks = 0; ks < p.k_stages; ++ks) {
-                    const bool last = ks + 1 == p.k_stages;
-                    const int nk = last ? p.last_ksteps : kBK / 16;  // 8, or 4 for a K % 128 == 64 tail
-                    const uint32_t a_tmem = tmem_base + static_cast<uint32_t>(C::kAccCols + as * kAColsPerStage);
-                    const uint32_t xb = smem_u32(x_smem + xs * C::kXStageBytes);
-                    const uint64_t bdesc0 = sdesc_kmajor_sw128(xb);
-                    const uint64_t bdesc1 = sdesc_kmajor_sw128(xb + C::kXBoxBytes);
-                    auto issue = [&](int kk) {
-                        const uint64_t bd = (kk < 4 ? bdesc0 : bdesc1) + static_cast<uint64_t>((kk & 3) * 2);
-                        mma_bf16_ts(d_tmem, a_tmem + kk * 8, bd, C::kIdesc, (ks | kk) != 0 ? 1u : 0u);
-                    };
-                    // All but the last two MMAs of this stage go first; the
-                    // next stage's barriers are then checked while those MMAs
-                    // keep the tensor pipe busy.
-                    if (nk == kBK / 16) {
-#pragma unroll
-                        for (int kk = 0; kk < kBK / 16 - 2; ++kk) issue(kk);
-                    } else {
-                        for (int kk = 0; kk < nk - 2; ++kk) issue(kk);
-                    }
-                    const int nxs = xs + 1 == C::kXStages ? 0 : xs + 1;
-                    const uint32_t nxph = xs + 1 == C::kXStages ? (xph ^ 1u) : xph;
-                    const int nas = as + 1 == kAStages ? 0 : as + 1;
-                    const uint32_t naph = as + 1 == kAStages ? (aph ^ 1u) : aph;
-                    bool next_ok = true;
-                    if (!last) {
-                        next_ok = mbar_wait(smem_u32(x_full + nxs), nxph, abort_flag, 3) &&
-                                  mbar_wait(smem_u32(a_full + nas), naph, abort_flag, 4);
-                    }
-                    issue(nk - 2);
-                    issue(nk - 1);
-                    tc_commit(smem_u32(x_empty + xs));
-                    tc_commit(smem_u32(a_done + gdone));
-                    if (++gdone == kADone) gdone = 0;
-                    xs = nxs;
-                    xph = nxph;
-                    as = nas;
-                    aph = naph;
-                    if (!next_ok) {
+                for (int ks = 0; ks < p.k_stages; ++ks, ++g) {
+                    const uint32_t rs = g % kRing;
+                    if (!mbar_wait(smem_u32(ready + rs), (g / kRing) & 1u, abort_flag, 3)) {
                         ok = false;
                         break;
                     }
-                    if (!last) tc_fence_after();
+                    tc_fence_after();
+                    const uint32_t lo = desc_lo + static_cast<uint32_t>(xs * (C::kXStageBytes >> 4));
+                    const uint32_t a_tmem = a_base + (rs % kAStages) * kAColsPerStage;
+                    const uint32_t first = ks != 0 ? 1u : 0u;
+                    // K step kk reads activation box kk / 4 at 32-byte offset kk % 4
+                    // and TMEM A columns 8 kk .. 8 kk + 7.
+                    auto issue = [&](int kk) {
+                        const uint32_t off = static_cast<uint32_t>((kk / 4) * (C::kXBoxBytes >> 4) + (kk % 4) * 2);
+                        mma_bf16_ts(d_tmem, a_tmem + kk * 8, make_desc(lo + off, desc_hi), C::kIdesc,
+                                    kk == 0 ? first : 1u);
+                    };
+                    if (ks + 1 < p.k_stages || p.last_ksteps == kBK / 16) {
+#pragma unroll
+                        for (int kk = 0; kk < kBK / 16; ++kk) issue(kk);
+                    } else {  // K % 128 == 64 tail: the first box only
+#pragma unroll
+                        for (int kk = 0; kk < kBK / 32; ++kk) issue(kk);
+                    }
+                    tc_commit(smem_u32(done + rs));
+                    if (++xs == C::kXStages) xs = 0;
                 }
                 if (!ok) break;
                 tc_commit(smem_u32(acc_full + acc));
@@ -379,7 +427,8 @@ __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
         const int q = warp & 3;
         const int r = q * 32 + lane;
         const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
-        uint32_t gstage = 0;
+        uint32_t gstage = 0;  // stage counter over all tiles of this CTA
+        uint32_t gchunk = 0;  // scale chunk counter over all tiles of this CTA
         bool ok = true;
         for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
             const int nb = tile % p.tiles_n;
@@ -388,62 +437,109 @@ __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
             const uint16_t* srow = p.scales + static_cast<size_t>(n_ok ? n : 0) * p.groups;
             const uint16_t* brow = p.qbiases + static_cast<size_t>(n_ok ? n : 0) * p.groups;
             // Scale and bias of the two 32-code quarters of this warp's K half
-            // of stage ks (a quarter never straddles a group: group sizes are
-            // multiples of 32).  Quarters beyond K (a K % 128 == 64 tail) read 0.
-            auto load_sb = [&](int ks, float (&sb)[4]) {
-#pragma unroll
-                for (int qq = 0; qq < 2; ++qq) {
-                    const int k = ks * kBK + half * 64 + qq * 32;
-                    const bool in = n_ok && k < p.K;
-                    const int g = in ? k / p.gs : 0;
-                    sb[2 * qq] = in ? bf16f(__ldg(srow + g)) : 0.0f;
-                    sb[2 * qq + 1] = in ? bf16f(__ldg(brow + g)) : 0.0f;
+            // of stage ks: one group for group sizes 64 and 128, two adjacent
+            // groups for 32.  A half beyond K (a K % 128 == 64 tail) gets 0.
+            // Staged path: group gi of the current chunk slot; otherwise a
+            // global load per lane, issued one stage of this set ahead.
+            auto load_sb = [&](int ks, const uint8_t* slot, float (&sb)[4]) {
+                const int k = ks * kBK + half * 64;
+                const bool in = n_ok && k < p.K;
+                const int g = in ? (k >> p.gs_shift) : 0;
+                if constexpr (kSbTma) {
+                    const int gi = g & (kSbGroups - 1);
+                    const uint16_t* srow_s = reinterpret_cast<const uint16_t*>(slot) + r * kSbGroups;
+                    const uint16_t* brow_s = srow_s + kSbBoxBytes / 2;
+                    sb[0] = in ? bf16f(srow_s[gi]) : 0.0f;
+                    sb[1] = in ? bf16f(brow_s[gi]) : 0.0f;
+                    if (p.gs == 32) {
+                        sb[2] = in ? bf16f(srow_s[gi + 1]) : 0.0f;
+                        sb[3] = in ? bf16f(brow_s[gi + 1]) : 0.0f;
+                    } else {
+                        sb[2] = sb[0];
+                        sb[3] = sb[1];
+                    }
+                } else {
+                    (void)slot;
+                    sb[0] = in ? bf16f(__ldg(srow + g)) : 0.0f;
+                    sb[1] = in ? bf16f(__ldg(brow + g)) : 0.0f;
+                    if (p.gs == 32) {
+                        sb[2] = in ? bf16f(__ldg(srow + g + 1)) : 0.0f;
+                        sb[3] = in ? bf16f(__ldg(brow + g + 1)) : 0.0f;
+                    } else {
+                        sb[2] = sb[0];
+                        sb[3] = sb[1];
+                    }
                 }
             };
             const uint32_t g_base = gstage;
             gstage += static_cast<uint32_t>(p.k_stages);
             int ks = static_cast<int>((static_cast<uint32_t>(set) + kDqSets - g_base % kDqSets) % kDqSets);
-            // Prefetch one set-period ahead so the global-load latency hides behind a stage.
             float sb_next[4];
-            if (ks < p.k_stages) load_sb(ks, sb_next);
-            for (; ks < p.k_stages; ks += kDqSets) {
-                const uint32_t g = g_base + static_cast<uint32_t>(ks);
-                const int cs = static_cast<int>(g % C::kCStages);
-                const uint32_t cph = (g / C::kCStages) & 1u;
-                const int as = static_cast<int>(g % kAStages);
-                float sb[4];
-#pragma unroll
-                for (int i = 0; i < 4; ++i) sb[i] = sb_next[i];
-                if (ks + kDqSets < p.k_stages) load_sb(ks + kDqSets, sb_next);
-                if (!warp_wait(smem_u32(c_full + cs), cph, abort_flag, 6)) {
-                    ok = false;
-                    break;
-                }
-                const uint4* src =
-                    reinterpret_cast<const uint4*>(c_smem + cs * kCodeStageBytes + r * kCodeRowBytes) + half * 3;
-                const uint4 c0 = src[0], c1 = src[1], c2 = src[2];
-                __syncwarp();
-                if (lane == 0) mbar_arrive(smem_u32(c_empty + cs));
-                uint32_t a[32];
-                dequant16_bf16x2(c0.x, c0.y, c0.z, sb[0], sb[1], a);
-                dequant16_bf16x2(c0.w, c1.x, c1.y, sb[0], sb[1], a + 8);
-                dequant16_bf16x2(c1.z, c1.w, c2.x, sb[2], sb[3], a + 16);
-                dequant16_bf16x2(c2.y, c2.z, c2.w, sb[2], sb[3], a + 24);
-                // A slot `as` was last read by the MMA of stage g - kAStages.
-                if (g >= static_cast<uint32_t>(kAStages)) {
-                    const uint32_t prev = g - kAStages;
-                    if (!warp_wait(smem_u32(a_done + prev % kADone), (prev / kADone) & 1u, abort_flag, 7)) {
+            if (!kSbTma && ks < p.k_stages) load_sb(ks, nullptr, sb_next);
+            // Chunks of 8 scale groups (the whole tile when scales are not staged).
+            // Every dequant warp takes every chunk slot and hands it back, also a
+            // chunk that holds none of its stages, so that each s_empty phase
+            // counts exactly one arrival per warp.
+            const int chunk_len = kSbTma ? (1 << p.sb_shift) : p.k_stages;
+            const int nchunks = kSbTma ? (p.k_stages + chunk_len - 1) >> p.sb_shift : 1;
+            for (int j = 0; j < nchunks && ok; ++j, ++gchunk) {
+                const int ks_end = (j + 1) * chunk_len < p.k_stages ? (j + 1) * chunk_len : p.k_stages;
+                const uint8_t* slot = sb_smem + (gchunk % kSbSlots) * kSbSlotBytes;
+                if constexpr (kSbTma) {
+                    if (!warp_wait(smem_u32(s_full + gchunk % kSbSlots), (gchunk / kSbSlots) & 1u, abort_flag, 10)) {
                         ok = false;
                         break;
                     }
                 }
-                tc_fence_after();
-                tmem_st_32x32b_x32(
-                    tmem_base + lane_base + static_cast<uint32_t>(C::kAccCols + as * kAColsPerStage + half * 32), a);
-                tmem_wait_st();
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(smem_u32(a_full + as));
+                for (; ks < ks_end; ks += kDqSets) {
+                    const uint32_t g = g_base + static_cast<uint32_t>(ks);
+                    const int cs = static_cast<int>(g % C::kCStages);
+                    const uint32_t cph = (g / C::kCStages) & 1u;
+                    const int as = static_cast<int>(g % kAStages);
+                    const uint32_t rs = g % kRing;
+                    float sb[4];
+                    if constexpr (kSbTma) {
+                        load_sb(ks, slot, sb);
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) sb[i] = sb_next[i];
+                        if (ks + kDqSets < p.k_stages) load_sb(ks + kDqSets, nullptr, sb_next);
+                    }
+                    if (!warp_wait(smem_u32(c_full + cs), cph, abort_flag, 6)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint4* src =
+                        reinterpret_cast<const uint4*>(c_smem + cs * kCodeStageBytes + r * kCodeRowBytes) + half * 3;
+                    const uint4 c0 = src[0], c1 = src[1], c2 = src[2];
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(smem_u32(c_empty + cs));
+                    uint32_t a[32];
+                    dequant16_bf16x2(c0.x, c0.y, c0.z, sb[0], sb[1], a);
+                    dequant16_bf16x2(c0.w, c1.x, c1.y, sb[0], sb[1], a + 8);
+                    dequant16_bf16x2(c1.z, c1.w, c2.x, sb[2], sb[3], a + 16);
+                    dequant16_bf16x2(c2.y, c2.z, c2.w, sb[2], sb[3], a + 24);
+                    // A slot `as` was last read by the MMAs of stage g - kAStages.
+                    if (g >= static_cast<uint32_t>(kAStages)) {
+                        const uint32_t prev = g - kAStages;
+                        if (!warp_wait(smem_u32(done + prev % kRing), (prev / kRing) & 1u, abort_flag, 7)) {
+                            ok = false;
+                            break;
+                        }
+                    }
+                    tc_fence_after();
+                    tmem_st_32x32b_x32(
+                        tmem_base + lane_base + static_cast<uint32_t>(C::kAccCols + as * kAColsPerStage + half * 32),
+                        a);
+                    tmem_wait_st();
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(smem_u32(ready + rs));
+                }
+                if constexpr (kSbTma) {
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(smem_u32(s_empty + gchunk % kSbSlots));
+                }
             }
         }
     }
@@ -486,19 +582,27 @@ bool make_map_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, 
     return r == CUDA_SUCCESS;
 }
 
-template <int NT, int kDqSets>
+// Scales and biases can be TMA-staged when every row of them starts on a
+// 16-byte boundary (groups a multiple of 8, 16-byte aligned bases).
+bool sb_tma_ok(const LinearArgs& a) {
+    const int64_t groups = a.K / a.group_size;
+    return groups % kSbGroups == 0 && reinterpret_cast<uintptr_t>(a.scales) % 16 == 0 &&
+           reinterpret_cast<uintptr_t>(a.qbiases) % 16 == 0;
+}
+
+template <int NT, bool kSbTma>
 int launch_tc(const LinearArgs& a, cudaStream_t stream) {
     using C = Cfg<NT>;
     static int attr_set_for_device[64] = {0};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return Q6_ERR_CUDA;
     if (dev >= 0 && dev < 64 && !attr_set_for_device[dev]) {
-        if (cudaFuncSetAttribute(q6_linear_tc_kernel<NT, kDqSets>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        if (cudaFuncSetAttribute(q6_linear_tc_kernel<NT, kSbTma>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  C::kSmemBytes) != cudaSuccess)
             return Q6_ERR_CUDA;
         attr_set_for_device[dev] = 1;
     }
-    CUtensorMap tmap_x, tmap_w;
+    CUtensorMap tmap_x, tmap_w, tmap_s, tmap_b;
     if (!make_map_2d(&tmap_x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.x, a.K, a.M, a.K * 2, kBoxK, NT,
                      CU_TENSOR_MAP_SWIZZLE_128B))
         return Q6_ERR_CUDA;
@@ -506,6 +610,17 @@ int launch_tc(const LinearArgs& a, cudaStream_t stream) {
     if (!make_map_2d(&tmap_w, CU_TENSOR_MAP_DATA_TYPE_UINT32, a.w, words, a.N, words * 4, kCodeWordsPerStage, kRows,
                      CU_TENSOR_MAP_SWIZZLE_NONE))
         return Q6_ERR_CUDA;
+    const uint64_t groups = static_cast<uint64_t>(a.K / a.group_size);
+    if constexpr (kSbTma) {
+        if (!make_map_2d(&tmap_s, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.scales, groups, a.N, groups * 2, kSbGroups,
+                         kRows, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+            !make_map_2d(&tmap_b, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.qbiases, groups, a.N, groups * 2, kSbGroups,
+                         kRows, CU_TENSOR_MAP_SWIZZLE_NONE))
+            return Q6_ERR_CUDA;
+    } else {
+        tmap_s = tmap_w;  // unused
+        tmap_b = tmap_w;
+    }
     TcParams p;
     p.scales = a.scales;
     p.qbiases = a.qbiases;
@@ -517,7 +632,9 @@ int launch_tc(const LinearArgs& a, cudaStream_t stream) {
     p.N = static_cast<int>(a.N);
     p.K = static_cast<int>(a.K);
     p.gs = a.group_size;
-    p.groups = static_cast<int>(a.K / a.group_size);
+    p.gs_shift = a.group_size == 32 ? 5 : (a.group_size == 64 ? 6 : 7);
+    p.sb_shift = p.gs_shift - 4;  // 8 groups of gs codes = gs / 16 stages of 128
+    p.groups = static_cast<int>(groups);
     p.flags = a.flags;
     p.tiles_n = static_cast<int>((a.N + kRows - 1) / kRows);
     const int tiles_m = static_cast<int>((a.M + NT - 1) / NT);
@@ -525,29 +642,14 @@ int launch_tc(const LinearArgs& a, cudaStream_t stream) {
     p.k_stages = static_cast<int>((a.K + kBK - 1) / kBK);
     p.last_ksteps = static_cast<int>((a.K - static_cast<int64_t>(p.k_stages - 1) * kBK) / 16);
     const int grid = std::min(p.num_tiles, device_sm_count());
-    q6_linear_tc_kernel<NT, kDqSets><<<grid, tc_threads(kDqSets), C::kSmemBytes, stream>>>(tmap_x, tmap_w, p);
+    q6_linear_tc_kernel<NT, kSbTma>
+        <<<grid, tc_threads(kDqSets), C::kSmemBytes, stream>>>(tmap_x, tmap_w, tmap_s, tmap_b, p);
     return cudaGetLastError() == cudaSuccess ? Q6_OK : Q6_ERR_CUDA;
 }
 
 template <int NT>
-int launch_tc_sets(const LinearArgs& a, int dq_sets, cudaStream_t stream) {
-    switch (dq_sets) {
-        case 1: return launch_tc<NT, 1>(a, stream);
-        case 2: return launch_tc<NT, 2>(a, stream);
-        default: return Q6_ERR_UNSUPPORTED;
-    }
-}
-
-// Dequant warp sets per CTA.  Q6_TC_DQ_SETS (1 or 2) overrides the default for tuning.
-int dq_sets_for(int token_tile) {
-    static int env = -1;
-    if (env < 0) {
-        const char* v = std::getenv("Q6_TC_DQ_SETS");
-        env = (v && v[0] >= '1' && v[0] <= '2' && v[1] == 0) ? (v[0] - '0') : 0;
-    }
-    if (env > 0) return env;
-    (void)token_tile;
-    return 2;
+int launch_tc_sb(const LinearArgs& a, cudaStream_t stream) {
+    return sb_tma_ok(a) ? launch_tc<NT, true>(a, stream) : launch_tc<NT, false>(a, stream);
 }
 
 }  // namespace
@@ -593,14 +695,13 @@ int choose_token_tile(int64_t M, int64_t N) {
 }
 
 int launch_linear_tc(const LinearArgs& a, int token_tile, cudaStream_t stream) {
-    const int sets = dq_sets_for(token_tile);
     switch (token_tile) {
-        case 256: return launch_tc_sets<256>(a, sets, stream);
-        case 192: return launch_tc_sets<192>(a, sets, stream);
-        case 128: return launch_tc_sets<128>(a, sets, stream);
-        case 64: return launch_tc_sets<64>(a, sets, stream);
-        case 32: return launch_tc_sets<32>(a, sets, stream);
-        case 16: return launch_tc_sets<16>(a, sets, stream);
+        case 256: return launch_tc_sb<256>(a, stream);
+        case 192: return launch_tc_sb<192>(a, stream);
+        case 128: return launch_tc_sb<128>(a, stream);
+        case 64: return launch_tc_sb<64>(a, stream);
+        case 32: return launch_tc_sb<32>(a, stream);
+        case 16: return launch_tc_sb<16>(a, stream);
         default: return Q6_ERR_UNSUPPORTED;
     }
 }

@@ -186,6 +186,12 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(int m, int n) {
            | (static_cast<uint32_t>(m >> 4) << 24); // M / 16
 }
 
+__device__ __forceinline__ uint64_t make_desc(uint32_t lo, uint32_t hi) {
+    uint64_t d;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "r"(lo), "r"(hi));
+    return d;
+}
+
 // Shared-memory matrix descriptor for a K-major tile written by TMA with
 // 128-byte swizzling: rows of 64 bf16 (128 B), 8-row swizzle atoms 1024 B
 // apart.  The tile base must be 1024-byte aligned; stepping K by 16 elements
