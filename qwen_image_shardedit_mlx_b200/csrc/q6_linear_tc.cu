@@ -118,6 +118,13 @@ struct Cfg {
     static_assert(kXBoxBytes % 1024 == 0, "activation boxes must stay 1024-byte aligned");
 };
 
+// Epilogue variants, chosen on the host so that the per-element loop carries
+// no flag tests: bias only, bias + GELU, and the general form (optional
+// GELU, gate and residual).
+constexpr int kEpiPlain = 0;
+constexpr int kEpiGelu = 1;
+constexpr int kEpiGeneral = 2;
+
 struct TcParams {
     const uint16_t* scales;
     const uint16_t* qbiases;
@@ -138,7 +145,7 @@ __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatil
     return __all_sync(0xffffffffu, ok);
 }
 
-template <int NT, bool kSbTma>
+template <int NT, bool kSbTma, int kEpi>
 __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
     q6_linear_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
                         const __grid_constant__ CUtensorMap tmap_s, const __grid_constant__ CUtensorMap tmap_b,
@@ -353,7 +360,7 @@ __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
         static_assert(NT % kChunk == 0, "token tile must be a multiple of the load width");
         const int q = warp & 3;
         const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
-        const bool gelu = (p.flags & Q6_EPI_GELU) != 0;
+        const bool gelu = kEpi == kEpiGelu || (kEpi == kEpiGeneral && (p.flags & Q6_EPI_GELU) != 0);
         // Paired stores: lanes 2i and 2i+1 swap one value so that each writes a
         // 32-bit word holding two adjacent output columns (even lane: token j,
         // odd lane: token j+1).  Needs an even row length and 4-byte aligned y.
@@ -381,13 +388,32 @@ __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
                 }
                 tmem_wait_ld();
                 const int m0 = mb * NT + c * kChunk;
+                if (kEpi != kEpiGeneral && paired && m0 + kChunk <= p.M) {
+                    // Whole chunk inside the token range: one paired 32-bit store
+                    // per token pair, the row pointer advanced by two rows each time.
+                    uint32_t* yp = reinterpret_cast<uint32_t*>(p.y + static_cast<size_t>(m0 + (odd ? 1 : 0)) * p.N +
+                                                               (n & ~1));
+                    const size_t step = static_cast<size_t>(p.N);  // two rows in 32-bit words
+#pragma unroll
+                    for (int j = 0; j < kChunk; j += 2) {
+                        float2 val = __fadd2_rn(make_float2(__uint_as_float(v[j]), __uint_as_float(v[j + 1])),
+                                                make_float2(bias_n, bias_n));
+                        if constexpr (kEpi == kEpiGelu) val = gelu_tanh2(val);
+                        const float send = odd ? val.x : val.y;
+                        const float recv = __shfl_xor_sync(0xffffffffu, send, 1);
+                        const uint32_t word = pack_bf16x2(odd ? recv : val.x, odd ? val.y : recv);
+                        if (n_ok) *yp = word;
+                        yp += step;
+                    }
+                    continue;
+                }
 #pragma unroll
                 for (int j = 0; j < kChunk; j += 2) {
                     // tokens m0 + j (x) and m0 + j + 1 (y) of this lane's column n
                     float2 val = make_float2(__uint_as_float(v[j]) + bias_n, __uint_as_float(v[j + 1]) + bias_n);
                     if (gelu) val = gelu_tanh2(val);
-                    if (p.gate) val = __fmul2_rn(val, make_float2(gate_n, gate_n));
-                    if (p.residual && n_ok) {
+                    if (kEpi == kEpiGeneral && p.gate) val = __fmul2_rn(val, make_float2(gate_n, gate_n));
+                    if (kEpi == kEpiGeneral && p.residual && n_ok) {
                         const size_t off = static_cast<size_t>(m0 + j) * p.N + n;
                         if (m0 + j < p.M) val.x += bf16f(p.residual[off]);
                         if (m0 + j + 1 < p.M) val.y += bf16f(p.residual[off + p.N]);
@@ -590,14 +616,14 @@ bool sb_tma_ok(const LinearArgs& a) {
            reinterpret_cast<uintptr_t>(a.qbiases) % 16 == 0;
 }
 
-template <int NT, bool kSbTma>
+template <int NT, bool kSbTma, int kEpi>
 int launch_tc(const LinearArgs& a, cudaStream_t stream) {
     using C = Cfg<NT>;
     static int attr_set_for_device[64] = {0};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return Q6_ERR_CUDA;
     if (dev >= 0 && dev < 64 && !attr_set_for_device[dev]) {
-        if (cudaFuncSetAttribute(q6_linear_tc_kernel<NT, kSbTma>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        if (cudaFuncSetAttribute(q6_linear_tc_kernel<NT, kSbTma, kEpi>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  C::kSmemBytes) != cudaSuccess)
             return Q6_ERR_CUDA;
         attr_set_for_device[dev] = 1;
@@ -642,14 +668,19 @@ int launch_tc(const LinearArgs& a, cudaStream_t stream) {
     p.k_stages = static_cast<int>((a.K + kBK - 1) / kBK);
     p.last_ksteps = static_cast<int>((a.K - static_cast<int64_t>(p.k_stages - 1) * kBK) / 16);
     const int grid = std::min(p.num_tiles, device_sm_count());
-    q6_linear_tc_kernel<NT, kSbTma>
+    q6_linear_tc_kernel<NT, kSbTma, kEpi>
         <<<grid, tc_threads(kDqSets), C::kSmemBytes, stream>>>(tmap_x, tmap_w, tmap_s, tmap_b, p);
     return cudaGetLastError() == cudaSuccess ? Q6_OK : Q6_ERR_CUDA;
 }
 
+// Staged scales with a specialised epilogue for the MLP's two shapes
+// (bias + GELU, bias only); everything else takes the general epilogue.
 template <int NT>
 int launch_tc_sb(const LinearArgs& a, cudaStream_t stream) {
-    return sb_tma_ok(a) ? launch_tc<NT, true>(a, stream) : launch_tc<NT, false>(a, stream);
+    if (!sb_tma_ok(a)) return launch_tc<NT, false, kEpiGeneral>(a, stream);
+    if (a.residual || a.gate) return launch_tc<NT, true, kEpiGeneral>(a, stream);
+    if (a.flags & Q6_EPI_GELU) return launch_tc<NT, true, kEpiGelu>(a, stream);
+    return launch_tc<NT, true, kEpiPlain>(a, stream);
 }
 
 }  // namespace

@@ -277,11 +277,12 @@ __device__ __forceinline__ float gelu_tanh(float x) {
 }
 
 // The same GELU on two values with packed fp32x2 arithmetic:
-// 0.5x + 0.5x * tanh(k (x + c x^3)).
+// 0.5x + 0.5x * tanh(x (k + k c x^2)), k = sqrt(2/pi), c = 0.044715.
 __device__ __forceinline__ float2 gelu_tanh2(float2 x) {
-    const float2 x3 = __fmul2_rn(__fmul2_rn(x, x), x);
-    const float2 inner = __fmul2_rn(make_float2(0.7978845608028654f, 0.7978845608028654f),
-                                    __ffma2_rn(make_float2(0.044715f, 0.044715f), x3, x));
+    constexpr float k = 0.7978845608028654f;
+    constexpr float kc = 0.7978845608028654f * 0.044715f;
+    const float2 x2 = __fmul2_rn(x, x);
+    const float2 inner = __fmul2_rn(x, __ffma2_rn(make_float2(kc, kc), x2, make_float2(k, k)));
 #if defined(Q6_PRECISE_GELU)
     const float2 t = make_float2(tanhf(inner.x), tanhf(inner.y));
 #else
