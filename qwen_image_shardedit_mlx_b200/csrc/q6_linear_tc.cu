@@ -356,7 +356,7 @@ __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
         }
     } else if (warp >= 4 && warp < 8) {
         // ------------------------------------------------ epilogue
-        constexpr int kChunk = NT >= 32 ? 32 : 16;  // accumulator columns per tcgen05.ld
+        constexpr int kChunk = 16;  // accumulator columns per tcgen05.ld (16 keeps the epilogue within registers)
         static_assert(NT % kChunk == 0, "token tile must be a multiple of the load width");
         const int q = warp & 3;
         const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
@@ -381,11 +381,7 @@ __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
             for (int c = 0; c < NT / kChunk; ++c) {
                 uint32_t v[kChunk];
                 const uint32_t taddr = tmem_base + lane_base + static_cast<uint32_t>(acc * NT + c * kChunk);
-                if constexpr (kChunk == 32) {
-                    tmem_ld_32x32b_x32(taddr, v);
-                } else {
-                    tmem_ld_32x32b_x16(taddr, v);
-                }
+                tmem_ld_32x32b_x16(taddr, v);
                 tmem_wait_ld();
                 const int m0 = mb * NT + c * kChunk;
                 if (kEpi != kEpiGeneral && paired && m0 + kChunk <= p.M) {
