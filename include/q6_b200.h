@@ -72,9 +72,11 @@ Q6_API int q6_dequantize_bf16(const uint32_t* w, const uint16_t* scales, const u
  * y = epi(x @ dequant(W)^T)      x bf16 [M, K], y bf16 [M, N]
  * epi: + bias[n] (if bias), GELU (if flags & Q6_EPI_GELU), then
  *      y = residual[m,n] + gate[n] * value  (each term only if its pointer is non-null).
- * LoRA (lora_a bf16 [K, r], lora_b bf16 [r, N], both non-null): the value gains
- *      lora_scale * ((x @ lora_a) @ lora_b) before the bias; needs
- *      q6_linear_workspace_bytes(M, r) bytes of workspace.
+ * LoRA (lora_xa bf16 [M, r] = x @ A computed by the caller, lora_b bf16 [r, N],
+ *      both non-null, r in {32, 64, 96, 128}): the value gains
+ *      lora_scale * (lora_xa @ lora_b) before the bias, accumulated in the same
+ *      fp32 tile as the q6 product (tensor-core path; Q6_PATH_SIMT returns
+ *      Q6_ERR_UNSUPPORTED).
  * Replaces `affine_q6_qmm_t` (shardedit_mlx/q6_metal_mlp.py:157-204), its tiled
  * and simdgroup twins (q6_steel_mlp.py:163-220, q6_simdgroup_mlp.py:133-181),
  * the stock `mx.quantized_matmul(x, w, scales, biases, transpose=True,
@@ -84,12 +86,13 @@ Q6_API int q6_dequantize_bf16(const uint32_t* w, const uint16_t* scales, const u
  */
 Q6_API int q6_linear_bf16(const uint16_t* x, const uint32_t* w, const uint16_t* scales,
                    const uint16_t* qbiases, const uint16_t* bias, const uint16_t* residual,
-                   const uint16_t* gate, const uint16_t* lora_a, const uint16_t* lora_b,
+                   const uint16_t* gate, const uint16_t* lora_xa, const uint16_t* lora_b,
                    float lora_scale, int lora_rank, uint16_t* y, int64_t M, int64_t N, int64_t K,
                    int group_size, int flags, int path, void* workspace, size_t workspace_bytes,
                    q6_stream_t stream);
 
-/* Workspace q6_linear_bf16 needs for a LoRA rank r at M tokens (0 without LoRA). */
+/* Workspace q6_linear_bf16 needs (0: no path of this build uses one; kept so
+   callers can size a buffer without knowing the path). */
 Q6_API size_t q6_linear_workspace_bytes(int64_t M, int lora_rank);
 
 /*

@@ -38,13 +38,14 @@ bool simt_aligned(const void* x, int64_t K, int elem_bytes) {
 int run_linear(const q6::LinearArgs& a, int path, cudaStream_t stream) {
     const bool tc_ok = q6::tc_supported(a);
     int chosen = path;
-    if (chosen == Q6_PATH_AUTO) chosen = (tc_ok && a.M > 4) ? Q6_PATH_TENSOR : Q6_PATH_SIMT;
+    if (chosen == Q6_PATH_AUTO) chosen = (tc_ok && (a.M > 4 || a.lora_rank > 0)) ? Q6_PATH_TENSOR : Q6_PATH_SIMT;
     if (chosen == Q6_PATH_TENSOR) {
         if (!tc_ok) return Q6_ERR_UNSUPPORTED;
         g_last_path = Q6_PATH_TENSOR;
         return q6::launch_linear_tc(a, q6::choose_token_tile(a.M, a.N), stream);
     }
     if (chosen == Q6_PATH_SIMT) {
+        if (a.lora_rank > 0) return Q6_ERR_UNSUPPORTED;  // the LoRA delta is fused on the tensor-core path
         if (!simt_aligned(a.x, a.K, 2)) return Q6_ERR_ALIGNMENT;
         g_last_path = Q6_PATH_SIMT;
         return q6::launch_linear_simt(a, false, stream);
@@ -83,25 +84,31 @@ int q6_dequantize_bf16(const uint32_t* w, const uint16_t* scales, const uint16_t
 }
 
 size_t q6_linear_workspace_bytes(int64_t M, int lora_rank) {
-    if (M <= 0 || lora_rank <= 0) return 0;
-    return static_cast<size_t>(M) * static_cast<size_t>(lora_rank) * 2;
+    (void)M;
+    (void)lora_rank;
+    return 0;  // every path (the fused LoRA delta included) works in registers, TMEM and shared memory
 }
 
 int q6_linear_bf16(const uint16_t* x, const uint32_t* w, const uint16_t* scales, const uint16_t* qbiases,
-                   const uint16_t* bias, const uint16_t* residual, const uint16_t* gate, const uint16_t* lora_a,
+                   const uint16_t* bias, const uint16_t* residual, const uint16_t* gate, const uint16_t* lora_xa,
                    const uint16_t* lora_b, float lora_scale, int lora_rank, uint16_t* y, int64_t M, int64_t N,
                    int64_t K, int group_size, int flags, int path, void* workspace, size_t workspace_bytes,
                    q6_stream_t stream) {
-    (void)lora_scale;
-    (void)lora_rank;
     (void)workspace;
     (void)workspace_bytes;
     int st = check_weights(w, scales, qbiases, N, K, group_size);
     if (st != Q6_OK) return st;
     if (!x || !y || M <= 0) return Q6_ERR_INVALID_ARGUMENT;
     if ((flags & ~Q6_EPI_GELU) != 0) return Q6_ERR_INVALID_ARGUMENT;
-    if (lora_a || lora_b) return Q6_ERR_UNSUPPORTED;
+    if ((lora_xa == nullptr) != (lora_b == nullptr)) return Q6_ERR_INVALID_ARGUMENT;
+    if (lora_xa && lora_rank <= 0) return Q6_ERR_INVALID_ARGUMENT;
     q6::LinearArgs a{x, w, scales, qbiases, bias, residual, gate, y, M, N, K, group_size, flags};
+    if (lora_xa) {
+        a.lora_xa = lora_xa;
+        a.lora_b = lora_b;
+        a.lora_scale = lora_scale;
+        a.lora_rank = lora_rank;
+    }
     return run_linear(a, path, reinterpret_cast<cudaStream_t>(stream));
 }
 

@@ -21,6 +21,12 @@ struct LinearArgs {
     int64_t M, N, K;
     int group_size;
     int flags;              // Q6_EPI_* bits
+    // Optional LoRA delta lora_scale * (lora_xa @ lora_b): xa = x @ A bf16 [M, r]
+    // (computed by the caller), B bf16 [r, N].  Tensor-core path only.
+    const uint16_t* lora_xa = nullptr;
+    const uint16_t* lora_b = nullptr;
+    float lora_scale = 0.0f;
+    int lora_rank = 0;
 };
 
 // Path selection recorded for tests and benchmarks.

@@ -135,6 +135,15 @@ struct TcParams {
     int M, N, K, gs, gs_shift, groups, flags;
     int sb_shift;  // log2(stages per 8-group chunk) when scales are TMA-staged
     int tiles_n, num_tiles, k_stages, last_ksteps;
+    // LoRA delta s * (xa @ B) (xa = x @ A, bf16 [M, r]; B bf16 [r, N]): two
+    // extra stages per tile after the q6 stages, each covering r / 2 of the
+    // rank (lora_ksteps = r / 32 MMAs of K = 16), with A(TMEM)[n, j] =
+    // bf16(s * B[j, n]) and the activation box loaded from xa.  0 stages
+    // without LoRA.  Two stages keep every stage's parity, so each dequant
+    // set still owns the code slots of its parity.
+    const uint16_t* lora_b;
+    float lora_scale;
+    int lora_rank, lora_stages, lora_ksteps;
 };
 
 __device__ __forceinline__ float bf16f(uint16_t v) { return __uint_as_float(static_cast<uint32_t>(v) << 16); }
@@ -149,7 +158,7 @@ template <int NT, bool kSbTma, int kEpi>
 __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
     q6_linear_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
                         const __grid_constant__ CUtensorMap tmap_s, const __grid_constant__ CUtensorMap tmap_b,
-                        const TcParams p) {
+                        const __grid_constant__ CUtensorMap tmap_xa, const TcParams p) {
     using C = Cfg<NT>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -206,12 +215,14 @@ __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
         // ------------------------------------------------ activation producer
         if (lane == 0) {
             tma_prefetch_map(&tmap_x);
+            if (p.lora_stages) tma_prefetch_map(&tmap_xa);
             uint32_t g = 0;  // stage counter over all tiles of this CTA
             int s = 0;       // g % kXStages
             bool ok = true;
+            const int stages = p.k_stages + p.lora_stages;
             for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
                 const int mb = tile / p.tiles_n;
-                for (int ks = 0; ks < p.k_stages; ++ks, ++g) {
+                for (int ks = 0; ks < stages; ++ks, ++g) {
                     // x slot s was last read by the MMAs of stage g - kXStages.
                     if (g >= static_cast<uint32_t>(C::kXStages)) {
                         const uint32_t prev = g - C::kXStages;
@@ -222,9 +233,14 @@ __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
                     }
                     const uint32_t fb = smem_u32(ready + g % kRing);
                     const uint32_t dst = smem_u32(x_smem + s * C::kXStageBytes);
-                    mbar_arrive_expect_tx(fb, C::kXStageBytes);
-                    tma_load_2d(dst, &tmap_x, fb, ks * kBK, mb * NT);
-                    tma_load_2d(dst + C::kXBoxBytes, &tmap_x, fb, ks * kBK + kBoxK, mb * NT);
+                    if (ks < p.k_stages) {
+                        mbar_arrive_expect_tx(fb, C::kXStageBytes);
+                        tma_load_2d(dst, &tmap_x, fb, ks * kBK, mb * NT);
+                        tma_load_2d(dst + C::kXBoxBytes, &tmap_x, fb, ks * kBK + kBoxK, mb * NT);
+                    } else {  // LoRA stage: columns [l r/2, l r/2 + 64) of xa in the first box
+                        mbar_arrive_expect_tx(fb, C::kXBoxBytes);
+                        tma_load_2d(dst, &tmap_xa, fb, (ks - p.k_stages) * (p.lora_rank / 2), mb * NT);
+                    }
                     if (++s == C::kXStages) s = 0;
                 }
             }
@@ -316,7 +332,7 @@ __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
             for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
                 if (!mbar_wait(smem_u32(acc_empty + acc), accph ^ 1u, abort_flag, 2)) break;
                 const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * NT);
-                for (int ks = 0; ks < p.k_stages; ++ks, ++g) {
+                for (int ks = 0; ks < p.k_stages + p.lora_stages; ++ks, ++g) {
                     const uint32_t rs = g % kRing;
                     if (!mbar_wait(smem_u32(ready + rs), (g / kRing) & 1u, abort_flag, 3)) {
                         ok = false;
@@ -333,12 +349,14 @@ __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
                         mma_bf16_ts(d_tmem, a_tmem + kk * 8, make_desc(lo + off, desc_hi), C::kIdesc,
                                     kk == 0 ? first : 1u);
                     };
-                    if (ks + 1 < p.k_stages || p.last_ksteps == kBK / 16) {
+                    if (ks + 1 < p.k_stages || (ks + 1 == p.k_stages && p.last_ksteps == kBK / 16)) {
 #pragma unroll
                         for (int kk = 0; kk < kBK / 16; ++kk) issue(kk);
-                    } else {  // K % 128 == 64 tail: the first box only
+                    } else if (ks < p.k_stages) {  // K % 128 == 64 tail: the first box only
 #pragma unroll
                         for (int kk = 0; kk < kBK / 32; ++kk) issue(kk);
+                    } else {  // LoRA stage: r / 32 K-steps in the first box
+                        for (int kk = 0; kk < p.lora_ksteps; ++kk) issue(kk);
                     }
                     tc_commit(smem_u32(done + rs));
                     if (++xs == C::kXStages) xs = 0;
@@ -450,6 +468,7 @@ __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
         const int r = q * 32 + lane;
         const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
         uint32_t gstage = 0;  // stage counter over all tiles of this CTA
+        uint32_t gqstage = 0; // q6 (code-carrying) stage counter: the code ring's index
         uint32_t gchunk = 0;  // scale chunk counter over all tiles of this CTA
         bool ok = true;
         for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
@@ -494,7 +513,9 @@ __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
                 }
             };
             const uint32_t g_base = gstage;
-            gstage += static_cast<uint32_t>(p.k_stages);
+            const uint32_t gq_base = gqstage;
+            gstage += static_cast<uint32_t>(p.k_stages + p.lora_stages);
+            gqstage += static_cast<uint32_t>(p.k_stages);
             int ks = static_cast<int>((static_cast<uint32_t>(set) + kDqSets - g_base % kDqSets) % kDqSets);
             float sb_next[4];
             if (!kSbTma && ks < p.k_stages) load_sb(ks, nullptr, sb_next);
@@ -515,8 +536,9 @@ __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
                 }
                 for (; ks < ks_end; ks += kDqSets) {
                     const uint32_t g = g_base + static_cast<uint32_t>(ks);
-                    const int cs = static_cast<int>(g % C::kCStages);
-                    const uint32_t cph = (g / C::kCStages) & 1u;
+                    const uint32_t gq = gq_base + static_cast<uint32_t>(ks);
+                    const int cs = static_cast<int>(gq % C::kCStages);
+                    const uint32_t cph = (gq / C::kCStages) & 1u;
                     const int as = static_cast<int>(g % kAStages);
                     const uint32_t rs = g % kRing;
                     float sb[4];
@@ -562,6 +584,44 @@ __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
                     __syncwarp();
                     if (lane == 0) mbar_arrive(smem_u32(s_empty + gchunk % kSbSlots));
                 }
+            }
+            // LoRA stages: A[n, k] = bf16(s * B[l r/2 + k, n]) for the r / 2 rank
+            // columns of stage l (zero beyond), one coalesced row of B per k.
+            for (; ok && ks < p.k_stages + p.lora_stages; ks += kDqSets) {
+                const uint32_t g = g_base + static_cast<uint32_t>(ks);
+                const int as = static_cast<int>(g % kAStages);
+                const uint32_t rs = g % kRing;
+                const int half_r = p.lora_rank / 2;
+                const int j0 = (ks - p.k_stages) * half_r;
+                if (g >= static_cast<uint32_t>(kAStages)) {
+                    const uint32_t prev = g - kAStages;
+                    if (!warp_wait(smem_u32(done + prev % kRing), (prev / kRing) & 1u, abort_flag, 7)) {
+                        ok = false;
+                        break;
+                    }
+                }
+                tc_fence_after();
+#pragma unroll 1
+                for (int hh = 0; hh < 2; ++hh) {  // 16 columns (32 rank values) at a time
+                    uint32_t a[16];
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        const int k = half * 64 + hh * 32 + 2 * i;  // stage-local K of the pair
+                        float v0 = 0.0f, v1 = 0.0f;
+                        if (n_ok && k < half_r)
+                            v0 = p.lora_scale * bf16f(p.lora_b[static_cast<size_t>(j0 + k) * p.N + n]);
+                        if (n_ok && k + 1 < half_r)
+                            v1 = p.lora_scale * bf16f(p.lora_b[static_cast<size_t>(j0 + k + 1) * p.N + n]);
+                        a[i] = pack_bf16x2(v0, v1);
+                    }
+                    tmem_st_32x32b_x16(tmem_base + lane_base +
+                                           static_cast<uint32_t>(C::kAccCols + as * kAColsPerStage + half * 32 + hh * 16),
+                                       a);
+                }
+                tmem_wait_st();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(smem_u32(ready + rs));
             }
         }
     }
@@ -624,7 +684,7 @@ int launch_tc(const LinearArgs& a, cudaStream_t stream) {
             return Q6_ERR_CUDA;
         attr_set_for_device[dev] = 1;
     }
-    CUtensorMap tmap_x, tmap_w, tmap_s, tmap_b;
+    CUtensorMap tmap_x, tmap_w, tmap_s, tmap_b, tmap_xa;
     if (!make_map_2d(&tmap_x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.x, a.K, a.M, a.K * 2, kBoxK, NT,
                      CU_TENSOR_MAP_SWIZZLE_128B))
         return Q6_ERR_CUDA;
@@ -642,6 +702,13 @@ int launch_tc(const LinearArgs& a, cudaStream_t stream) {
     } else {
         tmap_s = tmap_w;  // unused
         tmap_b = tmap_w;
+    }
+    if (a.lora_rank > 0) {
+        if (!make_map_2d(&tmap_xa, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.lora_xa, a.lora_rank, a.M,
+                         static_cast<uint64_t>(a.lora_rank) * 2, kBoxK, NT, CU_TENSOR_MAP_SWIZZLE_128B))
+            return Q6_ERR_CUDA;
+    } else {
+        tmap_xa = tmap_x;  // unused
     }
     TcParams p;
     p.scales = a.scales;
@@ -663,9 +730,14 @@ int launch_tc(const LinearArgs& a, cudaStream_t stream) {
     p.num_tiles = tiles_m * p.tiles_n;
     p.k_stages = static_cast<int>((a.K + kBK - 1) / kBK);
     p.last_ksteps = static_cast<int>((a.K - static_cast<int64_t>(p.k_stages - 1) * kBK) / 16);
+    p.lora_b = a.lora_b;
+    p.lora_scale = a.lora_scale;
+    p.lora_rank = a.lora_rank;
+    p.lora_stages = a.lora_rank > 0 ? 2 : 0;
+    p.lora_ksteps = a.lora_rank / 32;
     const int grid = std::min(p.num_tiles, device_sm_count());
     q6_linear_tc_kernel<NT, kSbTma, kEpi>
-        <<<grid, tc_threads(kDqSets), C::kSmemBytes, stream>>>(tmap_x, tmap_w, tmap_s, tmap_b, p);
+        <<<grid, tc_threads(kDqSets), C::kSmemBytes, stream>>>(tmap_x, tmap_w, tmap_s, tmap_b, tmap_xa, p);
     return cudaGetLastError() == cudaSuccess ? Q6_OK : Q6_ERR_CUDA;
 }
 
@@ -693,6 +765,11 @@ int error_word_tc(bool clear) {
 
 bool tc_supported(const LinearArgs& a) {
     if (a.K % kBoxK != 0) return false;
+    if (a.lora_rank != 0) {
+        // two LoRA stages of r / 2 rank columns each, within one 64-wide box
+        if (a.lora_rank < 32 || a.lora_rank > 128 || a.lora_rank % 32 != 0) return false;
+        if (!a.lora_xa || !a.lora_b || reinterpret_cast<uintptr_t>(a.lora_xa) % 16 != 0) return false;
+    }
     if (a.M > (int64_t(1) << 30) || a.N > (int64_t(1) << 30) || a.K > (int64_t(1) << 24)) return false;
     if (reinterpret_cast<uintptr_t>(a.x) % 16 != 0) return false;
     if (reinterpret_cast<uintptr_t>(a.w) % 16 != 0) return false;

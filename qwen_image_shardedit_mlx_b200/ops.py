@@ -146,23 +146,24 @@ def q6_linear(
     res_t = None
     if residual is not None:
         res_t = residual.reshape(m, n).to(torch.bfloat16).contiguous()
-    la = lb = None
+    xa = lb = None
     lscale, rank = 0.0, 0
-    workspace = None
     if lora is not None:
         a, b, lscale = lora
         rank = int(a.shape[-1])
-        la = a.to(torch.bfloat16).contiguous()
-        lb = b.to(torch.bfloat16).contiguous()
+        la = a.to(device=dev, dtype=torch.bfloat16)
+        lb = b.to(device=dev, dtype=torch.bfloat16).contiguous()
         if tuple(la.shape) != (k, rank) or tuple(lb.shape) != (rank, n):
             raise ValueError(f"LoRA A must be ({k}, r) and B (r, {n}); got {tuple(la.shape)}, {tuple(lb.shape)}")
-        nbytes = int(_lib.lib().q6_linear_workspace_bytes(m, rank))
-        workspace = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=dev)
+        # x @ A is a plain bf16 GEMM (fp32 accumulation, bf16 result, as the
+        # reference's LoRA linear computes it); the library fuses s * (xa @ B)
+        # into the q6 product's accumulator.
+        xa = torch.matmul(xb, la).contiguous()
     y = out if out is not None else torch.empty((m, n), dtype=torch.bfloat16, device=dev)
     st = _lib.lib().q6_linear_bf16(
         xb.data_ptr(), w.data_ptr(), sc.data_ptr(), qb.data_ptr(), _ptr(bias_t), _ptr(res_t), _ptr(gate_t),
-        _ptr(la), _ptr(lb), float(lscale), rank, y.data_ptr(), m, n, k, group_size, flags,
-        _lib.PATHS[path], _ptr(workspace), 0 if workspace is None else workspace.numel(), stream,
+        _ptr(xa), _ptr(lb), float(lscale), rank, y.data_ptr(), m, n, k, group_size, flags,
+        _lib.PATHS[path], None, 0, stream,
     )
     _lib.check(st, "q6_linear_bf16")
     return y.reshape(leading + (n,))

@@ -73,6 +73,7 @@ class QuantizedLinear(torch.nn.Module):
         self.group_size = int(group_size)
         self.bits = int(bits)
         self.mode = "affine"
+        self.lora: tuple[torch.Tensor, torch.Tensor, float] | None = None
 
     @classmethod
     def from_linear(cls, linear: torch.nn.Linear, *, bits: int = 6, group_size: int = 64) -> "QuantizedLinear":
@@ -90,8 +91,26 @@ class QuantizedLinear(torch.nn.Module):
     def out_features(self) -> int:
         return int(self.weight.shape[0])
 
+    def set_lora(self, a: torch.Tensor | None, b: torch.Tensor | None = None, scale: float = 1.0) -> None:
+        """Attach (or with ``a=None`` remove) a LoRA delta: the layer then
+        computes ``q6(x) + scale * ((x @ a) @ b)`` before its bias, as the
+        reference's LoRA-additive linear does (dense_img_ff_window.py:48-60).
+        ``a`` is [in_features, r], ``b`` is [r, out_features], r in {32, 64, 96, 128};
+        the ``(x @ a) @ b`` product is fused into the q6 kernel's accumulator."""
+
+        if a is None:
+            self.lora = None
+            return
+        if b is None:
+            raise ValueError("LoRA needs both A and B")
+        r = int(a.shape[-1])
+        if tuple(a.shape) != (self.in_features, r) or tuple(b.shape) != (r, self.out_features):
+            raise ValueError(f"LoRA A must be ({self.in_features}, r) and B (r, {self.out_features})")
+        self.lora = (a.to(torch.bfloat16).contiguous(), b.to(torch.bfloat16).contiguous(), float(scale))
+
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        return ops.q6_linear(x, self.weight, self.scales, self.biases, self.bias, group_size=self.group_size)
+        return ops.q6_linear(x, self.weight, self.scales, self.biases, self.bias, group_size=self.group_size,
+                             lora=self.lora)
 
 
 def quantized_linear_spec(layer: torch.nn.Module) -> Q6LinearSpec:

@@ -47,12 +47,13 @@ def test_status_strings():
 def test_workspace_sizes():
     lib = _lib.lib()
     assert lib.q6_mlp_workspace_bytes(3456, 12288) == 3456 * 12288 * 2
-    assert lib.q6_linear_workspace_bytes(3456, 64) == 3456 * 64 * 2
+    # The fused LoRA delta takes x @ A from the caller, so no path needs workspace.
+    assert lib.q6_linear_workspace_bytes(3456, 64) == 0
     assert lib.q6_linear_workspace_bytes(3456, 0) == 0
 
 
 def _linear(lib, **kw):
-    args = dict(x=256, w=256, scales=256, qbiases=256, bias=None, residual=None, gate=None, lora_a=None,
+    args = dict(x=256, w=256, scales=256, qbiases=256, bias=None, residual=None, gate=None, lora_xa=None,
                 lora_b=None, lora_scale=0.0, rank=0, y=256, M=4, N=128, K=64, gs=64, flags=0, path=0, ws=None, ws_bytes=0,
                 stream=None)
     args.update(kw)
@@ -68,6 +69,10 @@ def test_argument_validation_without_gpu():
     assert _linear(lib, K=96, gs=64) == _lib.Q6_ERR_SHAPE
     assert _linear(lib, flags=8) == _lib.Q6_ERR_INVALID_ARGUMENT
     assert _linear(lib, w=258) == _lib.Q6_ERR_ALIGNMENT
+    # LoRA: x @ A and B come together, with a positive rank
+    assert _linear(lib, lora_xa=256) == _lib.Q6_ERR_INVALID_ARGUMENT
+    assert _linear(lib, lora_b=256, rank=64) == _lib.Q6_ERR_INVALID_ARGUMENT
+    assert _linear(lib, lora_xa=256, lora_b=256, rank=0) == _lib.Q6_ERR_INVALID_ARGUMENT
     assert lib.q6_dequantize_bf16(None, 1, 1, 1, 4, 64, 64, None) == _lib.Q6_ERR_INVALID_ARGUMENT
     # q6_mlp needs a workspace large enough for the hidden activations
     st = lib.q6_mlp_bf16(16, 16, 16, 16, None, 16, 16, 16, None, None, None, 16, 8, 64, 256, 64, None, 0, None)

@@ -18,7 +18,7 @@ import pytest
 import torch
 
 import oracle
-from qwen_image_shardedit_mlx_b200 import ops
+from qwen_image_shardedit_mlx_b200 import _lib, ops
 from tests.conftest import golden_case
 from tests.helpers import (
     assert_close,
@@ -159,6 +159,63 @@ def test_simt_path_small_m(m):
     torch.cuda.synchronize()
     ref = oracle.linear(oracle.bf16_bits_to_f32(x), w, weight_dtype="f32")
     assert_close(f32(got), ref)
+
+
+LORA_CASES = [
+    (200, 384, 512, 64, 64, "bias_gelu"),
+    (17, 256, 192, 32, 32, "plain"),          # K % 128 == 64 tail before the LoRA stages
+    (130, 640, 1024, 128, 64, "residual_gate"),
+    (3, 512, 256, 96, 64, "bias_gelu"),       # a few rows: the auto path still takes the fused kernel
+    (1000, 3072, 3072, 64, 64, "plain"),      # image-FF width
+]
+
+
+@pytest.mark.parametrize("m,n,k,r,gs,epi", LORA_CASES)
+def test_lora_fused_vs_oracle(m, n, k, r, gs, epi):
+    """q6(x) + s * ((x @ A) @ B) with the LoRA product accumulated in the q6
+    tile (dense_img_ff_window.py:48-60), against the float64 oracle."""
+
+    rng = np.random.default_rng(m + n + k + r)
+    w = random_weights(rng, n, k, gs, bias=epi != "plain")
+    x = random_bf16(rng, (m, k))
+    a_bits = random_bf16(rng, (k, r), 0.01)
+    b_bits = random_bf16(rng, (r, n), 0.01)
+    s = 0.75
+    wt, st, bt, bias = weights_to_torch(w)
+    kwargs = {}
+    residual = gate = None
+    if epi == "residual_gate":
+        residual = random_bf16(rng, (m, n))
+        gate = random_bf16(rng, (n,), 0.5)
+        kwargs = dict(residual=from_bits(residual), gate=from_bits(gate))
+    out = torch.full((m, n), float("nan"), dtype=torch.bfloat16, device="cuda")
+    got = ops.q6_linear(from_bits(x), wt, st, bt, bias, group_size=gs, apply_gelu=epi == "bias_gelu",
+                        lora=(from_bits(a_bits), from_bits(b_bits), s), out=out, **kwargs)
+    torch.cuda.synchronize()
+    assert ops.last_path() == "tensor"
+    assert bool(torch.isfinite(got).all())
+    xf = oracle.bf16_bits_to_f32(x)
+    res_f = None if residual is None else oracle.bf16_bits_to_f32(residual)
+    gate_f = None if gate is None else oracle.bf16_bits_to_f32(gate)
+    ref = oracle.linear(xf, w, apply_gelu=epi == "bias_gelu", weight_dtype="bf16", residual=res_f, gate=gate_f,
+                        lora=(oracle.bf16_bits_to_f32(a_bits), oracle.bf16_bits_to_f32(b_bits), s))
+    assert_close(f32(got), ref, what=f"lora {m}x{n}x{k} r{r} gs{gs} {epi}")
+    # the delta is really in the output: without it the oracle moves by more than the tolerance allows
+    plain = oracle.linear(xf, w, apply_gelu=epi == "bias_gelu", weight_dtype="bf16", residual=res_f, gate=gate_f)
+    assert float(np.abs(ref - plain).max()) > 5e-3 * float(np.abs(ref).max())
+
+
+def test_lora_rejected_off_the_tensor_path():
+    rng = np.random.default_rng(9)
+    w = random_weights(rng, 128, 256, 64)
+    wt, st, bt, bias = weights_to_torch(w)
+    x = from_bits(random_bf16(rng, (8, 256)))
+    a = torch.zeros((256, 64), dtype=torch.bfloat16, device="cuda")
+    b = torch.zeros((64, 128), dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(_lib.Q6Error):
+        ops.q6_linear(x, wt, st, bt, bias, lora=(a, b, 1.0), path="simt")
+    with pytest.raises(_lib.Q6Error):  # rank 16 is below the fused kernel's granularity
+        ops.q6_linear(x, wt, st, bt, bias, lora=(a[:, :16], b[:16], 1.0))
 
 
 def test_auto_path_choice():
