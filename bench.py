@@ -196,12 +196,9 @@ def barrier(world: int) -> None:
 def max_over_ranks(value: float, world: int) -> float:
     if world == 1:
         return value
-    import torch
-    import torch.distributed as dist
+    from qwen_image_shardedit_mlx_b200.sharding import max_over_ranks as reduce_max
 
-    t = torch.tensor([value], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    return float(t.item())
+    return reduce_max(value, device="cuda")
 
 
 # ----------------------------------------------------------------- our arm
@@ -386,20 +383,34 @@ def measure_gemv(dev, peaks) -> dict:
         for i in range(count):
             launch(i)
         torch.cuda.synchronize()
-        reps = 4 * count
+        # One launch per weight copy, captured in a CUDA graph: replaying it
+        # times the kernels back to back on the device, without the host-side
+        # cost of each Python call (how a decode loop would issue them).
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=side):
+            for i in range(count):
+                launch(i)
+        torch.cuda.synchronize()
+        for _ in range(3):
+            graph.replay()
+        torch.cuda.synchronize()
+        reps = 8
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record()
-        for i in range(reps):
-            launch(i)
+        for _ in range(reps):
+            graph.replay()
         e1.record()
         torch.cuda.synchronize()
-        us = e0.elapsed_time(e1) * 1e3 / reps
+        us = e0.elapsed_time(e1) * 1e3 / (reps * count)
+        del graph
         nbytes = per_copy + 2 * m * (k + n)
         gbs = nbytes / (us * 1e-6) / 1e9
         out[f"m{m}"] = {"us": round(us, 2), "GB/s": round(gbs, 1), "frac_hbm": round(gbs / peaks["hbm_gbs"], 4),
                         "path": ops.last_path(), "bytes": nbytes}
-    out["note"] = f"3072->12288 gs64, {count} rotating weight copies ({count * per_copy / 2**20:.0f} MB > L2), back-to-back launches"
+    out["note"] = f"3072->12288 gs64, {count} rotating weight copies ({count * per_copy / 2**20:.0f} MB > L2), one CUDA graph of back-to-back launches, device time"
     return out
 
 
