@@ -48,6 +48,7 @@ int run_linear(const q6::LinearArgs& a, int path, cudaStream_t stream) {
         if (a.lora_rank > 0) return Q6_ERR_UNSUPPORTED;  // the LoRA delta is fused on the tensor-core path
         if (!simt_aligned(a.x, a.K, 2)) return Q6_ERR_ALIGNMENT;
         g_last_path = Q6_PATH_SIMT;
+        if (q6::gemv_supported(a)) return q6::launch_gemv(a, stream);
         return q6::launch_linear_simt(a, false, stream);
     }
     return Q6_ERR_INVALID_ARGUMENT;

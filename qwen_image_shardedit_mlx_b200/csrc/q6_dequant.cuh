@@ -7,7 +7,7 @@
 // Conversion: a code sitting at bit position P of a word is turned into an
 // fp32 value by splicing the masked word into the mantissa of 2^(23-P), which
 // gives exactly 2^(23-P) + q; subtracting 2^(23-P) again is exact.  One LOP3
-// per code plus one packed add and one packed FMA per code pair, then
+// per code plus one add per code and one packed FMA per code pair, then
 //   w = fma(q, scale, bias)            (fp32, rounded once; scale*q is exact)
 // and, for the tensor-core operand, bf16_rn(w) two at a time.  This is the
 // same value as the reference's `scale * float(code) + qbias`
@@ -37,13 +37,14 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
     return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// Dequantise one code pair given as spliced values with their offsets.
+// Dequantise one code pair given as spliced values with their offsets.  The
+// exact subtraction is two scalar adds: their constants are immediates, where
+// a packed add would need the constant pair in a register pair.
 template <int PA, int PB>
 __device__ __forceinline__ float2 pair_f32(float a_spliced, float b_spliced, float2 s2, float2 b2) {
-    const float2 v = make_float2(a_spliced, b_spliced);
-    const float2 off = make_float2(-code_offset<PA>(), -code_offset<PB>());
-    const float2 q = __fadd2_rn(v, off);  // exact integer codes
-    return __ffma2_rn(q, s2, b2);         // s*q + b, one rounding
+    const float2 q = make_float2(__fadd_rn(a_spliced, -code_offset<PA>()),  // exact integer codes
+                                 __fadd_rn(b_spliced, -code_offset<PB>()));
+    return __ffma2_rn(q, s2, b2);  // s*q + b, one rounding
 }
 
 // Sixteen codes (three packed words) -> sixteen fp32 weights.
@@ -70,6 +71,29 @@ __device__ __forceinline__ void dequant16_f32(uint32_t w0, uint32_t w1, uint32_t
     out[12] = r.x; out[13] = r.y;
     r = pair_f32<8, 14>(code_spliced<8>(t2), code_spliced<14>(t2), s2, b2);
     out[14] = r.x; out[15] = r.y;
+}
+
+// Sixteen codes -> their exact integer values as fp32 (q[i] = code i), no
+// scale or bias: for dot products that apply the group's affine map once per
+// group instead of once per weight.
+__device__ __forceinline__ void codes16_f32(uint32_t w0, uint32_t w1, uint32_t w2, float (&q)[16]) {
+    const uint32_t t0 = w0 >> 12, t1 = w1 >> 12, t2 = w2 >> 12;
+    const uint32_t f5 = __funnelshift_r(w0, w1, 30);
+    const uint32_t f10 = __funnelshift_r(w1, w2, 28);
+#define Q6_PAIR(i, PA, VA, PB, VB)                                                                       \
+    {                                                                                                    \
+        q[2 * (i)] = __fadd_rn(code_spliced<PA>(VA), -code_offset<PA>());                                \
+        q[2 * (i) + 1] = __fadd_rn(code_spliced<PB>(VB), -code_offset<PB>());                            \
+    }
+    Q6_PAIR(0, 0, w0, 6, w0);
+    Q6_PAIR(1, 12, w0, 6, t0);
+    Q6_PAIR(2, 12, t0, 0, f5);
+    Q6_PAIR(3, 4, w1, 10, w1);
+    Q6_PAIR(4, 16, w1, 10, t1);
+    Q6_PAIR(5, 0, f10, 2, w2);
+    Q6_PAIR(6, 8, w2, 14, w2);
+    Q6_PAIR(7, 8, t2, 14, t2);
+#undef Q6_PAIR
 }
 
 // Sixteen codes -> eight bf16x2 words (low half = even code).

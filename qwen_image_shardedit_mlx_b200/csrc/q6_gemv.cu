@@ -1,0 +1,304 @@
+// q6 linear for a few token rows (M <= 4): a memory-streaming GEMV.
+//
+// With one to four activation rows the linear is bound by reading the packed
+// weights (0.8125 bytes per weight with scales and biases).  The kernel keeps
+// HBM busy by decoupling loads from arithmetic:
+//
+//   * every warp works through pairs of weight rows (rows 2p, 2p+1), in
+//     K chunks of up to 4096 codes; a stage is one (pair, chunk): both rows'
+//     codes, scales and biases;
+//   * each warp owns a two-slot ring in shared memory; its lane 0 fetches the
+//     next stage with 1-D bulk copies (completing on the slot's mbarrier)
+//     while the warp computes the current one, so one stage per warp is
+//     always in flight;
+//   * within a stage, lane l takes the 16-code units j = l, l + 32, ... of
+//     both rows (K = 3072: six units per lane, an even split);
+//   * the reference kernel's sum_k x_k (scale * code_k + qbias)
+//     (shardedit_mlx/q6_metal_mlp.py:42-83) is evaluated per 16-code unit
+//     (one scale group) as scale * sum_k x_k code_k + qbias * sum_k x_k: codes
+//     become exact fp32 integers (splice + packed subtract), the dot with x
+//     runs on scalar FMAs (which issue to both FMA pipes), and the x sums per
+//     unit are computed once per CTA.  The activations sit in shared memory as
+//     fp32 with an XOR swizzle that keeps the unit-per-lane reads free of bank
+//     conflicts.
+//
+// Requirements (else the CUDA-core linear_simt_kernel runs): bf16 activations
+// and output, K % 64 == 0, K / group_size % 8 == 0 (16-byte aligned scale
+// rows), K <= 4096 or K % 4096 == 0, 16-byte aligned x, codes, scales and
+// biases, and the fp32 activations within the shared-memory budget.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+
+#include "q6_dequant.cuh"
+#include "q6_internal.h"
+#include "q6_ptx.cuh"
+
+namespace q6 {
+namespace {
+
+constexpr int kWarps = 8;          // warps per CTA, each with its own ring
+constexpr int kSlots = 2;          // ring slots per warp
+constexpr int kMaxChunk = 4096;    // codes per row per stage
+constexpr int kSmemCap = 220 * 1024;
+
+__device__ __forceinline__ float bf16f(uint16_t v) { return __uint_as_float(static_cast<uint32_t>(v) << 16); }
+
+__device__ __forceinline__ float gelu_ref(float x) {
+    const float x3 = x * x * x;
+    return 0.5f * x * (1.0f + tanhf(0.7978845608028654f * (x + 0.044715f * x3)));
+}
+
+// Physical float4 slot of logical float4 F of an activation row: F ^ ((F >> 3) & 7).
+// Lanes read float4 e of consecutive 16-code units j (F = 4j + e); eight such
+// lanes, starting at a multiple of 8, land in eight different 16-byte bank groups.
+__device__ __forceinline__ int xswz(int F) { return F ^ ((F >> 3) & 7); }
+
+struct GemvLayout {
+    int chunk;        // codes per row per stage
+    int code_bytes;   // per row per stage
+    int sb_bytes;     // scales (or biases) bytes per row per stage
+    int stage_bytes;  // two rows: codes, scales, biases (128-byte multiple)
+};
+
+__host__ __device__ inline GemvLayout gemv_layout(int K, int gs) {
+    GemvLayout L;
+    L.chunk = K < kMaxChunk ? K : kMaxChunk;
+    L.code_bytes = L.chunk * 6 / 8;
+    L.sb_bytes = (L.chunk / gs) * 2;
+    L.stage_bytes = (2 * L.code_bytes + 4 * L.sb_bytes + 127) & ~127;
+    return L;
+}
+
+template <int MT>
+__global__ void __launch_bounds__(kWarps * 32) gemv_stream_kernel(const LinearArgs a, int gs_shift) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int K = static_cast<int>(a.K);
+    const int N = static_cast<int>(a.N);
+    const int M = static_cast<int>(a.M);
+    const GemvLayout L = gemv_layout(K, 1 << gs_shift);
+    const int nchunks = K / L.chunk;
+    const int K4 = K / 4;
+    const int U16 = K / 16;
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    uint8_t* ring = smem + warp * kSlots * L.stage_bytes;
+    float4* xs4 = reinterpret_cast<float4*>(smem + kWarps * kSlots * L.stage_bytes);  // [MT][K/4]
+    float* xsum = reinterpret_cast<float*>(xs4 + MT * K4);                             // [MT][K/16]
+    uint64_t* full = reinterpret_cast<uint64_t*>(xsum + MT * U16) + warp * kSlots;
+
+    const int npairs = (N + 1) / 2;
+    const int gw = blockIdx.x * kWarps + warp;
+    const int total_warps = gridDim.x * kWarps;
+    const int words_per_row = K * 6 / 32;
+    const int groups = K >> gs_shift;
+    // This warp's stages t = 0, 1, ...: pair gw + (t / nchunks) * total_warps, chunk t % nchunks.
+    const int my_pairs = gw < npairs ? (npairs - gw + total_warps - 1) / total_warps : 0;
+    const int my_stages = my_pairs * nchunks;
+
+    auto issue = [&](int t) {  // lane 0 only
+        const int p = gw + (t / nchunks) * total_warps;
+        const int c = t - (t / nchunks) * nchunks;
+        const int n0 = 2 * p;
+        const bool two = n0 + 1 < N;
+        const uint32_t slot = smem_u32(ring + (t % kSlots) * L.stage_bytes);
+        const uint32_t bar = smem_u32(full + (t % kSlots));
+        const uint32_t cb = L.code_bytes, sbb = L.sb_bytes;
+        mbar_arrive_expect_tx(bar, (two ? 2u : 1u) * (cb + 2 * sbb));
+        const uint8_t* wrow = reinterpret_cast<const uint8_t*>(a.w + static_cast<size_t>(n0) * words_per_row) +
+                              static_cast<size_t>(c) * cb;
+        const uint8_t* srow = reinterpret_cast<const uint8_t*>(a.scales + static_cast<size_t>(n0) * groups) +
+                              static_cast<size_t>(c) * sbb;
+        const uint8_t* brow = reinterpret_cast<const uint8_t*>(a.qbiases + static_cast<size_t>(n0) * groups) +
+                              static_cast<size_t>(c) * sbb;
+        const size_t wstride = static_cast<size_t>(words_per_row) * 4, sstride = static_cast<size_t>(groups) * 2;
+        bulk_load(slot, wrow, cb, bar);
+        bulk_load(slot + 2 * cb, srow, sbb, bar);
+        bulk_load(slot + 2 * cb + 2 * sbb, brow, sbb, bar);
+        if (two) {
+            bulk_load(slot + cb, wrow + wstride, cb, bar);
+            bulk_load(slot + 2 * cb + sbb, srow + sstride, sbb, bar);
+            bulk_load(slot + 2 * cb + 3 * sbb, brow + sstride, sbb, bar);
+        }
+    };
+
+    if (lane == 0) {
+        for (int s = 0; s < kSlots; ++s) mbar_init(smem_u32(full + s), 1);
+        fence_mbar_init();
+        for (int t = 0; t < kSlots && t < my_stages; ++t) issue(t);
+    }
+    __syncwarp();
+
+    // Stage the activations (bf16 -> fp32, swizzled; rows M..MT-1 zero), then
+    // the per-unit sums.  The first weight stages are already in flight.
+    const uint16_t* x = static_cast<const uint16_t*>(a.x);
+    for (int i = threadIdx.x; i < MT * K / 8; i += blockDim.x) {
+        const uint4 v = i < M * K / 8 ? __ldg(reinterpret_cast<const uint4*>(x) + i) : make_uint4(0, 0, 0, 0);
+        const int m = (2 * i) / K4;
+        const int F = 2 * i - m * K4;
+        float4* row = xs4 + m * K4;
+        row[xswz(F)] = make_float4(__uint_as_float(v.x << 16), __uint_as_float(v.x & 0xFFFF0000u),
+                                   __uint_as_float(v.y << 16), __uint_as_float(v.y & 0xFFFF0000u));
+        row[xswz(F + 1)] = make_float4(__uint_as_float(v.z << 16), __uint_as_float(v.z & 0xFFFF0000u),
+                                       __uint_as_float(v.w << 16), __uint_as_float(v.w & 0xFFFF0000u));
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < MT * U16; i += blockDim.x) {
+        const int m = i / U16;
+        const int J = i - m * U16;
+        const float4* row = xs4 + m * K4;
+        float t = 0.0f;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const float4 v = row[xswz(4 * J + e)];
+            t += (v.x + v.y) + (v.z + v.w);
+        }
+        xsum[i] = t;
+    }
+    __syncthreads();
+
+    volatile int no_abort = 0;  // the ring is private to the warp: no CTA-wide abort
+    float acc0[MT], acc1[MT];
+#pragma unroll
+    for (int m = 0; m < MT; ++m) acc0[m] = acc1[m] = 0.0f;
+    for (int t = 0; t < my_stages; ++t) {
+        const int c = t % nchunks;
+        const int p = gw + (t / nchunks) * total_warps;
+        const int n0 = 2 * p;
+        const uint8_t* slot = ring + (t % kSlots) * L.stage_bytes;
+        if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(full + (t % kSlots)), static_cast<uint32_t>((t / kSlots) & 1),
+                                               &no_abort, 11)))
+            break;
+        const uint8_t* codes0 = slot;
+        const uint8_t* codes1 = slot + L.code_bytes;
+        const uint16_t* sc0 = reinterpret_cast<const uint16_t*>(slot + 2 * L.code_bytes);
+        const uint16_t* sc1 = sc0 + L.sb_bytes / 2;
+        const uint16_t* bi0 = sc0 + L.sb_bytes;
+        const uint16_t* bi1 = bi0 + L.sb_bytes / 2;
+        const int units = L.chunk / 16;
+        for (int j = lane; j < units; j += 32) {
+            const int J = c * units + j;          // unit index within the row
+            const int gl = (16 * j) >> gs_shift;  // group within the chunk
+            const uint32_t* wa = reinterpret_cast<const uint32_t*>(codes0 + 12 * j);
+            const uint32_t* wb = reinterpret_cast<const uint32_t*>(codes1 + 12 * j);
+            float qa[16], qb[16];
+            codes16_f32(wa[0], wa[1], wa[2], qa);
+            codes16_f32(wb[0], wb[1], wb[2], qb);  // stale slot bytes for an odd last row: never stored
+            const float s0 = bf16f(sc0[gl]), b0 = bf16f(bi0[gl]);
+            const float s1 = bf16f(sc1[gl]), b1 = bf16f(bi1[gl]);
+#pragma unroll
+            for (int m = 0; m < MT; ++m) {
+                const float4* xrow = xs4 + m * K4;
+                float d0 = 0.0f, d1 = 0.0f;
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float4 xv = xrow[xswz(4 * J + e)];
+                    d0 = fmaf(xv.x, qa[4 * e], d0);
+                    d0 = fmaf(xv.y, qa[4 * e + 1], d0);
+                    d0 = fmaf(xv.z, qa[4 * e + 2], d0);
+                    d0 = fmaf(xv.w, qa[4 * e + 3], d0);
+                    d1 = fmaf(xv.x, qb[4 * e], d1);
+                    d1 = fmaf(xv.y, qb[4 * e + 1], d1);
+                    d1 = fmaf(xv.z, qb[4 * e + 2], d1);
+                    d1 = fmaf(xv.w, qb[4 * e + 3], d1);
+                }
+                const float xj = xsum[m * U16 + J];
+                acc0[m] = fmaf(s0, d0, fmaf(b0, xj, acc0[m]));
+                acc1[m] = fmaf(s1, d1, fmaf(b1, xj, acc1[m]));
+            }
+        }
+        // Hand the slot back to this warp's producer lane for stage t + kSlots.
+        __syncwarp();
+        if (lane == 0 && t + kSlots < my_stages) {
+            fence_proxy_async_smem();
+            issue(t + kSlots);
+        }
+        if (c == nchunks - 1) {
+#pragma unroll
+            for (int m = 0; m < MT; ++m) {
+#pragma unroll
+                for (int off = 16; off > 0; off >>= 1) {
+                    acc0[m] += __shfl_xor_sync(0xffffffffu, acc0[m], off);
+                    acc1[m] += __shfl_xor_sync(0xffffffffu, acc1[m], off);
+                }
+            }
+            // Lane 2m + r writes token m of row n0 + r.
+            if (lane < 2 * MT) {
+                const int m = lane >> 1;
+                const int r = lane & 1;
+                float v = 0.0f;
+#pragma unroll
+                for (int mm = 0; mm < MT; ++mm)
+                    if (mm == m) v = r ? acc1[mm] : acc0[mm];
+                const int n = n0 + r;
+                if (m < M && n < N) {
+                    if (a.bias) v += bf16f(a.bias[n]);
+                    if (a.flags & Q6_EPI_GELU) v = gelu_ref(v);
+                    if (a.gate) v *= bf16f(a.gate[n]);
+                    if (a.residual) v += bf16f(a.residual[static_cast<size_t>(m) * N + n]);
+                    __nv_bfloat16 h = __float2bfloat16_rn(v);
+                    static_cast<uint16_t*>(a.y)[static_cast<size_t>(m) * N + n] = *reinterpret_cast<uint16_t*>(&h);
+                }
+            }
+#pragma unroll
+            for (int m = 0; m < MT; ++m) acc0[m] = acc1[m] = 0.0f;
+        }
+    }
+}
+
+size_t gemv_smem_bytes(int64_t K, int gs, int mt) {
+    const GemvLayout L = gemv_layout(static_cast<int>(K), gs);
+    return static_cast<size_t>(kWarps) * kSlots * L.stage_bytes + static_cast<size_t>(mt) * K * 4 +
+           static_cast<size_t>(mt) * (K / 16) * 4 + kWarps * kSlots * 8;
+}
+
+template <int MT>
+int launch_gemv_mt(const LinearArgs& a, cudaStream_t stream) {
+    const size_t smem = gemv_smem_bytes(a.K, a.group_size, MT);
+    static int attr_set_for_device[64] = {0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return Q6_ERR_CUDA;
+    if (dev >= 0 && dev < 64 && !attr_set_for_device[dev]) {
+        if (cudaFuncSetAttribute(gemv_stream_kernel<MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemCap) !=
+            cudaSuccess)
+            return Q6_ERR_CUDA;
+        attr_set_for_device[dev] = 1;
+    }
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemv_stream_kernel<MT>, kWarps * 32, smem) !=
+            cudaSuccess ||
+        per_sm <= 0)
+        return Q6_ERR_CUDA;
+    const int64_t pairs = (a.N + 1) / 2;
+    const int64_t want = (pairs + kWarps - 1) / kWarps;
+    const int blocks = static_cast<int>(std::min<int64_t>(want, static_cast<int64_t>(device_sm_count()) * per_sm));
+    const int gs_shift = a.group_size == 32 ? 5 : (a.group_size == 64 ? 6 : 7);
+    gemv_stream_kernel<MT><<<blocks, kWarps * 32, smem, stream>>>(a, gs_shift);
+    return cudaGetLastError() == cudaSuccess ? Q6_OK : Q6_ERR_CUDA;
+}
+
+}  // namespace
+
+bool gemv_supported(const LinearArgs& a) {
+    if (a.M < 1 || a.M > 4 || a.K % 64 != 0) return false;
+    if (a.K > (int64_t(1) << 20) || a.N > (int64_t(1) << 30)) return false;
+    if ((a.K / a.group_size) % 8 != 0) return false;
+    if (a.K > kMaxChunk && a.K % kMaxChunk != 0) return false;
+    const uintptr_t align = reinterpret_cast<uintptr_t>(a.x) | reinterpret_cast<uintptr_t>(a.w) |
+                            reinterpret_cast<uintptr_t>(a.scales) | reinterpret_cast<uintptr_t>(a.qbiases);
+    if (align % 16 != 0) return false;
+    const int mt = a.M == 3 ? 4 : static_cast<int>(a.M);  // token rows of the kernel instantiation
+    return gemv_smem_bytes(a.K, a.group_size, mt) <= static_cast<size_t>(kSmemCap);
+}
+
+int launch_gemv(const LinearArgs& a, cudaStream_t stream) {
+    switch (a.M) {
+        case 1: return launch_gemv_mt<1>(a, stream);
+        case 2: return launch_gemv_mt<2>(a, stream);
+        default: return launch_gemv_mt<4>(a, stream);  // M = 3 or 4
+    }
+}
+
+}  // namespace q6

@@ -39,6 +39,13 @@ int launch_dequantize(const uint32_t* w, const uint16_t* scales, const uint16_t*
 // fp32 (un-rounded) dequantised weights.
 int launch_linear_simt(const LinearArgs& a, bool f32_io, cudaStream_t stream);
 
+// Streaming GEMV for M <= 4 bf16 rows (fp32 dequantised weights, like the
+// CUDA-core path) when K % 64 == 0, K / group_size % 8 == 0, K <= 4096 or
+// K % 4096 == 0, the operands are 16-byte aligned and the fp32 activations fit
+// in shared memory.
+bool gemv_supported(const LinearArgs& a);
+int launch_gemv(const LinearArgs& a, cudaStream_t stream);
+
 // tcgen05 path: bf16 activations, bf16-dequantised weights, fp32 accumulate.
 // Requires K % 64 == 0 and 16-byte aligned x / w rows.
 int launch_linear_tc(const LinearArgs& a, int token_tile, cudaStream_t stream);

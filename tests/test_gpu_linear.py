@@ -161,6 +161,46 @@ def test_simt_path_small_m(m):
     assert_close(f32(got), ref)
 
 
+GEMV_SHAPES = [
+    (1001, 3072, 64),   # odd row count: the last row pair has one row
+    (257, 12288, 64),   # fc2-shaped K: three 4096-code chunks per row
+    (130, 1024, 32),    # one group per 32-code half unit
+    (64, 2048, 128),    # one group per two units
+    (3, 64, 64),        # one scale group per row: the CUDA-core fallback
+]
+
+
+@pytest.mark.parametrize("m", [1, 2, 3, 4])
+@pytest.mark.parametrize("n,k,gs", GEMV_SHAPES)
+@pytest.mark.parametrize("epi", ["plain", "bias_gelu", "residual_gate"])
+def test_gemv_path_vs_oracle(m, n, k, gs, epi):
+    """The streaming GEMV (M <= 4) against the fp32-weight oracle; the output
+    starts as NaN so every element must be written."""
+
+    rng = np.random.default_rng(m * 11 + n + k + gs)
+    w = random_weights(rng, n, k, gs, bias=epi != "plain")
+    x = random_bf16(rng, (m, k))
+    wt, st, bt, bias = weights_to_torch(w)
+    kwargs = {}
+    residual = gate = None
+    if epi == "residual_gate":
+        residual = random_bf16(rng, (m, n))
+        gate = random_bf16(rng, (n,), 0.5)
+        kwargs = dict(residual=from_bits(residual), gate=from_bits(gate))
+    out = torch.full((m, n), float("nan"), dtype=torch.bfloat16, device="cuda")
+    got = ops.q6_linear(from_bits(x), wt, st, bt, bias, group_size=gs, apply_gelu=epi == "bias_gelu",
+                        path="simt", out=out, **kwargs)
+    torch.cuda.synchronize()
+    assert ops.last_path() == "simt"
+    assert bool(torch.isfinite(got).all())
+    ref = oracle.linear(
+        oracle.bf16_bits_to_f32(x), w, apply_gelu=epi == "bias_gelu", weight_dtype="f32",
+        residual=None if residual is None else oracle.bf16_bits_to_f32(residual),
+        gate=None if gate is None else oracle.bf16_bits_to_f32(gate),
+    )
+    assert_close(f32(got), ref, what=f"gemv {m}x{n}x{k} gs{gs} {epi}")
+
+
 LORA_CASES = [
     (200, 384, 512, 64, 64, "bias_gelu"),
     (17, 256, 192, 32, 32, "plain"),          # K % 128 == 64 tail before the LoRA stages
