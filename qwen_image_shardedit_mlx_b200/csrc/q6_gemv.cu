@@ -71,7 +71,11 @@ __host__ __device__ inline GemvLayout gemv_layout(int K, int gs) {
     return L;
 }
 
-template <int MT>
+// UPL = 16-code units per lane per stage (chunk / 512) when it is a compile-
+// time constant (every K that is a multiple of 512), which unrolls the unit
+// loop so that all shared-memory addresses are a per-lane base plus an
+// immediate; UPL = 0 is the generic loop.
+template <int MT, int UPL>
 __global__ void __launch_bounds__(kWarps * 32) gemv_stream_kernel(const LinearArgs a, int gs_shift) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int K = static_cast<int>(a.K);
@@ -178,9 +182,7 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_stream_kernel(const LinearAr
         const uint16_t* bi0 = sc0 + L.sb_bytes;
         const uint16_t* bi1 = bi0 + L.sb_bytes / 2;
         const int units = L.chunk / 16;
-        for (int j = lane; j < units; j += 32) {
-            const int J = c * units + j;          // unit index within the row
-            const int gl = (16 * j) >> gs_shift;  // group within the chunk
+        auto unit = [&](int j, int J, int gl, int xslot_base, int e_slots[4]) {
             const uint32_t* wa = reinterpret_cast<const uint32_t*>(codes0 + 12 * j);
             const uint32_t* wb = reinterpret_cast<const uint32_t*>(codes1 + 12 * j);
             float qa[16], qb[16];
@@ -190,11 +192,11 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_stream_kernel(const LinearAr
             const float s1 = bf16f(sc1[gl]), b1 = bf16f(bi1[gl]);
 #pragma unroll
             for (int m = 0; m < MT; ++m) {
-                const float4* xrow = xs4 + m * K4;
+                const float4* xrow = xs4 + m * K4 + xslot_base;
                 float d0 = 0.0f, d1 = 0.0f;
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
-                    const float4 xv = xrow[xswz(4 * J + e)];
+                    const float4 xv = xrow[e_slots[e]];
                     d0 = fmaf(xv.x, qa[4 * e], d0);
                     d0 = fmaf(xv.y, qa[4 * e + 1], d0);
                     d0 = fmaf(xv.z, qa[4 * e + 2], d0);
@@ -207,6 +209,29 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_stream_kernel(const LinearAr
                 const float xj = xsum[m * U16 + J];
                 acc0[m] = fmaf(s0, d0, fmaf(b0, xj, acc0[m]));
                 acc1[m] = fmaf(s1, d1, fmaf(b1, xj, acc1[m]));
+            }
+        };
+        if constexpr (UPL > 0) {
+            // units j = lane + 32 i: the x swizzle term (J >> 1) & 7 = (lane >> 1) & 7
+            // is the same for every i, so the four float4 slots of a unit are
+            // per-lane constants plus 128 i.
+            const int h = (lane >> 1) & 7;
+            int e_slots[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) e_slots[e] = (4 * lane + e) ^ h;
+            const int gstep = 512 >> gs_shift;  // groups per 32 units
+#pragma unroll
+            for (int i = 0; i < UPL; ++i) {
+                const int j = lane + 32 * i;
+                unit(j, c * units + j, ((16 * lane) >> gs_shift) + i * gstep, 4 * (c * units + 32 * i), e_slots);
+            }
+        } else {
+            for (int j = lane; j < units; j += 32) {
+                const int J = c * units + j;
+                int e_slots[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) e_slots[e] = xswz(4 * J + e) - 4 * J;
+                unit(j, J, (16 * j) >> gs_shift, 4 * J, e_slots);
             }
         }
         // Hand the slot back to this warp's producer lane for stage t + kSlots.
@@ -254,20 +279,20 @@ size_t gemv_smem_bytes(int64_t K, int gs, int mt) {
            static_cast<size_t>(mt) * (K / 16) * 4 + kWarps * kSlots * 8;
 }
 
-template <int MT>
+template <int MT, int UPL>
 int launch_gemv_mt(const LinearArgs& a, cudaStream_t stream) {
     const size_t smem = gemv_smem_bytes(a.K, a.group_size, MT);
     static int attr_set_for_device[64] = {0};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return Q6_ERR_CUDA;
     if (dev >= 0 && dev < 64 && !attr_set_for_device[dev]) {
-        if (cudaFuncSetAttribute(gemv_stream_kernel<MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemCap) !=
+        if (cudaFuncSetAttribute(gemv_stream_kernel<MT, UPL>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemCap) !=
             cudaSuccess)
             return Q6_ERR_CUDA;
         attr_set_for_device[dev] = 1;
     }
     int per_sm = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemv_stream_kernel<MT>, kWarps * 32, smem) !=
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemv_stream_kernel<MT, UPL>, kWarps * 32, smem) !=
             cudaSuccess ||
         per_sm <= 0)
         return Q6_ERR_CUDA;
@@ -275,7 +300,7 @@ int launch_gemv_mt(const LinearArgs& a, cudaStream_t stream) {
     const int64_t want = (pairs + kWarps - 1) / kWarps;
     const int blocks = static_cast<int>(std::min<int64_t>(want, static_cast<int64_t>(device_sm_count()) * per_sm));
     const int gs_shift = a.group_size == 32 ? 5 : (a.group_size == 64 ? 6 : 7);
-    gemv_stream_kernel<MT><<<blocks, kWarps * 32, smem, stream>>>(a, gs_shift);
+    gemv_stream_kernel<MT, UPL><<<blocks, kWarps * 32, smem, stream>>>(a, gs_shift);
     return cudaGetLastError() == cudaSuccess ? Q6_OK : Q6_ERR_CUDA;
 }
 
@@ -293,11 +318,28 @@ bool gemv_supported(const LinearArgs& a) {
     return gemv_smem_bytes(a.K, a.group_size, mt) <= static_cast<size_t>(kSmemCap);
 }
 
+template <int MT>
+int launch_gemv_upl(const LinearArgs& a, cudaStream_t stream) {
+    const int64_t chunk = a.K < kMaxChunk ? a.K : kMaxChunk;
+    const int upl = chunk % 512 == 0 ? static_cast<int>(chunk / 512) : 0;
+    switch (upl) {
+        case 1: return launch_gemv_mt<MT, 1>(a, stream);
+        case 2: return launch_gemv_mt<MT, 2>(a, stream);
+        case 3: return launch_gemv_mt<MT, 3>(a, stream);
+        case 4: return launch_gemv_mt<MT, 4>(a, stream);
+        case 5: return launch_gemv_mt<MT, 5>(a, stream);
+        case 6: return launch_gemv_mt<MT, 6>(a, stream);
+        case 7: return launch_gemv_mt<MT, 7>(a, stream);
+        case 8: return launch_gemv_mt<MT, 8>(a, stream);
+        default: return launch_gemv_mt<MT, 0>(a, stream);
+    }
+}
+
 int launch_gemv(const LinearArgs& a, cudaStream_t stream) {
     switch (a.M) {
-        case 1: return launch_gemv_mt<1>(a, stream);
-        case 2: return launch_gemv_mt<2>(a, stream);
-        default: return launch_gemv_mt<4>(a, stream);  // M = 3 or 4
+        case 1: return launch_gemv_upl<1>(a, stream);
+        case 2: return launch_gemv_upl<2>(a, stream);
+        default: return launch_gemv_upl<4>(a, stream);  // M = 3 or 4
     }
 }
 
