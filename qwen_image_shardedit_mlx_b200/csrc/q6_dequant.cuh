@@ -96,6 +96,66 @@ __device__ __forceinline__ void codes16_f32(uint32_t w0, uint32_t w1, uint32_t w
 #undef Q6_PAIR
 }
 
+// ------------------------------------------------------------------------
+// Three-position splice.  Shifting the three words first puts every code of a
+// 16-code block at bit 0, 6 or 12 of some word, so a splice needs one of only
+// three exponent words.  Passed in as runtime values (kernel arguments, which
+// the compiler cannot fold into the instruction), each splice is a single
+// logic instruction with the mask as its immediate, where two constants force
+// two.  SpliceExp3 holds the exponent words of 2^23, 2^17 and 2^11.
+struct SpliceExp3 {
+    uint32_t e0, e6, e12;
+};
+
+inline SpliceExp3 splice_exp3_host() { return SpliceExp3{150u << 23, 144u << 23, 138u << 23}; }
+
+template <int P>
+__device__ __forceinline__ float code_at(uint32_t v, uint32_t e) {
+    return __fadd_rn(__uint_as_float((v & (0x3Fu << P)) | e), -code_offset<P>());
+}
+
+// Sixteen codes (three packed words) -> their exact integer values as fp32.
+__device__ __forceinline__ void codes16_f32_e3(uint32_t w0, uint32_t w1, uint32_t w2, SpliceExp3 x,
+                                               float (&q)[16]) {
+    const uint32_t a1 = w0 >> 18;                      // codes 3, 4 at 0, 6
+    const uint32_t f5 = __funnelshift_r(w0, w1, 30);   // code 5 at 0
+    const uint32_t b0 = w1 >> 4;                       // codes 6, 7, 8 at 0, 6, 12
+    const uint32_t b1 = w1 >> 22;                      // code 9 at 0
+    const uint32_t f10 = __funnelshift_r(w1, w2, 28);  // code 10 at 0
+    const uint32_t c0 = w2 >> 2;                       // codes 11, 12, 13 at 0, 6, 12
+    const uint32_t c1 = w2 >> 20;                      // codes 14, 15 at 0, 6
+    q[0] = code_at<0>(w0, x.e0);
+    q[1] = code_at<6>(w0, x.e6);
+    q[2] = code_at<12>(w0, x.e12);
+    q[3] = code_at<0>(a1, x.e0);
+    q[4] = code_at<6>(a1, x.e6);
+    q[5] = code_at<0>(f5, x.e0);
+    q[6] = code_at<0>(b0, x.e0);
+    q[7] = code_at<6>(b0, x.e6);
+    q[8] = code_at<12>(b0, x.e12);
+    q[9] = code_at<0>(b1, x.e0);
+    q[10] = code_at<0>(f10, x.e0);
+    q[11] = code_at<0>(c0, x.e0);
+    q[12] = code_at<6>(c0, x.e6);
+    q[13] = code_at<12>(c0, x.e12);
+    q[14] = code_at<0>(c1, x.e0);
+    q[15] = code_at<6>(c1, x.e6);
+}
+
+// Sixteen codes -> eight bf16x2 words (low half = even code), three-position
+// splice: the same values as dequant16_bf16x2.
+__device__ __forceinline__ void dequant16_bf16x2_e3(uint32_t w0, uint32_t w1, uint32_t w2, float s, float b,
+                                                    SpliceExp3 x, uint32_t* out) {
+    float q[16];
+    codes16_f32_e3(w0, w1, w2, x, q);
+    const float2 s2 = make_float2(s, s), b2 = make_float2(b, b);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float2 r = __ffma2_rn(make_float2(q[2 * i], q[2 * i + 1]), s2, b2);  // s*q + b, one rounding
+        out[i] = pack_bf16x2(r.x, r.y);
+    }
+}
+
 // Sixteen codes -> eight bf16x2 words (low half = even code).
 __device__ __forceinline__ void dequant16_bf16x2(uint32_t w0, uint32_t w1, uint32_t w2, float s, float b,
                                                  uint32_t* out) {

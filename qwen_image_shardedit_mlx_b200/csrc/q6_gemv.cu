@@ -76,7 +76,8 @@ __host__ __device__ inline GemvLayout gemv_layout(int K, int gs) {
 // loop so that all shared-memory addresses are a per-lane base plus an
 // immediate; UPL = 0 is the generic loop.
 template <int MT, int UPL>
-__global__ void __launch_bounds__(kWarps * 32) gemv_stream_kernel(const LinearArgs a, int gs_shift) {
+__global__ void __launch_bounds__(kWarps * 32) gemv_stream_kernel(const LinearArgs a, int gs_shift,
+                                                                  const SpliceExp3 sx) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int K = static_cast<int>(a.K);
     const int N = static_cast<int>(a.N);
@@ -186,8 +187,8 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_stream_kernel(const LinearAr
             const uint32_t* wa = reinterpret_cast<const uint32_t*>(codes0 + 12 * j);
             const uint32_t* wb = reinterpret_cast<const uint32_t*>(codes1 + 12 * j);
             float qa[16], qb[16];
-            codes16_f32(wa[0], wa[1], wa[2], qa);
-            codes16_f32(wb[0], wb[1], wb[2], qb);  // stale slot bytes for an odd last row: never stored
+            codes16_f32_e3(wa[0], wa[1], wa[2], sx, qa);
+            codes16_f32_e3(wb[0], wb[1], wb[2], sx, qb);  // stale slot bytes for an odd last row: never stored
             const float s0 = bf16f(sc0[gl]), b0 = bf16f(bi0[gl]);
             const float s1 = bf16f(sc1[gl]), b1 = bf16f(bi1[gl]);
 #pragma unroll
@@ -300,7 +301,7 @@ int launch_gemv_mt(const LinearArgs& a, cudaStream_t stream) {
     const int64_t want = (pairs + kWarps - 1) / kWarps;
     const int blocks = static_cast<int>(std::min<int64_t>(want, static_cast<int64_t>(device_sm_count()) * per_sm));
     const int gs_shift = a.group_size == 32 ? 5 : (a.group_size == 64 ? 6 : 7);
-    gemv_stream_kernel<MT, UPL><<<blocks, kWarps * 32, smem, stream>>>(a, gs_shift);
+    gemv_stream_kernel<MT, UPL><<<blocks, kWarps * 32, smem, stream>>>(a, gs_shift, splice_exp3_host());
     return cudaGetLastError() == cudaSuccess ? Q6_OK : Q6_ERR_CUDA;
 }
 

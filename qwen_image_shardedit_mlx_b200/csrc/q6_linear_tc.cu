@@ -144,6 +144,7 @@ struct TcParams {
     const uint16_t* lora_b;
     float lora_scale;
     int lora_rank, lora_stages, lora_ksteps;
+    SpliceExp3 sexp;  // splice exponent words, runtime values so each splice is one instruction
 };
 
 __device__ __forceinline__ float bf16f(uint16_t v) { return __uint_as_float(static_cast<uint32_t>(v) << 16); }
@@ -559,10 +560,10 @@ __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
                     __syncwarp();
                     if (lane == 0) mbar_arrive(smem_u32(c_empty + cs));
                     uint32_t a[32];
-                    dequant16_bf16x2(c0.x, c0.y, c0.z, sb[0], sb[1], a);
-                    dequant16_bf16x2(c0.w, c1.x, c1.y, sb[0], sb[1], a + 8);
-                    dequant16_bf16x2(c1.z, c1.w, c2.x, sb[2], sb[3], a + 16);
-                    dequant16_bf16x2(c2.y, c2.z, c2.w, sb[2], sb[3], a + 24);
+                    dequant16_bf16x2_e3(c0.x, c0.y, c0.z, sb[0], sb[1], p.sexp, a);
+                    dequant16_bf16x2_e3(c0.w, c1.x, c1.y, sb[0], sb[1], p.sexp, a + 8);
+                    dequant16_bf16x2_e3(c1.z, c1.w, c2.x, sb[2], sb[3], p.sexp, a + 16);
+                    dequant16_bf16x2_e3(c2.y, c2.z, c2.w, sb[2], sb[3], p.sexp, a + 24);
                     // A slot `as` was last read by the MMAs of stage g - kAStages.
                     if (g >= static_cast<uint32_t>(kAStages)) {
                         const uint32_t prev = g - kAStages;
@@ -735,6 +736,7 @@ int launch_tc(const LinearArgs& a, cudaStream_t stream) {
     p.lora_rank = a.lora_rank;
     p.lora_stages = a.lora_rank > 0 ? 2 : 0;
     p.lora_ksteps = a.lora_rank / 32;
+    p.sexp = splice_exp3_host();
     const int grid = std::min(p.num_tiles, device_sm_count());
     q6_linear_tc_kernel<NT, kSbTma, kEpi>
         <<<grid, tc_threads(kDqSets), C::kSmemBytes, stream>>>(tmap_x, tmap_w, tmap_s, tmap_b, tmap_xa, p);
