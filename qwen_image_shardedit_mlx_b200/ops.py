@@ -169,6 +169,12 @@ def q6_linear(
     return y.reshape(leading + (n,))
 
 
+def mlp_workspace_bytes(m: int, h: int) -> int:
+    """Bytes of device workspace q6_mlp needs for m tokens and hidden width h."""
+
+    return int(_lib.lib().q6_mlp_workspace_bytes(int(m), int(h)))
+
+
 def q6_mlp(
     x: torch.Tensor,
     w1: tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor | None],

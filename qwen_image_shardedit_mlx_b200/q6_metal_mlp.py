@@ -28,7 +28,7 @@ the C ABI reads - which carries exactly the same values.
 
 from __future__ import annotations
 
-from collections.abc import Callable
+from collections.abc import Callable, Sequence
 from dataclasses import dataclass
 
 import torch
@@ -243,4 +243,73 @@ class QwenFeedForward(torch.nn.Module):
         return cls(make(hidden, dim), make(dim, hidden))
 
     def forward(self, hidden: torch.Tensor) -> torch.Tensor:
+        if self.mlp_in.lora is not None or self.mlp_out.lora is not None:
+            # LoRA-carrying layers: each linear fuses its own delta
+            mid = ops.q6_linear(hidden, self.mlp_in.weight, self.mlp_in.scales, self.mlp_in.biases, self.mlp_in.bias,
+                                group_size=self.mlp_in.group_size, apply_gelu=True, lora=self.mlp_in.lora)
+            return self.mlp_out(mid)
         return fused_q6_mlp(hidden, quantized_linear_spec(self.mlp_in), quantized_linear_spec(self.mlp_out))
+
+    def forward_host_stream(self, xs: Sequence[torch.Tensor], ys: Sequence[torch.Tensor]) -> None:
+        """Run the MLP over a sequence of batches that live in (pinned) host
+        memory: ``ys[i] = ff(xs[i])``.
+
+        The upload of batch i + 1 and the download of batch i - 1 overlap
+        the kernels of batch i (one stream per direction plus the compute
+        stream, two device buffers each way), so a serving loop that holds
+        its activations on the host pays max(copy, compute) per batch instead
+        of their sum.  Returns once all work is queued; the current stream
+        waits for the last download, so synchronising it (or an event
+        recorded on it) marks the end.  Batches must share one shape.
+        """
+
+        if len(xs) != len(ys):
+            raise ValueError("xs and ys must pair up")
+        if not xs:
+            return
+        dev = self.mlp_in.weight.device
+        d, h = self.mlp_in.in_features, self.mlp_in.out_features
+        m = int(xs[0].reshape(-1, d).shape[0])
+        key = (m, d, h, str(dev))
+        if getattr(self, "_stream_key", None) != key:
+            self._stream_bufs = (
+                [torch.empty((m, d), dtype=torch.bfloat16, device=dev) for _ in range(2)],
+                [torch.empty((m, d), dtype=torch.bfloat16, device=dev) for _ in range(2)],
+                torch.empty(int(ops.mlp_workspace_bytes(m, h)), dtype=torch.uint8, device=dev),
+                [torch.cuda.Stream(dev) for _ in range(3)],
+            )
+            self._stream_key = key
+        x_dev, y_dev, workspace, (s_in, s_comp, s_out) = self._stream_bufs
+        caller = torch.cuda.current_stream(dev)
+        for s in (s_in, s_comp, s_out):
+            s.wait_stream(caller)
+        w1 = (self.mlp_in.weight, self.mlp_in.scales, self.mlp_in.biases, self.mlp_in.bias)
+        w2 = (self.mlp_out.weight, self.mlp_out.scales, self.mlp_out.biases, self.mlp_out.bias)
+        read_x = [None, None]   # compute of the batch that last read x_dev[slot]
+        read_y = [None, None]   # download of the batch that last read y_dev[slot]
+        for i, (xh, yh) in enumerate(zip(xs, ys)):
+            slot = i % 2
+            if xh.reshape(-1, d).shape[0] != m or yh.numel() != m * d:
+                raise ValueError("all batches must have the first batch's shape")
+            with torch.cuda.stream(s_in):
+                if read_x[slot] is not None:
+                    s_in.wait_event(read_x[slot])
+                x_dev[slot].copy_(xh.reshape(m, d), non_blocking=True)
+                loaded = torch.cuda.Event()
+                loaded.record(s_in)
+            with torch.cuda.stream(s_comp):
+                s_comp.wait_event(loaded)
+                if read_y[slot] is not None:
+                    s_comp.wait_event(read_y[slot])
+                ops.q6_mlp(x_dev[slot], w1, w2, group_size=self.mlp_in.group_size, workspace=workspace,
+                           out=y_dev[slot])
+                computed = torch.cuda.Event()
+                computed.record(s_comp)
+                read_x[slot] = computed
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(computed)
+                yh.reshape(m, d).copy_(y_dev[slot], non_blocking=True)
+                done = torch.cuda.Event()
+                done.record(s_out)
+                read_y[slot] = done
+        caller.wait_stream(s_out)
