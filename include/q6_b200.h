@@ -91,9 +91,21 @@ Q6_API int q6_linear_bf16(const uint16_t* x, const uint32_t* w, const uint16_t* 
                    int group_size, int flags, int path, void* workspace, size_t workspace_bytes,
                    q6_stream_t stream);
 
-/* Workspace q6_linear_bf16 needs (0: no path of this build uses one; kept so
-   callers can size a buffer without knowing the path). */
+/* Lower bound of the workspace any q6_linear_bf16 call needs (0: every path
+   runs without one); see q6_linear_tc_workspace_bytes for the size that lets
+   the tensor-core path split K. */
 Q6_API size_t q6_linear_workspace_bytes(int64_t M, int lora_rank);
+
+/*
+ * Workspace bytes with which q6_linear_bf16's tensor-core path splits K across
+ * CTAs for an (M, N, K) problem whose tiles alone would leave SMs idle (few
+ * tokens, or few output rows: 12288 -> 3072 at M <= 256).  0 when it would not
+ * split.  Given at least this much 16-byte aligned workspace, the call writes
+ * fp32 partial sums there and reduces them in a second kernel on the same
+ * stream; with less (or none) it runs unsplit.  The split has no counterpart
+ * in the reference, whose Metal kernels compute one output per thread.
+ */
+Q6_API size_t q6_linear_tc_workspace_bytes(int64_t M, int64_t N, int64_t K);
 
 /*
  * fp32 activations in and out, fp32 dequantised weights (no bf16 rounding):

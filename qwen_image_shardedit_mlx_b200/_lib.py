@@ -44,6 +44,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_P, _P, _P, _P, _P, _P, _P, _P, _P, _F, _I, _P, _I64, _I64, _I64, _I, _I, _I, _P, _SZ, _P],
     ),
     "q6_linear_workspace_bytes": (_SZ, [_I64, _I]),
+    "q6_linear_tc_workspace_bytes": (_SZ, [_I64, _I64, _I64]),
     "q6_linear_f32": (_I, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I, _I, _P]),
     "q6_mlp_bf16": (
         _I,

@@ -84,6 +84,8 @@ int q6_dequantize_bf16(const uint32_t* w, const uint16_t* scales, const uint16_t
     return q6::launch_dequantize(w, scales, qbiases, out, N, K, group_size, reinterpret_cast<cudaStream_t>(stream));
 }
 
+size_t q6_linear_tc_workspace_bytes(int64_t M, int64_t N, int64_t K) { return q6::tc_workspace_bytes(M, N, K); }
+
 size_t q6_linear_workspace_bytes(int64_t M, int lora_rank) {
     (void)M;
     (void)lora_rank;
@@ -95,8 +97,6 @@ int q6_linear_bf16(const uint16_t* x, const uint32_t* w, const uint16_t* scales,
                    const uint16_t* lora_b, float lora_scale, int lora_rank, uint16_t* y, int64_t M, int64_t N,
                    int64_t K, int group_size, int flags, int path, void* workspace, size_t workspace_bytes,
                    q6_stream_t stream) {
-    (void)workspace;
-    (void)workspace_bytes;
     int st = check_weights(w, scales, qbiases, N, K, group_size);
     if (st != Q6_OK) return st;
     if (!x || !y || M <= 0) return Q6_ERR_INVALID_ARGUMENT;
@@ -110,6 +110,8 @@ int q6_linear_bf16(const uint16_t* x, const uint32_t* w, const uint16_t* scales,
         a.lora_scale = lora_scale;
         a.lora_rank = lora_rank;
     }
+    a.workspace = workspace;
+    a.workspace_bytes = workspace ? workspace_bytes : 0;
     return run_linear(a, path, reinterpret_cast<cudaStream_t>(stream));
 }
 

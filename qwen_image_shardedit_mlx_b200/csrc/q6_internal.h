@@ -27,6 +27,11 @@ struct LinearArgs {
     const uint16_t* lora_b = nullptr;
     float lora_scale = 0.0f;
     int lora_rank = 0;
+    // Caller workspace (device memory).  The tensor-core path splits K across
+    // CTAs when the tiles alone would leave SMs idle and this holds
+    // tc_workspace_bytes(M, N, K) bytes; otherwise it is not touched.
+    void* workspace = nullptr;
+    size_t workspace_bytes = 0;
 };
 
 // Path selection recorded for tests and benchmarks.
@@ -52,6 +57,9 @@ int launch_linear_tc(const LinearArgs& a, int token_tile, cudaStream_t stream);
 
 // Token tile the tensor-core path picks for an (M, N) problem.
 int choose_token_tile(int64_t M, int64_t N);
+
+// Workspace bytes the tensor-core path's split-K uses for (M, N, K) (0: no split).
+size_t tc_workspace_bytes(int64_t M, int64_t N, int64_t K);
 
 bool tc_supported(const LinearArgs& a);
 

@@ -145,7 +145,35 @@ struct TcParams {
     float lora_scale;
     int lora_rank, lora_stages, lora_ksteps;
     SpliceExp3 sexp;  // splice exponent words, runtime values so each splice is one instruction
+    // Split-K: work item it covers tile it / ksplit and the q6 stages
+    // [s * ks_per, min((s + 1) * ks_per, k_stages)) of split s = it % ksplit
+    // (ks_per a multiple of 8, so scale chunks never straddle splits).  With
+    // ksplit > 1 the epilogue stores fp32 partials [ksplit][M][N] and a second
+    // kernel sums them in split order and applies the epilogue.
+    int ksplit, ks_per, num_items;
+    float* partial;
 };
+
+struct Item {
+    int mb, nb, split, ks0, ks1, lora;
+    __device__ __forceinline__ int stages() const { return ks1 - ks0 + lora; }
+    // q6 stage of local index l, or k_stages + (LoRA stage index) past ks1
+    __device__ __forceinline__ int ks_of(int l, int k_stages) const {
+        return l < ks1 - ks0 ? ks0 + l : k_stages + (l - (ks1 - ks0));
+    }
+};
+
+__device__ __forceinline__ Item item_at(const TcParams& p, int it) {
+    Item I;
+    const int tile = it / p.ksplit;
+    I.split = it - tile * p.ksplit;
+    I.mb = tile / p.tiles_n;
+    I.nb = tile - I.mb * p.tiles_n;
+    I.ks0 = I.split * p.ks_per;
+    I.ks1 = I.ks0 + p.ks_per < p.k_stages ? I.ks0 + p.ks_per : p.k_stages;
+    I.lora = I.split == p.ksplit - 1 ? p.lora_stages : 0;  // the LoRA delta once per tile
+    return I;
+}
 
 __device__ __forceinline__ float bf16f(uint16_t v) { return __uint_as_float(static_cast<uint32_t>(v) << 16); }
 
@@ -220,10 +248,11 @@ __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
             uint32_t g = 0;  // stage counter over all tiles of this CTA
             int s = 0;       // g % kXStages
             bool ok = true;
-            const int stages = p.k_stages + p.lora_stages;
-            for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
-                const int mb = tile / p.tiles_n;
-                for (int ks = 0; ks < stages; ++ks, ++g) {
+            for (int it = blockIdx.x; it < p.num_items && ok; it += gridDim.x) {
+                const Item I = item_at(p, it);
+                const int mb = I.mb;
+                for (int l = 0; l < I.stages(); ++l, ++g) {
+                    const int ks = I.ks_of(l, p.k_stages);
                     // x slot s was last read by the MMAs of stage g - kXStages.
                     if (g >= static_cast<uint32_t>(C::kXStages)) {
                         const uint32_t prev = g - C::kXStages;
@@ -268,9 +297,10 @@ __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
             uint32_t sph = 0;
             long s_issued = 0;
             bool ok = true;
-            for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
-                const int nb = tile % p.tiles_n;
-                for (int ks = 0; ks < p.k_stages; ++ks) {
+            for (int it = blockIdx.x; it < p.num_items && ok; it += gridDim.x) {
+                const Item I = item_at(p, it);
+                const int nb = I.nb;
+                for (int ks = I.ks0; ks < I.ks1; ++ks) {
                     if (kSbTma && (ks & ((1 << p.sb_shift) - 1)) == 0) {
                         // first stage of a chunk: its scales and biases
                         if (!mbar_wait(smem_u32(s_empty + ss), sph ^ 1u, abort_flag, 9)) {
@@ -330,10 +360,12 @@ __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
             int xs = 0, acc = 0;
             uint32_t accph = 0;
             bool ok = true;
-            for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+            for (int it = blockIdx.x; it < p.num_items && ok; it += gridDim.x) {
+                const Item I = item_at(p, it);
                 if (!mbar_wait(smem_u32(acc_empty + acc), accph ^ 1u, abort_flag, 2)) break;
                 const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * NT);
-                for (int ks = 0; ks < p.k_stages + p.lora_stages; ++ks, ++g) {
+                for (int l = 0; l < I.stages(); ++l, ++g) {
+                    const int ks = I.ks_of(l, p.k_stages);
                     const uint32_t rs = g % kRing;
                     if (!mbar_wait(smem_u32(ready + rs), (g / kRing) & 1u, abort_flag, 3)) {
                         ok = false;
@@ -342,7 +374,7 @@ __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
                     tc_fence_after();
                     const uint32_t lo = desc_lo + static_cast<uint32_t>(xs * (C::kXStageBytes >> 4));
                     const uint32_t a_tmem = a_base + (rs % kAStages) * kAColsPerStage;
-                    const uint32_t first = ks != 0 ? 1u : 0u;
+                    const uint32_t first = l != 0 ? 1u : 0u;
                     // K step kk reads activation box kk / 4 at 32-byte offset kk % 4
                     // and TMEM A columns 8 kk .. 8 kk + 7.
                     auto issue = [&](int kk) {
@@ -387,9 +419,10 @@ __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
         const bool odd = (lane & 1) != 0;
         int acc = 0;
         uint32_t accph = 0;
-        for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
-            const int mb = tile / p.tiles_n;
-            const int nb = tile - mb * p.tiles_n;
+        for (int it = blockIdx.x; it < p.num_items; it += gridDim.x) {
+            const Item I = item_at(p, it);
+            const int mb = I.mb;
+            const int nb = I.nb;
             const int n = nb * kRows + q * 32 + lane;
             const bool n_ok = n < p.N;
             const float bias_n = (n_ok && p.bias) ? bf16f(p.bias[n]) : 0.0f;
@@ -403,6 +436,14 @@ __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
                 tmem_ld_32x32b_x16(taddr, v);
                 tmem_wait_ld();
                 const int m0 = mb * NT + c * kChunk;
+                if (p.ksplit > 1) {
+                    // split-K partial: fp32, epilogue applied after the sum
+                    float* dst = p.partial + (static_cast<size_t>(I.split) * p.M + m0) * p.N + n;
+#pragma unroll
+                    for (int j = 0; j < kChunk; ++j)
+                        if (n_ok && m0 + j < p.M) dst[static_cast<size_t>(j) * p.N] = __uint_as_float(v[j]);
+                    continue;
+                }
                 if (kEpi != kEpiGeneral && paired && m0 + kChunk <= p.M) {
                     // Whole chunk inside the token range: one paired 32-bit store
                     // per token pair, the row pointer advanced by two rows each time.
@@ -472,8 +513,9 @@ __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
         uint32_t gqstage = 0; // q6 (code-carrying) stage counter: the code ring's index
         uint32_t gchunk = 0;  // scale chunk counter over all tiles of this CTA
         bool ok = true;
-        for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
-            const int nb = tile % p.tiles_n;
+        for (int it = blockIdx.x; it < p.num_items && ok; it += gridDim.x) {
+            const Item I = item_at(p, it);
+            const int nb = I.nb;
             const int n = nb * kRows + r;
             const bool n_ok = n < p.N;
             const uint16_t* srow = p.scales + static_cast<size_t>(n_ok ? n : 0) * p.groups;
@@ -515,19 +557,20 @@ __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
             };
             const uint32_t g_base = gstage;
             const uint32_t gq_base = gqstage;
-            gstage += static_cast<uint32_t>(p.k_stages + p.lora_stages);
-            gqstage += static_cast<uint32_t>(p.k_stages);
-            int ks = static_cast<int>((static_cast<uint32_t>(set) + kDqSets - g_base % kDqSets) % kDqSets);
+            gstage += static_cast<uint32_t>(I.stages());
+            gqstage += static_cast<uint32_t>(I.ks1 - I.ks0);
+            int ks = I.ks0 + static_cast<int>((static_cast<uint32_t>(set) + kDqSets - g_base % kDqSets) % kDqSets);
             float sb_next[4];
-            if (!kSbTma && ks < p.k_stages) load_sb(ks, nullptr, sb_next);
+            if (!kSbTma && ks < I.ks1) load_sb(ks, nullptr, sb_next);
             // Chunks of 8 scale groups (the whole tile when scales are not staged).
             // Every dequant warp takes every chunk slot and hands it back, also a
             // chunk that holds none of its stages, so that each s_empty phase
             // counts exactly one arrival per warp.
             const int chunk_len = kSbTma ? (1 << p.sb_shift) : p.k_stages;
-            const int nchunks = kSbTma ? (p.k_stages + chunk_len - 1) >> p.sb_shift : 1;
-            for (int j = 0; j < nchunks && ok; ++j, ++gchunk) {
-                const int ks_end = (j + 1) * chunk_len < p.k_stages ? (j + 1) * chunk_len : p.k_stages;
+            const int c_first = kSbTma ? (I.ks0 >> p.sb_shift) : 0;
+            const int c_last = kSbTma ? (I.ks1 + chunk_len - 1) >> p.sb_shift : 1;
+            for (int j = c_first; j < c_last && ok; ++j, ++gchunk) {
+                const int ks_end = kSbTma ? ((j + 1) * chunk_len < I.ks1 ? (j + 1) * chunk_len : I.ks1) : I.ks1;
                 const uint8_t* slot = sb_smem + (gchunk % kSbSlots) * kSbSlotBytes;
                 if constexpr (kSbTma) {
                     if (!warp_wait(smem_u32(s_full + gchunk % kSbSlots), (gchunk / kSbSlots) & 1u, abort_flag, 10)) {
@@ -536,8 +579,8 @@ __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
                     }
                 }
                 for (; ks < ks_end; ks += kDqSets) {
-                    const uint32_t g = g_base + static_cast<uint32_t>(ks);
-                    const uint32_t gq = gq_base + static_cast<uint32_t>(ks);
+                    const uint32_t g = g_base + static_cast<uint32_t>(ks - I.ks0);
+                    const uint32_t gq = gq_base + static_cast<uint32_t>(ks - I.ks0);
                     const int cs = static_cast<int>(gq % C::kCStages);
                     const uint32_t cph = (gq / C::kCStages) & 1u;
                     const int as = static_cast<int>(g % kAStages);
@@ -548,7 +591,7 @@ __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
                     } else {
 #pragma unroll
                         for (int i = 0; i < 4; ++i) sb[i] = sb_next[i];
-                        if (ks + kDqSets < p.k_stages) load_sb(ks + kDqSets, nullptr, sb_next);
+                        if (ks + kDqSets < I.ks1) load_sb(ks + kDqSets, nullptr, sb_next);
                     }
                     if (!warp_wait(smem_u32(c_full + cs), cph, abort_flag, 6)) {
                         ok = false;
@@ -588,12 +631,12 @@ __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
             }
             // LoRA stages: A[n, k] = bf16(s * B[l r/2 + k, n]) for the r / 2 rank
             // columns of stage l (zero beyond), one coalesced row of B per k.
-            for (; ok && ks < p.k_stages + p.lora_stages; ks += kDqSets) {
-                const uint32_t g = g_base + static_cast<uint32_t>(ks);
+            for (; ok && ks < I.ks1 + I.lora; ks += kDqSets) {
+                const uint32_t g = g_base + static_cast<uint32_t>(ks - I.ks0);
                 const int as = static_cast<int>(g % kAStages);
                 const uint32_t rs = g % kRing;
                 const int half_r = p.lora_rank / 2;
-                const int j0 = (ks - p.k_stages) * half_r;
+                const int j0 = (ks - I.ks1) * half_r;
                 if (g >= static_cast<uint32_t>(kAStages)) {
                     const uint32_t prev = g - kAStages;
                     if (!warp_wait(smem_u32(done + prev % kRing), (prev / kRing) & 1u, abort_flag, 7)) {
@@ -673,6 +716,61 @@ bool sb_tma_ok(const LinearArgs& a) {
            reinterpret_cast<uintptr_t>(a.qbiases) % 16 == 0;
 }
 
+// Split-K plan: how many K splits (stages per split a multiple of 8) the
+// tensor-core path uses at token tile NT.  One when the tiles already fill
+// half the GPU; otherwise the count that minimises waves x (stages per split
+// + a fixed per-item cost of about 8 stages), plus the reduce pass.
+// Q6_TC_KSPLIT (1..16) overrides the choice for tuning.
+struct KSplit {
+    int splits, stages_per_split;
+};
+
+KSplit plan_ksplit(int64_t M, int64_t N, int64_t K, int NT) {
+    const int64_t sms = device_sm_count();
+    const int64_t tiles = ((M + NT - 1) / NT) * ((N + kRows - 1) / kRows);
+    const int64_t k_stages = (K + kBK - 1) / kBK;
+    auto per_split = [&](int64_t s) { return ((k_stages + s - 1) / s + 7) / 8 * 8; };
+    int want = 0;
+    if (const char* v = std::getenv("Q6_TC_KSPLIT")) want = std::atoi(v);
+    if (want >= 1 && want <= 16) {
+        const int64_t ps = per_split(want);
+        return KSplit{static_cast<int>((k_stages + ps - 1) / ps), static_cast<int>(ps)};
+    }
+    KSplit best{1, static_cast<int>(k_stages)};
+    if (tiles * 2 > sms) return best;
+    int64_t best_cost = ((tiles + sms - 1) / sms) * (k_stages + 8);
+    for (int64_t s = 2; s <= 8; ++s) {
+        const int64_t ps = per_split(s);
+        const int64_t splits = (k_stages + ps - 1) / ps;
+        if (splits != s) continue;
+        const int64_t cost = ((tiles * s + sms - 1) / sms) * (ps + 8) + 4;
+        if (cost < best_cost) {
+            best_cost = cost;
+            best = KSplit{static_cast<int>(s), static_cast<int>(ps)};
+        }
+    }
+    return best;
+}
+
+// Sums the split-K partials [splits][M][N] in split order and applies the
+// epilogue of the tensor-core kernel: + bias, GELU, * gate, + residual, bf16.
+__global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restrict__ partial, int splits, int64_t M,
+                                                           int64_t N, const uint16_t* bias, const uint16_t* gate,
+                                                           const uint16_t* residual, int flags, uint16_t* y) {
+    const int64_t total = M * N;
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t n = i % N;
+        float v = 0.0f;
+        for (int s = 0; s < splits; ++s) v += partial[s * total + i];
+        if (bias) v += bf16f(bias[n]);
+        if (flags & Q6_EPI_GELU) v = gelu_tanh(v);
+        if (gate) v *= bf16f(gate[n]);
+        if (residual) v += bf16f(residual[i]);
+        y[i] = static_cast<uint16_t>(pack_bf16x2(v, 0.0f) & 0xFFFFu);
+    }
+}
+
 template <int NT, bool kSbTma, int kEpi>
 int launch_tc(const LinearArgs& a, cudaStream_t stream) {
     using C = Cfg<NT>;
@@ -737,10 +835,26 @@ int launch_tc(const LinearArgs& a, cudaStream_t stream) {
     p.lora_stages = a.lora_rank > 0 ? 2 : 0;
     p.lora_ksteps = a.lora_rank / 32;
     p.sexp = splice_exp3_host();
-    const int grid = std::min(p.num_tiles, device_sm_count());
+    const KSplit ksp = plan_ksplit(a.M, a.N, a.K, NT);
+    const size_t need = static_cast<size_t>(ksp.splits) * a.M * a.N * sizeof(float);
+    const bool split = ksp.splits > 1 && a.workspace && a.workspace_bytes >= need &&
+                       reinterpret_cast<uintptr_t>(a.workspace) % 16 == 0;
+    p.ksplit = split ? ksp.splits : 1;
+    p.ks_per = split ? ksp.stages_per_split : p.k_stages;
+    p.num_items = p.num_tiles * p.ksplit;
+    p.partial = split ? static_cast<float*>(a.workspace) : nullptr;
+    const int grid = std::min(p.num_items, device_sm_count());
     q6_linear_tc_kernel<NT, kSbTma, kEpi>
         <<<grid, tc_threads(kDqSets), C::kSmemBytes, stream>>>(tmap_x, tmap_w, tmap_s, tmap_b, tmap_xa, p);
-    return cudaGetLastError() == cudaSuccess ? Q6_OK : Q6_ERR_CUDA;
+    if (cudaGetLastError() != cudaSuccess) return Q6_ERR_CUDA;
+    if (split) {
+        const int64_t total = a.M * a.N;
+        const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, int64_t(device_sm_count()) * 8));
+        splitk_reduce_kernel<<<blocks, 256, 0, stream>>>(p.partial, p.ksplit, a.M, a.N, a.bias, a.gate, a.residual,
+                                                        a.flags, static_cast<uint16_t*>(a.y));
+        if (cudaGetLastError() != cudaSuccess) return Q6_ERR_CUDA;
+    }
+    return Q6_OK;
 }
 
 // Staged scales with a specialised epilogue for the MLP's two shapes
@@ -776,6 +890,12 @@ bool tc_supported(const LinearArgs& a) {
     if (reinterpret_cast<uintptr_t>(a.x) % 16 != 0) return false;
     if (reinterpret_cast<uintptr_t>(a.w) % 16 != 0) return false;
     return true;
+}
+
+size_t tc_workspace_bytes(int64_t M, int64_t N, int64_t K) {
+    if (M <= 0 || N <= 0 || K <= 0) return 0;
+    const KSplit ksp = plan_ksplit(M, N, K, choose_token_tile(M, N));
+    return ksp.splits > 1 ? static_cast<size_t>(ksp.splits) * M * N * sizeof(float) : 0;
 }
 
 int choose_token_tile(int64_t M, int64_t N) {

@@ -160,10 +160,13 @@ def q6_linear(
         # into the q6 product's accumulator.
         xa = torch.matmul(xb, la).contiguous()
     y = out if out is not None else torch.empty((m, n), dtype=torch.bfloat16, device=dev)
+    # split-K workspace for the tensor-core path when its tiles alone leave SMs idle
+    ws_bytes = int(_lib.lib().q6_linear_tc_workspace_bytes(m, n, k)) if path != "simt" else 0
+    workspace = torch.empty(ws_bytes, dtype=torch.uint8, device=dev) if ws_bytes else None
     st = _lib.lib().q6_linear_bf16(
         xb.data_ptr(), w.data_ptr(), sc.data_ptr(), qb.data_ptr(), _ptr(bias_t), _ptr(res_t), _ptr(gate_t),
         _ptr(xa), _ptr(lb), float(lscale), rank, y.data_ptr(), m, n, k, group_size, flags,
-        _lib.PATHS[path], None, 0, stream,
+        _lib.PATHS[path], _ptr(workspace), ws_bytes, stream,
     )
     _lib.check(st, "q6_linear_bf16")
     return y.reshape(leading + (n,))

@@ -312,3 +312,67 @@ def test_dropin_feed_forward_module():
     assert float((ye.float() - yf.float()).abs().max()) < 0.05
     assert float((yd.float() - yf.float()).abs().max()) < 0.05
     assert torch.equal(ff(x), yf)
+
+
+SPLITK_CASES = [
+    # (M, N, K, gs, epi, forced splits or None for the planner's choice)
+    (16, 3072, 12288, 64, "plain", None),         # 24 weight tiles: the planner splits K
+    (16, 12288, 3072, 64, "bias_gelu", 3),
+    (200, 640, 3072, 64, "residual_gate", 3),
+    (37, 256, 1536, 32, "bias_gelu", 2),          # scale chunks of 2 stages
+    (40, 384, 2048, 128, "plain", 2),             # scale chunks of 8 stages
+    (24, 256, 1088, 64, "plain", 2),              # K % 128 == 64: the tail stage in the last split
+    (24, 256, 1216, 64, "bias_gelu", 2),          # K / gs % 8 != 0: per-lane scale loads
+]
+
+
+@pytest.mark.parametrize("m,n,k,gs,epi,splits", SPLITK_CASES)
+def test_split_k_vs_oracle(m, n, k, gs, epi, splits, monkeypatch):
+    """Split-K on the tensor-core path: fp32 partials per K split, summed in
+    split order by the reduce kernel, which applies the epilogue."""
+
+    if splits is not None:
+        monkeypatch.setenv("Q6_TC_KSPLIT", str(splits))
+    lib = _lib.lib()
+    assert lib.q6_linear_tc_workspace_bytes(m, n, k) > 0
+    rng = np.random.default_rng(m + n + k + gs)
+    w = random_weights(rng, n, k, gs, bias=epi != "plain")
+    x = random_bf16(rng, (m, k))
+    wt, st, bt, bias = weights_to_torch(w)
+    kwargs = {}
+    residual = gate = None
+    if epi == "residual_gate":
+        residual = random_bf16(rng, (m, n))
+        gate = random_bf16(rng, (n,), 0.5)
+        kwargs = dict(residual=from_bits(residual), gate=from_bits(gate))
+    outs = []
+    for _ in range(2):
+        out = torch.full((m, n), float("nan"), dtype=torch.bfloat16, device="cuda")
+        outs.append(ops.q6_linear(from_bits(x), wt, st, bt, bias, group_size=gs, apply_gelu=epi == "bias_gelu",
+                                  path="tensor", out=out, **kwargs))
+    torch.cuda.synchronize()
+    assert torch.equal(outs[0], outs[1])  # the split order is fixed: bitwise reproducible
+    assert bool(torch.isfinite(outs[0]).all())
+    ref = oracle.linear(
+        oracle.bf16_bits_to_f32(x), w, apply_gelu=epi == "bias_gelu", weight_dtype="bf16",
+        residual=None if residual is None else oracle.bf16_bits_to_f32(residual),
+        gate=None if gate is None else oracle.bf16_bits_to_f32(gate),
+    )
+    assert_close(f32(outs[0]), ref, what=f"splitk {m}x{n}x{k} gs{gs} {epi} s{splits}")
+
+
+def test_split_k_with_lora(monkeypatch):
+    monkeypatch.setenv("Q6_TC_KSPLIT", "2")
+    rng = np.random.default_rng(77)
+    m, n, k, r, gs = 64, 512, 2048, 64, 64
+    w = random_weights(rng, n, k, gs)
+    x = random_bf16(rng, (m, k))
+    a_bits = random_bf16(rng, (k, r), 0.01)
+    b_bits = random_bf16(rng, (r, n), 0.01)
+    wt, st, bt, bias = weights_to_torch(w)
+    got = ops.q6_linear(from_bits(x), wt, st, bt, bias, group_size=gs,
+                        lora=(from_bits(a_bits), from_bits(b_bits), 0.5))
+    torch.cuda.synchronize()
+    ref = oracle.linear(oracle.bf16_bits_to_f32(x), w, weight_dtype="bf16",
+                        lora=(oracle.bf16_bits_to_f32(a_bits), oracle.bf16_bits_to_f32(b_bits), 0.5))
+    assert_close(f32(got), ref, what="splitk lora")
