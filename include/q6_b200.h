@@ -73,7 +73,7 @@ Q6_API int q6_dequantize_bf16(const uint32_t* w, const uint16_t* scales, const u
  * epi: + bias[n] (if bias), GELU (if flags & Q6_EPI_GELU), then
  *      y = residual[m,n] + gate[n] * value  (each term only if its pointer is non-null).
  * LoRA (lora_xa bf16 [M, r] = x @ A computed by the caller, lora_b bf16 [r, N],
- *      both non-null, r in {32, 64, 96, 128}): the value gains
+ *      both non-null, r a multiple of 32 in [32, 256]): the value gains
  *      lora_scale * (lora_xa @ lora_b) before the bias, accumulated in the same
  *      fp32 tile as the q6 product (tensor-core path; Q6_PATH_SIMT returns
  *      Q6_ERR_UNSUPPORTED).

@@ -295,7 +295,7 @@ def linear(
     weight_dtype: str = "bf16",
     residual: np.ndarray | None = None,
     gate: np.ndarray | None = None,
-    lora: tuple[np.ndarray, np.ndarray, float] | None = None,
+    lora: tuple[np.ndarray, np.ndarray, float] | list[tuple[np.ndarray, np.ndarray, float]] | None = None,
 ) -> np.ndarray:
     """fp32 result of one q6 linear (BLAS in float64, then fp32).
 
@@ -304,14 +304,15 @@ def linear(
     fp32 weights like the reference's naive kernel.  ``x`` holds fp32 values
     (bf16 activations widened).  Epilogue: ``+bias``, GELU, then
     ``residual + gate * value`` (block residual gate, benchmarks/profile_qwen_block.py:294-301),
-    LoRA added before the bias (dense_img_ff_window.py:54-59).
+    LoRA added before the bias (dense_img_ff_window.py:54-59); a list of
+    adapters adds sum_i s_i (x A_i) B_i, the delta the reference folds for
+    several adapters (dense_img_ff_window.py:121-131).
     """
 
     wd = dequantize(w.weight, w.scales, w.biases, w.group_size, dtype=weight_dtype)
     wf = bf16_bits_to_f32(wd) if weight_dtype == "bf16" else wd
     acc = np.asarray(x, dtype=np.float64) @ wf.astype(np.float64).T
-    if lora is not None:
-        a, b, s = lora
+    for a, b, s in ([] if lora is None else [lora] if isinstance(lora, tuple) else lora):
         xa = np.asarray(x, dtype=np.float64) @ np.asarray(a, dtype=np.float64)
         acc = acc + float(s) * (xa @ np.asarray(b, dtype=np.float64))
     acc = acc.astype(np.float32)

@@ -137,8 +137,9 @@ struct TcParams {
     int tiles_n, num_tiles, k_stages, last_ksteps;
     // LoRA delta s * (xa @ B) (xa = x @ A, bf16 [M, r]; B bf16 [r, N]): two
     // extra stages per tile after the q6 stages, each covering r / 2 of the
-    // rank (lora_ksteps = r / 32 MMAs of K = 16), with A(TMEM)[n, j] =
-    // bf16(s * B[j, n]) and the activation box loaded from xa.  0 stages
+    // rank (lora_ksteps = r / 32 MMAs of K = 16, r <= 256 so a stage fits
+    // the two 64-wide activation boxes), with A(TMEM)[n, j] =
+    // bf16(s * B[j, n]) and the activation boxes loaded from xa.  0 stages
     // without LoRA.  Two stages keep every stage's parity, so each dequant
     // set still owns the code slots of its parity.
     const uint16_t* lora_b;
@@ -267,9 +268,12 @@ __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
                         mbar_arrive_expect_tx(fb, C::kXStageBytes);
                         tma_load_2d(dst, &tmap_x, fb, ks * kBK, mb * NT);
                         tma_load_2d(dst + C::kXBoxBytes, &tmap_x, fb, ks * kBK + kBoxK, mb * NT);
-                    } else {  // LoRA stage: columns [l r/2, l r/2 + 64) of xa in the first box
-                        mbar_arrive_expect_tx(fb, C::kXBoxBytes);
-                        tma_load_2d(dst, &tmap_xa, fb, (ks - p.k_stages) * (p.lora_rank / 2), mb * NT);
+                    } else {  // LoRA stage l: xa columns [l r/2, (l + 1) r/2), one box per 64
+                        const int x0 = (ks - p.k_stages) * (p.lora_rank / 2);
+                        const bool two = p.lora_rank > 2 * kBoxK;
+                        mbar_arrive_expect_tx(fb, two ? C::kXStageBytes : C::kXBoxBytes);
+                        tma_load_2d(dst, &tmap_xa, fb, x0, mb * NT);
+                        if (two) tma_load_2d(dst + C::kXBoxBytes, &tmap_xa, fb, x0 + kBoxK, mb * NT);
                     }
                     if (++s == C::kXStages) s = 0;
                 }
@@ -388,7 +392,7 @@ __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
                     } else if (ks < p.k_stages) {  // K % 128 == 64 tail: the first box only
 #pragma unroll
                         for (int kk = 0; kk < kBK / 32; ++kk) issue(kk);
-                    } else {  // LoRA stage: r / 32 K-steps in the first box
+                    } else {  // LoRA stage: r / 32 K-steps (the second box once r > 128)
                         for (int kk = 0; kk < p.lora_ksteps; ++kk) issue(kk);
                     }
                     tc_commit(smem_u32(done + rs));
@@ -882,8 +886,8 @@ int error_word_tc(bool clear) {
 bool tc_supported(const LinearArgs& a) {
     if (a.K % kBoxK != 0) return false;
     if (a.lora_rank != 0) {
-        // two LoRA stages of r / 2 rank columns each, within one 64-wide box
-        if (a.lora_rank < 32 || a.lora_rank > 128 || a.lora_rank % 32 != 0) return false;
+        // two LoRA stages of r / 2 rank columns each, within the stage's two 64-wide boxes
+        if (a.lora_rank < 32 || a.lora_rank > 256 || a.lora_rank % 32 != 0) return false;
         if (!a.lora_xa || !a.lora_b || reinterpret_cast<uintptr_t>(a.lora_xa) % 16 != 0) return false;
     }
     if (a.M > (int64_t(1) << 30) || a.N > (int64_t(1) << 30) || a.K > (int64_t(1) << 24)) return false;

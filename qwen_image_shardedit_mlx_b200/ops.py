@@ -12,6 +12,7 @@ import ctypes
 import torch
 
 from qwen_image_shardedit_mlx_b200 import _lib
+from qwen_image_shardedit_mlx_b200.lora import MAX_FUSED_RANK, pad_lora_rank
 
 GROUP_SIZES = (32, 64, 128)
 
@@ -153,8 +154,12 @@ def q6_linear(
         rank = int(a.shape[-1])
         la = a.to(device=dev, dtype=torch.bfloat16)
         lb = b.to(device=dev, dtype=torch.bfloat16).contiguous()
-        if tuple(la.shape) != (k, rank) or tuple(lb.shape) != (rank, n):
+        if tuple(la.shape) != (k, rank) or tuple(lb.shape) != (rank, n) or rank == 0:
             raise ValueError(f"LoRA A must be ({k}, r) and B (r, {n}); got {tuple(la.shape)}, {tuple(lb.shape)}")
+        if rank > MAX_FUSED_RANK:
+            raise ValueError(f"LoRA rank {rank} exceeds the fused maximum {MAX_FUSED_RANK}")
+        la, lb = pad_lora_rank(la, lb)  # the kernel takes ranks in steps of 32
+        rank = int(la.shape[1])
         # x @ A is a plain bf16 GEMM (fp32 accumulation, bf16 result, as the
         # reference's LoRA linear computes it); the library fuses s * (xa @ B)
         # into the q6 product's accumulator.

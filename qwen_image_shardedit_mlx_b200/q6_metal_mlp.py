@@ -35,6 +35,7 @@ import torch
 import torch.nn.functional as F
 
 from qwen_image_shardedit_mlx_b200 import ops
+from qwen_image_shardedit_mlx_b200.lora import LoRAAdapter, fold_lora_adapters
 from qwen_image_shardedit_mlx_b200.quantize import quantize_affine_q6
 
 
@@ -73,7 +74,8 @@ class QuantizedLinear(torch.nn.Module):
         self.group_size = int(group_size)
         self.bits = int(bits)
         self.mode = "affine"
-        self.lora: tuple[torch.Tensor, torch.Tensor, float] | None = None
+        self.loras: list[LoRAAdapter] = []
+        self.lora: tuple[torch.Tensor, torch.Tensor, float] | None = None  # the fused delta of ``loras``
 
     @classmethod
     def from_linear(cls, linear: torch.nn.Linear, *, bits: int = 6, group_size: int = 64) -> "QuantizedLinear":
@@ -92,21 +94,31 @@ class QuantizedLinear(torch.nn.Module):
         return int(self.weight.shape[0])
 
     def set_lora(self, a: torch.Tensor | None, b: torch.Tensor | None = None, scale: float = 1.0) -> None:
-        """Attach (or with ``a=None`` remove) a LoRA delta: the layer then
-        computes ``q6(x) + scale * ((x @ a) @ b)`` before its bias, as the
-        reference's LoRA-additive linear does (dense_img_ff_window.py:48-60).
-        ``a`` is [in_features, r], ``b`` is [r, out_features], r in {32, 64, 96, 128};
-        the ``(x @ a) @ b`` product is fused into the q6 kernel's accumulator."""
+        """Attach (or with ``a=None`` remove) a LoRA delta, replacing any
+        adapters: the layer then computes ``q6(x) + scale * ((x @ a) @ b)``
+        before its bias, as the reference's LoRA-additive linear does
+        (dense_img_ff_window.py:48-60).  ``a`` is [in_features, r], ``b`` is
+        [r, out_features]; the ``(x @ a) @ b`` product is fused into the q6
+        kernel's accumulator."""
 
         if a is None:
+            self.loras = []
             self.lora = None
             return
         if b is None:
             raise ValueError("LoRA needs both A and B")
-        r = int(a.shape[-1])
-        if tuple(a.shape) != (self.in_features, r) or tuple(b.shape) != (r, self.out_features):
-            raise ValueError(f"LoRA A must be ({self.in_features}, r) and B (r, {self.out_features})")
-        self.lora = (a.to(torch.bfloat16).contiguous(), b.to(torch.bfloat16).contiguous(), float(scale))
+        self.loras = []
+        self.add_lora(a, b, scale)
+
+    def add_lora(self, a: torch.Tensor, b: torch.Tensor, scale: float = 1.0) -> None:
+        """Add one more adapter.  Several adapters are stacked into one fused
+        delta of rank sum(r_i) <= 256 (``lora.fold_lora_adapters``); each adds
+        exactly what it would add alone."""
+
+        ad = LoRAAdapter(a.to(torch.bfloat16).contiguous(), b.to(torch.bfloat16).contiguous(), float(scale))
+        adapters = [*self.loras, ad]
+        self.lora = fold_lora_adapters(adapters, in_features=self.in_features, out_features=self.out_features)
+        self.loras = adapters
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         return ops.q6_linear(x, self.weight, self.scales, self.biases, self.bias, group_size=self.group_size,

@@ -207,6 +207,10 @@ LORA_CASES = [
     (130, 640, 1024, 128, 64, "residual_gate"),
     (3, 512, 256, 96, 64, "bias_gelu"),       # a few rows: the auto path still takes the fused kernel
     (1000, 3072, 3072, 64, 64, "plain"),      # image-FF width
+    (64, 256, 320, 8, 64, "bias_gelu"),       # rank 8: zero-padded to 32 on the host
+    (150, 384, 448, 160, 64, "plain"),        # r > 128: each LoRA stage spans both activation boxes
+    (40, 512, 1024, 256, 128, "residual_gate"),  # the fused maximum
+    (129, 320, 192, 224, 32, "bias_gelu"),    # r > 128 after a K % 128 == 64 tail
 ]
 
 
@@ -254,8 +258,10 @@ def test_lora_rejected_off_the_tensor_path():
     b = torch.zeros((64, 128), dtype=torch.bfloat16, device="cuda")
     with pytest.raises(_lib.Q6Error):
         ops.q6_linear(x, wt, st, bt, bias, lora=(a, b, 1.0), path="simt")
-    with pytest.raises(_lib.Q6Error):  # rank 16 is below the fused kernel's granularity
-        ops.q6_linear(x, wt, st, bt, bias, lora=(a[:, :16], b[:16], 1.0))
+    big_a = torch.zeros((256, 288), dtype=torch.bfloat16, device="cuda")
+    big_b = torch.zeros((288, 128), dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(ValueError, match="exceeds"):  # past the two fused LoRA stages
+        ops.q6_linear(x, wt, st, bt, bias, lora=(big_a, big_b, 1.0))
 
 
 def test_auto_path_choice():
@@ -361,10 +367,11 @@ def test_split_k_vs_oracle(m, n, k, gs, epi, splits, monkeypatch):
     assert_close(f32(outs[0]), ref, what=f"splitk {m}x{n}x{k} gs{gs} {epi} s{splits}")
 
 
-def test_split_k_with_lora(monkeypatch):
+@pytest.mark.parametrize("r", [64, 256])
+def test_split_k_with_lora(monkeypatch, r):
     monkeypatch.setenv("Q6_TC_KSPLIT", "2")
-    rng = np.random.default_rng(77)
-    m, n, k, r, gs = 64, 512, 2048, 64, 64
+    rng = np.random.default_rng(77 + r)
+    m, n, k, gs = 64, 512, 2048, 64
     w = random_weights(rng, n, k, gs)
     x = random_bf16(rng, (m, k))
     a_bits = random_bf16(rng, (k, r), 0.01)
@@ -375,4 +382,4 @@ def test_split_k_with_lora(monkeypatch):
     torch.cuda.synchronize()
     ref = oracle.linear(oracle.bf16_bits_to_f32(x), w, weight_dtype="bf16",
                         lora=(oracle.bf16_bits_to_f32(a_bits), oracle.bf16_bits_to_f32(b_bits), 0.5))
-    assert_close(f32(got), ref, what="splitk lora")
+    assert_close(f32(got), ref, what=f"splitk lora r{r}")
