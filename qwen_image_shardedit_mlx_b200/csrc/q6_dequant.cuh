@@ -102,12 +102,17 @@ __device__ __forceinline__ void codes16_f32(uint32_t w0, uint32_t w1, uint32_t w
 // three exponent words.  Passed in as runtime values (kernel arguments, which
 // the compiler cannot fold into the instruction), each splice is a single
 // logic instruction with the mask as its immediate, where two constants force
-// two.  SpliceExp3 holds the exponent words of 2^23, 2^17 and 2^11.
+// two.  SpliceExp3 holds the exponent words of 2^23, 2^17 and 2^11 (codes at
+// bits 0, 6, 12), and of 2^12 and 2^6 (codes at bits 11 and 17, the folded
+// dequant below).
 struct SpliceExp3 {
     uint32_t e0, e6, e12;
+    uint32_t e11, e17;
 };
 
-inline SpliceExp3 splice_exp3_host() { return SpliceExp3{150u << 23, 144u << 23, 138u << 23}; }
+inline SpliceExp3 splice_exp3_host() {
+    return SpliceExp3{150u << 23, 144u << 23, 138u << 23, 139u << 23, 133u << 23};
+}
 
 template <int P>
 __device__ __forceinline__ float code_at(uint32_t v, uint32_t e) {
@@ -180,6 +185,48 @@ __device__ __forceinline__ void dequant16_bf16x2(uint32_t w0, uint32_t w1, uint3
     out[6] = pack_bf16x2(r.x, r.y);
     r = pair_f32<8, 14>(code_spliced<8>(t2), code_spliced<14>(t2), s2, b2);
     out[7] = pack_bf16x2(r.x, r.y);
+}
+
+// ------------------------------------------------------------------------
+// Folded-offset dequant.  A code spliced at bit 11 under exponent 2^12 reads
+// 4096 + q, at bit 17 under 2^6 it reads 64 + q (exact).  Folding the offset
+// into the bias, w = fma(s, 4096 + q, b - 4096 s) (resp. 64), drops the
+// subtract of the exact path: one FFMA2 per code pair.  The result equals
+// bf16_rn(s q + b) exactly whenever b - 4096 s and b - 64 s are exact in fp32
+// (the FMA then rounds the same real number once), which holds unless |b| is
+// below about s / 32 without being zero.  FoldedBias carries the two folded
+// biases and whether both are exact; an inexact group must take the exact
+// path (dequant16_bf16x2_e3).
+struct FoldedBias {
+    float2 b;  // (b - 4096 s, b - 64 s): the even code of a pair sits at bit 11, the odd at 17
+    bool exact;
+};
+
+__device__ __forceinline__ FoldedBias fold_bias(float s, float b) {
+    FoldedBias f;
+    f.b.x = fmaf(-4096.0f, s, b);
+    f.b.y = fmaf(-64.0f, s, b);
+    // Adding the offset back recovers b exactly iff the fold rounded nothing:
+    // a rounding error is a multiple of b's bf16 unit, far above half its fp32 ulp.
+    f.exact = fmaf(4096.0f, s, f.b.x) == b && fmaf(64.0f, s, f.b.y) == b;
+    return f;
+}
+
+// Sixteen codes -> eight bf16x2 words (low half = even code).  Each of eight
+// shifts places one code pair at bits 11 and 17; two splices, one FFMA2 and
+// one pack per pair.
+__device__ __forceinline__ void dequant16_bf16x2_fold(uint32_t w0, uint32_t w1, uint32_t w2, float s, float2 fb,
+                                                      SpliceExp3 x, uint32_t* out) {
+    const uint32_t v[8] = {w0 << 11, w0 >> 1, __funnelshift_r(w0, w1, 13), w1 << 7,
+                           w1 >> 5, __funnelshift_r(w1, w2, 17), w2 << 3, w2 >> 9};
+    const float2 s2 = make_float2(s, s);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float lo = __uint_as_float((v[i] & (0x3Fu << 11)) | x.e11);
+        const float hi = __uint_as_float((v[i] & (0x3Fu << 17)) | x.e17);
+        const float2 r = __ffma2_rn(make_float2(lo, hi), s2, fb);
+        out[i] = pack_bf16x2(r.x, r.y);
+    }
 }
 
 }  // namespace q6

@@ -129,12 +129,14 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_stream_kernel(const LinearAr
         }
     };
 
+    pdl_launch_dependents();
     if (lane == 0) {
         for (int s = 0; s < kSlots; ++s) mbar_init(smem_u32(full + s), 1);
         fence_mbar_init();
-        for (int t = 0; t < kSlots && t < my_stages; ++t) issue(t);
+        for (int t = 0; t < kSlots && t < my_stages; ++t) issue(t);  // weights: before the dependency wait
     }
     __syncwarp();
+    pdl_wait();  // x, y and the epilogue operands may come from the previous kernel
 
     // Stage the activations (bf16 -> fp32, swizzled; rows M..MT-1 zero), then
     // the per-unit sums.  The first weight stages are already in flight.
@@ -301,8 +303,9 @@ int launch_gemv_mt(const LinearArgs& a, cudaStream_t stream) {
     const int64_t want = (pairs + kWarps - 1) / kWarps;
     const int blocks = static_cast<int>(std::min<int64_t>(want, static_cast<int64_t>(device_sm_count()) * per_sm));
     const int gs_shift = a.group_size == 32 ? 5 : (a.group_size == 64 ? 6 : 7);
-    gemv_stream_kernel<MT, UPL><<<blocks, kWarps * 32, smem, stream>>>(a, gs_shift, splice_exp3_host());
-    return cudaGetLastError() == cudaSuccess ? Q6_OK : Q6_ERR_CUDA;
+    const cudaError_t err = launch_pdl(gemv_stream_kernel<MT, UPL>, dim3(blocks), dim3(kWarps * 32), smem, stream, a,
+                                       gs_shift, splice_exp3_host());
+    return err == cudaSuccess ? Q6_OK : Q6_ERR_CUDA;
 }
 
 }  // namespace

@@ -4,6 +4,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 #include "q6_b200.h"
 
 namespace q6 {
@@ -64,6 +66,26 @@ size_t tc_workspace_bytes(int64_t M, int64_t N, int64_t K);
 bool tc_supported(const LinearArgs& a);
 
 int device_sm_count();
+
+// Programmatic dependent launch for the kernels that execute pdl_wait before
+// their dependent reads and writes (Q6_PDL=0 turns the attribute off).
+bool pdl_enabled();
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // Per-translation-unit device error words (value, optionally cleared; -1 on
 // a failed copy).

@@ -240,12 +240,14 @@ __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    pdl_launch_dependents();
 
     if (warp == 0) {
         // ------------------------------------------------ activation producer
         if (lane == 0) {
             tma_prefetch_map(&tmap_x);
             if (p.lora_stages) tma_prefetch_map(&tmap_xa);
+            pdl_wait();  // the activations may come from the previous kernel
             uint32_t g = 0;  // stage counter over all tiles of this CTA
             int s = 0;       // g % kXStages
             bool ok = true;
@@ -421,6 +423,7 @@ __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
         // odd lane: token j+1).  Needs an even row length and 4-byte aligned y.
         const bool paired = (p.N % 2 == 0) && ((reinterpret_cast<uintptr_t>(p.y) & 3) == 0);
         const bool odd = (lane & 1) != 0;
+        pdl_wait();  // y, the residual, the gate and the partials may be the previous kernel's
         int acc = 0;
         uint32_t accph = 0;
         for (int it = blockIdx.x; it < p.num_items; it += gridDim.x) {
@@ -607,10 +610,20 @@ __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
                     __syncwarp();
                     if (lane == 0) mbar_arrive(smem_u32(c_empty + cs));
                     uint32_t a[32];
-                    dequant16_bf16x2_e3(c0.x, c0.y, c0.z, sb[0], sb[1], p.sexp, a);
-                    dequant16_bf16x2_e3(c0.w, c1.x, c1.y, sb[0], sb[1], p.sexp, a + 8);
-                    dequant16_bf16x2_e3(c1.z, c1.w, c2.x, sb[2], sb[3], p.sexp, a + 16);
-                    dequant16_bf16x2_e3(c2.y, c2.z, c2.w, sb[2], sb[3], p.sexp, a + 24);
+                    // Folded-offset dequant unless a lane's group needs the exact path.
+                    const FoldedBias f0 = fold_bias(sb[0], sb[1]);
+                    const FoldedBias f1 = fold_bias(sb[2], sb[3]);
+                    if (__all_sync(0xffffffffu, f0.exact && f1.exact)) {
+                        dequant16_bf16x2_fold(c0.x, c0.y, c0.z, sb[0], f0.b, p.sexp, a);
+                        dequant16_bf16x2_fold(c0.w, c1.x, c1.y, sb[0], f0.b, p.sexp, a + 8);
+                        dequant16_bf16x2_fold(c1.z, c1.w, c2.x, sb[2], f1.b, p.sexp, a + 16);
+                        dequant16_bf16x2_fold(c2.y, c2.z, c2.w, sb[2], f1.b, p.sexp, a + 24);
+                    } else {
+                        dequant16_bf16x2_e3(c0.x, c0.y, c0.z, sb[0], sb[1], p.sexp, a);
+                        dequant16_bf16x2_e3(c0.w, c1.x, c1.y, sb[0], sb[1], p.sexp, a + 8);
+                        dequant16_bf16x2_e3(c1.z, c1.w, c2.x, sb[2], sb[3], p.sexp, a + 16);
+                        dequant16_bf16x2_e3(c2.y, c2.z, c2.w, sb[2], sb[3], p.sexp, a + 24);
+                    }
                     // A slot `as` was last read by the MMAs of stage g - kAStages.
                     if (g >= static_cast<uint32_t>(kAStages)) {
                         const uint32_t prev = g - kAStages;
@@ -761,6 +774,8 @@ KSplit plan_ksplit(int64_t M, int64_t N, int64_t K, int NT) {
 __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restrict__ partial, int splits, int64_t M,
                                                            int64_t N, const uint16_t* bias, const uint16_t* gate,
                                                            const uint16_t* residual, int flags, uint16_t* y) {
+    pdl_launch_dependents();
+    pdl_wait();  // the partials of the kernel before
     const int64_t total = M * N;
     for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
          i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -848,15 +863,16 @@ int launch_tc(const LinearArgs& a, cudaStream_t stream) {
     p.num_items = p.num_tiles * p.ksplit;
     p.partial = split ? static_cast<float*>(a.workspace) : nullptr;
     const int grid = std::min(p.num_items, device_sm_count());
-    q6_linear_tc_kernel<NT, kSbTma, kEpi>
-        <<<grid, tc_threads(kDqSets), C::kSmemBytes, stream>>>(tmap_x, tmap_w, tmap_s, tmap_b, tmap_xa, p);
-    if (cudaGetLastError() != cudaSuccess) return Q6_ERR_CUDA;
+    if (launch_pdl(q6_linear_tc_kernel<NT, kSbTma, kEpi>, dim3(grid), dim3(tc_threads(kDqSets)), C::kSmemBytes,
+                   stream, tmap_x, tmap_w, tmap_s, tmap_b, tmap_xa, p) != cudaSuccess)
+        return Q6_ERR_CUDA;
     if (split) {
         const int64_t total = a.M * a.N;
         const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, int64_t(device_sm_count()) * 8));
-        splitk_reduce_kernel<<<blocks, 256, 0, stream>>>(p.partial, p.ksplit, a.M, a.N, a.bias, a.gate, a.residual,
-                                                        a.flags, static_cast<uint16_t*>(a.y));
-        if (cudaGetLastError() != cudaSuccess) return Q6_ERR_CUDA;
+        if (launch_pdl(splitk_reduce_kernel, dim3(blocks), dim3(256), 0, stream,
+                       static_cast<const float*>(p.partial), p.ksplit, a.M, a.N, a.bias, a.gate, a.residual, a.flags,
+                       static_cast<uint16_t*>(a.y)) != cudaSuccess)
+            return Q6_ERR_CUDA;
     }
     return Q6_OK;
 }

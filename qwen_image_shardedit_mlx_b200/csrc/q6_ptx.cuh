@@ -280,6 +280,18 @@ __device__ __forceinline__ void tmem_wait_ld() {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// --------------------------------------------------------------- programmatic dependent launch
+// A kernel launched with programmatic stream serialization may start while
+// the previous kernel of the stream is still running (once every CTA of that
+// kernel has executed pdl_launch_dependents, or it has completed).  Before
+// its first read of anything the previous kernel may have written, and its
+// first global write, it must execute pdl_wait: that returns once the
+// previous grids have completed and their memory is visible.  Weights are
+// never written by these kernels, so their prefetch may precede the wait.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // --------------------------------------------------------------- numerics
 
 __device__ __forceinline__ float tanh_fast(float x) {

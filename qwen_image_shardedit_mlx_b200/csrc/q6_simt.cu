@@ -7,6 +7,8 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
+#include <cstdlib>
+
 #include <algorithm>
 
 #include "q6_dequant.cuh"
@@ -149,6 +151,15 @@ int error_word_simt(bool clear) {
         if (cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int)) != cudaSuccess) return -1;
     }
     return v;
+}
+
+bool pdl_enabled() {
+    static int v = -1;  // a benign race: every thread computes the same value
+    if (v < 0) {
+        const char* e = std::getenv("Q6_PDL");
+        v = (e && e[0] == '0') ? 0 : 1;
+    }
+    return v == 1;
 }
 
 int device_sm_count() {
