@@ -212,19 +212,34 @@ __device__ __forceinline__ FoldedBias fold_bias(float s, float b) {
     return f;
 }
 
-// Sixteen codes -> eight bf16x2 words (low half = even code).  Each of eight
-// shifts places one code pair at bits 11 and 17; two splices, one FFMA2 and
-// one pack per pair.
+// Eight shifts of a 16-code block (three packed words) that place code pair
+// (2i, 2i+1) at bits 11 and 17 of v[i].
+__device__ __forceinline__ void pair_words16(uint32_t w0, uint32_t w1, uint32_t w2, uint32_t (&v)[8]) {
+    v[0] = w0 << 11;
+    v[1] = w0 >> 1;
+    v[2] = __funnelshift_r(w0, w1, 13);
+    v[3] = w1 << 7;
+    v[4] = w1 >> 5;
+    v[5] = __funnelshift_r(w1, w2, 17);
+    v[6] = w2 << 3;
+    v[7] = w2 >> 9;
+}
+
+// The pair of v as fp32 (4096 + even code, 64 + odd code): one splice each.
+__device__ __forceinline__ float2 pair_at11_17(uint32_t v, SpliceExp3 x) {
+    return make_float2(__uint_as_float((v & (0x3Fu << 11)) | x.e11), __uint_as_float((v & (0x3Fu << 17)) | x.e17));
+}
+
+// Sixteen codes -> eight bf16x2 words (low half = even code): per pair one
+// shift, two splices, one FFMA2 and one pack.
 __device__ __forceinline__ void dequant16_bf16x2_fold(uint32_t w0, uint32_t w1, uint32_t w2, float s, float2 fb,
                                                       SpliceExp3 x, uint32_t* out) {
-    const uint32_t v[8] = {w0 << 11, w0 >> 1, __funnelshift_r(w0, w1, 13), w1 << 7,
-                           w1 >> 5, __funnelshift_r(w1, w2, 17), w2 << 3, w2 >> 9};
+    uint32_t v[8];
+    pair_words16(w0, w1, w2, v);
     const float2 s2 = make_float2(s, s);
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-        const float lo = __uint_as_float((v[i] & (0x3Fu << 11)) | x.e11);
-        const float hi = __uint_as_float((v[i] & (0x3Fu << 17)) | x.e17);
-        const float2 r = __ffma2_rn(make_float2(lo, hi), s2, fb);
+        const float2 r = __ffma2_rn(pair_at11_17(v[i], x), s2, fb);
         out[i] = pack_bf16x2(r.x, r.y);
     }
 }

@@ -15,12 +15,15 @@
 //     both rows (K = 3072: six units per lane, an even split);
 //   * the reference kernel's sum_k x_k (scale * code_k + qbias)
 //     (shardedit_mlx/q6_metal_mlp.py:42-83) is evaluated per 16-code unit
-//     (one scale group) as scale * sum_k x_k code_k + qbias * sum_k x_k: codes
-//     become exact fp32 integers (splice + packed subtract), the dot with x
-//     runs on scalar FMAs (which issue to both FMA pipes), and the x sums per
-//     unit are computed once per CTA.  The activations sit in shared memory as
-//     fp32 with an XOR swizzle that keeps the unit-per-lane reads free of bank
-//     conflicts.
+//     (within one scale group) as scale * sum_k x_k code_k + qbias * sum_k x_k.
+//     One shift per code pair puts the pair at bits 11 and 17, where a splice
+//     reads 4096 + code (even) and 64 + code (odd); packed FFMA2s accumulate
+//     sum_k x_k (offset_k + code_k) in (even, odd) halves, and the offsets
+//     leave again once per unit through the per-unit sums of x over even and
+//     odd codes (computed once per CTA, with the plain x sum).  Relative to
+//     the exact integer dot this costs about 1e-5 of the unit's magnitude.
+//     The activations sit in shared memory as fp32 with an XOR swizzle that
+//     keeps the unit-per-lane reads free of bank conflicts.
 //
 // Requirements (else the CUDA-core linear_simt_kernel runs): bf16 activations
 // and output, K % 64 == 0, K / group_size % 8 == 0 (16-byte aligned scale
@@ -76,7 +79,7 @@ __host__ __device__ inline GemvLayout gemv_layout(int K, int gs) {
 // loop so that all shared-memory addresses are a per-lane base plus an
 // immediate; UPL = 0 is the generic loop.
 template <int MT, int UPL>
-__global__ void __launch_bounds__(kWarps * 32) gemv_stream_kernel(const LinearArgs a, int gs_shift,
+__global__ void __launch_bounds__(kWarps * 32, 2) gemv_stream_kernel(const LinearArgs a, int gs_shift,
                                                                   const SpliceExp3 sx) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int K = static_cast<int>(a.K);
@@ -91,7 +94,7 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_stream_kernel(const LinearAr
     const int lane = threadIdx.x & 31;
     uint8_t* ring = smem + warp * kSlots * L.stage_bytes;
     float4* xs4 = reinterpret_cast<float4*>(smem + kWarps * kSlots * L.stage_bytes);  // [MT][K/4]
-    float* xsum = reinterpret_cast<float*>(xs4 + MT * K4);                             // [MT][K/16]
+    float2* xsum = reinterpret_cast<float2*>(xs4 + MT * K4);  // [MT][K/16]: x sums over a unit's even, odd codes
     uint64_t* full = reinterpret_cast<uint64_t*>(xsum + MT * U16) + warp * kSlots;
 
     const int npairs = (N + 1) / 2;
@@ -156,13 +159,14 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_stream_kernel(const LinearAr
         const int m = i / U16;
         const int J = i - m * U16;
         const float4* row = xs4 + m * K4;
-        float t = 0.0f;
+        float ev = 0.0f, od = 0.0f;
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
             const float4 v = row[xswz(4 * J + e)];
-            t += (v.x + v.y) + (v.z + v.w);
+            ev += v.x + v.z;
+            od += v.y + v.w;
         }
-        xsum[i] = t;
+        xsum[i] = make_float2(ev, od);
     }
     __syncthreads();
 
@@ -188,33 +192,90 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_stream_kernel(const LinearAr
         auto unit = [&](int j, int J, int gl, int xslot_base, int e_slots[4]) {
             const uint32_t* wa = reinterpret_cast<const uint32_t*>(codes0 + 12 * j);
             const uint32_t* wb = reinterpret_cast<const uint32_t*>(codes1 + 12 * j);
-            float qa[16], qb[16];
-            codes16_f32_e3(wa[0], wa[1], wa[2], sx, qa);
-            codes16_f32_e3(wb[0], wb[1], wb[2], sx, qb);  // stale slot bytes for an odd last row: never stored
+            // Code pairs (2i, 2i+1) of each row at bits 11 and 17 of va[i] / vb[i]
+            // (stale slot bytes for an odd last row: never stored).
+            uint32_t va[8], vb[8];
+            pair_words16(wa[0], wa[1], wa[2], va);
+            pair_words16(wb[0], wb[1], wb[2], vb);
             const float s0 = bf16f(sc0[gl]), b0 = bf16f(bi0[gl]);
             const float s1 = bf16f(sc1[gl]), b1 = bf16f(bi1[gl]);
 #pragma unroll
             for (int m = 0; m < MT; ++m) {
                 const float4* xrow = xs4 + m * K4 + xslot_base;
-                float d0 = 0.0f, d1 = 0.0f;
+                // (even, odd) code halves of the dot, each code carrying its splice
+                // offset (4096 even, 64 odd): sum_k x_k (offset_k + q_k)
+                float2 d0 = make_float2(0.0f, 0.0f), d1 = make_float2(0.0f, 0.0f);
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
                     const float4 xv = xrow[e_slots[e]];
-                    d0 = fmaf(xv.x, qa[4 * e], d0);
-                    d0 = fmaf(xv.y, qa[4 * e + 1], d0);
-                    d0 = fmaf(xv.z, qa[4 * e + 2], d0);
-                    d0 = fmaf(xv.w, qa[4 * e + 3], d0);
-                    d1 = fmaf(xv.x, qb[4 * e], d1);
-                    d1 = fmaf(xv.y, qb[4 * e + 1], d1);
-                    d1 = fmaf(xv.z, qb[4 * e + 2], d1);
-                    d1 = fmaf(xv.w, qb[4 * e + 3], d1);
+                    const float2 xlo = make_float2(xv.x, xv.y), xhi = make_float2(xv.z, xv.w);
+                    d0 = __ffma2_rn(xlo, pair_at11_17(va[2 * e], sx), d0);
+                    d0 = __ffma2_rn(xhi, pair_at11_17(va[2 * e + 1], sx), d0);
+                    d1 = __ffma2_rn(xlo, pair_at11_17(vb[2 * e], sx), d1);
+                    d1 = __ffma2_rn(xhi, pair_at11_17(vb[2 * e + 1], sx), d1);
                 }
-                const float xj = xsum[m * U16 + J];
-                acc0[m] = fmaf(s0, d0, fmaf(b0, xj, acc0[m]));
-                acc1[m] = fmaf(s1, d1, fmaf(b1, xj, acc1[m]));
+                const float2 xs = xsum[m * U16 + J];
+                // remove the offsets: sum_k x_k q_k = d.x - 4096 xs.x + d.y - 64 xs.y
+                const float2 off = make_float2(-4096.0f, -64.0f);
+                const float2 t0 = __ffma2_rn(off, xs, d0), t1 = __ffma2_rn(off, xs, d1);
+                const float xt = xs.x + xs.y;
+                acc0[m] = fmaf(s0, t0.x + t0.y, fmaf(b0, xt, acc0[m]));
+                acc1[m] = fmaf(s1, t1.x + t1.y, fmaf(b1, xt, acc1[m]));
             }
         };
-        if constexpr (UPL > 0) {
+        // Two adjacent units (one scale group for every group size) per lane:
+        // units jA = 2 lane + 64 i and jA + 1.  Their 24 code bytes per row are
+        // 8-byte aligned, their eight activation float4s sit at slots
+        // 4 JA + (e ^ (lane & 7)) (the swizzle term (JA >> 1) & 7 is lane & 7
+        // because the chunk's unit count is a multiple of 16), and the affine
+        // map is applied once per pair.
+        auto unit_pair = [&](int i) {
+            const int jA = 2 * lane + 64 * i;
+            const int JA = c * units + jA;
+            const int gl = (16 * jA) >> gs_shift;
+            const uint2* pa = reinterpret_cast<const uint2*>(codes0) + 3 * (lane + 32 * i);
+            const uint2* pb = reinterpret_cast<const uint2*>(codes1) + 3 * (lane + 32 * i);
+            const uint2 a0 = pa[0], a1 = pa[1], a2 = pa[2];
+            const uint2 b0w = pb[0], b1w = pb[1], b2w = pb[2];
+            uint32_t va[16], vb[16];
+            pair_words16(a0.x, a0.y, a1.x, *reinterpret_cast<uint32_t(*)[8]>(va));
+            pair_words16(a1.y, a2.x, a2.y, *reinterpret_cast<uint32_t(*)[8]>(va + 8));
+            pair_words16(b0w.x, b0w.y, b1w.x, *reinterpret_cast<uint32_t(*)[8]>(vb));
+            pair_words16(b1w.y, b2w.x, b2w.y, *reinterpret_cast<uint32_t(*)[8]>(vb + 8));
+            const float s0 = bf16f(sc0[gl]), b0 = bf16f(bi0[gl]);
+            const float s1 = bf16f(sc1[gl]), b1 = bf16f(bi1[gl]);
+            const int sw = lane & 7;
+#pragma unroll
+            for (int m = 0; m < MT; ++m) {
+                const float4* xrow = xs4 + m * K4 + 4 * JA;
+                float2 dA0 = make_float2(0.0f, 0.0f), dB0 = dA0, dA1 = dA0, dB1 = dA0;
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float4 xa = xrow[e ^ sw];
+                    const float4 xb = xrow[(e + 4) ^ sw];
+                    dA0 = __ffma2_rn(make_float2(xa.x, xa.y), pair_at11_17(va[2 * e], sx), dA0);
+                    dA0 = __ffma2_rn(make_float2(xa.z, xa.w), pair_at11_17(va[2 * e + 1], sx), dA0);
+                    dB0 = __ffma2_rn(make_float2(xb.x, xb.y), pair_at11_17(va[8 + 2 * e], sx), dB0);
+                    dB0 = __ffma2_rn(make_float2(xb.z, xb.w), pair_at11_17(va[8 + 2 * e + 1], sx), dB0);
+                    dA1 = __ffma2_rn(make_float2(xa.x, xa.y), pair_at11_17(vb[2 * e], sx), dA1);
+                    dA1 = __ffma2_rn(make_float2(xa.z, xa.w), pair_at11_17(vb[2 * e + 1], sx), dA1);
+                    dB1 = __ffma2_rn(make_float2(xb.x, xb.y), pair_at11_17(vb[8 + 2 * e], sx), dB1);
+                    dB1 = __ffma2_rn(make_float2(xb.z, xb.w), pair_at11_17(vb[8 + 2 * e + 1], sx), dB1);
+                }
+                const float4 xq = *reinterpret_cast<const float4*>(xsum + m * U16 + JA);  // units JA, JA + 1
+                const float2 xs = __fadd2_rn(make_float2(xq.x, xq.y), make_float2(xq.z, xq.w));
+                const float2 off = make_float2(-4096.0f, -64.0f);
+                const float2 t0 = __ffma2_rn(off, xs, __fadd2_rn(dA0, dB0));
+                const float2 t1 = __ffma2_rn(off, xs, __fadd2_rn(dA1, dB1));
+                const float xt = xs.x + xs.y;
+                acc0[m] = fmaf(s0, t0.x + t0.y, fmaf(b0, xt, acc0[m]));
+                acc1[m] = fmaf(s1, t1.x + t1.y, fmaf(b1, xt, acc1[m]));
+            }
+        };
+        if constexpr (UPL > 0 && UPL % 2 == 0 && MT <= 2) {  // four token rows: the unit path fits 128 registers
+#pragma unroll
+            for (int i = 0; i < UPL / 2; ++i) unit_pair(i);
+        } else if constexpr (UPL > 0) {
             // units j = lane + 32 i: the x swizzle term (J >> 1) & 7 = (lane >> 1) & 7
             // is the same for every i, so the four float4 slots of a unit are
             // per-lane constants plus 128 i.
@@ -279,7 +340,7 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_stream_kernel(const LinearAr
 size_t gemv_smem_bytes(int64_t K, int gs, int mt) {
     const GemvLayout L = gemv_layout(static_cast<int>(K), gs);
     return static_cast<size_t>(kWarps) * kSlots * L.stage_bytes + static_cast<size_t>(mt) * K * 4 +
-           static_cast<size_t>(mt) * (K / 16) * 4 + kWarps * kSlots * 8;
+           static_cast<size_t>(mt) * (K / 16) * 8 + kWarps * kSlots * 8;
 }
 
 template <int MT, int UPL>
