@@ -154,6 +154,28 @@ Q6_API int q6_mlp_bf16_noalloc(const uint16_t* x, const uint32_t* w1, const uint
                                const uint16_t* residual, const uint16_t* gate, uint16_t* y, int64_t M,
                                int64_t D, int64_t H, int group_size, q6_stream_t stream);
 
+/*
+ * MMDiT block steps around the q6 linears (the block's adaLN modulation and
+ * attention pre-processing, benchmarks/profile_qwen_block.py:172-217).
+ *
+ * q6_layernorm_modulate_bf16: y[m, :] = LayerNorm(x[m, :]) * (1 + scale) + shift,
+ *   LayerNorm without affine parameters (mean and variance over D, eps),
+ *   computed in fp32 and rounded to bf16 once; shift / scale bf16 [D] (one
+ *   sample's modulation vectors).  Replaces `_modulate(img_norm1(x), mod1)`.
+ *   D in {256, 512, 768, 1024, 1536, 2048, 3072, 4096}, 16-byte aligned pointers.
+ * q6_qk_rmsnorm_rope_bf16: in place on M rows of `heads` heads of head_dim
+ *   (128) values, row stride `row_stride` elements: per head
+ *   x <- rope(x * rsqrt(mean(x^2) + eps) * weight), weight bf16 [128]; the
+ *   rotation turns interleaved pairs (x[2i], x[2i+1]) by the angle whose
+ *   cosine / sine are cos[m, i] / sin[m, i] (fp32 [M, 64]).  Replaces
+ *   norm_q / norm_k followed by `_apply_rope_qwen`.
+ */
+Q6_API int q6_layernorm_modulate_bf16(const uint16_t* x, const uint16_t* shift, const uint16_t* scale, uint16_t* y,
+                                      int64_t M, int64_t D, float eps, q6_stream_t stream);
+Q6_API int q6_qk_rmsnorm_rope_bf16(uint16_t* qk, int64_t row_stride, int64_t M, int heads, int head_dim,
+                                   const uint16_t* weight, const float* cos, const float* sin, float eps,
+                                   q6_stream_t stream);
+
 /* Device error word (0 = none).  Reading it synchronises the current device. */
 Q6_API int q6_get_device_error(int* code);
 Q6_API int q6_clear_device_error(void);

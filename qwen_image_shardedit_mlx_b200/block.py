@@ -1,0 +1,250 @@
+"""One Qwen-Image MMDiT dual-stream block on the q6 kernels.
+
+The block the reference profiles stage by stage
+(benchmarks/profile_qwen_block.py:163-301; mflux ``QwenTransformerBlock``):
+
+=====================================  =========================================================
+reference stage                         here
+=====================================  =========================================================
+img/txt_mod_linear(silu(temb))         ``q6_linear`` on the few-row streaming GEMV
+_modulate(norm1(x), mod1)              ``q6_layernorm_modulate_bf16`` (one fused kernel)
+to_q/k/v, add_q/k/v_proj               ``q6_linear`` writing straight into the joint
+                                        [text; image] q / k / v buffers
+norm_q/k, norm_added_q/k + rope        ``q6_qk_rmsnorm_rope_bf16`` in place on those buffers
+joint attention (_compute_attention)   torch scaled_dot_product_attention (library kernel)
+attn_to_out[0] / to_add_out + gate1    ``q6_linear`` with the residual and gate in its epilogue
+_modulate(norm2(x), mod2)              ``q6_layernorm_modulate_bf16``
+img_ff / txt_ff + gate2 residual       ``q6_mlp`` with the residual and gate in fc2's epilogue
+=====================================  =========================================================
+
+Tensor names follow the reference's checkpoint layout (``img_mod_linear``,
+``attn.to_q``, ``attn.attn_to_out.0``, ``img_ff.mlp_in``, ``attn.norm_q``
+...), so ``from_block_weights`` builds a block from a loaded checkpoint block.
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.nn.functional as F
+
+from qwen_image_shardedit_mlx_b200 import _lib, ops
+from qwen_image_shardedit_mlx_b200.q6_metal_mlp import QuantizedLinear, QwenFeedForward
+from qwen_image_shardedit_mlx_b200.quantize import quantize_affine_q6
+
+HEAD_DIM = 128
+LINEAR_SHAPES = {
+    # name: (out_features, in_features) as multiples of the hidden size D (FF hidden = 4 D)
+    "img_mod_linear": (6, 1), "txt_mod_linear": (6, 1),
+    "attn.to_q": (1, 1), "attn.to_k": (1, 1), "attn.to_v": (1, 1),
+    "attn.add_q_proj": (1, 1), "attn.add_k_proj": (1, 1), "attn.add_v_proj": (1, 1),
+    "attn.attn_to_out.0": (1, 1), "attn.to_add_out": (1, 1),
+    "img_ff.mlp_in": (4, 1), "img_ff.mlp_out": (1, 4),
+    "txt_ff.mlp_in": (4, 1), "txt_ff.mlp_out": (1, 4),
+}
+NORM_NAMES = ("attn.norm_q", "attn.norm_k", "attn.norm_added_q", "attn.norm_added_k")
+
+
+def layernorm_modulate(x: torch.Tensor, shift: torch.Tensor, scale: torch.Tensor, *, eps: float = 1e-6,
+                       out: torch.Tensor | None = None) -> torch.Tensor:
+    """``LayerNorm(x) * (1 + scale) + shift`` over the last axis (bf16 in and out)."""
+
+    d = x.shape[-1]
+    xb = x.reshape(-1, d)
+    if xb.dtype != torch.bfloat16 or not xb.is_contiguous():
+        xb = xb.to(torch.bfloat16).contiguous()
+    sh = shift.reshape(d).to(torch.bfloat16).contiguous()
+    sc = scale.reshape(d).to(torch.bfloat16).contiguous()
+    y = out if out is not None else torch.empty_like(xb)
+    st = _lib.lib().q6_layernorm_modulate_bf16(xb.data_ptr(), sh.data_ptr(), sc.data_ptr(), y.data_ptr(),
+                                               xb.shape[0], d, float(eps), ops._stream(xb.device))
+    _lib.check(st, "q6_layernorm_modulate_bf16")
+    return y.reshape(x.shape)
+
+
+def qk_rmsnorm_rope_(qk: torch.Tensor, weight: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, *,
+                     eps: float = 1e-6) -> torch.Tensor:
+    """In place on rows [M, H * 128] (row stride may exceed H * 128): per head
+    RMSNorm with ``weight`` then the interleaved-pair rotation by cos / sin [M, 64]."""
+
+    if qk.dtype != torch.bfloat16 or qk.dim() != 2 or qk.stride(1) != 1:
+        raise ValueError("qk must be a 2-D bf16 view with unit column stride")
+    m, width = qk.shape
+    if width % HEAD_DIM:
+        raise ValueError(f"row width {width} is not a multiple of {HEAD_DIM}")
+    c = cos.to(device=qk.device, dtype=torch.float32).contiguous()
+    s = sin.to(device=qk.device, dtype=torch.float32).contiguous()
+    if c.shape != (m, HEAD_DIM // 2) or s.shape != (m, HEAD_DIM // 2):
+        raise ValueError(f"cos/sin must be ({m}, {HEAD_DIM // 2})")
+    w = weight.to(device=qk.device, dtype=torch.bfloat16).contiguous()
+    st = _lib.lib().q6_qk_rmsnorm_rope_bf16(qk.data_ptr(), qk.stride(0), m, width // HEAD_DIM, HEAD_DIM,
+                                            w.data_ptr(), c.data_ptr(), s.data_ptr(), float(eps),
+                                            ops._stream(qk.device))
+    _lib.check(st, "q6_qk_rmsnorm_rope_bf16")
+    return qk
+
+
+def qwen_rope_angles(img_shapes: list[tuple[int, int]], txt_len: int, *, theta: float = 10000.0,
+                     axes: tuple[int, int, int] = (16, 56, 56), device: torch.device | str = "cpu"):
+    """Rotary angles (radians, float64) [S_img, 64] and [S_txt, 64].
+
+    Three axes (frame, height, width) of 16 / 56 / 56 dimensions with base
+    ``theta``: image ``f`` of (h, w) patches takes frame position f and
+    centred grid positions; text positions continue after the largest image
+    position on all three axes (the published Qwen-Image rotary layout).
+    """
+
+    def freqs(dim: int) -> torch.Tensor:
+        return 1.0 / theta ** (torch.arange(0, dim, 2, dtype=torch.float64) / dim)
+
+    fr, fh, fw = (freqs(a) for a in axes)
+    rows, max_pos = [], 0
+    for f, (h, w) in enumerate(img_shapes):
+        hp = torch.arange(h, dtype=torch.float64) - h // 2
+        wp = torch.arange(w, dtype=torch.float64) - w // 2
+        hh, ww = torch.meshgrid(hp, wp, indexing="ij")
+        rows.append(torch.cat([(f * fr).expand(h * w, -1), hh.reshape(-1, 1) * fh, ww.reshape(-1, 1) * fw], dim=1))
+        max_pos = max(max_pos, h // 2, w // 2)
+    img = torch.cat(rows, dim=0)
+    tp = (max_pos + torch.arange(txt_len, dtype=torch.float64)).reshape(-1, 1)
+    txt = torch.cat([tp * fr, tp * fh, tp * fw], dim=1)
+    return img.to(device), txt.to(device)
+
+
+def rope_tables(img_angles: torch.Tensor, txt_angles: torch.Tensor, device: torch.device | str):
+    """(img_cos, img_sin, txt_cos, txt_sin) fp32 on ``device``."""
+
+    return tuple(t.to(device=device, dtype=torch.float32).contiguous()
+                 for t in (img_angles.cos(), img_angles.sin(), txt_angles.cos(), txt_angles.sin()))
+
+
+class QwenTransformerBlock(torch.nn.Module):
+    """Dual-stream MMDiT block: q6 linears by reference name, bf16 norm weights."""
+
+    def __init__(self, linears: dict[str, QuantizedLinear], norms: dict[str, torch.Tensor], *,
+                 heads: int, eps: float = 1e-6) -> None:
+        super().__init__()
+        missing = [n for n in LINEAR_SHAPES if n not in linears] + [n for n in NORM_NAMES if n not in norms]
+        if missing:
+            raise ValueError(f"block is missing {missing}")
+        self.linears = linears
+        self.norms = {k: v.to(torch.bfloat16).contiguous() for k, v in norms.items()}
+        self.heads = int(heads)
+        self.dim = linears["attn.to_q"].out_features
+        if self.dim != self.heads * HEAD_DIM:
+            raise ValueError(f"hidden size {self.dim} != heads {heads} x {HEAD_DIM}")
+        self.eps = float(eps)
+        self.img_ff = QwenFeedForward(linears["img_ff.mlp_in"], linears["img_ff.mlp_out"])
+        self.txt_ff = QwenFeedForward(linears["txt_ff.mlp_in"], linears["txt_ff.mlp_out"])
+        self._ws: torch.Tensor | None = None
+
+    @classmethod
+    def random(cls, dim: int = 3072, heads: int = 24, *, group_size: int = 64, std: float = 0.02,
+               bias_std: float = 0.01, generator: torch.Generator | None = None,
+               device: torch.device | str = "cuda") -> "QwenTransformerBlock":
+        linears = {}
+        for name, (fo, fi) in LINEAR_SHAPES.items():
+            w = torch.randn((fo * dim, fi * dim), generator=generator, device=device) * std
+            q, s, b = quantize_affine_q6(w, group_size)
+            bias = (torch.randn((fo * dim,), generator=generator, device=device) * bias_std).to(torch.bfloat16)
+            linears[name] = QuantizedLinear(q, s, b, bias, group_size=group_size)
+        norms = {n: (1.0 + 0.1 * torch.randn((HEAD_DIM,), generator=generator, device=device)).to(torch.bfloat16)
+                 for n in NORM_NAMES}
+        return cls(linears, norms, heads=heads)
+
+    @classmethod
+    def from_block_weights(cls, block, *, heads: int | None = None) -> "QwenTransformerBlock":
+        """From a loaded checkpoint block (``qwen_block_loader.QwenBlockWeights``)."""
+
+        norms = {n: block.tensors[f"{n}.weight"] for n in NORM_NAMES}
+        dim = block.linears["attn.to_q"].out_features
+        return cls(dict(block.linears), norms, heads=heads or dim // HEAD_DIM)
+
+    def _workspace(self, m: int, device: torch.device) -> torch.Tensor:
+        need = int(ops.mlp_workspace_bytes(m, 4 * self.dim))
+        if self._ws is None or self._ws.numel() < need or self._ws.device != device:
+            self._ws = torch.empty(need, dtype=torch.uint8, device=device)
+        return self._ws
+
+    def _mlp(self, ff: QwenFeedForward, x: torch.Tensor, residual: torch.Tensor, gate: torch.Tensor) -> torch.Tensor:
+        if ff.mlp_in.lora is not None or ff.mlp_out.lora is not None:
+            mid = ops.q6_linear(x, ff.mlp_in.weight, ff.mlp_in.scales, ff.mlp_in.biases, ff.mlp_in.bias,
+                                group_size=ff.mlp_in.group_size, apply_gelu=True, lora=ff.mlp_in.lora)
+            lo = ff.mlp_out
+            return ops.q6_linear(mid, lo.weight, lo.scales, lo.biases, lo.bias, group_size=lo.group_size,
+                                 residual=residual, gate=gate, lora=lo.lora)
+        w1 = (ff.mlp_in.weight, ff.mlp_in.scales, ff.mlp_in.biases, ff.mlp_in.bias)
+        w2 = (ff.mlp_out.weight, ff.mlp_out.scales, ff.mlp_out.biases, ff.mlp_out.bias)
+        return ops.q6_mlp(x, w1, w2, group_size=ff.mlp_in.group_size, residual=residual, gate=gate,
+                          workspace=self._workspace(x.shape[0], x.device))
+
+    def _linear(self, name: str, x: torch.Tensor, **kw) -> torch.Tensor:
+        lin = self.linears[name]
+        return ops.q6_linear(x, lin.weight, lin.scales, lin.biases, lin.bias, group_size=lin.group_size,
+                             lora=lin.lora, **kw)
+
+    def forward_sample(self, hidden: torch.Tensor, encoder: torch.Tensor, mod_img: torch.Tensor,
+                       mod_txt: torch.Tensor, rope: tuple[torch.Tensor, ...]) -> tuple[torch.Tensor, torch.Tensor]:
+        """One sample: hidden [S_img, D], encoder [S_txt, D], modulation
+        vectors [6, D] per stream; returns (text out, image out)."""
+
+        img_cos, img_sin, txt_cos, txt_sin = rope
+        s_img, s_txt, d = hidden.shape[0], encoder.shape[0], self.dim
+        ish1, isc1, ig1, ish2, isc2, ig2 = mod_img
+        tsh1, tsc1, tg1, tsh2, tsc2, tg2 = mod_txt
+        img_in = layernorm_modulate(hidden, ish1, isc1, eps=self.eps)
+        txt_in = layernorm_modulate(encoder, tsh1, tsc1, eps=self.eps)
+        # joint [text; image] projections, written in place
+        s = s_txt + s_img
+        q = torch.empty((s, d), dtype=torch.bfloat16, device=hidden.device)
+        k = torch.empty_like(q)
+        v = torch.empty_like(q)
+        for buf, img_name, txt_name in ((q, "attn.to_q", "attn.add_q_proj"), (k, "attn.to_k", "attn.add_k_proj"),
+                                        (v, "attn.to_v", "attn.add_v_proj")):
+            self._linear(txt_name, txt_in, out=buf[:s_txt])
+            self._linear(img_name, img_in, out=buf[s_txt:])
+        qk_rmsnorm_rope_(q[:s_txt], self.norms["attn.norm_added_q"], txt_cos, txt_sin, eps=self.eps)
+        qk_rmsnorm_rope_(q[s_txt:], self.norms["attn.norm_q"], img_cos, img_sin, eps=self.eps)
+        qk_rmsnorm_rope_(k[:s_txt], self.norms["attn.norm_added_k"], txt_cos, txt_sin, eps=self.eps)
+        qk_rmsnorm_rope_(k[s_txt:], self.norms["attn.norm_k"], img_cos, img_sin, eps=self.eps)
+        h = self.heads
+        att = F.scaled_dot_product_attention(
+            q.view(1, s, h, HEAD_DIM).transpose(1, 2), k.view(1, s, h, HEAD_DIM).transpose(1, 2),
+            v.view(1, s, h, HEAD_DIM).transpose(1, 2), scale=1.0 / math.sqrt(HEAD_DIM))
+        joint = att.transpose(1, 2).reshape(s, d)
+        img_h = self._linear("attn.attn_to_out.0", joint[s_txt:], residual=hidden, gate=ig1)
+        txt_h = self._linear("attn.to_add_out", joint[:s_txt], residual=encoder, gate=tg1)
+        img_ff_in = layernorm_modulate(img_h, ish2, isc2, eps=self.eps)
+        txt_ff_in = layernorm_modulate(txt_h, tsh2, tsc2, eps=self.eps)
+        img_out = self._mlp(self.img_ff, img_ff_in, img_h, ig2)
+        txt_out = self._mlp(self.txt_ff, txt_ff_in, txt_h, tg2)
+        return txt_out, img_out
+
+    def modulation(self, temb: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        """(img, txt) modulation vectors [B, 6, D] from the timestep embedding [B, D]."""
+
+        t = F.silu(temb.to(torch.bfloat16))
+        b = t.shape[0]
+        return (self._linear("img_mod_linear", t).reshape(b, 6, self.dim),
+                self._linear("txt_mod_linear", t).reshape(b, 6, self.dim))
+
+    def forward(self, hidden: torch.Tensor, encoder: torch.Tensor, temb: torch.Tensor,
+                rope: tuple[torch.Tensor, ...]) -> tuple[torch.Tensor, torch.Tensor]:
+        """hidden [B, S_img, D], encoder [B, S_txt, D], temb [B, D] (bf16);
+        ``rope`` = (img_cos, img_sin, txt_cos, txt_sin) fp32 [S, 64].
+        Returns (encoder_out, hidden_out) like the reference block."""
+
+        mod_img, mod_txt = self.modulation(temb)
+        outs = [self.forward_sample(hidden[b], encoder[b], mod_img[b], mod_txt[b], rope)
+                for b in range(hidden.shape[0])]
+        return torch.stack([o[0] for o in outs]), torch.stack([o[1] for o in outs])
+
+
+def block_flops(s_img: int, s_txt: int, dim: int) -> int:
+    """FLOPs of one block forward (one sample): per token 8 D^2 for q, k, v
+    and the output projection and 16 D^2 for the 4x feed-forward, 4 S^2 D for
+    the joint attention (q k^T and p v), 24 D^2 for the two modulation linears."""
+
+    s = s_img + s_txt
+    return 24 * s * dim * dim + 4 * s * s * dim + 24 * dim * dim

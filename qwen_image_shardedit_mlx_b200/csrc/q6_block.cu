@@ -1,0 +1,182 @@
+// The MMDiT block's memory-bound steps around the q6 linears:
+//
+//   * q6_layernorm_modulate_bf16: y = LayerNorm(x) * (1 + scale) + shift, the
+//     adaLN `_modulate(norm(x), mod)` of the Qwen-Image block
+//     (benchmarks/profile_qwen_block.py:172-181 and :262-263: LayerNorm
+//     without affine parameters, eps 1e-6, then shift / scale from the
+//     modulation linear).  One warp per row, the row held in registers, mean
+//     and variance in fp32 (two passes over the registers), one bf16 rounding
+//     at the output.
+//   * q6_qk_rmsnorm_rope_bf16: per head of 128, x <- rope(rmsnorm(x) * w), in
+//     place (profile_qwen_block.py:203-217: norm_q / norm_k, then
+//     _apply_rope_qwen).  The rotation acts on interleaved pairs
+//     (x[2i], x[2i+1]) with the per-token angle tables cos / sin [M, 64] (the
+//     complex form of the Qwen-Image rotary embedding).  One warp per (token,
+//     head): four values per lane, a warp reduction for the mean square.
+//
+// Both read and write each element once: HBM-bound, ~12 bytes per element
+// for the modulate (x in, y out, shift/scale from L1) and 4 for the in-place
+// rope (+ 2 floats of table per pair, shared by the heads of a token).
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include "q6_internal.h"
+#include "q6_ptx.cuh"
+
+namespace q6 {
+namespace {
+
+__device__ __forceinline__ float lo_f(uint32_t v) { return __uint_as_float(v << 16); }
+__device__ __forceinline__ float hi_f(uint32_t v) { return __uint_as_float(v & 0xFFFF0000u); }
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+constexpr int kLnWarps = 4;  // rows per CTA
+
+// NV uint4 (8 bf16) per lane: D = 256 NV.
+template <int NV>
+__global__ void __launch_bounds__(kLnWarps * 32) layernorm_modulate_kernel(const uint4* __restrict__ x,
+                                                                           const uint4* __restrict__ shift,
+                                                                           const uint4* __restrict__ scale,
+                                                                           uint4* __restrict__ y, int64_t M,
+                                                                           float eps) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const int lane = threadIdx.x & 31;
+    const int64_t row = static_cast<int64_t>(blockIdx.x) * kLnWarps + (threadIdx.x >> 5);
+    if (row >= M) return;
+    constexpr int D = 256 * NV;
+    const uint4* xr = x + row * (D / 8);
+    uint4 v[NV];
+#pragma unroll
+    for (int j = 0; j < NV; ++j) v[j] = xr[lane + 32 * j];
+    float s = 0.0f;
+#pragma unroll
+    for (int j = 0; j < NV; ++j)
+        s += (lo_f(v[j].x) + hi_f(v[j].x)) + (lo_f(v[j].y) + hi_f(v[j].y)) + (lo_f(v[j].z) + hi_f(v[j].z)) +
+             (lo_f(v[j].w) + hi_f(v[j].w));
+    const float mean = warp_sum(s) * (1.0f / D);
+    float q = 0.0f;
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+        const uint32_t w[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float a = lo_f(w[i]) - mean, b = hi_f(w[i]) - mean;
+            q = fmaf(a, a, fmaf(b, b, q));
+        }
+    }
+    const float rstd = rsqrtf(warp_sum(q) * (1.0f / D) + eps);
+    uint4* yr = y + row * (D / 8);
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+        const uint4 sh = __ldg(shift + lane + 32 * j), sc = __ldg(scale + lane + 32 * j);
+        const uint32_t w[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+        const uint32_t shw[4] = {sh.x, sh.y, sh.z, sh.w}, scw[4] = {sc.x, sc.y, sc.z, sc.w};
+        uint32_t o[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float a = (lo_f(w[i]) - mean) * rstd, b = (hi_f(w[i]) - mean) * rstd;
+            o[i] = pack2(fmaf(a, 1.0f + lo_f(scw[i]), lo_f(shw[i])), fmaf(b, 1.0f + hi_f(scw[i]), hi_f(shw[i])));
+        }
+        yr[lane + 32 * j] = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+}
+
+template <int NV>
+int launch_ln(const void* x, const void* shift, const void* scale, void* y, int64_t M, float eps,
+              cudaStream_t stream) {
+    const int64_t blocks = (M + kLnWarps - 1) / kLnWarps;
+    const cudaError_t e =
+        launch_pdl(layernorm_modulate_kernel<NV>, dim3(static_cast<unsigned>(blocks)), dim3(kLnWarps * 32), 0, stream,
+                   static_cast<const uint4*>(x), static_cast<const uint4*>(shift), static_cast<const uint4*>(scale),
+                   static_cast<uint4*>(y), M, eps);
+    return e == cudaSuccess ? Q6_OK : Q6_ERR_CUDA;
+}
+
+constexpr int kRopeWarps = 8;
+
+// One warp per (row, head); head_dim 128: lane l holds elements 4l .. 4l+3,
+// i.e. rotary pairs 2l and 2l+1.
+__global__ void __launch_bounds__(kRopeWarps * 32) qk_rmsnorm_rope_kernel(uint2* __restrict__ qk, int64_t row_stride8,
+                                                                         int64_t M, int H,
+                                                                         const uint2* __restrict__ weight,
+                                                                         const float4* __restrict__ cs,
+                                                                         const float4* __restrict__ sn, float eps) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const int lane = threadIdx.x & 31;
+    const int64_t item = static_cast<int64_t>(blockIdx.x) * kRopeWarps + (threadIdx.x >> 5);
+    if (item >= M * H) return;
+    const int64_t row = item / H;
+    const int head = static_cast<int>(item - row * H);
+    uint2* p = qk + row * row_stride8 + head * 32 + lane;  // 128 bf16 = 32 uint2 per head
+    const uint2 v = *p;
+    const float x0 = lo_f(v.x), x1 = hi_f(v.x), x2 = lo_f(v.y), x3 = hi_f(v.y);
+    const float ms = warp_sum(fmaf(x0, x0, fmaf(x1, x1, fmaf(x2, x2, x3 * x3)))) * (1.0f / 128.0f);
+    const float r = rsqrtf(ms + eps);
+    const uint2 w = __ldg(weight + lane);
+    const float a0 = x0 * r * lo_f(w.x), a1 = x1 * r * hi_f(w.x);
+    const float a2 = x2 * r * lo_f(w.y), a3 = x3 * r * hi_f(w.y);
+    // pairs 2 lane and 2 lane + 1 of this row's 64 angles
+    const float2 c = reinterpret_cast<const float2*>(cs + row * 16)[lane];
+    const float2 s = reinterpret_cast<const float2*>(sn + row * 16)[lane];
+    const float o0 = a0 * c.x - a1 * s.x, o1 = a0 * s.x + a1 * c.x;
+    const float o2 = a2 * c.y - a3 * s.y, o3 = a2 * s.y + a3 * c.y;
+    *p = make_uint2(pack2(o0, o1), pack2(o2, o3));
+}
+
+}  // namespace
+}  // namespace q6
+
+extern "C" {
+
+Q6_API int q6_layernorm_modulate_bf16(const uint16_t* x, const uint16_t* shift, const uint16_t* scale, uint16_t* y,
+                                      int64_t M, int64_t D, float eps, q6_stream_t stream) {
+    if (!x || !shift || !scale || !y || M <= 0 || D <= 0 || !(eps >= 0.0f)) return Q6_ERR_INVALID_ARGUMENT;
+    if (D % 256 != 0) return Q6_ERR_SHAPE;
+    const uintptr_t al = reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(shift) |
+                         reinterpret_cast<uintptr_t>(scale) | reinterpret_cast<uintptr_t>(y);
+    if (al % 16 != 0) return Q6_ERR_ALIGNMENT;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    switch (D / 256) {
+        case 1: return q6::launch_ln<1>(x, shift, scale, y, M, eps, s);
+        case 2: return q6::launch_ln<2>(x, shift, scale, y, M, eps, s);
+        case 3: return q6::launch_ln<3>(x, shift, scale, y, M, eps, s);
+        case 4: return q6::launch_ln<4>(x, shift, scale, y, M, eps, s);
+        case 6: return q6::launch_ln<6>(x, shift, scale, y, M, eps, s);
+        case 8: return q6::launch_ln<8>(x, shift, scale, y, M, eps, s);
+        case 12: return q6::launch_ln<12>(x, shift, scale, y, M, eps, s);
+        case 16: return q6::launch_ln<16>(x, shift, scale, y, M, eps, s);
+        default: return Q6_ERR_UNSUPPORTED;
+    }
+}
+
+Q6_API int q6_qk_rmsnorm_rope_bf16(uint16_t* qk, int64_t row_stride, int64_t M, int heads, int head_dim,
+                                   const uint16_t* weight, const float* cos, const float* sin, float eps,
+                                   q6_stream_t stream) {
+    if (!qk || !weight || !cos || !sin || M <= 0 || heads <= 0 || !(eps >= 0.0f)) return Q6_ERR_INVALID_ARGUMENT;
+    if (head_dim != 128 || row_stride < static_cast<int64_t>(heads) * head_dim || row_stride % 4 != 0)
+        return Q6_ERR_SHAPE;
+    const uintptr_t al = reinterpret_cast<uintptr_t>(qk) | reinterpret_cast<uintptr_t>(weight);
+    if (al % 8 != 0 || (reinterpret_cast<uintptr_t>(cos) | reinterpret_cast<uintptr_t>(sin)) % 16 != 0)
+        return Q6_ERR_ALIGNMENT;
+    const int64_t items = M * heads;
+    const int64_t blocks = (items + q6::kRopeWarps - 1) / q6::kRopeWarps;
+    const cudaError_t e = q6::launch_pdl(q6::qk_rmsnorm_rope_kernel, dim3(static_cast<unsigned>(blocks)),
+                                         dim3(q6::kRopeWarps * 32), 0, reinterpret_cast<cudaStream_t>(stream),
+                                         reinterpret_cast<uint2*>(qk), row_stride / 4, M, heads,
+                                         reinterpret_cast<const uint2*>(weight), reinterpret_cast<const float4*>(cos),
+                                         reinterpret_cast<const float4*>(sin), eps);
+    return e == cudaSuccess ? Q6_OK : Q6_ERR_CUDA;
+}
+
+}  // extern "C"

@@ -1,0 +1,125 @@
+"""GPU parity of the MMDiT block pieces and of whole blocks against the block oracle.
+
+* ``q6_layernorm_modulate_bf16`` and ``q6_qk_rmsnorm_rope_bf16`` against the
+  oracle's float64 restatements, rounded to bf16 once;
+* whole blocks (every q6 linear, the fused epilogues, the attention) at
+  reduced widths against ``oracle.block.block_forward``, which rounds to bf16
+  where the GPU path stores bf16 (north-star matmul tolerance on the outputs);
+* the full Qwen-Image block shape (3072 wide, 24 heads, 3456 + 256 tokens)
+  runs and stays finite.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from helpers import assert_close, f32, from_bits, random_bf16, random_weights, weights_to_torch
+from oracle import block as ob
+from qwen_image_shardedit_mlx_b200 import _lib
+from qwen_image_shardedit_mlx_b200.block import (
+    QwenTransformerBlock,
+    layernorm_modulate,
+    qk_rmsnorm_rope_,
+    qwen_rope_angles,
+    rope_tables,
+)
+from qwen_image_shardedit_mlx_b200.q6_metal_mlp import QuantizedLinear
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("m,d", [(1, 256), (37, 768), (130, 3072), (3456, 3072)])
+def test_layernorm_modulate_vs_oracle(m, d):
+    rng = np.random.default_rng(m + d)
+    x = random_bf16(rng, (m, d), 2.0)
+    shift = random_bf16(rng, (d,), 0.5)
+    scale = random_bf16(rng, (d,), 0.5)
+    got = layernorm_modulate(from_bits(x), from_bits(shift), from_bits(scale))
+    torch.cuda.synchronize()
+    ref = ob.layernorm_modulate(oracle.bf16_bits_to_f32(x), oracle.bf16_bits_to_f32(shift),
+                                oracle.bf16_bits_to_f32(scale))
+    refb = oracle.round_bf16(ref)
+    g = f32(got)
+    # one fp32 pass vs float64: equal after the bf16 rounding but for rare one-unit flips
+    assert np.mean(g == refb) > 0.99
+    assert np.all(np.abs(g - refb) <= 2.0 ** -7 * np.abs(refb) + 1e-6)
+
+
+def test_layernorm_modulate_rejects_bad_arguments():
+    x = torch.zeros((4, 320), dtype=torch.bfloat16, device="cuda")
+    v = torch.zeros(320, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(_lib.Q6Error):  # D not a multiple of 256
+        layernorm_modulate(x, v, v)
+    x = torch.zeros((4, 1280), dtype=torch.bfloat16, device="cuda")
+    v = torch.zeros(1280, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(_lib.Q6Error):  # 5 x 256: no instantiation
+        layernorm_modulate(x, v, v)
+
+
+@pytest.mark.parametrize("m,heads,extra", [(1, 2, 0), (45, 6, 64), (3456, 24, 0), (256, 24, 256)])
+def test_qk_rmsnorm_rope_vs_oracle(m, heads, extra):
+    rng = np.random.default_rng(m * heads + extra)
+    width = heads * 128
+    buf = from_bits(random_bf16(rng, (m, width + extra), 1.5))
+    before = buf.clone()
+    w = oracle.f32_to_bf16_bits((1.0 + 0.1 * rng.standard_normal(128)).astype(np.float32))
+    ang = rng.uniform(-20, 20, (m, 64))
+    cos, sin = torch.tensor(np.cos(ang), dtype=torch.float32), torch.tensor(np.sin(ang), dtype=torch.float32)
+    qk_rmsnorm_rope_(buf[:, :width], from_bits(w), cos, sin)
+    torch.cuda.synchronize()
+    ref = oracle.round_bf16(ob.qk_rmsnorm_rope(f32(before[:, :width]), oracle.bf16_bits_to_f32(w),
+                                               np.float32(np.cos(ang)), np.float32(np.sin(ang))))
+    g = f32(buf[:, :width])
+    assert np.all(np.abs(g - ref) <= 2.0 ** -7 * np.abs(ref) + 2e-3)
+    assert np.mean(np.abs(g - ref) <= 2.0 ** -8 * np.abs(ref) + 1e-6) > 0.98
+    if extra:  # columns past the heads are untouched
+        assert torch.equal(buf[:, width:], before[:, width:])
+
+
+def _block_pair(rng, dim: int, heads: int, gs: int = 64):
+    lin_o, lin_t = {}, {}
+    for name, (fo, fi) in ob.BLOCK_LINEARS.items():
+        w = random_weights(rng, fo * dim, fi * dim, gs)
+        lin_o[name] = w
+        wt, st, bt, bias = weights_to_torch(w)
+        lin_t[name] = QuantizedLinear(wt, st, bt, bias, group_size=gs)
+    norms_bits = {n: oracle.f32_to_bf16_bits((1.0 + 0.1 * rng.standard_normal(128)).astype(np.float32))
+                  for n in ob.NORMS}
+    ow = ob.BlockWeights(lin_o, {n: oracle.bf16_bits_to_f32(b) for n, b in norms_bits.items()}, heads)
+    tb = QwenTransformerBlock(lin_t, {n: from_bits(b) for n, b in norms_bits.items()}, heads=heads)
+    return ow, tb
+
+
+@pytest.mark.parametrize("dim,heads,img_hw,txt", [(256, 2, (8, 12), 32), (768, 6, (10, 20), 40)])
+def test_block_vs_oracle(dim, heads, img_hw, txt):
+    rng = np.random.default_rng(dim + txt)
+    ow, tb = _block_pair(rng, dim, heads)
+    s_img = img_hw[0] * img_hw[1]
+    hidden = random_bf16(rng, (s_img, dim))
+    enc = random_bf16(rng, (txt, dim))
+    temb = random_bf16(rng, (dim,))
+    ia, ta = qwen_rope_angles([img_hw], txt)
+    rope = rope_tables(ia, ta, "cuda")
+    t_out, i_out = tb(from_bits(hidden)[None], from_bits(enc)[None], from_bits(temb)[None], rope)
+    torch.cuda.synchronize()
+    rf = [f32(r) for r in rope]
+    t_ref, i_ref = ob.block_forward(ow, oracle.bf16_bits_to_f32(hidden), oracle.bf16_bits_to_f32(enc),
+                                    oracle.bf16_bits_to_f32(temb), *rf)
+    assert_close(f32(i_out[0]), i_ref, what=f"block image stream d{dim}")
+    assert_close(f32(t_out[0]), t_ref, what=f"block text stream d{dim}")
+
+
+def test_full_size_block_runs():
+    g = torch.Generator(device="cuda").manual_seed(5)
+    blk = QwenTransformerBlock.random(generator=g)
+    hidden = torch.randn((1, 3456, 3072), generator=g, device="cuda").to(torch.bfloat16)
+    enc = torch.randn((1, 256, 3072), generator=g, device="cuda").to(torch.bfloat16)
+    temb = torch.randn((1, 3072), generator=g, device="cuda").to(torch.bfloat16)
+    ia, ta = qwen_rope_angles([(36, 48), (36, 48)], 256)
+    t_out, i_out = blk(hidden, enc, temb, rope_tables(ia, ta, "cuda"))
+    torch.cuda.synchronize()
+    assert t_out.shape == (1, 256, 3072) and i_out.shape == (1, 3456, 3072)
+    assert bool(torch.isfinite(t_out).all()) and bool(torch.isfinite(i_out).all())
