@@ -14,6 +14,10 @@ rank runs its own 3456-token batch with replicated weights and no collective
 on the data path (weak scaling); the job value is all ranks' FLOPs over the
 slowest rank's device time.  Rank 0 prints one JSON line.
 
+Beside the headline, the line carries the skinny-M GEMV (``gemv``) and one
+full Qwen-Image MMDiT block (``block``: 3456 image + 256 text tokens, all 14
+linears q6, joint attention), tensor-parallel over the ranks when N > 1.
+
 --impl reference times the reference's own q6 kernel source
 (shardedit_mlx/q6_metal_mlp.py SOURCE_QMM_T, compiled for the host by
 oracle/build_ref.py) on the host cores, on a bounded token sample.
@@ -48,6 +52,7 @@ def parse_args() -> argparse.Namespace:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the host-core baseline leg")
     ap.add_argument("--no-gemv", action="store_true", help="skip the skinny-M GEMV side measurement")
+    ap.add_argument("--no-block", action="store_true", help="skip the full MMDiT block measurement")
     return ap.parse_args()
 
 
@@ -301,6 +306,9 @@ def run_ours(args, world: int, rank: int, local: int) -> dict | None:
     torch.cuda.synchronize()
     e2e_serial_ms = max_over_ranks(e0.elapsed_time(e1), world)
 
+    # ---- one full MMDiT block (3456 image + 256 text tokens), tensor-parallel over the ranks
+    block = None if args.no_block else measure_block(dev, world, rank)
+
     # ---- skinny-M GEMV side measurement (HBM-bound), rank 0 only
     gemv = None
     if rank == 0 and not args.no_gemv:
@@ -364,9 +372,73 @@ def run_ours(args, world: int, rank: int, local: int) -> dict | None:
     }
     if gemv is not None:
         line["gemv"] = gemv
+    if block is not None:
+        line["block"] = block
     if not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline_port()
     return line
+
+
+BLOCK_IMG, BLOCK_TXT, BLOCK_HEADS = 3456, 256, 24
+
+
+def measure_block(dev, world: int, rank: int, steps: int = 10) -> dict | None:
+    """Device time of one Qwen-Image MMDiT block forward (batch 1, all 14
+    linears q6 gs64, joint attention over 3712 tokens).  With N ranks the
+    block is tensor-parallel (heads and FF columns split, two NCCL
+    all-reduces per block); the time is the slowest rank's."""
+
+    import torch
+
+    from qwen_image_shardedit_mlx_b200 import ops
+    from qwen_image_shardedit_mlx_b200.block import (
+        QwenTransformerBlock,
+        TensorParallelQwenBlock,
+        block_flops,
+        qwen_rope_angles,
+        rope_tables,
+    )
+
+    g = torch.Generator(device=dev).manual_seed(2025)  # the same block on every rank
+    full = QwenTransformerBlock.random(DIM, BLOCK_HEADS, generator=g, device=dev)
+    blk = full if world == 1 else TensorParallelQwenBlock(full, world, rank)
+    hidden = torch.randn((1, BLOCK_IMG, DIM), generator=g, device=dev).to(torch.bfloat16)
+    enc = torch.randn((1, BLOCK_TXT, DIM), generator=g, device=dev).to(torch.bfloat16)
+    temb = torch.randn((1, DIM), generator=g, device=dev).to(torch.bfloat16)
+    ia, ta = qwen_rope_angles([(36, 48), (36, 48)], BLOCK_TXT)
+    rope = rope_tables(ia, ta, dev)
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(3):
+        blk(hidden, enc, temb, rope)
+    torch.cuda.synchronize()
+    barrier(world)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        out = blk(hidden, enc, temb, rope)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    ms = max_over_ranks(e0.elapsed_time(e1) / steps, world)
+    finite = bool(torch.isfinite(out[0]).all()) and bool(torch.isfinite(out[1]).all())
+    assert ops.device_error() == 0 and finite, "block benchmark produced a device error or non-finite output"
+    if rank != 0:
+        return None
+    flop = block_flops(BLOCK_IMG, BLOCK_TXT, DIM)
+    return {
+        "ms": round(ms, 4),
+        "TFLOP/s": round(flop / (ms * 1e-3) / 1e12, 1),
+        "n_gpus": world,
+        "parallelism": "single GPU" if world == 1 else f"tensor-parallel x{world} (heads and FF columns), "
+                                                        "2 NCCL all-reduces per block",
+        "flop_per_block": flop,
+        "shape": f"{BLOCK_IMG} image + {BLOCK_TXT} text tokens, hidden {DIM}, {BLOCK_HEADS} heads x 128, "
+                 "FF 4x, all 14 linears q6 gs64, batch 1",
+        "steps": steps,
+        "note": "device time per block forward (CUDA events, max over ranks); attention is the library "
+                "scaled_dot_product_attention kernel",
+    }
 
 
 def measure_gemv(dev, peaks) -> dict:

@@ -248,3 +248,123 @@ def block_flops(s_img: int, s_txt: int, dim: int) -> int:
 
     s = s_img + s_txt
     return 24 * s * dim * dim + 4 * s * s * dim + 24 * dim * dim
+
+
+class TensorParallelQwenBlock(torch.nn.Module):
+    """The block split over the ranks of a process group (one rank per GPU).
+
+    Heads and the feed-forward hidden columns are divided: q / k / v and
+    mlp_in are column-parallel (each rank holds its heads' / columns' rows of
+    codes, scales and biases), the output projections and mlp_out are
+    row-parallel (each rank holds the matching K slice).  The modulation
+    linears, the norms and the residual streams are replicated.  A
+    row-parallel partial carries the residual and the output bias on rank 0
+    only and the gate on every rank, so that the all-reduce sum of the
+    partials is ``residual + gate * (x W^T + bias)`` exactly as the
+    single-GPU epilogue computes it.  Two all-reduces per block, each over
+    the joint [text; image] rows.
+    """
+
+    def __init__(self, full: QwenTransformerBlock, world: int, rank: int, group=None) -> None:
+        super().__init__()
+        from qwen_image_shardedit_mlx_b200.sharding import split_k, split_rows
+
+        if full.heads % world:
+            raise ValueError(f"{full.heads} heads do not split over {world} ranks")
+        if any(lin.lora is not None for lin in full.linears.values()):
+            raise ValueError("fold LoRA adapters before sharding the block")
+        self.world, self.rank, self.group = int(world), int(rank), group
+        self.dim, self.heads_local, self.eps = full.dim, full.heads // world, full.eps
+        self.norms = full.norms
+
+        def rows(name: str) -> QuantizedLinear:
+            lin = full.linears[name]
+            return QuantizedLinear(*split_rows(lin.weight, lin.scales, lin.biases, lin.bias, world, rank),
+                                   group_size=lin.group_size)
+
+        def cols(name: str) -> QuantizedLinear:
+            lin = full.linears[name]
+            w, s, b = split_k(lin.weight, lin.scales, lin.biases, lin.group_size, world, rank)
+            return QuantizedLinear(w, s, b, lin.bias if rank == 0 else None, group_size=lin.group_size)
+
+        self.linears = {"img_mod_linear": full.linears["img_mod_linear"],
+                        "txt_mod_linear": full.linears["txt_mod_linear"]}
+        for name in ("attn.to_q", "attn.to_k", "attn.to_v", "attn.add_q_proj", "attn.add_k_proj",
+                     "attn.add_v_proj", "img_ff.mlp_in", "txt_ff.mlp_in"):
+            self.linears[name] = rows(name)
+        for name in ("attn.attn_to_out.0", "attn.to_add_out", "img_ff.mlp_out", "txt_ff.mlp_out"):
+            self.linears[name] = cols(name)
+        self._ws: torch.Tensor | None = None
+
+    def _linear(self, name: str, x: torch.Tensor, **kw) -> torch.Tensor:
+        lin = self.linears[name]
+        return ops.q6_linear(x, lin.weight, lin.scales, lin.biases, lin.bias, group_size=lin.group_size, **kw)
+
+    def _all_reduce(self, t: torch.Tensor) -> None:
+        import torch.distributed as dist
+
+        if self.world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.SUM, group=self.group)
+
+    def _mlp(self, prefix: str, x: torch.Tensor, residual: torch.Tensor | None, gate: torch.Tensor,
+             out: torch.Tensor) -> None:
+        l1, l2 = self.linears[f"{prefix}.mlp_in"], self.linears[f"{prefix}.mlp_out"]
+        need = int(ops.mlp_workspace_bytes(x.shape[0], l1.out_features))
+        if self._ws is None or self._ws.numel() < need or self._ws.device != x.device:
+            self._ws = torch.empty(need, dtype=torch.uint8, device=x.device)
+        ops.q6_mlp(x, (l1.weight, l1.scales, l1.biases, l1.bias), (l2.weight, l2.scales, l2.biases, l2.bias),
+                   group_size=l1.group_size, residual=residual, gate=gate, workspace=self._ws, out=out)
+
+    def modulation(self, temb: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        t = F.silu(temb.to(torch.bfloat16))
+        b = t.shape[0]
+        return (self._linear("img_mod_linear", t).reshape(b, 6, self.dim),
+                self._linear("txt_mod_linear", t).reshape(b, 6, self.dim))
+
+    def forward_sample(self, hidden: torch.Tensor, encoder: torch.Tensor, mod_img: torch.Tensor,
+                       mod_txt: torch.Tensor, rope: tuple[torch.Tensor, ...]) -> tuple[torch.Tensor, torch.Tensor]:
+        img_cos, img_sin, txt_cos, txt_sin = rope
+        s_img, s_txt = hidden.shape[0], encoder.shape[0]
+        s, dl, lead = s_txt + s_img, self.heads_local * HEAD_DIM, self.rank == 0
+        ish1, isc1, ig1, ish2, isc2, ig2 = mod_img
+        tsh1, tsc1, tg1, tsh2, tsc2, tg2 = mod_txt
+        img_in = layernorm_modulate(hidden, ish1, isc1, eps=self.eps)
+        txt_in = layernorm_modulate(encoder, tsh1, tsc1, eps=self.eps)
+        q = torch.empty((s, dl), dtype=torch.bfloat16, device=hidden.device)
+        k = torch.empty_like(q)
+        v = torch.empty_like(q)
+        for buf, img_name, txt_name in ((q, "attn.to_q", "attn.add_q_proj"), (k, "attn.to_k", "attn.add_k_proj"),
+                                        (v, "attn.to_v", "attn.add_v_proj")):
+            self._linear(txt_name, txt_in, out=buf[:s_txt])
+            self._linear(img_name, img_in, out=buf[s_txt:])
+        qk_rmsnorm_rope_(q[:s_txt], self.norms["attn.norm_added_q"], txt_cos, txt_sin, eps=self.eps)
+        qk_rmsnorm_rope_(q[s_txt:], self.norms["attn.norm_q"], img_cos, img_sin, eps=self.eps)
+        qk_rmsnorm_rope_(k[:s_txt], self.norms["attn.norm_added_k"], txt_cos, txt_sin, eps=self.eps)
+        qk_rmsnorm_rope_(k[s_txt:], self.norms["attn.norm_k"], img_cos, img_sin, eps=self.eps)
+        h = self.heads_local
+        att = F.scaled_dot_product_attention(
+            q.view(1, s, h, HEAD_DIM).transpose(1, 2), k.view(1, s, h, HEAD_DIM).transpose(1, 2),
+            v.view(1, s, h, HEAD_DIM).transpose(1, 2), scale=1.0 / math.sqrt(HEAD_DIM))
+        joint = att.transpose(1, 2).reshape(s, dl)
+        # row-parallel output projections into one joint [text; image] buffer, one all-reduce
+        streams = torch.empty((s, self.dim), dtype=torch.bfloat16, device=hidden.device)
+        self._linear("attn.attn_to_out.0", joint[s_txt:], residual=hidden if lead else None, gate=ig1,
+                     out=streams[s_txt:])
+        self._linear("attn.to_add_out", joint[:s_txt], residual=encoder if lead else None, gate=tg1,
+                     out=streams[:s_txt])
+        self._all_reduce(streams)
+        txt_h, img_h = streams[:s_txt], streams[s_txt:]
+        img_ff_in = layernorm_modulate(img_h, ish2, isc2, eps=self.eps)
+        txt_ff_in = layernorm_modulate(txt_h, tsh2, tsc2, eps=self.eps)
+        outs = torch.empty_like(streams)
+        self._mlp("img_ff", img_ff_in, img_h if lead else None, ig2, outs[s_txt:])
+        self._mlp("txt_ff", txt_ff_in, txt_h if lead else None, tg2, outs[:s_txt])
+        self._all_reduce(outs)
+        return outs[:s_txt], outs[s_txt:]
+
+    def forward(self, hidden: torch.Tensor, encoder: torch.Tensor, temb: torch.Tensor,
+                rope: tuple[torch.Tensor, ...]) -> tuple[torch.Tensor, torch.Tensor]:
+        mod_img, mod_txt = self.modulation(temb)
+        outs = [self.forward_sample(hidden[b], encoder[b], mod_img[b], mod_txt[b], rope)
+                for b in range(hidden.shape[0])]
+        return torch.stack([o[0] for o in outs]), torch.stack([o[1] for o in outs])

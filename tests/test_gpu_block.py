@@ -123,3 +123,43 @@ def test_full_size_block_runs():
     torch.cuda.synchronize()
     assert t_out.shape == (1, 256, 3072) and i_out.shape == (1, 3456, 3072)
     assert bool(torch.isfinite(t_out).all()) and bool(torch.isfinite(i_out).all())
+
+
+def test_tensor_parallel_block_world1_is_the_block():
+    """One rank holds every head and column: the sharded block must reproduce
+    the single-GPU block bit for bit (same kernels, residual and bias on rank 0)."""
+
+    from qwen_image_shardedit_mlx_b200.block import TensorParallelQwenBlock
+
+    rng = np.random.default_rng(77)
+    _, tb = _block_pair(rng, 512, 4)
+    tp = TensorParallelQwenBlock(tb, 1, 0)
+    hidden = from_bits(random_bf16(rng, (1, 96, 512)))
+    enc = from_bits(random_bf16(rng, (1, 24, 512)))
+    temb = from_bits(random_bf16(rng, (1, 512)))
+    ia, ta = qwen_rope_angles([(8, 12)], 24)
+    rope = rope_tables(ia, ta, "cuda")
+    a = tb(hidden, enc, temb, rope)
+    b = tp(hidden, enc, temb, rope)
+    torch.cuda.synchronize()
+    assert torch.equal(a[0], b[0]) and torch.equal(a[1], b[1])
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_tensor_parallel_block_over_nccl_world2():
+    import os
+    import socket
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    with socket.socket() as sck:
+        sck.bind(("127.0.0.1", 0))
+        port = sck.getsockname()[1]
+    script = Path(__file__).with_name("tp_block_check.py")
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
+           "--master-addr", "127.0.0.1", "--master-port", str(port), str(script)]
+    r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
+    assert r.stdout.count("OK") == 2

@@ -1,0 +1,47 @@
+"""Tensor-parallel MMDiT block over NCCL, one process per GPU (launched by
+tests/test_gpu_block.py through torch.distributed.run): heads and FF columns
+split, two all-reduces per block; checked against the single-GPU block."""
+
+import datetime
+import os
+import sys
+from pathlib import Path
+
+import torch
+import torch.distributed as dist
+
+sys.path.insert(0, str(Path(__file__).resolve().parents[1]))
+from qwen_image_shardedit_mlx_b200.block import (  # noqa: E402
+    QwenTransformerBlock,
+    TensorParallelQwenBlock,
+    qwen_rope_angles,
+    rope_tables,
+)
+
+rank = int(os.environ["RANK"]); world = int(os.environ["WORLD_SIZE"]); local = int(os.environ["LOCAL_RANK"])
+torch.cuda.set_device(local)
+dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", local))
+g = torch.Generator(device="cuda").manual_seed(11)
+dim, heads = 1024, 8
+full = QwenTransformerBlock.random(dim, heads, generator=g)
+hidden = torch.randn((1, 600, dim), generator=g, device="cuda").to(torch.bfloat16)
+enc = torch.randn((1, 64, dim), generator=g, device="cuda").to(torch.bfloat16)
+temb = torch.randn((1, dim), generator=g, device="cuda").to(torch.bfloat16)
+ia, ta = qwen_rope_angles([(20, 30)], 64)
+rope = rope_tables(ia, ta, "cuda")
+ref = full(hidden, enc, temb, rope)
+tp = TensorParallelQwenBlock(full, world, rank)
+out = tp(hidden, enc, temb, rope)
+torch.cuda.synchronize()
+ok = True
+for name, a, b in (("text", out[0], ref[0]), ("image", out[1], ref[1])):
+    err = (a.float() - b.float()).abs()
+    rel_max = float(err.max() / b.float().abs().max())
+    rel_mean = float(err.mean() / b.float().pow(2).mean().sqrt())
+    good = rel_max < 3e-2 and rel_mean < 3e-3
+    ok = ok and good
+    print(f"rank {rank}: tp{world} {name} stream vs single-GPU block max_rel {rel_max:.2e} mean_rel {rel_mean:.2e}",
+          flush=True)
+print(f"rank {rank}: {'OK' if ok else 'FAIL'}", flush=True)
+dist.destroy_process_group()
+sys.exit(0 if ok else 1)
