@@ -421,7 +421,8 @@ __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
         // Paired stores: lanes 2i and 2i+1 swap one value so that each writes a
         // 32-bit word holding two adjacent output columns (even lane: token j,
         // odd lane: token j+1).  Needs an even row length and 4-byte aligned y.
-        const bool paired = (p.N % 2 == 0) && ((reinterpret_cast<uintptr_t>(p.y) & 3) == 0);
+        const bool paired = (p.N % 2 == 0) && ((reinterpret_cast<uintptr_t>(p.y) & 3) == 0) &&
+                            ((reinterpret_cast<uintptr_t>(p.residual) & 3) == 0);
         const bool odd = (lane & 1) != 0;
         pdl_wait();  // y, the residual, the gate and the partials may be the previous kernel's
         int acc = 0;
@@ -434,6 +435,10 @@ __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
             const bool n_ok = n < p.N;
             const float bias_n = (n_ok && p.bias) ? bf16f(p.bias[n]) : 0.0f;
             const float gate_n = (n_ok && p.gate) ? bf16f(p.gate[n]) : 1.0f;
+            // the gate of the two columns of this lane's paired word (n & ~1, n | 1)
+            const int ne = n & ~1;
+            const float2 gate_w = (n_ok && p.gate) ? make_float2(bf16f(p.gate[ne]), bf16f(p.gate[ne + 1]))
+                                                   : make_float2(1.0f, 1.0f);
             if (!warp_wait(smem_u32(acc_full + acc), accph, abort_flag, 5)) break;
             tc_fence_after();
 #pragma unroll 1
@@ -467,6 +472,39 @@ __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
                         const uint32_t word = pack_bf16x2(odd ? recv : val.x, odd ? val.y : recv);
                         if (n_ok) *yp = word;
                         yp += step;
+                    }
+                    continue;
+                }
+                if (kEpi == kEpiGeneral && paired) {
+                    // Paired words as above; the gate and the residual act on the
+                    // word's two columns: one 32-bit residual load per store.  All
+                    // the chunk's residual words are loaded before its first store
+                    // (y may alias the residual, so loads after a store would wait
+                    // for it: one memory round trip per chunk instead of per word).
+                    uint32_t rw[kChunk / 2];
+#pragma unroll
+                    for (int j = 0; j < kChunk; j += 2) {
+                        const int row = m0 + j + (odd ? 1 : 0);
+                        rw[j / 2] = (p.residual && n_ok && row < p.M)
+                                        ? *reinterpret_cast<const uint32_t*>(p.residual + static_cast<size_t>(row) * p.N + ne)
+                                        : 0u;
+                    }
+#pragma unroll
+                    for (int j = 0; j < kChunk; j += 2) {
+                        float2 val = make_float2(__uint_as_float(v[j]) + bias_n, __uint_as_float(v[j + 1]) + bias_n);
+                        if (gelu) val = gelu_tanh2(val);
+                        const float send = odd ? val.x : val.y;
+                        const float recv = __shfl_xor_sync(0xffffffffu, send, 1);
+                        const int row = m0 + j + (odd ? 1 : 0);
+                        float2 w2 = odd ? make_float2(recv, val.y) : make_float2(val.x, recv);
+                        if (p.gate) w2 = __fmul2_rn(w2, gate_w);
+                        if (p.residual) {
+                            const uint32_t r = rw[j / 2];
+                            w2 = __fadd2_rn(w2, make_float2(__uint_as_float(r << 16), __uint_as_float(r & 0xFFFF0000u)));
+                        }
+                        if (n_ok && row < p.M)
+                            *reinterpret_cast<uint32_t*>(p.y + static_cast<size_t>(row) * p.N + ne) =
+                                pack_bf16x2(w2.x, w2.y);
                     }
                     continue;
                 }
