@@ -411,17 +411,38 @@ def measure_block(dev, world: int, rank: int, steps: int = 10) -> dict | None:
     for _ in range(3):
         blk(hidden, enc, temb, rope)
     torch.cuda.synchronize()
-    barrier(world)
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(steps):
-        out = blk(hidden, enc, temb, rope)
-    e1.record(stream)
+
+    def timed(run) -> float:
+        barrier(world)
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(steps):
+            run()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier(world)
+        return max_over_ranks(e0.elapsed_time(e1) / steps, world)
+
+    eager_ms = timed(lambda: blk(hidden, enc, temb, rope))
+    # the block's ~30 launches (and all-reduces) captured once and replayed: a
+    # serving loop pays no per-launch host cost
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(stream)
+    with torch.cuda.stream(side):
+        blk(hidden, enc, temb, rope)
+    stream.wait_stream(side)
     torch.cuda.synchronize()
-    barrier(world)
-    ms = max_over_ranks(e0.elapsed_time(e1) / steps, world)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        out = blk(hidden, enc, temb, rope)
+    graph.replay()
+    torch.cuda.synchronize()
+    ms = timed(graph.replay)
     finite = bool(torch.isfinite(out[0]).all()) and bool(torch.isfinite(out[1]).all())
+    del graph  # holds NCCL work on N > 1: released before the process group goes
+    torch.cuda.synchronize()
     assert ops.device_error() == 0 and finite, "block benchmark produced a device error or non-finite output"
     if rank != 0:
         return None
@@ -429,6 +450,7 @@ def measure_block(dev, world: int, rank: int, steps: int = 10) -> dict | None:
     return {
         "ms": round(ms, 4),
         "TFLOP/s": round(flop / (ms * 1e-3) / 1e12, 1),
+        "eager_ms": round(eager_ms, 4),
         "n_gpus": world,
         "parallelism": "single GPU" if world == 1 else f"tensor-parallel x{world} (heads and FF columns), "
                                                         "2 NCCL all-reduces per block",
@@ -436,7 +458,8 @@ def measure_block(dev, world: int, rank: int, steps: int = 10) -> dict | None:
         "shape": f"{BLOCK_IMG} image + {BLOCK_TXT} text tokens, hidden {DIM}, {BLOCK_HEADS} heads x 128, "
                  "FF 4x, all 14 linears q6 gs64, batch 1",
         "steps": steps,
-        "note": "device time per block forward (CUDA events, max over ranks); attention is the library "
+        "note": "device time per block forward replayed from a CUDA graph (eager_ms: launched from Python "
+                "each time); CUDA events, max over ranks; attention is the library "
                 "scaled_dot_product_attention kernel",
     }
 

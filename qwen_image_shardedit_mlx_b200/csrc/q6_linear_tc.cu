@@ -148,7 +148,8 @@ struct TcParams {
     SpliceExp3 sexp;  // splice exponent words, runtime values so each splice is one instruction
     // Split-K: work item it covers tile it / ksplit and the q6 stages
     // [s * ks_per, min((s + 1) * ks_per, k_stages)) of split s = it % ksplit
-    // (ks_per a multiple of 8, so scale chunks never straddle splits).  With
+    // (ks_per a multiple of the stages per staged scale chunk, so chunks never
+    // straddle splits).  With
     // ksplit > 1 the epilogue stores fp32 partials [ksplit][M][N] and a second
     // kernel sums them in split order and applies the epilogue.
     int ksplit, ks_per, num_items;
@@ -771,20 +772,21 @@ bool sb_tma_ok(const LinearArgs& a) {
            reinterpret_cast<uintptr_t>(a.qbiases) % 16 == 0;
 }
 
-// Split-K plan: how many K splits (stages per split a multiple of 8) the
-// tensor-core path uses at token tile NT.  One when the tiles already fill
-// half the GPU; otherwise the count that minimises waves x (stages per split
-// + a fixed per-item cost of about 8 stages), plus the reduce pass.
-// Q6_TC_KSPLIT (1..16) overrides the choice for tuning.
+// Split-K plan: how many K splits the tensor-core path uses at token tile
+// NT, with stages per split a multiple of `align` (the stages one staged scale
+// chunk covers: 2, 4 or 8 for group sizes 32, 64, 128; 1 without staging).
+// One split when the tiles already fill half the GPU; otherwise the count that
+// minimises waves x (stages per split + a fixed per-item cost of about 8
+// stages), plus the reduce pass.  Q6_TC_KSPLIT (1..16) overrides the choice.
 struct KSplit {
     int splits, stages_per_split;
 };
 
-KSplit plan_ksplit(int64_t M, int64_t N, int64_t K, int NT) {
+KSplit plan_ksplit(int64_t M, int64_t N, int64_t K, int NT, int align) {
     const int64_t sms = device_sm_count();
     const int64_t tiles = ((M + NT - 1) / NT) * ((N + kRows - 1) / kRows);
     const int64_t k_stages = (K + kBK - 1) / kBK;
-    auto per_split = [&](int64_t s) { return ((k_stages + s - 1) / s + 7) / 8 * 8; };
+    auto per_split = [&](int64_t s) { return ((k_stages + s - 1) / s + align - 1) / align * align; };
     int want = 0;
     if (const char* v = std::getenv("Q6_TC_KSPLIT")) want = std::atoi(v);
     if (want >= 1 && want <= 16) {
@@ -794,7 +796,7 @@ KSplit plan_ksplit(int64_t M, int64_t N, int64_t K, int NT) {
     KSplit best{1, static_cast<int>(k_stages)};
     if (tiles * 2 > sms) return best;
     int64_t best_cost = ((tiles + sms - 1) / sms) * (k_stages + 8);
-    for (int64_t s = 2; s <= 8; ++s) {
+    for (int64_t s = 2; s <= 16; ++s) {
         const int64_t ps = per_split(s);
         const int64_t splits = (k_stages + ps - 1) / ps;
         if (splits != s) continue;
@@ -892,7 +894,7 @@ int launch_tc(const LinearArgs& a, cudaStream_t stream) {
     p.lora_stages = a.lora_rank > 0 ? 2 : 0;
     p.lora_ksteps = a.lora_rank / 32;
     p.sexp = splice_exp3_host();
-    const KSplit ksp = plan_ksplit(a.M, a.N, a.K, NT);
+    const KSplit ksp = plan_ksplit(a.M, a.N, a.K, NT, kSbTma ? (1 << p.sb_shift) : 1);
     const size_t need = static_cast<size_t>(ksp.splits) * a.M * a.N * sizeof(float);
     const bool split = ksp.splits > 1 && a.workspace && a.workspace_bytes >= need &&
                        reinterpret_cast<uintptr_t>(a.workspace) % 16 == 0;
@@ -952,8 +954,13 @@ bool tc_supported(const LinearArgs& a) {
 
 size_t tc_workspace_bytes(int64_t M, int64_t N, int64_t K) {
     if (M <= 0 || N <= 0 || K <= 0) return 0;
-    const KSplit ksp = plan_ksplit(M, N, K, choose_token_tile(M, N));
-    return ksp.splits > 1 ? static_cast<size_t>(ksp.splits) * M * N * sizeof(float) : 0;
+    // the largest plan any group size (scale-chunk alignment) can choose
+    size_t need = 0;
+    for (int align : {1, 2, 4, 8}) {
+        const KSplit ksp = plan_ksplit(M, N, K, choose_token_tile(M, N), align);
+        if (ksp.splits > 1) need = std::max(need, static_cast<size_t>(ksp.splits) * M * N * sizeof(float));
+    }
+    return need;
 }
 
 int choose_token_tile(int64_t M, int64_t N) {
@@ -964,12 +971,17 @@ int choose_token_tile(int64_t M, int64_t N) {
     static const int kTiles[] = {256, 192, 128, 64, 32, 16};
     const int64_t sms = device_sm_count();
     const int64_t tiles_n = (N + kRows - 1) / kRows;
+    // A tile costs about max(nt, floor) + 32 token-columns per K stage: below
+    // ~128 tokens the dequantisation of its 128 weight rows, not the MMA, sets
+    // the pace, so narrower tiles only multiply the dequantisation work (the
+    // floor stops at M itself for a few token rows).
+    const int64_t floor = std::min<int64_t>(128, (M + 15) / 16 * 16);
     int best = 16;
     int64_t best_cost = -1;
     for (int nt : kTiles) {
         const int64_t tiles = ((M + nt - 1) / nt) * tiles_n;
         const int64_t waves = (tiles + sms - 1) / sms;
-        const int64_t cost = waves * (nt + 32);  // per-tile fixed overhead ~ 32 token-columns
+        const int64_t cost = waves * (std::max<int64_t>(nt, floor) + 32);
         if (best_cost < 0 || cost < best_cost) {
             best_cost = cost;
             best = nt;
