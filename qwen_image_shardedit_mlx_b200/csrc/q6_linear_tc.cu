@@ -58,7 +58,6 @@ constexpr int kBoxK = 64;                                // K per activation TMA
 constexpr int kCodeRowBytes = kBK * 6 / 8;               // 96 bytes of codes per row per stage
 constexpr int kCodeStageBytes = kRows * kCodeRowBytes;   // 12288
 constexpr int kCodeWordsPerStage = kBK * 6 / 32;         // 24
-constexpr int kAStages = 2;                              // TMEM ring of dequantised A tiles
 // Stage g is announced to the MMA issuer by one barrier, ready[g % kRing]
 // (the activation TMA bytes plus one arrival per dequant warp of the stage),
 // and handed back by one MMA commit, done[g % kRing], which frees both its
@@ -96,11 +95,15 @@ constexpr int pow2_at_least(int v) {
 
 constexpr int clampi(int v, int lo, int hi) { return v < lo ? lo : (v > hi ? hi : v); }
 
-template <int NT>
+// kPair: a cluster of two CTAs shares each cta_group::2 MMA (M = 256 weight
+// rows, 128 per CTA); each CTA stages only its half of the NT activation rows.
+template <int NT, bool kPair = false>
 struct Cfg {
     static_assert(NT % 16 == 0 && NT >= 16 && NT <= 256, "MMA N must be a multiple of 16 in [16, 256]");
+    static constexpr int kAStages = 2;  // TMEM ring of dequantised A tiles, one slot per dequant set
     static constexpr int kNAcc = (2 * NT + kAStages * kAColsPerStage <= 512) ? 2 : 1;
-    static constexpr int kXBoxBytes = NT * 128;  // NT rows of 64 bf16
+    static constexpr int kXRows = kPair ? NT / 2 : NT;  // activation rows this CTA stages
+    static constexpr int kXBoxBytes = kXRows * 128;     // kXRows rows of 64 bf16
     static constexpr int kXStageBytes = 2 * kXBoxBytes;
     static constexpr int kUsable = kSmemBudget - 1024 - kBarrierBytes;
     static constexpr int kXStages = clampi((kUsable * 2 / 3) / kXStageBytes, 2, 8);
@@ -111,7 +114,7 @@ struct Cfg {
                                       kSbSlots * kSbSlotBytes + kBarrierBytes;
     static constexpr int kAccCols = kNAcc * NT;
     static constexpr int kTmemCols = pow2_at_least(kAccCols + kAStages * kAColsPerStage);
-    static constexpr uint32_t kIdesc = idesc_bf16_f32(kRows, NT);
+    static constexpr uint32_t kIdesc = idesc_bf16_f32(kPair ? 2 * kRows : kRows, NT);
     static_assert(kSmemBytes <= kSmemBudget, "shared memory budget");
     static_assert(kXStages <= kRing && kRing % kAStages == 0, "stage barrier ring");
     static_assert(kTmemCols <= 512, "TMEM budget");
@@ -180,17 +183,18 @@ __device__ __forceinline__ Item item_at(const TcParams& p, int it) {
 __device__ __forceinline__ float bf16f(uint16_t v) { return __uint_as_float(static_cast<uint32_t>(v) << 16); }
 
 // Warp-uniform bounded wait: every lane polls, the warp proceeds only if all succeeded.
+template <bool kCluster = false>
 __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int site) {
-    const bool ok = mbar_wait(bar, parity, abort_flag, site);
+    const bool ok = mbar_wait<kCluster>(bar, parity, abort_flag, site);
     return __all_sync(0xffffffffu, ok);
 }
 
-template <int NT, bool kSbTma, int kEpi>
+template <int NT, bool kSbTma, int kEpi, bool kPair>
 __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
     q6_linear_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
                         const __grid_constant__ CUtensorMap tmap_s, const __grid_constant__ CUtensorMap tmap_b,
                         const __grid_constant__ CUtensorMap tmap_xa, const TcParams p) {
-    using C = Cfg<NT>;
+    using C = Cfg<NT, kPair>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* x_smem = smem;
@@ -211,10 +215,19 @@ __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
+    // CTA pairs: rank 0 issues the MMAs of both; work items are per pair, and
+    // this CTA's weight rows are the (rank)th 128 of the pair's 256.
+    const uint32_t rank = kPair ? cluster_ctarank() : 0u;
+    const bool leader = rank == 0;
+    const int it0 = kPair ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+    const int istep = kPair ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
+    constexpr int kTileRows = kPair ? 2 * kRows : kRows;
+    const int row0 = static_cast<int>(rank) * kRows;
+    constexpr int kPeers = kPair ? 2 : 1;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kRing; ++s) {
-            mbar_init(smem_u32(ready + s), 1 + kDqWarpsPerSet);  // activation producer + dequant set
+            mbar_init(smem_u32(ready + s), 1 + kPeers * kDqWarpsPerSet);  // activation producer + dequant sets
             mbar_init(smem_u32(done + s), 1);                    // MMA commit
         }
         for (int s = 0; s < C::kCStages; ++s) {
@@ -227,18 +240,24 @@ __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
         }
         for (int s = 0; s < C::kNAcc; ++s) {
             mbar_init(smem_u32(acc_full + s), 1);
-            mbar_init(smem_u32(acc_empty + s), 4);
+            mbar_init(smem_u32(acc_empty + s), 4 * kPeers);
         }
         mbar_init(smem_u32(drain), 1);
         *abort_flag = 0;
         fence_mbar_init();
     }
     if (warp == 2) {
-        tmem_alloc(smem_u32(tmem_slot), C::kTmemCols);
-        tmem_relinquish();
+        if constexpr (kPair) {
+            tmem_alloc_pair(smem_u32(tmem_slot), C::kTmemCols);
+            tmem_relinquish_pair();
+        } else {
+            tmem_alloc(smem_u32(tmem_slot), C::kTmemCols);
+            tmem_relinquish();
+        }
     }
     tc_fence_before();
     __syncthreads();
+    if constexpr (kPair) cluster_sync();  // both CTAs' barriers exist before any cross-CTA arrival
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
     pdl_launch_dependents();
@@ -252,7 +271,7 @@ __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
             uint32_t g = 0;  // stage counter over all tiles of this CTA
             int s = 0;       // g % kXStages
             bool ok = true;
-            for (int it = blockIdx.x; it < p.num_items && ok; it += gridDim.x) {
+            for (int it = it0; it < p.num_items && ok; it += istep) {
                 const Item I = item_at(p, it);
                 const int mb = I.mb;
                 for (int l = 0; l < I.stages(); ++l, ++g) {
@@ -260,14 +279,30 @@ __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
                     // x slot s was last read by the MMAs of stage g - kXStages.
                     if (g >= static_cast<uint32_t>(C::kXStages)) {
                         const uint32_t prev = g - C::kXStages;
-                        if (!mbar_wait(smem_u32(done + prev % kRing), (prev / kRing) & 1u, abort_flag, 1)) {
+                        if (!mbar_wait<kPair>(smem_u32(done + prev % kRing), (prev / kRing) & 1u, abort_flag, 1)) {
                             ok = false;
                             break;
                         }
                     }
                     const uint32_t fb = smem_u32(ready + g % kRing);
                     const uint32_t dst = smem_u32(x_smem + s * C::kXStageBytes);
-                    if (ks < p.k_stages) {
+                    if constexpr (kPair) {
+                        // Each CTA loads its half of the token rows; both halves count
+                        // on the leader's barrier, which expects the pair's bytes.
+                        const uint32_t fbc = mapa_shared(fb, 0);
+                        const int y0 = mb * NT + static_cast<int>(rank) * C::kXRows;
+                        if (ks < p.k_stages) {
+                            if (leader) mbar_arrive_expect_tx(fb, 2u * C::kXStageBytes);
+                            tma_load_2d_pair(dst, &tmap_x, fbc, ks * kBK, y0);
+                            tma_load_2d_pair(dst + C::kXBoxBytes, &tmap_x, fbc, ks * kBK + kBoxK, y0);
+                        } else {
+                            const int x0 = (ks - p.k_stages) * (p.lora_rank / 2);
+                            const bool two = p.lora_rank > 2 * kBoxK;
+                            if (leader) mbar_arrive_expect_tx(fb, 2u * (two ? C::kXStageBytes : C::kXBoxBytes));
+                            tma_load_2d_pair(dst, &tmap_xa, fbc, x0, y0);
+                            if (two) tma_load_2d_pair(dst + C::kXBoxBytes, &tmap_xa, fbc, x0 + kBoxK, y0);
+                        }
+                    } else if (ks < p.k_stages) {
                         mbar_arrive_expect_tx(fb, C::kXStageBytes);
                         tma_load_2d(dst, &tmap_x, fb, ks * kBK, mb * NT);
                         tma_load_2d(dst + C::kXBoxBytes, &tmap_x, fb, ks * kBK + kBoxK, mb * NT);
@@ -304,7 +339,7 @@ __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
             uint32_t sph = 0;
             long s_issued = 0;
             bool ok = true;
-            for (int it = blockIdx.x; it < p.num_items && ok; it += gridDim.x) {
+            for (int it = it0; it < p.num_items && ok; it += istep) {
                 const Item I = item_at(p, it);
                 const int nb = I.nb;
                 for (int ks = I.ks0; ks < I.ks1; ++ks) {
@@ -318,8 +353,8 @@ __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
                         const uint32_t dst = smem_u32(sb_smem + ss * kSbSlotBytes);
                         const int gx = (ks >> p.sb_shift) * kSbGroups;
                         mbar_arrive_expect_tx(fb, kSbSlotBytes);
-                        tma_load_2d(dst, &tmap_s, fb, gx, nb * kRows);
-                        tma_load_2d(dst + kSbBoxBytes, &tmap_b, fb, gx, nb * kRows);
+                        tma_load_2d(dst, &tmap_s, fb, gx, nb * kTileRows + row0);
+                        tma_load_2d(dst + kSbBoxBytes, &tmap_b, fb, gx, nb * kTileRows + row0);
                         ++s_issued;
                         if (++ss == kSbSlots) {
                             ss = 0;
@@ -333,7 +368,7 @@ __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
                     const uint32_t fb = smem_u32(c_full + s);
                     mbar_arrive_expect_tx(fb, kCodeStageBytes);
                     tma_load_2d(smem_u32(c_smem + s * kCodeStageBytes), &tmap_w, fb, ks * kCodeWordsPerStage,
-                                nb * kRows);
+                                nb * kTileRows + row0);
                     ++issued;
                     if (++s == C::kCStages) {
                         s = 0;
@@ -358,7 +393,7 @@ __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
         // tcgen05.commit, so its loop carries nothing else it can avoid: one
         // wait, one fence, eight MMAs whose operand addresses are immediate
         // offsets from per-stage bases, one commit.
-        if (lane == 0) {
+        if (lane == 0 && leader) {
             const uint64_t desc_base = sdesc_kmajor_sw128(smem_u32(x_smem));
             const uint32_t desc_lo = static_cast<uint32_t>(desc_base);
             const uint32_t desc_hi = static_cast<uint32_t>(desc_base >> 32);
@@ -367,27 +402,31 @@ __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
             int xs = 0, acc = 0;
             uint32_t accph = 0;
             bool ok = true;
-            for (int it = blockIdx.x; it < p.num_items && ok; it += gridDim.x) {
+            for (int it = it0; it < p.num_items && ok; it += istep) {
                 const Item I = item_at(p, it);
-                if (!mbar_wait(smem_u32(acc_empty + acc), accph ^ 1u, abort_flag, 2)) break;
+                if (!mbar_wait<kPair>(smem_u32(acc_empty + acc), accph ^ 1u, abort_flag, 2)) break;
                 const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * NT);
                 for (int l = 0; l < I.stages(); ++l, ++g) {
                     const int ks = I.ks_of(l, p.k_stages);
                     const uint32_t rs = g % kRing;
-                    if (!mbar_wait(smem_u32(ready + rs), (g / kRing) & 1u, abort_flag, 3)) {
+                    if (!mbar_wait<kPair>(smem_u32(ready + rs), (g / kRing) & 1u, abort_flag, 3)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
                     const uint32_t lo = desc_lo + static_cast<uint32_t>(xs * (C::kXStageBytes >> 4));
-                    const uint32_t a_tmem = a_base + (rs % kAStages) * kAColsPerStage;
+                    const uint32_t a_tmem = a_base + (rs % C::kAStages) * kAColsPerStage;
                     const uint32_t first = l != 0 ? 1u : 0u;
                     // K step kk reads activation box kk / 4 at 32-byte offset kk % 4
                     // and TMEM A columns 8 kk .. 8 kk + 7.
                     auto issue = [&](int kk) {
                         const uint32_t off = static_cast<uint32_t>((kk / 4) * (C::kXBoxBytes >> 4) + (kk % 4) * 2);
-                        mma_bf16_ts(d_tmem, a_tmem + kk * 8, make_desc(lo + off, desc_hi), C::kIdesc,
-                                    kk == 0 ? first : 1u);
+                        if constexpr (kPair)
+                            mma_bf16_ts_pair(d_tmem, a_tmem + kk * 8, make_desc(lo + off, desc_hi), C::kIdesc,
+                                             kk == 0 ? first : 1u);
+                        else
+                            mma_bf16_ts(d_tmem, a_tmem + kk * 8, make_desc(lo + off, desc_hi), C::kIdesc,
+                                        kk == 0 ? first : 1u);
                     };
                     if (ks + 1 < p.k_stages || (ks + 1 == p.k_stages && p.last_ksteps == kBK / 16)) {
 #pragma unroll
@@ -398,18 +437,27 @@ __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
                     } else {  // LoRA stage: r / 32 K-steps (the second box once r > 128)
                         for (int kk = 0; kk < p.lora_ksteps; ++kk) issue(kk);
                     }
-                    tc_commit(smem_u32(done + rs));
+                    if constexpr (kPair)
+                        tc_commit_pair(smem_u32(done + rs), 3);
+                    else
+                        tc_commit(smem_u32(done + rs));
                     if (++xs == C::kXStages) xs = 0;
                 }
                 if (!ok) break;
-                tc_commit(smem_u32(acc_full + acc));
+                if constexpr (kPair)
+                    tc_commit_pair(smem_u32(acc_full + acc), 3);
+                else
+                    tc_commit(smem_u32(acc_full + acc));
                 if (++acc == C::kNAcc) {
                     acc = 0;
                     accph ^= 1u;
                 }
             }
             // All issued MMAs complete before TMEM may be released.
-            tc_commit(smem_u32(drain));
+            if constexpr (kPair)
+                tc_commit_pair(smem_u32(drain), 1);
+            else
+                tc_commit(smem_u32(drain));
             mbar_wait_drain(smem_u32(drain), 0);
         }
     } else if (warp >= 4 && warp < 8) {
@@ -428,11 +476,11 @@ __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
         pdl_wait();  // y, the residual, the gate and the partials may be the previous kernel's
         int acc = 0;
         uint32_t accph = 0;
-        for (int it = blockIdx.x; it < p.num_items; it += gridDim.x) {
+        for (int it = it0; it < p.num_items; it += istep) {
             const Item I = item_at(p, it);
             const int mb = I.mb;
             const int nb = I.nb;
-            const int n = nb * kRows + q * 32 + lane;
+            const int n = nb * kTileRows + row0 + q * 32 + lane;
             const bool n_ok = n < p.N;
             const float bias_n = (n_ok && p.bias) ? bf16f(p.bias[n]) : 0.0f;
             const float gate_n = (n_ok && p.gate) ? bf16f(p.gate[n]) : 1.0f;
@@ -440,7 +488,7 @@ __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
             const int ne = n & ~1;
             const float2 gate_w = (n_ok && p.gate) ? make_float2(bf16f(p.gate[ne]), bf16f(p.gate[ne + 1]))
                                                    : make_float2(1.0f, 1.0f);
-            if (!warp_wait(smem_u32(acc_full + acc), accph, abort_flag, 5)) break;
+            if (!warp_wait<kPair>(smem_u32(acc_full + acc), accph, abort_flag, 5)) break;
             tc_fence_after();
 #pragma unroll 1
             for (int c = 0; c < NT / kChunk; ++c) {
@@ -537,7 +585,12 @@ __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(smem_u32(acc_empty + acc));
+            if (lane == 0) {
+                if constexpr (kPair)
+                    mbar_arrive_cluster(mapa_shared(smem_u32(acc_empty + acc), 0));
+                else
+                    mbar_arrive(smem_u32(acc_empty + acc));
+            }
             if (++acc == C::kNAcc) {
                 acc = 0;
                 accph ^= 1u;
@@ -559,10 +612,10 @@ __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
         uint32_t gqstage = 0; // q6 (code-carrying) stage counter: the code ring's index
         uint32_t gchunk = 0;  // scale chunk counter over all tiles of this CTA
         bool ok = true;
-        for (int it = blockIdx.x; it < p.num_items && ok; it += gridDim.x) {
+        for (int it = it0; it < p.num_items && ok; it += istep) {
             const Item I = item_at(p, it);
             const int nb = I.nb;
-            const int n = nb * kRows + r;
+            const int n = nb * kTileRows + row0 + r;
             const bool n_ok = n < p.N;
             const uint16_t* srow = p.scales + static_cast<size_t>(n_ok ? n : 0) * p.groups;
             const uint16_t* brow = p.qbiases + static_cast<size_t>(n_ok ? n : 0) * p.groups;
@@ -629,7 +682,7 @@ __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
                     const uint32_t gq = gq_base + static_cast<uint32_t>(ks - I.ks0);
                     const int cs = static_cast<int>(gq % C::kCStages);
                     const uint32_t cph = (gq / C::kCStages) & 1u;
-                    const int as = static_cast<int>(g % kAStages);
+                    const int as = static_cast<int>(g % C::kAStages);
                     const uint32_t rs = g % kRing;
                     float sb[4];
                     if constexpr (kSbTma) {
@@ -663,10 +716,10 @@ __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
                         dequant16_bf16x2_e3(c1.z, c1.w, c2.x, sb[2], sb[3], p.sexp, a + 16);
                         dequant16_bf16x2_e3(c2.y, c2.z, c2.w, sb[2], sb[3], p.sexp, a + 24);
                     }
-                    // A slot `as` was last read by the MMAs of stage g - kAStages.
-                    if (g >= static_cast<uint32_t>(kAStages)) {
-                        const uint32_t prev = g - kAStages;
-                        if (!warp_wait(smem_u32(done + prev % kRing), (prev / kRing) & 1u, abort_flag, 7)) {
+                    // A slot `as` was last read by the MMAs of stage g - C::kAStages.
+                    if (g >= static_cast<uint32_t>(C::kAStages)) {
+                        const uint32_t prev = g - C::kAStages;
+                        if (!warp_wait<kPair>(smem_u32(done + prev % kRing), (prev / kRing) & 1u, abort_flag, 7)) {
                             ok = false;
                             break;
                         }
@@ -678,7 +731,12 @@ __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
                     tmem_wait_st();
                     tc_fence_before();
                     __syncwarp();
-                    if (lane == 0) mbar_arrive(smem_u32(ready + rs));
+                    if (lane == 0) {
+                    if constexpr (kPair)
+                        mbar_arrive_cluster(mapa_shared(smem_u32(ready + rs), 0));
+                    else
+                        mbar_arrive(smem_u32(ready + rs));
+                }
                 }
                 if constexpr (kSbTma) {
                     __syncwarp();
@@ -689,13 +747,13 @@ __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
             // columns of stage l (zero beyond), one coalesced row of B per k.
             for (; ok && ks < I.ks1 + I.lora; ks += kDqSets) {
                 const uint32_t g = g_base + static_cast<uint32_t>(ks - I.ks0);
-                const int as = static_cast<int>(g % kAStages);
+                const int as = static_cast<int>(g % C::kAStages);
                 const uint32_t rs = g % kRing;
                 const int half_r = p.lora_rank / 2;
                 const int j0 = (ks - I.ks1) * half_r;
-                if (g >= static_cast<uint32_t>(kAStages)) {
-                    const uint32_t prev = g - kAStages;
-                    if (!warp_wait(smem_u32(done + prev % kRing), (prev / kRing) & 1u, abort_flag, 7)) {
+                if (g >= static_cast<uint32_t>(C::kAStages)) {
+                    const uint32_t prev = g - C::kAStages;
+                    if (!warp_wait<kPair>(smem_u32(done + prev % kRing), (prev / kRing) & 1u, abort_flag, 7)) {
                         ok = false;
                         break;
                     }
@@ -721,16 +779,25 @@ __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
                 tmem_wait_st();
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(smem_u32(ready + rs));
+                if (lane == 0) {
+                    if constexpr (kPair)
+                        mbar_arrive_cluster(mapa_shared(smem_u32(ready + rs), 0));
+                    else
+                        mbar_arrive(smem_u32(ready + rs));
+                }
             }
         }
     }
 
     tc_fence_before();
     __syncthreads();
+    if constexpr (kPair) cluster_sync();  // the leader's MMAs into this CTA's tensor memory have retired
     if (warp == 2) {
         tc_fence_after();
-        tmem_dealloc(tmem_base, C::kTmemCols);
+        if constexpr (kPair)
+            tmem_dealloc_pair(tmem_base, C::kTmemCols);
+        else
+            tmem_dealloc(tmem_base, C::kTmemCols);
     }
 }
 
@@ -830,20 +897,42 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restr
     }
 }
 
-template <int NT, bool kSbTma, int kEpi>
+// Launches a CTA-pair grid: clusters of two along x, with programmatic
+// dependent launch when it is enabled.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pair_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                            Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 2 : 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+template <int NT, bool kSbTma, int kEpi, bool kPair>
 int launch_tc(const LinearArgs& a, cudaStream_t stream) {
-    using C = Cfg<NT>;
+    using C = Cfg<NT, kPair>;
     static int attr_set_for_device[64] = {0};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return Q6_ERR_CUDA;
     if (dev >= 0 && dev < 64 && !attr_set_for_device[dev]) {
-        if (cudaFuncSetAttribute(q6_linear_tc_kernel<NT, kSbTma, kEpi>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 C::kSmemBytes) != cudaSuccess)
+        if (cudaFuncSetAttribute(q6_linear_tc_kernel<NT, kSbTma, kEpi, kPair>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes) != cudaSuccess)
             return Q6_ERR_CUDA;
         attr_set_for_device[dev] = 1;
     }
     CUtensorMap tmap_x, tmap_w, tmap_s, tmap_b, tmap_xa;
-    if (!make_map_2d(&tmap_x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.x, a.K, a.M, a.K * 2, kBoxK, NT,
+    if (!make_map_2d(&tmap_x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.x, a.K, a.M, a.K * 2, kBoxK, C::kXRows,
                      CU_TENSOR_MAP_SWIZZLE_128B))
         return Q6_ERR_CUDA;
     const uint64_t words = static_cast<uint64_t>(a.K) * 6 / 32;
@@ -863,7 +952,7 @@ int launch_tc(const LinearArgs& a, cudaStream_t stream) {
     }
     if (a.lora_rank > 0) {
         if (!make_map_2d(&tmap_xa, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.lora_xa, a.lora_rank, a.M,
-                         static_cast<uint64_t>(a.lora_rank) * 2, kBoxK, NT, CU_TENSOR_MAP_SWIZZLE_128B))
+                         static_cast<uint64_t>(a.lora_rank) * 2, kBoxK, C::kXRows, CU_TENSOR_MAP_SWIZZLE_128B))
             return Q6_ERR_CUDA;
     } else {
         tmap_xa = tmap_x;  // unused
@@ -883,7 +972,8 @@ int launch_tc(const LinearArgs& a, cudaStream_t stream) {
     p.sb_shift = p.gs_shift - 4;  // 8 groups of gs codes = gs / 16 stages of 128
     p.groups = static_cast<int>(groups);
     p.flags = a.flags;
-    p.tiles_n = static_cast<int>((a.N + kRows - 1) / kRows);
+    constexpr int kTileRows = kPair ? 2 * kRows : kRows;  // weight rows per work item
+    p.tiles_n = static_cast<int>((a.N + kTileRows - 1) / kTileRows);
     const int tiles_m = static_cast<int>((a.M + NT - 1) / NT);
     p.num_tiles = tiles_m * p.tiles_n;
     p.k_stages = static_cast<int>((a.K + kBK - 1) / kBK);
@@ -894,7 +984,7 @@ int launch_tc(const LinearArgs& a, cudaStream_t stream) {
     p.lora_stages = a.lora_rank > 0 ? 2 : 0;
     p.lora_ksteps = a.lora_rank / 32;
     p.sexp = splice_exp3_host();
-    const KSplit ksp = plan_ksplit(a.M, a.N, a.K, NT, kSbTma ? (1 << p.sb_shift) : 1);
+    const KSplit ksp = kPair ? KSplit{1, p.k_stages} : plan_ksplit(a.M, a.N, a.K, NT, kSbTma ? (1 << p.sb_shift) : 1);
     const size_t need = static_cast<size_t>(ksp.splits) * a.M * a.N * sizeof(float);
     const bool split = ksp.splits > 1 && a.workspace && a.workspace_bytes >= need &&
                        reinterpret_cast<uintptr_t>(a.workspace) % 16 == 0;
@@ -902,10 +992,17 @@ int launch_tc(const LinearArgs& a, cudaStream_t stream) {
     p.ks_per = split ? ksp.stages_per_split : p.k_stages;
     p.num_items = p.num_tiles * p.ksplit;
     p.partial = split ? static_cast<float*>(a.workspace) : nullptr;
-    const int grid = std::min(p.num_items, device_sm_count());
-    if (launch_pdl(q6_linear_tc_kernel<NT, kSbTma, kEpi>, dim3(grid), dim3(tc_threads(kDqSets)), C::kSmemBytes,
-                   stream, tmap_x, tmap_w, tmap_s, tmap_b, tmap_xa, p) != cudaSuccess)
-        return Q6_ERR_CUDA;
+    if constexpr (kPair) {
+        const int pairs = std::min(p.num_items, device_sm_count() / 2);
+        if (launch_pair_pdl(q6_linear_tc_kernel<NT, kSbTma, kEpi, true>, dim3(2 * pairs), dim3(tc_threads(kDqSets)),
+                            C::kSmemBytes, stream, tmap_x, tmap_w, tmap_s, tmap_b, tmap_xa, p) != cudaSuccess)
+            return Q6_ERR_CUDA;
+    } else {
+        const int grid = std::min(p.num_items, device_sm_count());
+        if (launch_pdl(q6_linear_tc_kernel<NT, kSbTma, kEpi, false>, dim3(grid), dim3(tc_threads(kDqSets)),
+                       C::kSmemBytes, stream, tmap_x, tmap_w, tmap_s, tmap_b, tmap_xa, p) != cudaSuccess)
+            return Q6_ERR_CUDA;
+    }
     if (split) {
         const int64_t total = a.M * a.N;
         const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, int64_t(device_sm_count()) * 8));
@@ -919,12 +1016,20 @@ int launch_tc(const LinearArgs& a, cudaStream_t stream) {
 
 // Staged scales with a specialised epilogue for the MLP's two shapes
 // (bias + GELU, bias only); everything else takes the general epilogue.
-template <int NT>
+template <int NT, bool kPair = false>
 int launch_tc_sb(const LinearArgs& a, cudaStream_t stream) {
-    if (!sb_tma_ok(a)) return launch_tc<NT, false, kEpiGeneral>(a, stream);
-    if (a.residual || a.gate) return launch_tc<NT, true, kEpiGeneral>(a, stream);
-    if (a.flags & Q6_EPI_GELU) return launch_tc<NT, true, kEpiGelu>(a, stream);
-    return launch_tc<NT, true, kEpiPlain>(a, stream);
+    if (!sb_tma_ok(a)) return launch_tc<NT, false, kEpiGeneral, kPair>(a, stream);
+    if (a.residual || a.gate) return launch_tc<NT, true, kEpiGeneral, kPair>(a, stream);
+    if (a.flags & Q6_EPI_GELU) return launch_tc<NT, true, kEpiGelu, kPair>(a, stream);
+    return launch_tc<NT, true, kEpiPlain, kPair>(a, stream);
+}
+
+// CTA pairs (one cta_group::2 MMA over 256 weight rows) for token tiles of
+// 128 and more; Q6_TC_PAIR=1 selects them.
+bool pair_mode(int token_tile) {
+    if (token_tile < 128) return false;
+    const char* v = std::getenv("Q6_TC_PAIR");
+    return v && v[0] == '1';
 }
 
 }  // namespace
@@ -991,6 +1096,14 @@ int choose_token_tile(int64_t M, int64_t N) {
 }
 
 int launch_linear_tc(const LinearArgs& a, int token_tile, cudaStream_t stream) {
+    if (pair_mode(token_tile)) {
+        switch (token_tile) {
+            case 256: return launch_tc_sb<256, true>(a, stream);
+            case 192: return launch_tc_sb<192, true>(a, stream);
+            case 128: return launch_tc_sb<128, true>(a, stream);
+            default: break;
+        }
+    }
     switch (token_tile) {
         case 256: return launch_tc_sb<256>(a, stream);
         case 192: return launch_tc_sb<192>(a, stream);

@@ -87,15 +87,44 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parit
     return ok != 0;
 }
 
+// The same waits with cluster-scope acquire, for barriers that threads of the
+// other CTA of a CTA pair arrive on (their writes must be visible after the wait).
+__device__ __forceinline__ bool mbar_try_wait_cl(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred P;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 P, [%1], %2;\n\t"
+        "selp.b32 %0, 1, 0, P;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+__device__ __forceinline__ bool mbar_try_wait_sleep_cl(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred P;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 P, [%1], %2, %3;\n\t"
+        "selp.b32 %0, 1, 0, P;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+
 // Wait for the phase with the given parity to complete.  Gives up (returns
 // false) when the CTA-wide abort flag is raised or after kWaitLimitNs; in the
 // latter case it raises the abort flag and records `site` in g_device_error.
+// kCluster selects cluster-scope acquire.
+template <bool kCluster = false>
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
                                           int site) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (kCluster ? mbar_try_wait_cl(bar, parity) : mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_timer_ns();
     for (uint32_t i = 1;; ++i) {
-        if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
+        if (kCluster ? mbar_try_wait_sleep_cl(bar, parity, 20000u) : mbar_try_wait_sleep(bar, parity, 20000u))
+            return true;
         if ((i & 15u) == 0) {
             if (*abort_flag) return false;
             if (global_timer_ns() - t0 > kWaitLimitNs) {
@@ -144,6 +173,45 @@ __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_
         : "memory");
 }
 
+// ------------------------------------------------------------ CTA pairs
+// A cluster of two CTAs sharing one cta_group::2 MMA: rank 0 (the leader)
+// issues the MMAs for both; barriers the leader waits on collect arrivals
+// from both CTAs.
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+// Shared::cluster address of this CTA's shared variable `addr` in CTA `rank`.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+    return r;
+}
+
+// Arrive on a barrier given by its shared::cluster address (this CTA's or the peer's).
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// 2-D tiled copy into this CTA's shared memory whose completion counts on a
+// barrier of either CTA of the pair (`bar` a shared::cluster address).  No
+// multicast: each CTA fetches its own half of the tile.
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, uint32_t bar, int32_t x,
+                                                 int32_t y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+        "l"(map), "r"(bar), "r"(x), "r"(y)
+        : "memory");
+}
+
 // Orders this thread's earlier generic-proxy shared-memory accesses before
 // its later async-proxy ones (a bulk copy that overwrites a buffer just read).
 __device__ __forceinline__ void fence_proxy_async_smem() {
@@ -167,6 +235,23 @@ __device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
                  : "memory");
 }
 
+// Pair forms: both CTAs' allocating warps (same warp index) allocate the same
+// columns; the leader's MMAs then address both CTAs' tensor memory.
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t dst_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem),
+                 "r"(ncols)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_relinquish_pair() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+                 : "memory");
+}
+
 __device__ __forceinline__ void tc_fence_before() {
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
 }
@@ -180,6 +265,27 @@ __device__ __forceinline__ void tc_commit(uint32_t bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
                      bar)
                  : "memory");
+}
+
+// Commit of the leader's pair MMAs, arriving on the barrier at the same
+// shared-memory offset in every CTA of `mask` (bit r = cluster rank r).
+__device__ __forceinline__ void tc_commit_pair(uint32_t bar, uint16_t mask) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::
+                     "r"(bar), "h"(mask)
+                 : "memory");
+}
+
+// Pair MMA issued by the leader: D rows 0-127 in the leader's tensor memory
+// and 128-255 in the peer's, A likewise, B's N columns split in halves
+// between the two CTAs' shared memory at the same offset.
+__device__ __forceinline__ void mma_bf16_ts_pair(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                                 uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
 }
 
 // D(tmem) (+)= A(tmem) * B(smem)^T, kind::f16 (bf16 inputs, fp32 accumulate).

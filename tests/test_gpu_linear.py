@@ -383,3 +383,51 @@ def test_split_k_with_lora(monkeypatch, r):
     ref = oracle.linear(oracle.bf16_bits_to_f32(x), w, weight_dtype="bf16",
                         lora=(oracle.bf16_bits_to_f32(a_bits), oracle.bf16_bits_to_f32(b_bits), 0.5))
     assert_close(f32(got), ref, what=f"splitk lora r{r}")
+
+
+PAIR_CASES = [
+    # (m, n, k, gs, epi, token tile, lora rank)
+    (3456, 1536, 1024, 128, "bias_gelu", 192, 0),  # the image-FF token count
+    (700, 640, 512, 32, "residual_gate", 128, 0),  # N % 256 != 0: the second CTA of the last pair is idle
+    (513, 384, 1088, 64, "plain", 256, 0),         # ragged M, K % 128 == 64, scales not staged (17 groups)
+    (300, 512, 768, 64, "plain", 128, 64),         # LoRA stages: each CTA stages half of x @ A
+]
+
+
+@pytest.mark.parametrize("m,n,k,gs,epi,tile,r", PAIR_CASES)
+def test_cta_pair_mode(m, n, k, gs, epi, tile, r, monkeypatch):
+    """CTA pairs (Q6_TC_PAIR=1): one cta_group::2 MMA per 256 weight rows,
+    each CTA staging half of the token rows.  The accumulation order per
+    output is the single-CTA one (split-K off, which pairs never use), so
+    the outputs are bitwise equal."""
+
+    monkeypatch.setenv("Q6_TC_TOKEN_TILE", str(tile))
+    monkeypatch.setenv("Q6_TC_KSPLIT", "1")
+    rng = np.random.default_rng(m + n + k + r)
+    w = random_weights(rng, n, k, gs, bias=epi != "plain")
+    x = random_bf16(rng, (m, k))
+    wt, st, bt, bias = weights_to_torch(w)
+    kwargs = {}
+    residual = gate = lora_ref = None
+    if epi == "residual_gate":
+        residual = random_bf16(rng, (m, n))
+        gate = random_bf16(rng, (n,), 0.5)
+        kwargs = dict(residual=from_bits(residual), gate=from_bits(gate))
+    if r:
+        a_bits, b_bits = random_bf16(rng, (k, r), 0.02), random_bf16(rng, (r, n), 0.02)
+        kwargs["lora"] = (from_bits(a_bits), from_bits(b_bits), 0.75)
+        lora_ref = (oracle.bf16_bits_to_f32(a_bits), oracle.bf16_bits_to_f32(b_bits), 0.75)
+    outs = {}
+    for pair in ("0", "1"):
+        monkeypatch.setenv("Q6_TC_PAIR", pair)
+        out = torch.full((m, n), float("nan"), dtype=torch.bfloat16, device="cuda")
+        outs[pair] = ops.q6_linear(from_bits(x), wt, st, bt, bias, group_size=gs, apply_gelu=epi == "bias_gelu",
+                                   path="tensor", out=out, **kwargs)
+    torch.cuda.synchronize()
+    assert torch.equal(outs["0"], outs["1"])
+    ref = oracle.linear(
+        oracle.bf16_bits_to_f32(x), w, apply_gelu=epi == "bias_gelu", weight_dtype="bf16",
+        residual=None if residual is None else oracle.bf16_bits_to_f32(residual),
+        gate=None if gate is None else oracle.bf16_bits_to_f32(gate), lora=lora_ref,
+    )
+    assert_close(f32(outs["1"]), ref, what=f"pair {m}x{n}x{k} gs{gs} {epi} nt{tile} r{r}")
