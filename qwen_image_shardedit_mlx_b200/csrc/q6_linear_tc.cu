@@ -183,9 +183,8 @@ __device__ __forceinline__ Item item_at(const TcParams& p, int it) {
 __device__ __forceinline__ float bf16f(uint16_t v) { return __uint_as_float(static_cast<uint32_t>(v) << 16); }
 
 // Warp-uniform bounded wait: every lane polls, the warp proceeds only if all succeeded.
-template <bool kCluster = false>
 __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int site) {
-    const bool ok = mbar_wait<kCluster>(bar, parity, abort_flag, site);
+    const bool ok = mbar_wait(bar, parity, abort_flag, site);
     return __all_sync(0xffffffffu, ok);
 }
 
@@ -279,7 +278,7 @@ __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
                     // x slot s was last read by the MMAs of stage g - kXStages.
                     if (g >= static_cast<uint32_t>(C::kXStages)) {
                         const uint32_t prev = g - C::kXStages;
-                        if (!mbar_wait<kPair>(smem_u32(done + prev % kRing), (prev / kRing) & 1u, abort_flag, 1)) {
+                        if (!mbar_wait(smem_u32(done + prev % kRing), (prev / kRing) & 1u, abort_flag, 1)) {
                             ok = false;
                             break;
                         }
@@ -404,12 +403,12 @@ __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
             bool ok = true;
             for (int it = it0; it < p.num_items && ok; it += istep) {
                 const Item I = item_at(p, it);
-                if (!mbar_wait<kPair>(smem_u32(acc_empty + acc), accph ^ 1u, abort_flag, 2)) break;
+                if (!mbar_wait(smem_u32(acc_empty + acc), accph ^ 1u, abort_flag, 2)) break;
                 const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * NT);
                 for (int l = 0; l < I.stages(); ++l, ++g) {
                     const int ks = I.ks_of(l, p.k_stages);
                     const uint32_t rs = g % kRing;
-                    if (!mbar_wait<kPair>(smem_u32(ready + rs), (g / kRing) & 1u, abort_flag, 3)) {
+                    if (!mbar_wait(smem_u32(ready + rs), (g / kRing) & 1u, abort_flag, 3)) {
                         ok = false;
                         break;
                     }
@@ -488,7 +487,7 @@ __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
             const int ne = n & ~1;
             const float2 gate_w = (n_ok && p.gate) ? make_float2(bf16f(p.gate[ne]), bf16f(p.gate[ne + 1]))
                                                    : make_float2(1.0f, 1.0f);
-            if (!warp_wait<kPair>(smem_u32(acc_full + acc), accph, abort_flag, 5)) break;
+            if (!warp_wait(smem_u32(acc_full + acc), accph, abort_flag, 5)) break;
             tc_fence_after();
 #pragma unroll 1
             for (int c = 0; c < NT / kChunk; ++c) {
@@ -719,7 +718,7 @@ __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
                     // A slot `as` was last read by the MMAs of stage g - C::kAStages.
                     if (g >= static_cast<uint32_t>(C::kAStages)) {
                         const uint32_t prev = g - C::kAStages;
-                        if (!warp_wait<kPair>(smem_u32(done + prev % kRing), (prev / kRing) & 1u, abort_flag, 7)) {
+                        if (!warp_wait(smem_u32(done + prev % kRing), (prev / kRing) & 1u, abort_flag, 7)) {
                             ok = false;
                             break;
                         }
@@ -753,7 +752,7 @@ __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
                 const int j0 = (ks - I.ks1) * half_r;
                 if (g >= static_cast<uint32_t>(C::kAStages)) {
                     const uint32_t prev = g - C::kAStages;
-                    if (!warp_wait<kPair>(smem_u32(done + prev % kRing), (prev / kRing) & 1u, abort_flag, 7)) {
+                    if (!warp_wait(smem_u32(done + prev % kRing), (prev / kRing) & 1u, abort_flag, 7)) {
                         ok = false;
                         break;
                     }
@@ -1025,11 +1024,15 @@ int launch_tc_sb(const LinearArgs& a, cudaStream_t stream) {
 }
 
 // CTA pairs (one cta_group::2 MMA over 256 weight rows) for token tiles of
-// 128 and more; Q6_TC_PAIR=1 selects them.
-bool pair_mode(int token_tile) {
+// 128 and more when the pairs' tiles fill every SM pair at least once (so no
+// split-K plan is given up).  Q6_TC_PAIR=0 turns them off, =1 forces them.
+bool pair_mode(const LinearArgs& a, int token_tile) {
     if (token_tile < 128) return false;
     const char* v = std::getenv("Q6_TC_PAIR");
-    return v && v[0] == '1';
+    if (v && v[0] == '0') return false;
+    if (v && v[0] == '1') return true;
+    const int64_t pair_tiles = ((a.M + token_tile - 1) / token_tile) * ((a.N + 2 * kRows - 1) / (2 * kRows));
+    return pair_tiles >= device_sm_count() / 2;
 }
 
 }  // namespace
@@ -1096,7 +1099,7 @@ int choose_token_tile(int64_t M, int64_t N) {
 }
 
 int launch_linear_tc(const LinearArgs& a, int token_tile, cudaStream_t stream) {
-    if (pair_mode(token_tile)) {
+    if (pair_mode(a, token_tile)) {
         switch (token_tile) {
             case 256: return launch_tc_sb<256, true>(a, stream);
             case 192: return launch_tc_sb<192, true>(a, stream);

@@ -87,44 +87,15 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parit
     return ok != 0;
 }
 
-// The same waits with cluster-scope acquire, for barriers that threads of the
-// other CTA of a CTA pair arrive on (their writes must be visible after the wait).
-__device__ __forceinline__ bool mbar_try_wait_cl(uint32_t bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred P;\n\t"
-        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 P, [%1], %2;\n\t"
-        "selp.b32 %0, 1, 0, P;\n\t}"
-        : "=r"(ok)
-        : "r"(bar), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-
-__device__ __forceinline__ bool mbar_try_wait_sleep_cl(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred P;\n\t"
-        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 P, [%1], %2, %3;\n\t"
-        "selp.b32 %0, 1, 0, P;\n\t}"
-        : "=r"(ok)
-        : "r"(bar), "r"(parity), "r"(hint_ns)
-        : "memory");
-    return ok != 0;
-}
-
 // Wait for the phase with the given parity to complete.  Gives up (returns
 // false) when the CTA-wide abort flag is raised or after kWaitLimitNs; in the
 // latter case it raises the abort flag and records `site` in g_device_error.
-// kCluster selects cluster-scope acquire.
-template <bool kCluster = false>
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
                                           int site) {
-    if (kCluster ? mbar_try_wait_cl(bar, parity) : mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_timer_ns();
     for (uint32_t i = 1;; ++i) {
-        if (kCluster ? mbar_try_wait_sleep_cl(bar, parity, 20000u) : mbar_try_wait_sleep(bar, parity, 20000u))
-            return true;
+        if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
         if ((i & 15u) == 0) {
             if (*abort_flag) return false;
             if (global_timer_ns() - t0 > kWaitLimitNs) {
@@ -191,9 +162,12 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
     return r;
 }
 
-// Arrive on a barrier given by its shared::cluster address (this CTA's or the peer's).
+// Arrive on a barrier given by its shared::cluster address (this CTA's or the
+// peer's), with the default (CTA-scope release) semantics: what it publishes
+// is tensor-memory or accumulator state, ordered by the tcgen05 fences around
+// it.  A cluster-scope release here costs 1-2 k cycles per arrival on B200.
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 
 __device__ __forceinline__ void cluster_sync() {
