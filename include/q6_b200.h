@@ -121,7 +121,11 @@ Q6_API int q6_linear_f32(const float* x, const uint32_t* w, const uint16_t* scal
  * Image feed-forward MLP  y = fc2(gelu(fc1(x)))  [+ residual/gate epilogue]:
  *   x bf16 [M, D]; fc1: D -> H (+ bias, GELU); fc2: H -> D (+ bias); y bf16 [M, D].
  * The bf16 hidden [M, H] lives in the caller's workspace
- * (q6_mlp_workspace_bytes(M, H) bytes).
+ * (q6_mlp_workspace_bytes(M, H) bytes).  Workspace beyond that, counted
+ * from the next 256-byte boundary, is split-K space for the two linears:
+ * with max(q6_linear_tc_workspace_bytes(M, H, D),
+ * q6_linear_tc_workspace_bytes(M, D, H)) bytes there, a linear whose tiles
+ * alone would leave SMs idle (a few hundred tokens) splits K.
  * Replaces `fused_q6_mlp` (shardedit_mlx/q6_metal_mlp.py:207-215) and the
  * QwenFeedForward `img_ff(x)` call it stands in for (dense_img_ff_window.py:62-67).
  */

@@ -162,7 +162,7 @@ class QwenTransformerBlock(torch.nn.Module):
         return cls(dict(block.linears), norms, heads=heads or dim // HEAD_DIM)
 
     def _workspace(self, m: int, device: torch.device) -> torch.Tensor:
-        need = int(ops.mlp_workspace_bytes(m, 4 * self.dim))
+        need = int(ops.mlp_workspace_bytes(m, 4 * self.dim, self.dim))
         if self._ws is None or self._ws.numel() < need or self._ws.device != device:
             self._ws = torch.empty(need, dtype=torch.uint8, device=device)
         return self._ws
@@ -200,10 +200,7 @@ class QwenTransformerBlock(torch.nn.Module):
         q = torch.empty((s, d), dtype=torch.bfloat16, device=hidden.device)
         k = torch.empty_like(q)
         v = torch.empty_like(q)
-        for buf, img_name, txt_name in ((q, "attn.to_q", "attn.add_q_proj"), (k, "attn.to_k", "attn.add_k_proj"),
-                                        (v, "attn.to_v", "attn.add_v_proj")):
-            self._linear(txt_name, txt_in, out=buf[:s_txt])
-            self._linear(img_name, img_in, out=buf[s_txt:])
+        project_qkv(self, txt_in, img_in, q, k, v)
         qk_rmsnorm_rope_(q[:s_txt], self.norms["attn.norm_added_q"], txt_cos, txt_sin, eps=self.eps)
         qk_rmsnorm_rope_(q[s_txt:], self.norms["attn.norm_q"], img_cos, img_sin, eps=self.eps)
         qk_rmsnorm_rope_(k[:s_txt], self.norms["attn.norm_added_k"], txt_cos, txt_sin, eps=self.eps)
@@ -239,6 +236,65 @@ class QwenTransformerBlock(torch.nn.Module):
         outs = [self.forward_sample(hidden[b], encoder[b], mod_img[b], mod_txt[b], rope)
                 for b in range(hidden.shape[0])]
         return torch.stack([o[0] for o in outs]), torch.stack([o[1] for o in outs])
+
+
+_TXT_QKV = ("attn.add_q_proj", "attn.add_k_proj", "attn.add_v_proj")
+
+
+def fused_rows(owner: torch.nn.Module, names: tuple[str, ...]) -> QuantizedLinear | None:
+    """Row concatenation of q6 linears of ``owner.linears`` that read the same
+    input (the text stream's q, k and v projections): one GEMM whose output
+    columns are theirs side by side.  At a few hundred tokens the three
+    3072-row GEMMs each fill a third of the GPU's tiles (and need split-K);
+    their concatenation fills it alone.  The members' tensors are rebound to
+    views of the concatenation, so no weight is held twice.  None when a
+    member carries a LoRA delta or the members differ in input or group size."""
+
+    lins = [owner.linears[n] for n in names]
+    if any(lin.lora is not None for lin in lins):
+        return None
+    if len({(lin.in_features, lin.group_size, lin.weight.device) for lin in lins}) != 1:
+        return None
+    cache = owner.__dict__.setdefault("_fused_rows", {})
+    hit = cache.get(names)
+    if hit is not None and all(lin.weight.data_ptr() == ptr for lin, ptr in zip(lins, hit[0])):
+        return hit[1]
+    w = torch.cat([lin.weight for lin in lins])
+    sc = torch.cat([lin.scales for lin in lins])
+    bi = torch.cat([lin.biases for lin in lins])
+    bias = torch.cat([lin.bias if lin.bias is not None else
+                      torch.zeros(lin.out_features, dtype=torch.bfloat16, device=w.device) for lin in lins])
+    fused = QuantizedLinear(w, sc, bi, bias, group_size=lins[0].group_size)
+    off = 0
+    for lin in lins:
+        n = lin.out_features
+        lin.weight, lin.scales, lin.biases = w[off:off + n], sc[off:off + n], bi[off:off + n]
+        if lin.bias is not None:
+            lin.bias = bias[off:off + n]
+        off += n
+    cache[names] = (tuple(lin.weight.data_ptr() for lin in lins), fused)
+    return fused
+
+
+def project_qkv(owner: torch.nn.Module, txt_in: torch.Tensor, img_in: torch.Tensor, q: torch.Tensor,
+                k: torch.Tensor, v: torch.Tensor) -> None:
+    """Joint [text; image] q, k, v projections written in place: the image
+    rows by three GEMMs, the text rows by one GEMM of the concatenated text
+    projections (``fused_rows``) copied into place."""
+
+    s_txt = txt_in.shape[0]
+    fused = fused_rows(owner, _TXT_QKV) if s_txt else None
+    if fused is not None:
+        t = ops.q6_linear(txt_in, fused.weight, fused.scales, fused.biases, fused.bias,
+                          group_size=fused.group_size)
+        width = q.shape[1]
+        for j, buf in enumerate((q, k, v)):
+            buf[:s_txt].copy_(t[:, j * width:(j + 1) * width])
+    for buf, img_name, txt_name in ((q, "attn.to_q", "attn.add_q_proj"), (k, "attn.to_k", "attn.add_k_proj"),
+                                    (v, "attn.to_v", "attn.add_v_proj")):
+        if fused is None:
+            owner._linear(txt_name, txt_in, out=buf[:s_txt])
+        owner._linear(img_name, img_in, out=buf[s_txt:])
 
 
 def block_flops(s_img: int, s_txt: int, dim: int) -> int:
@@ -309,7 +365,7 @@ class TensorParallelQwenBlock(torch.nn.Module):
     def _mlp(self, prefix: str, x: torch.Tensor, residual: torch.Tensor | None, gate: torch.Tensor,
              out: torch.Tensor) -> None:
         l1, l2 = self.linears[f"{prefix}.mlp_in"], self.linears[f"{prefix}.mlp_out"]
-        need = int(ops.mlp_workspace_bytes(x.shape[0], l1.out_features))
+        need = int(ops.mlp_workspace_bytes(x.shape[0], l1.out_features, l1.in_features))
         if self._ws is None or self._ws.numel() < need or self._ws.device != x.device:
             self._ws = torch.empty(need, dtype=torch.uint8, device=x.device)
         ops.q6_mlp(x, (l1.weight, l1.scales, l1.biases, l1.bias), (l2.weight, l2.scales, l2.biases, l2.bias),
@@ -333,10 +389,7 @@ class TensorParallelQwenBlock(torch.nn.Module):
         q = torch.empty((s, dl), dtype=torch.bfloat16, device=hidden.device)
         k = torch.empty_like(q)
         v = torch.empty_like(q)
-        for buf, img_name, txt_name in ((q, "attn.to_q", "attn.add_q_proj"), (k, "attn.to_k", "attn.add_k_proj"),
-                                        (v, "attn.to_v", "attn.add_v_proj")):
-            self._linear(txt_name, txt_in, out=buf[:s_txt])
-            self._linear(img_name, img_in, out=buf[s_txt:])
+        project_qkv(self, txt_in, img_in, q, k, v)
         qk_rmsnorm_rope_(q[:s_txt], self.norms["attn.norm_added_q"], txt_cos, txt_sin, eps=self.eps)
         qk_rmsnorm_rope_(q[s_txt:], self.norms["attn.norm_q"], img_cos, img_sin, eps=self.eps)
         qk_rmsnorm_rope_(k[:s_txt], self.norms["attn.norm_added_k"], txt_cos, txt_sin, eps=self.eps)

@@ -147,10 +147,20 @@ int q6_mlp_bf16(const uint16_t* x, const uint32_t* w1, const uint16_t* scales1, 
     if (!aligned(workspace, 16)) return Q6_ERR_ALIGNMENT;
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     uint16_t* hidden = static_cast<uint16_t*>(workspace);
+    // Workspace past the hidden activations (from a 256-byte boundary) is the
+    // linears' split-K space: with q6_linear_tc_workspace_bytes of a linear
+    // there, a few-hundred-token fc2 (K = H) splits K instead of leaving SMs idle.
+    const size_t split_off = (q6_mlp_workspace_bytes(M, H) + 255) & ~size_t(255);
+    void* split_ws = workspace_bytes > split_off ? static_cast<char*>(workspace) + split_off : nullptr;
+    const size_t split_bytes = workspace_bytes > split_off ? workspace_bytes - split_off : 0;
     q6::LinearArgs a1{x, w1, scales1, qbiases1, bias1, nullptr, nullptr, hidden, M, H, D, group_size, Q6_EPI_GELU};
+    a1.workspace = split_ws;
+    a1.workspace_bytes = split_bytes;
     st = run_linear(a1, Q6_PATH_AUTO, s);
     if (st != Q6_OK) return st;
     q6::LinearArgs a2{hidden, w2, scales2, qbiases2, bias2, residual, gate, y, M, D, H, group_size, Q6_EPI_NONE};
+    a2.workspace = split_ws;
+    a2.workspace_bytes = split_bytes;
     return run_linear(a2, Q6_PATH_AUTO, s);
 }
 

@@ -177,10 +177,19 @@ def q6_linear(
     return y.reshape(leading + (n,))
 
 
-def mlp_workspace_bytes(m: int, h: int) -> int:
-    """Bytes of device workspace q6_mlp needs for m tokens and hidden width h."""
+def mlp_workspace_bytes(m: int, h: int, d: int | None = None) -> int:
+    """Bytes of device workspace q6_mlp needs for m tokens and hidden width h
+    (the bf16 hidden activations).  With the model width d it also counts the
+    split-K space of the two linears, placed from the next 256-byte boundary,
+    which lets a few-hundred-token MLP spread its K loop over idle SMs."""
 
-    return int(_lib.lib().q6_mlp_workspace_bytes(int(m), int(h)))
+    base = int(_lib.lib().q6_mlp_workspace_bytes(int(m), int(h)))
+    if d is None:
+        return base
+    lib = _lib.lib()
+    split = max(int(lib.q6_linear_tc_workspace_bytes(int(m), int(h), int(d))),
+                int(lib.q6_linear_tc_workspace_bytes(int(m), int(d), int(h))))
+    return (base + 255) // 256 * 256 + split if split else base
 
 
 def q6_mlp(
@@ -206,9 +215,10 @@ def q6_mlp(
     leading = tuple(x.shape[:-1])
     xb = x.reshape(-1, d).to(torch.bfloat16).contiguous()
     m = int(xb.shape[0])
-    need = int(_lib.lib().q6_mlp_workspace_bytes(m, h))
-    if workspace is None or workspace.numel() * workspace.element_size() < need:
-        workspace = torch.empty(need, dtype=torch.uint8, device=dev)
+    # a caller's workspace needs the hidden activations at least; one made here
+    # also holds the linears' split-K space
+    if workspace is None or workspace.numel() * workspace.element_size() < mlp_workspace_bytes(m, h):
+        workspace = torch.empty(mlp_workspace_bytes(m, h, d), dtype=torch.uint8, device=dev)
     y = out if out is not None else torch.empty((m, d), dtype=torch.bfloat16, device=dev)
     res_t = None if residual is None else residual.reshape(m, d).to(torch.bfloat16).contiguous()
     gate_t = _bf16_vec(gate, d, "gate")

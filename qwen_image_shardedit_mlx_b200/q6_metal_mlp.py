@@ -287,7 +287,7 @@ class QwenFeedForward(torch.nn.Module):
             self._stream_bufs = (
                 [torch.empty((m, d), dtype=torch.bfloat16, device=dev) for _ in range(2)],
                 [torch.empty((m, d), dtype=torch.bfloat16, device=dev) for _ in range(2)],
-                torch.empty(int(ops.mlp_workspace_bytes(m, h)), dtype=torch.uint8, device=dev),
+                torch.empty(int(ops.mlp_workspace_bytes(m, h, d)), dtype=torch.uint8, device=dev),
                 [torch.cuda.Stream(dev) for _ in range(3)],
             )
             self._stream_key = key

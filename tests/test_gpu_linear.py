@@ -289,6 +289,31 @@ def test_mlp_vs_oracle_fused_order():
     assert float(np.abs(f32(y) - eager).max()) < 0.05
 
 
+def test_mlp_split_k_workspace():
+    """A text-stream-sized MLP (few hundred tokens, fc2 with K = H): the fused
+    MLP's workspace past the hidden activations lets both linears split K;
+    with the hidden activations only, they do not.  Both agree with the oracle."""
+
+    rng = np.random.default_rng(22)
+    m, d, h = 256, 512, 4096
+    assert ops.mlp_workspace_bytes(m, h, d) > ops.mlp_workspace_bytes(m, h)  # split-K space planned
+    fc1 = random_weights(rng, h, d, 64)
+    fc2 = random_weights(rng, d, h, 64)
+    x = random_bf16(rng, (m, d))
+    residual = random_bf16(rng, (m, d))
+    gate = random_bf16(rng, (d,), 0.5)
+    args = (from_bits(x), weights_to_torch(fc1), weights_to_torch(fc2))
+    kw = dict(group_size=64, residual=from_bits(residual), gate=from_bits(gate))
+    y_split = ops.q6_mlp(*args, **kw)
+    base_ws = torch.empty(ops.mlp_workspace_bytes(m, h), dtype=torch.uint8, device="cuda")
+    y_plain = ops.q6_mlp(*args, workspace=base_ws, **kw)
+    torch.cuda.synchronize()
+    hid = oracle.round_bf16(oracle.linear(oracle.bf16_bits_to_f32(x), fc1, apply_gelu=True))
+    ref = oracle.linear(hid, fc2, residual=oracle.bf16_bits_to_f32(residual), gate=oracle.bf16_bits_to_f32(gate))
+    assert_close(f32(y_split), ref, what="mlp split-K workspace")
+    assert_close(f32(y_plain), ref, what="mlp hidden-only workspace")
+
+
 def test_mlp_image_ff_full_size_rows_sample():
     """Config-2 shapes (3456 tokens, 3072 -> 12288 -> 3072): full run on the GPU,
     oracle on a sample of rows (each output row depends only on its input row)."""
