@@ -896,6 +896,62 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restr
     }
 }
 
+// The same sum and epilogue, eight consecutive outputs per thread: 16-byte
+// loads of the partials, bias, gate and residual and one 16-byte store
+// (N % 8 == 0, every operand 16-byte aligned).  Each output is summed in split
+// order exactly as above, so the results are bitwise those of the scalar kernel.
+__device__ __forceinline__ void bf16x8_to_f32(uint4 w, float (&f)[8]) {
+    const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        f[2 * j] = __uint_as_float(u[j] << 16);
+        f[2 * j + 1] = __uint_as_float(u[j] & 0xFFFF0000u);
+    }
+}
+
+__global__ void __launch_bounds__(256) splitk_reduce8_kernel(const float* __restrict__ partial, int splits, int64_t M,
+                                                            int64_t N, const uint16_t* bias, const uint16_t* gate,
+                                                            const uint16_t* residual, int flags, uint16_t* y) {
+    pdl_launch_dependents();
+    pdl_wait();  // the partials of the kernel before
+    const int64_t total = M * N;
+    const int64_t groups = total / 8;
+    for (int64_t gi = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; gi < groups;
+         gi += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t i = gi * 8;
+        const int64_t n = i % N;
+        float v[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+        for (int s = 0; s < splits; ++s) {
+            const float4* src = reinterpret_cast<const float4*>(partial + s * total + i);
+            const float4 a = src[0], b = src[1];
+            v[0] += a.x; v[1] += a.y; v[2] += a.z; v[3] += a.w;
+            v[4] += b.x; v[5] += b.y; v[6] += b.z; v[7] += b.w;
+        }
+        float t[8];
+        if (bias) {
+            bf16x8_to_f32(*reinterpret_cast<const uint4*>(bias + n), t);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[j] += t[j];
+        }
+        if (flags & Q6_EPI_GELU) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[j] = gelu_tanh(v[j]);
+        }
+        if (gate) {
+            bf16x8_to_f32(*reinterpret_cast<const uint4*>(gate + n), t);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[j] *= t[j];
+        }
+        if (residual) {
+            bf16x8_to_f32(*reinterpret_cast<const uint4*>(residual + i), t);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[j] += t[j];
+        }
+        *reinterpret_cast<uint4*>(y + i) = make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]),
+                                                      pack_bf16x2(v[4], v[5]), pack_bf16x2(v[6], v[7]));
+    }
+}
+
 // Launches a CTA-pair grid: clusters of two along x, with programmatic
 // dependent launch when it is enabled.
 template <typename... KArgs, typename... Args>
@@ -1004,6 +1060,17 @@ int launch_tc(const LinearArgs& a, cudaStream_t stream) {
     }
     if (split) {
         const int64_t total = a.M * a.N;
+        const uintptr_t al = reinterpret_cast<uintptr_t>(a.y) | reinterpret_cast<uintptr_t>(a.bias) |
+                             reinterpret_cast<uintptr_t>(a.gate) | reinterpret_cast<uintptr_t>(a.residual);
+        if (a.N % 8 == 0 && al % 16 == 0) {
+            const int blocks =
+                static_cast<int>(std::min<int64_t>((total / 8 + 255) / 256, int64_t(device_sm_count()) * 8));
+            if (launch_pdl(splitk_reduce8_kernel, dim3(blocks), dim3(256), 0, stream,
+                           static_cast<const float*>(p.partial), p.ksplit, a.M, a.N, a.bias, a.gate, a.residual,
+                           a.flags, static_cast<uint16_t*>(a.y)) != cudaSuccess)
+                return Q6_ERR_CUDA;
+            return Q6_OK;
+        }
         const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, int64_t(device_sm_count()) * 8));
         if (launch_pdl(splitk_reduce_kernel, dim3(blocks), dim3(256), 0, stream,
                        static_cast<const float*>(p.partial), p.ksplit, a.M, a.N, a.bias, a.gate, a.residual, a.flags,

@@ -456,3 +456,28 @@ def test_cta_pair_mode(m, n, k, gs, epi, tile, r, monkeypatch):
         gate=None if gate is None else oracle.bf16_bits_to_f32(gate), lora=lora_ref,
     )
     assert_close(f32(outs["1"]), ref, what=f"pair {m}x{n}x{k} gs{gs} {epi} nt{tile} r{r}")
+
+
+def test_split_k_reduce_vector_matches_scalar(monkeypatch):
+    """The split-K reduce takes 16-byte loads and stores when N % 8 == 0 and
+    every operand is 16-byte aligned; an output two bytes off that alignment
+    takes the one-element-per-thread kernel.  Same sums in the same order:
+    bitwise equal outputs."""
+
+    monkeypatch.setenv("Q6_TC_KSPLIT", "3")
+    rng = np.random.default_rng(31)
+    m, n, k = 200, 512, 3072
+    w = random_weights(rng, n, k, 64)
+    wt, st, bt, bias = weights_to_torch(w)
+    x = from_bits(random_bf16(rng, (m, k)))
+    residual = from_bits(random_bf16(rng, (m, n)))
+    gate = from_bits(random_bf16(rng, (n,), 0.5))
+    outs = []
+    for off in (0, 1):
+        buf = torch.full((m * n + 8,), float("nan"), dtype=torch.bfloat16, device="cuda")
+        out = buf[off:off + m * n].view(m, n)
+        outs.append(ops.q6_linear(x, wt, st, bt, bias, group_size=64, apply_gelu=True, residual=residual,
+                                  gate=gate, path="tensor", out=out))
+    torch.cuda.synchronize()
+    assert bool(torch.isfinite(outs[0]).all())
+    assert torch.equal(outs[0], outs[1])
