@@ -388,11 +388,13 @@ __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
         }
     } else if (warp == 1) {
         // ------------------------------------------------ MMA issuer
-        // The issuing thread blocks for tens of cycles in every tcgen05.mma and
-        // tcgen05.commit, so its loop carries nothing else it can avoid: one
-        // wait, one fence, eight MMAs whose operand addresses are immediate
-        // offsets from per-stage bases, one commit.
-        if (lane == 0 && leader) {
+        // The whole warp runs the loop, so every operand is warp-uniform and
+        // stays in uniform registers; one elected lane (the same one each time,
+        // which its commits require) issues each tcgen05.mma and commit.  With
+        // the loop on lane 0 alone, each MMA cost ~100 cycles of issue and each
+        // stage ~380 cycles between its commit and the next stage's first MMA,
+        // whatever the MMA's size.
+        if (leader) {
             const uint64_t desc_base = sdesc_kmajor_sw128(smem_u32(x_smem));
             const uint32_t desc_lo = static_cast<uint32_t>(desc_base);
             const uint32_t desc_hi = static_cast<uint32_t>(desc_base >> 32);
@@ -403,12 +405,12 @@ __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
             bool ok = true;
             for (int it = it0; it < p.num_items && ok; it += istep) {
                 const Item I = item_at(p, it);
-                if (!mbar_wait(smem_u32(acc_empty + acc), accph ^ 1u, abort_flag, 2)) break;
+                if (!warp_wait(smem_u32(acc_empty + acc), accph ^ 1u, abort_flag, 2)) break;
                 const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * NT);
                 for (int l = 0; l < I.stages(); ++l, ++g) {
                     const int ks = I.ks_of(l, p.k_stages);
                     const uint32_t rs = g % kRing;
-                    if (!mbar_wait(smem_u32(ready + rs), (g / kRing) & 1u, abort_flag, 3)) {
+                    if (!warp_wait(smem_u32(ready + rs), (g / kRing) & 1u, abort_flag, 3)) {
                         ok = false;
                         break;
                     }
@@ -420,12 +422,14 @@ __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
                     // and TMEM A columns 8 kk .. 8 kk + 7.
                     auto issue = [&](int kk) {
                         const uint32_t off = static_cast<uint32_t>((kk / 4) * (C::kXBoxBytes >> 4) + (kk % 4) * 2);
-                        if constexpr (kPair)
-                            mma_bf16_ts_pair(d_tmem, a_tmem + kk * 8, make_desc(lo + off, desc_hi), C::kIdesc,
-                                             kk == 0 ? first : 1u);
-                        else
-                            mma_bf16_ts(d_tmem, a_tmem + kk * 8, make_desc(lo + off, desc_hi), C::kIdesc,
-                                        kk == 0 ? first : 1u);
+                        if (elect_one()) {
+                            if constexpr (kPair)
+                                mma_bf16_ts_pair(d_tmem, a_tmem + kk * 8, make_desc(lo + off, desc_hi), C::kIdesc,
+                                                 kk == 0 ? first : 1u);
+                            else
+                                mma_bf16_ts(d_tmem, a_tmem + kk * 8, make_desc(lo + off, desc_hi), C::kIdesc,
+                                            kk == 0 ? first : 1u);
+                        }
                     };
                     if (ks + 1 < p.k_stages || (ks + 1 == p.k_stages && p.last_ksteps == kBK / 16)) {
 #pragma unroll
@@ -436,28 +440,37 @@ __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
                     } else {  // LoRA stage: r / 32 K-steps (the second box once r > 128)
                         for (int kk = 0; kk < p.lora_ksteps; ++kk) issue(kk);
                     }
-                    if constexpr (kPair)
-                        tc_commit_pair(smem_u32(done + rs), 3);
-                    else
-                        tc_commit(smem_u32(done + rs));
+                    if (elect_one()) {
+                        if constexpr (kPair)
+                            tc_commit_pair(smem_u32(done + rs), 3);
+                        else
+                            tc_commit(smem_u32(done + rs));
+                    }
+                    __syncwarp();
                     if (++xs == C::kXStages) xs = 0;
                 }
                 if (!ok) break;
-                if constexpr (kPair)
-                    tc_commit_pair(smem_u32(acc_full + acc), 3);
-                else
-                    tc_commit(smem_u32(acc_full + acc));
+                if (elect_one()) {
+                    if constexpr (kPair)
+                        tc_commit_pair(smem_u32(acc_full + acc), 3);
+                    else
+                        tc_commit(smem_u32(acc_full + acc));
+                }
+                __syncwarp();
                 if (++acc == C::kNAcc) {
                     acc = 0;
                     accph ^= 1u;
                 }
             }
             // All issued MMAs complete before TMEM may be released.
-            if constexpr (kPair)
-                tc_commit_pair(smem_u32(drain), 1);
-            else
-                tc_commit(smem_u32(drain));
-            mbar_wait_drain(smem_u32(drain), 0);
+            if (elect_one()) {
+                if constexpr (kPair)
+                    tc_commit_pair(smem_u32(drain), 1);
+                else
+                    tc_commit(smem_u32(drain));
+                mbar_wait_drain(smem_u32(drain), 0);
+            }
+            __syncwarp();
         }
     } else if (warp >= 4 && warp < 8) {
         // ------------------------------------------------ epilogue
