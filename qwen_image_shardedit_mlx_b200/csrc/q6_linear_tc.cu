@@ -390,7 +390,7 @@ __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
         // ------------------------------------------------ MMA issuer
         // The whole warp runs the loop, so every operand is warp-uniform and
         // stays in uniform registers; one elected lane (the same one each time,
-        // which its commits require) issues each tcgen05.mma and commit.  With
+        // which its commits require) issues each stage's tcgen05.mma and commit.  With
         // the loop on lane 0 alone, each MMA cost ~100 cycles of issue and each
         // stage ~380 cycles between its commit and the next stage's first MMA,
         // whatever the MMA's size.
@@ -422,25 +422,23 @@ __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
                     // and TMEM A columns 8 kk .. 8 kk + 7.
                     auto issue = [&](int kk) {
                         const uint32_t off = static_cast<uint32_t>((kk / 4) * (C::kXBoxBytes >> 4) + (kk % 4) * 2);
-                        if (elect_one()) {
-                            if constexpr (kPair)
-                                mma_bf16_ts_pair(d_tmem, a_tmem + kk * 8, make_desc(lo + off, desc_hi), C::kIdesc,
-                                                 kk == 0 ? first : 1u);
-                            else
-                                mma_bf16_ts(d_tmem, a_tmem + kk * 8, make_desc(lo + off, desc_hi), C::kIdesc,
-                                            kk == 0 ? first : 1u);
-                        }
+                        if constexpr (kPair)
+                            mma_bf16_ts_pair(d_tmem, a_tmem + kk * 8, make_desc(lo + off, desc_hi), C::kIdesc,
+                                             kk == 0 ? first : 1u);
+                        else
+                            mma_bf16_ts(d_tmem, a_tmem + kk * 8, make_desc(lo + off, desc_hi), C::kIdesc,
+                                        kk == 0 ? first : 1u);
                     };
-                    if (ks + 1 < p.k_stages || (ks + 1 == p.k_stages && p.last_ksteps == kBK / 16)) {
+                    if (elect_one()) {  // one lane issues the stage's MMAs and its commit
+                        if (ks + 1 < p.k_stages || (ks + 1 == p.k_stages && p.last_ksteps == kBK / 16)) {
 #pragma unroll
-                        for (int kk = 0; kk < kBK / 16; ++kk) issue(kk);
-                    } else if (ks < p.k_stages) {  // K % 128 == 64 tail: the first box only
+                            for (int kk = 0; kk < kBK / 16; ++kk) issue(kk);
+                        } else if (ks < p.k_stages) {  // K % 128 == 64 tail: the first box only
 #pragma unroll
-                        for (int kk = 0; kk < kBK / 32; ++kk) issue(kk);
-                    } else {  // LoRA stage: r / 32 K-steps (the second box once r > 128)
-                        for (int kk = 0; kk < p.lora_ksteps; ++kk) issue(kk);
-                    }
-                    if (elect_one()) {
+                            for (int kk = 0; kk < kBK / 32; ++kk) issue(kk);
+                        } else {  // LoRA stage: r / 32 K-steps (the second box once r > 128)
+                            for (int kk = 0; kk < p.lora_ksteps; ++kk) issue(kk);
+                        }
                         if constexpr (kPair)
                             tc_commit_pair(smem_u32(done + rs), 3);
                         else
