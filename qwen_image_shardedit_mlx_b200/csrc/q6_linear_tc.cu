@@ -1178,12 +1178,17 @@ int choose_token_tile(int64_t M, int64_t N) {
 
 int launch_linear_tc(const LinearArgs& a, int token_tile, cudaStream_t stream) {
     if (pair_mode(a, token_tile)) {
+        int st = Q6_ERR_UNSUPPORTED;
         switch (token_tile) {
-            case 256: return launch_tc_sb<256, true>(a, stream);
-            case 192: return launch_tc_sb<192, true>(a, stream);
-            case 128: return launch_tc_sb<128, true>(a, stream);
+            case 256: st = launch_tc_sb<256, true>(a, stream); break;
+            case 192: st = launch_tc_sb<192, true>(a, stream); break;
+            case 128: st = launch_tc_sb<128, true>(a, stream); break;
             default: break;
         }
+        if (st == Q6_OK) return st;
+        // A device or context that cannot co-schedule two-CTA clusters refuses
+        // the launch itself (nothing ran): clear that error and run one CTA per tile.
+        if (st == Q6_ERR_CUDA) (void)cudaGetLastError();
     }
     switch (token_tile) {
         case 256: return launch_tc_sb<256>(a, stream);
