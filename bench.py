@@ -20,7 +20,8 @@ linears q6, joint attention), tensor-parallel over the ranks when N > 1.
 
 --impl reference times the reference's own q6 kernel source
 (shardedit_mlx/q6_metal_mlp.py SOURCE_QMM_T, compiled for the host by
-oracle/build_ref.py) on the host cores, on a bounded token sample.
+oracle/build_ref.py) on the host cores, on full 3456-token steps of the same
+workload (as many as fit about 110 s, at least one).
 """
 
 from __future__ import annotations
@@ -53,6 +54,7 @@ def parse_args() -> argparse.Namespace:
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the host-core baseline leg")
     ap.add_argument("--no-gemv", action="store_true", help="skip the skinny-M GEMV side measurement")
     ap.add_argument("--no-block", action="store_true", help="skip the full MMDiT block measurement")
+    ap.add_argument("--no-sweep", action="store_true", help="skip the q6 linear shape / M / group-size sweep")
     return ap.parse_args()
 
 
@@ -222,6 +224,21 @@ def make_weights(seed: int, device):
     return (*w1, b1), (*w2, b2)
 
 
+def workload_config(world: int) -> dict:
+    """The workload both arms run (the reference arm on one host, world 1)."""
+
+    return {
+        "workload": WORKLOAD,
+        "tokens_per_gpu": TOKENS,
+        "dim": DIM,
+        "hidden": HIDDEN,
+        "group_size": GROUP,
+        "global_batch_tokens": TOKENS * world,
+        "parallelism": f"token-sharded x{world}, weights replicated, no data-path collective",
+        "l2": "no flush: per-step working set ~190 MB (x 21 MB, codes+scales 61 MB, hidden 85 MB, y 21 MB) > 126 MB L2",
+    }
+
+
 def run_ours(args, world: int, rank: int, local: int) -> dict | None:
     import torch
 
@@ -314,6 +331,11 @@ def run_ours(args, world: int, rank: int, local: int) -> dict | None:
     if rank == 0 and not args.no_gemv:
         gemv = measure_gemv(dev, peaks)
 
+    # ---- config 1 and the shape / M / group-size sweep with the LoRA comparison, rank 0 only
+    sweep = None
+    if rank == 0 and not args.no_sweep:
+        sweep = measure_sweep(dev, peaks)
+
     if rank != 0:
         return None
     value = FLOP_PER_STEP * steps * world / (total_ms * 1e-3) / 1e12
@@ -334,17 +356,7 @@ def run_ours(args, world: int, rank: int, local: int) -> dict | None:
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights quantised to MLX affine q6 gs64)",
-        "config": {
-            "workload": WORKLOAD,
-            "tokens_per_gpu": TOKENS,
-            "dim": DIM,
-            "hidden": HIDDEN,
-            "group_size": GROUP,
-            "global_batch_tokens": TOKENS * world,
-            "parallelism": f"token-sharded x{world}, weights replicated, no data-path collective",
-            "l2": "no flush: per-step working set ~190 MB (x 21 MB, codes+scales 61 MB, hidden 85 MB, y 21 MB) > 126 MB L2",
-            "token_tile": int(_lib.lib().q6_tensor_token_tile(TOKENS, HIDDEN)),
-        },
+        "config": workload_config(world),
         "fc1_ms": round(fc1_ms, 4),
         "fc2_ms": round(fc2_ms, 4),
         "pct_of_bf16_peak": round(100.0 * value / world / peaks["bf16_tflops"], 2),
@@ -368,10 +380,14 @@ def run_ours(args, world: int, rank: int, local: int) -> dict | None:
             "serial_api": "QwenFeedForward(x) one call at a time: copy in, ff, copy out on one stream",
         },
         "gpu_launches": 2 * steps,
+        "token_tile": int(_lib.lib().q6_tensor_token_tile(TOKENS, HIDDEN)),
         "clocks": clock,
     }
     if gemv is not None:
         line["gemv"] = gemv
+    if sweep is not None:
+        line["c1"] = sweep.pop("c1")
+        line["sweep"] = sweep
     if block is not None:
         line["block"] = block
     if not args.no_cpu_baseline:
@@ -522,6 +538,145 @@ def measure_gemv(dev, peaks) -> dict:
     return out
 
 
+SWEEP_SHAPES = [(3072, 3072), (12288, 3072), (3072, 12288), (18432, 3072)]  # (N, K): q6_linear_profile.py:144-159
+SWEEP_M = (1, 16, 128, 512, 1728, 3456, 8192)
+SWEEP_GS = (32, 64, 128)
+
+
+def _time_launches(launch, count: int, reps: int = 5) -> float:
+    """Mean device microseconds per launch of ``launch(i)`` for i in 0..count-1,
+    replayed from a CUDA graph of back-to-back launches (no host cost)."""
+
+    import torch
+
+    for i in range(count):
+        launch(i)
+    torch.cuda.synchronize()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=side):
+        for i in range(count):
+            launch(i)
+    torch.cuda.synchronize()
+    graph.replay()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    del graph
+    return e0.elapsed_time(e1) * 1e3 / (reps * count)
+
+
+def measure_sweep(dev, peaks) -> dict:
+    """Config 1 (x [1728, 3072] -> 12288, gs64) and the config-4 grid: the
+    block's four projection shapes x M in {1, 16, 128, 512, 1728, 3456, 8192}
+    x group sizes {32, 64, 128}, no bias (benchmarks/benchmark_qwen_gemm.py:119-200
+    times the same grid).  Each point is timed from a CUDA graph of
+    back-to-back launches; below 512 tokens the launches rotate over weight
+    copies whose total exceeds L2 four times, so the weights stream from HBM.
+    A point is HBM-bound when its FLOP per algorithmic byte is below the
+    measured ridge (bf16 peak / HBM bandwidth), else tensor-bound; ``frac`` is
+    against that roofline.  Plus rank-64 LoRA at config 1 and image-FF fc1:
+    plain q6, unfused (pre-pass, q6, then a separate s (xa @ B) GEMM added to
+    y) and fused into the q6 tile."""
+
+    import torch
+
+    from qwen_image_shardedit_mlx_b200 import ops
+    from qwen_image_shardedit_mlx_b200.quantize import random_q6
+
+    g = torch.Generator(device=dev).manual_seed(4096)
+    ridge = peaks["bf16_tflops"] * 1e12 / (peaks["hbm_gbs"] * 1e9)
+    xs = {m: torch.randn((m, 12288), generator=g, device=dev).to(torch.bfloat16) for m in SWEEP_M}
+    points = []
+    for (n, k) in SWEEP_SHAPES:
+        for gs in SWEEP_GS:
+            w0 = random_q6(n, k, group_size=gs, generator=g, device=dev)
+            per_copy = n * k * 6 // 8 + 2 * 2 * n * (k // gs)
+            count = max(2, -(-4 * L2_BYTES // per_copy))
+            copies = [w0] + [tuple(t.clone() for t in w0) for _ in range(count - 1)]
+            for m in SWEEP_M:
+                x = xs[m][:, :k].contiguous()
+                y = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
+                rot = count if m < 512 else 1
+
+                def launch(i, x=x, y=y, gs=gs, rot=rot):
+                    w, s, b = copies[i % rot]
+                    ops.q6_linear(x, w, s, b, group_size=gs, out=y)
+
+                us = _time_launches(launch, max(rot, 8) if m < 512 else 8)
+                flop = 2.0 * m * n * k
+                nbytes = per_copy + 2 * m * (k + n)
+                bound = "hbm" if flop / nbytes < ridge else "tensor"
+                tflops = flop / (us * 1e-6) / 1e12
+                gbs = nbytes / (us * 1e-6) / 1e9
+                frac = gbs / peaks["hbm_gbs"] if bound == "hbm" else tflops / peaks["bf16_tflops"]
+                points.append({"n": n, "k": k, "m": m, "gs": gs, "us": round(us, 2), "TFLOP/s": round(tflops, 2),
+                               "GB/s": round(gbs, 1), "bound": bound, "frac": round(frac, 4),
+                               "path": ops.last_path()})
+            del copies, w0
+            torch.cuda.empty_cache()
+
+    c1 = next(p for p in points if (p["n"], p["k"], p["m"], p["gs"]) == (12288, 3072, 1728, 64))
+
+    # rank-64 LoRA: plain vs unfused vs fused
+    lora = {}
+    for name, (m, n, k, gelu) in {"config1": (1728, 12288, 3072, False), "image_ff_fc1": (3456, 12288, 3072, True)}.items():
+        w, s, b = random_q6(n, k, group_size=64, generator=g, device=dev)
+        bias = (torch.randn(n, generator=g, device=dev) * 0.01).to(torch.bfloat16)
+        a_l = (torch.randn((k, 64), generator=g, device=dev) * 0.01).to(torch.bfloat16)
+        b_l = (torch.randn((64, n), generator=g, device=dev) * 0.01).to(torch.bfloat16)
+        x = xs[m][:, :k].contiguous()
+        y = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
+        xa = torch.empty((m, 64), dtype=torch.bfloat16, device=dev)
+
+        def plain(i, x=x, w=w, s=s, b=b, bias=bias, y=y, gelu=gelu):
+            ops.q6_linear(x, w, s, b, bias, group_size=64, apply_gelu=gelu, out=y)
+
+        def unfused(i, x=x, w=w, s=s, b=b, bias=bias, y=y, gelu=gelu, a_l=a_l, b_l=b_l, xa=xa):
+            # the reference's order: y = act(q6(x) + bias + s (x A) B) needs the delta before the
+            # activation, so without fusion the q6 GEMM runs without its epilogue activation
+            ops.lora_xa(x, a_l, out=xa)
+            ops.q6_linear(x, w, s, b, group_size=64, out=y)
+            y.addmm_(xa, b_l, alpha=1.0)
+            if gelu:
+                y.copy_(torch.nn.functional.gelu(y + bias, approximate="tanh"))
+            else:
+                y.add_(bias)
+
+        def fused(i, x=x, w=w, s=s, b=b, bias=bias, y=y, gelu=gelu, a_l=a_l, b_l=b_l):
+            ops.q6_linear(x, w, s, b, bias, group_size=64, apply_gelu=gelu, lora=(a_l, b_l, 1.0), out=y)
+
+        t_plain = _time_launches(plain, 8)
+        t_unf = _time_launches(unfused, 8)
+        t_fused = _time_launches(fused, 8)
+        lora[name] = {"m": m, "n": n, "k": k, "rank": 64, "gelu": gelu, "plain_us": round(t_plain, 2),
+                      "unfused_us": round(t_unf, 2), "fused_us": round(t_fused, 2),
+                      "fused_overhead_pct": round(100.0 * (t_fused / t_plain - 1.0), 2),
+                      "unfused_overhead_pct": round(100.0 * (t_unf / t_plain - 1.0), 2)}
+    tensor_pts = [p for p in points if p["bound"] == "tensor"]
+    hbm_pts = [p for p in points if p["bound"] == "hbm"]
+    return {
+        "c1": {**c1, "workload": "config 1: x [1728, 3072] bf16 -> q6 gs64 3072->12288, no bias",
+               "roofline_peak": peaks["bf16_tflops"]},
+        "points": points,
+        "lora_rank64": lora,
+        "summary": {
+            "tensor_points": len(tensor_pts), "hbm_points": len(hbm_pts),
+            "tensor_frac_median": round(statistics.median(p["frac"] for p in tensor_pts), 4) if tensor_pts else None,
+            "hbm_frac_median": round(statistics.median(p["frac"] for p in hbm_pts), 4) if hbm_pts else None,
+            "ridge_flop_per_byte": round(ridge, 1),
+        },
+        "note": "device time per launch from CUDA graphs of back-to-back launches; weights rotate over copies "
+                "totalling > 4x L2 below 512 tokens; no bias; frac against the measured peak of the point's bound",
+    }
+
+
 # ------------------------------------------------------------ host baselines
 
 
@@ -542,12 +697,16 @@ def cpu_baseline_port(budget_s: float = 12.0) -> dict:
 
 
 def run_reference(args, world: int, rank: int) -> dict | None:
+    """The reference's own q6 kernel (SOURCE_QMM_T compiled for the host) on
+    full 3456-token steps of the same MLP workload, rank 0 only."""
+
     if rank != 0:
         return None
     from oracle.cpu_port import time_reference_kernel_mlp
 
-    res = time_reference_kernel_mlp(DIM, HIDDEN, GROUP, steps=args.steps, warmup=min(args.warmup, 1))
+    res = time_reference_kernel_mlp(DIM, HIDDEN, GROUP, tokens=TOKENS, steps=args.steps)
     value = res["tflops"]
+    seconds_per_step = FLOP_PER_STEP / (value * 1e12)
     return {
         "impl": "reference",
         "metric": METRIC,
@@ -556,12 +715,13 @@ def run_reference(args, world: int, rank: int) -> dict | None:
         "n_gpus": world,
         "steps": res["steps"],
         "warmup": args.warmup,
+        "ms_per_step": round(seconds_per_step * 1e3, 1),
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
         "dtype": "bf16",
-        "data": "synthetic",
-        "config": {"workload": WORKLOAD, "tokens_per_step_sample": res["tokens"]},
+        "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights quantised to MLX affine q6 gs64)",
+        "config": workload_config(1),
         "cpu_baseline": {"value": round(value, 6), "unit": "TFLOP/s", "cores": res["cores"], "kind": res["kind"],
                          "sample": res["sample"]},
         "e2e": {"value": round(value, 6), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},

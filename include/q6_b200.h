@@ -50,7 +50,17 @@ enum q6_status {
 /* Epilogue flags (bit set). */
 enum q6_epilogue {
     Q6_EPI_NONE = 0,
-    Q6_EPI_GELU = 1 /* GELU-tanh after the bias (mlx nn.gelu_approx) */
+    Q6_EPI_GELU = 1,        /* GELU-tanh after the bias (mlx nn.gelu_approx), hardware tanh.approx */
+    Q6_EPI_GELU_PRECISE = 2 /* the same GELU with the IEEE-accurate tanhf the reference kernel
+                               calls (metal::precise::tanh, q6_metal_mlp.py:21-26); implies GELU */
+};
+
+/* Site codes a kernel writes into the device error word when one of its
+   bounded waits gives up (q6_get_device_error). */
+enum q6_error_site {
+    Q6_SITE_GEMM_MIN = 1,       /* 1..11: tcgen05 GEMM and GEMV pipeline barriers */
+    Q6_SITE_GEMM_MAX = 11,
+    Q6_SITE_SELFTEST = 64       /* q6_selftest_bounded_wait */
 };
 
 /* Kernel path for q6_linear_bf16 (Q6_PATH_AUTO picks one). */
@@ -70,7 +80,8 @@ Q6_API int q6_dequantize_bf16(const uint32_t* w, const uint16_t* scales, const u
 
 /*
  * y = epi(x @ dequant(W)^T)      x bf16 [M, K], y bf16 [M, N]
- * epi: + bias[n] (if bias), GELU (if flags & Q6_EPI_GELU), then
+ * epi: + bias[n] (if bias), GELU (if flags & Q6_EPI_GELU, or with an accurate tanh if
+ *      flags & Q6_EPI_GELU_PRECISE), then
  *      y = residual[m,n] + gate[n] * value  (each term only if its pointer is non-null).
  * LoRA (lora_xa bf16 [M, r] = x @ A computed by the caller, lora_b bf16 [r, N],
  *      both non-null, r a multiple of 32 in [32, 256]): the value gains
@@ -91,10 +102,16 @@ Q6_API int q6_linear_bf16(const uint16_t* x, const uint32_t* w, const uint16_t* 
                    int group_size, int flags, int path, void* workspace, size_t workspace_bytes,
                    q6_stream_t stream);
 
-/* Lower bound of the workspace any q6_linear_bf16 call needs (0: every path
-   runs without one); see q6_linear_tc_workspace_bytes for the size that lets
-   the tensor-core path split K. */
-Q6_API size_t q6_linear_workspace_bytes(int64_t M, int lora_rank);
+/*
+ * LoRA pre-pass xa = x @ A (bf16 in, fp32 accumulation, bf16 out) for the
+ * fused LoRA delta of q6_linear_bf16:  x bf16 [M, K], A bf16 [K, r] (row-major,
+ * the adapter's down projection as the reference stores it), xa bf16 [M, r].
+ * r a multiple of 32 in [32, 256], K a multiple of 16, 16-byte aligned
+ * pointers.  Replaces the `x @ lora_A` half of the LoRA-additive linear
+ * (dense_img_ff_window.py:48-60).  HBM-bound: each x row is read once.
+ */
+Q6_API int q6_lora_xa_bf16(const uint16_t* x, const uint16_t* a, uint16_t* xa, int64_t M, int64_t K, int r,
+                           q6_stream_t stream);
 
 /*
  * Workspace bytes with which q6_linear_bf16's tensor-core path splits K across
@@ -176,19 +193,58 @@ Q6_API int q6_mlp_bf16_noalloc(const uint16_t* x, const uint32_t* w1, const uint
  */
 Q6_API int q6_layernorm_modulate_bf16(const uint16_t* x, const uint16_t* shift, const uint16_t* scale, uint16_t* y,
                                       int64_t M, int64_t D, float eps, q6_stream_t stream);
+
+/*
+ * The residual add and adaLN modulate of a block over rows of a joint,
+ * batched sequence (several samples, each [text; image] rows):
+ *   h[m, :] = x[m, :] + add[m, :]        (bf16 rounding once; h = x when add is null)
+ *   y[m, :] = LayerNorm(h[m, :]) * (1 + scale[v]) + shift[v]
+ * where local row m is global row g = row0 + m of sequences of seq_len rows,
+ * the first text_len of each from the text stream:
+ *   v = (g / seq_len) * 2 + ((g % seq_len) >= text_len ? 1 : 0),
+ * i.e. shift / scale hold [samples][text, image][D] vectors.  h_out (nullable)
+ * receives h.  With seq_len = text_len = 0 every row takes vector 0 (the
+ * plain q6_layernorm_modulate_bf16).  Replaces `x + gate * attn_out` /
+ * `x + gate * ff` followed by `_modulate(norm2(x), mod2)` and the next block's
+ * `_modulate(norm1(x), mod1)` (benchmarks/profile_qwen_block.py:253-263) when
+ * the gated term arrives from a reduce-scatter of tensor-parallel partials.
+ * D and alignment as q6_layernorm_modulate_bf16.
+ */
+Q6_API int q6_add_layernorm_modulate_bf16(const uint16_t* x, const uint16_t* add, uint16_t* h_out,
+                                          const uint16_t* shift, const uint16_t* scale, uint16_t* y, int64_t M,
+                                          int64_t D, int64_t row0, int64_t seq_len, int64_t text_len, float eps,
+                                          q6_stream_t stream);
 Q6_API int q6_qk_rmsnorm_rope_bf16(uint16_t* qk, int64_t row_stride, int64_t M, int heads, int head_dim,
                                    const uint16_t* weight, const float* cos, const float* sin, float eps,
                                    q6_stream_t stream);
 
-/* Device error word (0 = none).  Reading it synchronises the current device. */
+/* Device error word (0 = none, else a q6_error_site code).  Reading it
+   synchronises the current device. */
 Q6_API int q6_get_device_error(int* code);
 Q6_API int q6_clear_device_error(void);
+
+/*
+ * Self-test of the failure path every pipeline wait in this library takes:
+ * one CTA initialises an mbarrier that nothing ever arrives at and waits on
+ * it through the same bounded wait the GEMM's barriers use, with a limit of
+ * limit_ns (1 us .. 1 s).  When the limit passes the wait records
+ * Q6_SITE_SELFTEST in the device error word and the kernel returns; no copy
+ * is in flight.  The call returns Q6_OK once launched; the result is read
+ * with q6_get_device_error.  No counterpart in the reference (it has no
+ * device-side hang detection).
+ */
+Q6_API int q6_selftest_bounded_wait(int64_t limit_ns, q6_stream_t stream);
 
 /* Path the last q6_linear_bf16 / q6_mlp_bf16 call on this host thread launched. */
 Q6_API int q6_last_path(void);
 
 /* Token tile (MMA N) the tensor path would use for an M x N problem. */
 Q6_API int q6_tensor_token_tile(int64_t M, int64_t N);
+
+/* How many tensor-path launches in this process asked for CTA pairs (two-CTA
+   clusters sharing one cta_group::2 MMA), were refused by the device before
+   anything ran, and ran one CTA per tile instead. */
+Q6_API int64_t q6_pair_fallback_count(void);
 
 Q6_API const char* q6_status_string(int status);
 Q6_API int q6_abi_version(void);

@@ -105,8 +105,22 @@ def qwen_rope_angles(img_shapes: list[tuple[int, int]], txt_len: int, *, theta: 
     return img, txt
 
 
-def attention(q: np.ndarray, k: np.ndarray, v: np.ndarray, heads: int) -> np.ndarray:
-    """softmax(q k^T / sqrt(d)) v per head; rows [S, H * d]."""
+def joint_key_mask(text_mask: np.ndarray | None, s_img: int) -> np.ndarray | None:
+    """Keys a joint [text; image] query may attend to, from the encoder's text
+    mask [S_txt] (1 = real token, 0 = padding): padded text tokens are masked
+    out as keys, every image token stays (the reference converts its
+    ``encoder_hidden_states_mask`` this way before SDPA,
+    benchmarks/profile_qwen_block.py:228-248)."""
+
+    if text_mask is None:
+        return None
+    return np.concatenate([np.asarray(text_mask).reshape(-1) > 0.5, np.ones(s_img, dtype=bool)])
+
+
+def attention(q: np.ndarray, k: np.ndarray, v: np.ndarray, heads: int,
+              key_mask: np.ndarray | None = None) -> np.ndarray:
+    """softmax(q k^T / sqrt(d)) v per head; rows [S, H * d]; ``key_mask``
+    [S_k] bool drops the keys it marks False."""
 
     s = q.shape[0]
     d = q.shape[1] // heads
@@ -114,6 +128,8 @@ def attention(q: np.ndarray, k: np.ndarray, v: np.ndarray, heads: int) -> np.nda
     kh = np.asarray(k, dtype=np.float64).reshape(-1, heads, d).transpose(1, 0, 2)
     vh = np.asarray(v, dtype=np.float64).reshape(-1, heads, d).transpose(1, 0, 2)
     logits = qh @ kh.transpose(0, 2, 1) / np.sqrt(d)
+    if key_mask is not None:
+        logits = np.where(np.asarray(key_mask, dtype=bool)[None, None, :], logits, -np.inf)
     logits -= logits.max(axis=-1, keepdims=True)
     p = np.exp(logits)
     p /= p.sum(axis=-1, keepdims=True)
@@ -135,12 +151,74 @@ def _lin(w: BlockWeights, name: str, x: np.ndarray, **kw) -> np.ndarray:
 
 def block_forward(w: BlockWeights, hidden: np.ndarray, encoder: np.ndarray, temb: np.ndarray,
                   img_cos: np.ndarray, img_sin: np.ndarray, txt_cos: np.ndarray, txt_sin: np.ndarray,
-                  eps: float = 1e-6) -> tuple[np.ndarray, np.ndarray]:
+                  eps: float = 1e-6, text_mask: np.ndarray | None = None) -> tuple[np.ndarray, np.ndarray]:
     """One sample through the block: returns (text stream out, image stream out), fp32 values of bf16.
 
     ``hidden`` [S_img, D], ``encoder`` [S_txt, D], ``temb`` [D] hold the
-    values of bf16 inputs.
+    values of bf16 inputs; ``text_mask`` [S_txt] (optional) marks real text
+    tokens with 1 and padding with 0.
     """
+
+    return block_forward_rows(w, hidden, encoder, temb, img_cos, img_sin, txt_cos, txt_sin, eps=eps,
+                              text_mask=text_mask)
+
+
+def block_forward_rows(w: BlockWeights, hidden: np.ndarray, encoder: np.ndarray, temb: np.ndarray,
+                       img_cos: np.ndarray, img_sin: np.ndarray, txt_cos: np.ndarray, txt_sin: np.ndarray,
+                       eps: float = 1e-6, text_mask: np.ndarray | None = None,
+                       img_rows: np.ndarray | None = None,
+                       txt_rows: np.ndarray | None = None) -> tuple[np.ndarray, np.ndarray]:
+    """``block_forward`` restricted to the output rows ``txt_rows`` /
+    ``img_rows`` (all rows when None).  Keys and values still come from every
+    row; only the query side (attention output, output projections, feed
+    forward) is computed for the selected rows, each of which depends on its
+    own input row and on all keys and values.  Returns the selected rows."""
+
+    d = hidden.shape[1]
+    s_txt, s_img = encoder.shape[0], hidden.shape[0]
+    ir = np.arange(s_img) if img_rows is None else np.asarray(img_rows)
+    tr = np.arange(s_txt) if txt_rows is None else np.asarray(txt_rows)
+    t = round_bf16(silu(temb).reshape(1, d))
+    img_mod = _lin(w, "img_mod_linear", t).reshape(6, d)
+    txt_mod = _lin(w, "txt_mod_linear", t).reshape(6, d)
+    ish1, isc1, ig1, ish2, isc2, ig2 = img_mod
+    tsh1, tsc1, tg1, tsh2, tsc2, tg2 = txt_mod
+
+    img_in = round_bf16(layernorm_modulate(hidden, ish1, isc1, eps))
+    txt_in = round_bf16(layernorm_modulate(encoder, tsh1, tsc1, eps))
+    # keys and values of every row
+    k_i = round_bf16(qk_rmsnorm_rope(_lin(w, "attn.to_k", img_in), w.norms["attn.norm_k"], img_cos, img_sin, eps))
+    k_t = round_bf16(qk_rmsnorm_rope(_lin(w, "attn.add_k_proj", txt_in), w.norms["attn.norm_added_k"], txt_cos,
+                                     txt_sin, eps))
+    v_i = _lin(w, "attn.to_v", img_in)
+    v_t = _lin(w, "attn.add_v_proj", txt_in)
+    # queries of the selected rows only
+    q_i = round_bf16(qk_rmsnorm_rope(_lin(w, "attn.to_q", img_in[ir]), w.norms["attn.norm_q"], img_cos[ir],
+                                     img_sin[ir], eps))
+    q_t = round_bf16(qk_rmsnorm_rope(_lin(w, "attn.add_q_proj", txt_in[tr]), w.norms["attn.norm_added_q"],
+                                     txt_cos[tr], txt_sin[tr], eps))
+    key_mask = joint_key_mask(text_mask, s_img)
+    keys, vals = np.concatenate([k_t, k_i]), np.concatenate([v_t, v_i])
+    att_t = round_bf16(attention(q_t, keys, vals, w.heads, key_mask).astype(np.float32))
+    att_i = round_bf16(attention(q_i, keys, vals, w.heads, key_mask).astype(np.float32))
+    img_h = _lin(w, "attn.attn_to_out.0", att_i, residual=hidden[ir], gate=ig1)
+    txt_h = _lin(w, "attn.to_add_out", att_t, residual=encoder[tr], gate=tg1)
+
+    img_ff_in = round_bf16(layernorm_modulate(img_h, ish2, isc2, eps))
+    txt_ff_in = round_bf16(layernorm_modulate(txt_h, tsh2, tsc2, eps))
+    img_mid = _lin(w, "img_ff.mlp_in", img_ff_in, apply_gelu=True)
+    txt_mid = _lin(w, "txt_ff.mlp_in", txt_ff_in, apply_gelu=True)
+    img_out = _lin(w, "img_ff.mlp_out", img_mid, residual=img_h, gate=ig2)
+    txt_out = _lin(w, "txt_ff.mlp_out", txt_mid, residual=txt_h, gate=tg2)
+    return txt_out, img_out
+
+
+def _block_forward_full(w: BlockWeights, hidden: np.ndarray, encoder: np.ndarray, temb: np.ndarray,
+                        img_cos: np.ndarray, img_sin: np.ndarray, txt_cos: np.ndarray, txt_sin: np.ndarray,
+                        eps: float = 1e-6) -> tuple[np.ndarray, np.ndarray]:
+    """The whole-sequence form of the block (every row through every stage),
+    kept as the plain statement of the stage order that block_forward_rows
+    restricts to selected rows."""
 
     d = hidden.shape[1]
     t = round_bf16(silu(temb).reshape(1, d))
@@ -185,6 +263,7 @@ BLOCK_LINEARS = {
 NORMS = ("attn.norm_q", "attn.norm_k", "attn.norm_added_q", "attn.norm_added_k")
 
 __all__ = [
-    "BLOCK_LINEARS", "NORMS", "BlockWeights", "attention", "block_forward", "gelu", "layernorm_modulate",
+    "BLOCK_LINEARS", "NORMS", "BlockWeights", "attention", "block_forward", "block_forward_rows", "gelu",
+    "joint_key_mask", "layernorm_modulate",
     "qk_rmsnorm_rope", "qwen_rope_angles", "rmsnorm_heads", "rope_pairs", "silu", "bf16_bits_to_f32",
 ]

@@ -11,7 +11,8 @@ the small stand-in header oracle/ref_shim/metal_stdlib.
 Outputs go to oracle/_ref/ only (git-ignored; the built .so travels to the GPU
 box so tests can use it there).  Nothing from the reference is committed.
 
-Usage:  python oracle/build_ref.py [--reference /root/reference]
+Usage:  python oracle/build_ref.py --reference <reference checkout>
+        (or set Q6_REFERENCE_ROOT to the checkout)
 """
 
 from __future__ import annotations
@@ -144,9 +145,16 @@ def build(reference: Path, *, verbose: bool = False) -> Path:
 
 def main() -> int:
     parser = argparse.ArgumentParser(description=__doc__)
-    parser.add_argument("--reference", type=Path, default=Path("/root/reference"))
+    parser.add_argument("--reference", type=Path, default=None,
+                        help="checkout of the reference project (default: $Q6_REFERENCE_ROOT)")
     parser.add_argument("-v", "--verbose", action="store_true")
     args = parser.parse_args()
+    if args.reference is None:
+        env = os.environ.get("Q6_REFERENCE_ROOT")
+        if not env:
+            print("give --reference or set Q6_REFERENCE_ROOT; nothing built", file=sys.stderr)
+            return 1
+        args.reference = Path(env)
     if not (args.reference / REF_FILE).exists():
         print(f"reference source not found under {args.reference}; nothing built", file=sys.stderr)
         return 1

@@ -71,18 +71,22 @@ def time_mlp_port(max_tokens: int, dim: int, hidden: int, gs: int, *, budget_s: 
     return tokens, elapsed, steps
 
 
-def time_reference_kernel_mlp(dim: int, hidden: int, gs: int, *, steps: int, warmup: int = 1,
-                              step_budget_s: float = 1.5, total_budget_s: float = 150.0) -> dict:
+def time_reference_kernel_mlp(dim: int, hidden: int, gs: int, *, tokens: int, steps: int,
+                              total_budget_s: float = 110.0) -> dict:
+    """The reference kernel's fused_q6_mlp composition on full ``tokens``-row
+    steps: a 16-token warm-up (which also estimates the step time), then as
+    many full steps as fit ``total_budget_s`` (at least one, at most ``steps``)."""
+
     ref = _o.load_ref()
     cores = int(os.environ.get("Q6REF_THREADS", "0")) or (os.cpu_count() or 1)
     if ref is None:
         import torch
 
         torch.set_num_threads(cores)
-        tokens, seconds, nsteps = time_mlp_port(3456, dim, hidden, gs, budget_s=min(total_budget_s, 30.0))
-        return {"tflops": mlp_port_flops(tokens, dim, hidden) * nsteps / seconds / 1e12, "steps": nsteps,
-                "tokens": tokens, "cores": torch.get_num_threads(), "kind": "port",
-                "sample": f"oracle/_ref not built; torch-CPU port, {nsteps} x {tokens} tokens"}
+        ntok, seconds, nsteps = time_mlp_port(tokens, dim, hidden, gs, budget_s=min(total_budget_s, 30.0))
+        return {"tflops": mlp_port_flops(ntok, dim, hidden) * nsteps / seconds / 1e12, "steps": nsteps,
+                "tokens": ntok, "cores": torch.get_num_threads(), "kind": "port",
+                "sample": f"oracle/_ref not built; torch-CPU port, {nsteps} x {ntok} tokens"}
 
     rng = np.random.default_rng(98)
     fc1 = _weights(rng, hidden, dim, gs)
@@ -92,25 +96,23 @@ def time_reference_kernel_mlp(dim: int, hidden: int, gs: int, *, steps: int, war
         prepared.append((np.ascontiguousarray(w.weight), np.ascontiguousarray(w.scales_f32()),
                          np.ascontiguousarray(w.biases_f32()), np.ascontiguousarray(w.bias_f32())))
 
-    def run(tokens: int) -> float:
-        x = _o.f32_to_bf16_bits(rng.standard_normal((tokens, dim)).astype(np.float32))
-        h = np.zeros((tokens, hidden), dtype=np.uint16)
-        y = np.zeros((tokens, dim), dtype=np.uint16)
+    def run(ntok: int) -> float:
+        x = _o.f32_to_bf16_bits(rng.standard_normal((ntok, dim)).astype(np.float32))
+        h = np.zeros((ntok, hidden), dtype=np.uint16)
+        y = np.zeros((ntok, dim), dtype=np.uint16)
         (w1, s1, q1, b1), (w2, s2, q2, b2) = prepared
         t0 = time.perf_counter()
         ref.q6ref_qmm_t_bf16(x.ctypes.data, w1.ctypes.data, s1.ctypes.data, q1.ctypes.data, b1.ctypes.data,
-                             h.ctypes.data, tokens, hidden, dim, gs, w1.shape[1], s1.shape[1], 1, 1)
+                             h.ctypes.data, ntok, hidden, dim, gs, w1.shape[1], s1.shape[1], 1, 1)
         ref.q6ref_qmm_t_bf16(h.ctypes.data, w2.ctypes.data, s2.ctypes.data, q2.ctypes.data, b2.ctypes.data,
-                             y.ctypes.data, tokens, dim, hidden, gs, w2.shape[1], s2.shape[1], 1, 0)
+                             y.ctypes.data, ntok, dim, hidden, gs, w2.shape[1], s2.shape[1], 1, 0)
         return time.perf_counter() - t0
 
-    per_token = run(1)
-    tokens = int(max(1, min(3456, step_budget_s / max(per_token, 1e-6))))
-    steps = int(max(1, min(steps, total_budget_s / max(per_token * tokens, 1e-6))))
-    for _ in range(warmup):
-        run(tokens)
-    elapsed = sum(run(tokens) for _ in range(steps))
-    return {"tflops": mlp_port_flops(tokens, dim, hidden) * steps / elapsed / 1e12, "steps": steps, "tokens": tokens,
-            "cores": cores, "kind": "reference",
-            "sample": (f"{steps} step(s) of {tokens} tokens through the reference's SOURCE_QMM_T compiled for the "
-                       f"host (fc1+GELU, then fc2), {cores} threads")}
+    probe_tokens = 16
+    per_token = run(probe_tokens) / probe_tokens
+    nsteps = int(max(1, min(steps, total_budget_s // max(per_token * tokens, 1e-6))))
+    elapsed = sum(run(tokens) for _ in range(nsteps))
+    return {"tflops": mlp_port_flops(tokens, dim, hidden) * nsteps / elapsed / 1e12, "steps": nsteps,
+            "tokens": tokens, "cores": cores, "kind": "reference",
+            "sample": (f"{nsteps} full step(s) of {tokens} tokens (after a {probe_tokens}-token warm-up) through "
+                       f"the reference's SOURCE_QMM_T compiled for the host (fc1+GELU, then fc2), {cores} threads")}

@@ -24,6 +24,9 @@ Q6_ERR_WORKSPACE = 8
 
 Q6_EPI_NONE = 0
 Q6_EPI_GELU = 1
+Q6_EPI_GELU_PRECISE = 2
+
+Q6_SITE_SELFTEST = 64
 
 Q6_PATH_AUTO = 0
 Q6_PATH_SIMT = 1
@@ -43,7 +46,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         _I,
         [_P, _P, _P, _P, _P, _P, _P, _P, _P, _F, _I, _P, _I64, _I64, _I64, _I, _I, _I, _P, _SZ, _P],
     ),
-    "q6_linear_workspace_bytes": (_SZ, [_I64, _I]),
+    "q6_lora_xa_bf16": (_I, [_P, _P, _P, _I64, _I64, _I, _P]),
     "q6_linear_tc_workspace_bytes": (_SZ, [_I64, _I64, _I64]),
     "q6_linear_f32": (_I, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I, _I, _P]),
     "q6_mlp_bf16": (
@@ -56,11 +59,14 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I, _P],
     ),
     "q6_layernorm_modulate_bf16": (_I, [_P, _P, _P, _P, _I64, _I64, _F, _P]),
+    "q6_add_layernorm_modulate_bf16": (_I, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _F, _P]),
     "q6_qk_rmsnorm_rope_bf16": (_I, [_P, _I64, _I64, _I, _I, _P, _P, _P, _F, _P]),
     "q6_get_device_error": (_I, [ctypes.POINTER(ctypes.c_int)]),
     "q6_clear_device_error": (_I, []),
     "q6_last_path": (_I, []),
     "q6_tensor_token_tile": (_I, [_I64, _I64]),
+    "q6_pair_fallback_count": (_I64, []),
+    "q6_selftest_bounded_wait": (_I, [_I64, _P]),
     "q6_status_string": (ctypes.c_char_p, [_I]),
     "q6_abi_version": (_I, []),
 }

@@ -185,9 +185,11 @@ class QwenTransformerBlock(torch.nn.Module):
                              lora=lin.lora, **kw)
 
     def forward_sample(self, hidden: torch.Tensor, encoder: torch.Tensor, mod_img: torch.Tensor,
-                       mod_txt: torch.Tensor, rope: tuple[torch.Tensor, ...]) -> tuple[torch.Tensor, torch.Tensor]:
+                       mod_txt: torch.Tensor, rope: tuple[torch.Tensor, ...],
+                       text_mask: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
         """One sample: hidden [S_img, D], encoder [S_txt, D], modulation
-        vectors [6, D] per stream; returns (text out, image out)."""
+        vectors [6, D] per stream, optional text mask [S_txt] (1 = token,
+        0 = padding); returns (text out, image out)."""
 
         img_cos, img_sin, txt_cos, txt_sin = rope
         s_img, s_txt, d = hidden.shape[0], encoder.shape[0], self.dim
@@ -205,11 +207,7 @@ class QwenTransformerBlock(torch.nn.Module):
         qk_rmsnorm_rope_(q[s_txt:], self.norms["attn.norm_q"], img_cos, img_sin, eps=self.eps)
         qk_rmsnorm_rope_(k[:s_txt], self.norms["attn.norm_added_k"], txt_cos, txt_sin, eps=self.eps)
         qk_rmsnorm_rope_(k[s_txt:], self.norms["attn.norm_k"], img_cos, img_sin, eps=self.eps)
-        h = self.heads
-        att = F.scaled_dot_product_attention(
-            q.view(1, s, h, HEAD_DIM).transpose(1, 2), k.view(1, s, h, HEAD_DIM).transpose(1, 2),
-            v.view(1, s, h, HEAD_DIM).transpose(1, 2), scale=1.0 / math.sqrt(HEAD_DIM))
-        joint = att.transpose(1, 2).reshape(s, d)
+        joint = joint_attention(q, k, v, self.heads, s_txt, text_mask)
         img_h = self._linear("attn.attn_to_out.0", joint[s_txt:], residual=hidden, gate=ig1)
         txt_h = self._linear("attn.to_add_out", joint[:s_txt], residual=encoder, gate=tg1)
         img_ff_in = layernorm_modulate(img_h, ish2, isc2, eps=self.eps)
@@ -227,15 +225,40 @@ class QwenTransformerBlock(torch.nn.Module):
                 self._linear("txt_mod_linear", t).reshape(b, 6, self.dim))
 
     def forward(self, hidden: torch.Tensor, encoder: torch.Tensor, temb: torch.Tensor,
-                rope: tuple[torch.Tensor, ...]) -> tuple[torch.Tensor, torch.Tensor]:
+                rope: tuple[torch.Tensor, ...],
+                encoder_mask: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
         """hidden [B, S_img, D], encoder [B, S_txt, D], temb [B, D] (bf16);
-        ``rope`` = (img_cos, img_sin, txt_cos, txt_sin) fp32 [S, 64].
-        Returns (encoder_out, hidden_out) like the reference block."""
+        ``rope`` = (img_cos, img_sin, txt_cos, txt_sin) fp32 [S, 64];
+        ``encoder_mask`` [B, S_txt] (1 = text token, 0 = padding; None = no
+        padding).  Returns (encoder_out, hidden_out) like the reference block."""
 
         mod_img, mod_txt = self.modulation(temb)
-        outs = [self.forward_sample(hidden[b], encoder[b], mod_img[b], mod_txt[b], rope)
+        outs = [self.forward_sample(hidden[b], encoder[b], mod_img[b], mod_txt[b], rope,
+                                    None if encoder_mask is None else encoder_mask[b])
                 for b in range(hidden.shape[0])]
         return torch.stack([o[0] for o in outs]), torch.stack([o[1] for o in outs])
+
+
+def joint_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, heads: int, s_txt: int,
+                    text_mask: torch.Tensor | None = None) -> torch.Tensor:
+    """Joint [text; image] attention of one sample over rows [S, heads * 128]
+    (torch scaled_dot_product_attention).  ``text_mask`` [S_txt] (1 = token,
+    0 = padding) removes padded text tokens as keys, every image token stays
+    a key: the joint mask the reference builds from
+    ``encoder_hidden_states_mask`` (benchmarks/profile_qwen_block.py:228-248).
+    Without a mask the library's unmasked flash kernel runs."""
+
+    s = q.shape[0]
+    shape = (1, s, heads, HEAD_DIM)
+    mask = None
+    if text_mask is not None:
+        keep = torch.ones(s, dtype=torch.bool, device=q.device)
+        keep[:s_txt] = text_mask.reshape(-1).to(q.device) > 0.5
+        mask = keep.view(1, 1, 1, s)
+    att = F.scaled_dot_product_attention(q.view(shape).transpose(1, 2), k.view(shape).transpose(1, 2),
+                                         v.view(shape).transpose(1, 2), attn_mask=mask,
+                                         scale=1.0 / math.sqrt(HEAD_DIM))
+    return att.transpose(1, 2).reshape(s, heads * HEAD_DIM)
 
 
 _TXT_QKV = ("attn.add_q_proj", "attn.add_k_proj", "attn.add_v_proj")
@@ -378,7 +401,8 @@ class TensorParallelQwenBlock(torch.nn.Module):
                 self._linear("txt_mod_linear", t).reshape(b, 6, self.dim))
 
     def forward_sample(self, hidden: torch.Tensor, encoder: torch.Tensor, mod_img: torch.Tensor,
-                       mod_txt: torch.Tensor, rope: tuple[torch.Tensor, ...]) -> tuple[torch.Tensor, torch.Tensor]:
+                       mod_txt: torch.Tensor, rope: tuple[torch.Tensor, ...],
+                       text_mask: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
         img_cos, img_sin, txt_cos, txt_sin = rope
         s_img, s_txt = hidden.shape[0], encoder.shape[0]
         s, dl, lead = s_txt + s_img, self.heads_local * HEAD_DIM, self.rank == 0
@@ -394,11 +418,7 @@ class TensorParallelQwenBlock(torch.nn.Module):
         qk_rmsnorm_rope_(q[s_txt:], self.norms["attn.norm_q"], img_cos, img_sin, eps=self.eps)
         qk_rmsnorm_rope_(k[:s_txt], self.norms["attn.norm_added_k"], txt_cos, txt_sin, eps=self.eps)
         qk_rmsnorm_rope_(k[s_txt:], self.norms["attn.norm_k"], img_cos, img_sin, eps=self.eps)
-        h = self.heads_local
-        att = F.scaled_dot_product_attention(
-            q.view(1, s, h, HEAD_DIM).transpose(1, 2), k.view(1, s, h, HEAD_DIM).transpose(1, 2),
-            v.view(1, s, h, HEAD_DIM).transpose(1, 2), scale=1.0 / math.sqrt(HEAD_DIM))
-        joint = att.transpose(1, 2).reshape(s, dl)
+        joint = joint_attention(q, k, v, self.heads_local, s_txt, text_mask)
         # row-parallel output projections into one joint [text; image] buffer, one all-reduce
         streams = torch.empty((s, self.dim), dtype=torch.bfloat16, device=hidden.device)
         self._linear("attn.attn_to_out.0", joint[s_txt:], residual=hidden if lead else None, gate=ig1,
@@ -416,8 +436,10 @@ class TensorParallelQwenBlock(torch.nn.Module):
         return outs[:s_txt], outs[s_txt:]
 
     def forward(self, hidden: torch.Tensor, encoder: torch.Tensor, temb: torch.Tensor,
-                rope: tuple[torch.Tensor, ...]) -> tuple[torch.Tensor, torch.Tensor]:
+                rope: tuple[torch.Tensor, ...],
+                encoder_mask: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
         mod_img, mod_txt = self.modulation(temb)
-        outs = [self.forward_sample(hidden[b], encoder[b], mod_img[b], mod_txt[b], rope)
+        outs = [self.forward_sample(hidden[b], encoder[b], mod_img[b], mod_txt[b], rope,
+                                    None if encoder_mask is None else encoder_mask[b])
                 for b in range(hidden.shape[0])]
         return torch.stack([o[0] for o in outs]), torch.stack([o[1] for o in outs])

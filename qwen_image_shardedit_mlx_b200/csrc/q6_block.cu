@@ -41,13 +41,15 @@ __device__ __forceinline__ float warp_sum(float v) {
 
 constexpr int kLnWarps = 4;  // rows per CTA
 
-// NV uint4 (8 bf16) per lane: D = 256 NV.
-template <int NV>
-__global__ void __launch_bounds__(kLnWarps * 32) layernorm_modulate_kernel(const uint4* __restrict__ x,
-                                                                           const uint4* __restrict__ shift,
-                                                                           const uint4* __restrict__ scale,
-                                                                           uint4* __restrict__ y, int64_t M,
-                                                                           float eps) {
+// NV uint4 (8 bf16) per lane: D = 256 NV.  kAdd: the row is first formed as
+// h = bf16(x + add) (stored to h_out when given).  Row g = row0 + m of the
+// joint batched sequence takes modulation vector
+// v = (g / seq_len) * 2 + (g % seq_len >= text_len) (0 when seq_len == 0).
+template <int NV, bool kAdd>
+__global__ void __launch_bounds__(kLnWarps * 32) layernorm_modulate_kernel(
+    const uint4* __restrict__ x, const uint4* __restrict__ add, uint4* h_out, const uint4* __restrict__ shift,
+    const uint4* __restrict__ scale, uint4* y, int64_t M, int64_t row0, int64_t seq_len, int64_t text_len,
+    float eps) {
     pdl_launch_dependents();
     pdl_wait();
     const int lane = threadIdx.x & 31;
@@ -58,6 +60,29 @@ __global__ void __launch_bounds__(kLnWarps * 32) layernorm_modulate_kernel(const
     uint4 v[NV];
 #pragma unroll
     for (int j = 0; j < NV; ++j) v[j] = xr[lane + 32 * j];
+    if constexpr (kAdd) {
+        const uint4* ar = add + row * (D / 8);
+#pragma unroll
+        for (int j = 0; j < NV; ++j) {
+            const uint4 b = ar[lane + 32 * j];
+            v[j] = make_uint4(pack2(lo_f(v[j].x) + lo_f(b.x), hi_f(v[j].x) + hi_f(b.x)),
+                              pack2(lo_f(v[j].y) + lo_f(b.y), hi_f(v[j].y) + hi_f(b.y)),
+                              pack2(lo_f(v[j].z) + lo_f(b.z), hi_f(v[j].z) + hi_f(b.z)),
+                              pack2(lo_f(v[j].w) + lo_f(b.w), hi_f(v[j].w) + hi_f(b.w)));
+        }
+        if (h_out) {
+            uint4* hr = h_out + row * (D / 8);
+#pragma unroll
+            for (int j = 0; j < NV; ++j) hr[lane + 32 * j] = v[j];
+        }
+    }
+    int64_t vec = 0;
+    if (seq_len > 0) {
+        const int64_t g = row0 + row;
+        vec = (g / seq_len) * 2 + ((g % seq_len) >= text_len ? 1 : 0);
+    }
+    shift += vec * (D / 8);
+    scale += vec * (D / 8);
     float s = 0.0f;
 #pragma unroll
     for (int j = 0; j < NV; ++j)
@@ -91,15 +116,43 @@ __global__ void __launch_bounds__(kLnWarps * 32) layernorm_modulate_kernel(const
     }
 }
 
+struct LnArgs {
+    const void* x;
+    const void* add;
+    void* h_out;
+    const void* shift;
+    const void* scale;
+    void* y;
+    int64_t M, row0, seq_len, text_len;
+    float eps;
+};
+
 template <int NV>
-int launch_ln(const void* x, const void* shift, const void* scale, void* y, int64_t M, float eps,
-              cudaStream_t stream) {
-    const int64_t blocks = (M + kLnWarps - 1) / kLnWarps;
-    const cudaError_t e =
-        launch_pdl(layernorm_modulate_kernel<NV>, dim3(static_cast<unsigned>(blocks)), dim3(kLnWarps * 32), 0, stream,
-                   static_cast<const uint4*>(x), static_cast<const uint4*>(shift), static_cast<const uint4*>(scale),
-                   static_cast<uint4*>(y), M, eps);
+int launch_ln(const LnArgs& a, cudaStream_t stream) {
+    const int64_t blocks = (a.M + kLnWarps - 1) / kLnWarps;
+    auto go = [&](auto kernel) {
+        return launch_pdl(kernel, dim3(static_cast<unsigned>(blocks)), dim3(kLnWarps * 32), 0, stream,
+                          static_cast<const uint4*>(a.x), static_cast<const uint4*>(a.add),
+                          static_cast<uint4*>(a.h_out), static_cast<const uint4*>(a.shift),
+                          static_cast<const uint4*>(a.scale), static_cast<uint4*>(a.y), a.M, a.row0, a.seq_len,
+                          a.text_len, a.eps);
+    };
+    const cudaError_t e = a.add ? go(layernorm_modulate_kernel<NV, true>) : go(layernorm_modulate_kernel<NV, false>);
     return e == cudaSuccess ? Q6_OK : Q6_ERR_CUDA;
+}
+
+int dispatch_ln(const LnArgs& a, int64_t D, cudaStream_t s) {
+    switch (D / 256) {
+        case 1: return launch_ln<1>(a, s);
+        case 2: return launch_ln<2>(a, s);
+        case 3: return launch_ln<3>(a, s);
+        case 4: return launch_ln<4>(a, s);
+        case 6: return launch_ln<6>(a, s);
+        case 8: return launch_ln<8>(a, s);
+        case 12: return launch_ln<12>(a, s);
+        case 16: return launch_ln<16>(a, s);
+        default: return Q6_ERR_UNSUPPORTED;
+    }
 }
 
 constexpr int kRopeWarps = 8;
@@ -141,23 +194,23 @@ extern "C" {
 
 Q6_API int q6_layernorm_modulate_bf16(const uint16_t* x, const uint16_t* shift, const uint16_t* scale, uint16_t* y,
                                       int64_t M, int64_t D, float eps, q6_stream_t stream) {
+    return q6_add_layernorm_modulate_bf16(x, nullptr, nullptr, shift, scale, y, M, D, 0, 0, 0, eps, stream);
+}
+
+Q6_API int q6_add_layernorm_modulate_bf16(const uint16_t* x, const uint16_t* add, uint16_t* h_out,
+                                          const uint16_t* shift, const uint16_t* scale, uint16_t* y, int64_t M,
+                                          int64_t D, int64_t row0, int64_t seq_len, int64_t text_len, float eps,
+                                          q6_stream_t stream) {
     if (!x || !shift || !scale || !y || M <= 0 || D <= 0 || !(eps >= 0.0f)) return Q6_ERR_INVALID_ARGUMENT;
+    if (h_out && !add) return Q6_ERR_INVALID_ARGUMENT;
+    if (row0 < 0 || seq_len < 0 || text_len < 0 || text_len > seq_len) return Q6_ERR_INVALID_ARGUMENT;
     if (D % 256 != 0) return Q6_ERR_SHAPE;
     const uintptr_t al = reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(shift) |
-                         reinterpret_cast<uintptr_t>(scale) | reinterpret_cast<uintptr_t>(y);
+                         reinterpret_cast<uintptr_t>(scale) | reinterpret_cast<uintptr_t>(y) |
+                         reinterpret_cast<uintptr_t>(add) | reinterpret_cast<uintptr_t>(h_out);
     if (al % 16 != 0) return Q6_ERR_ALIGNMENT;
-    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-    switch (D / 256) {
-        case 1: return q6::launch_ln<1>(x, shift, scale, y, M, eps, s);
-        case 2: return q6::launch_ln<2>(x, shift, scale, y, M, eps, s);
-        case 3: return q6::launch_ln<3>(x, shift, scale, y, M, eps, s);
-        case 4: return q6::launch_ln<4>(x, shift, scale, y, M, eps, s);
-        case 6: return q6::launch_ln<6>(x, shift, scale, y, M, eps, s);
-        case 8: return q6::launch_ln<8>(x, shift, scale, y, M, eps, s);
-        case 12: return q6::launch_ln<12>(x, shift, scale, y, M, eps, s);
-        case 16: return q6::launch_ln<16>(x, shift, scale, y, M, eps, s);
-        default: return Q6_ERR_UNSUPPORTED;
-    }
+    const q6::LnArgs a{x, add, h_out, shift, scale, y, M, row0, seq_len, text_len, eps};
+    return q6::dispatch_ln(a, D, reinterpret_cast<cudaStream_t>(stream));
 }
 
 Q6_API int q6_qk_rmsnorm_rope_bf16(uint16_t* qk, int64_t row_stride, int64_t M, int heads, int head_dim,

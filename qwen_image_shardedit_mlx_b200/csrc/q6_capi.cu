@@ -16,6 +16,8 @@ namespace {
 
 thread_local int g_last_path = Q6_PATH_AUTO;
 
+constexpr int kEpiFlags = Q6_EPI_GELU | Q6_EPI_GELU_PRECISE;
+
 bool valid_group_size(int gs) { return gs == 32 || gs == 64 || gs == 128; }
 
 bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
@@ -58,7 +60,7 @@ int run_linear(const q6::LinearArgs& a, int path, cudaStream_t stream) {
 
 extern "C" {
 
-int q6_abi_version(void) { return 1; }
+int q6_abi_version(void) { return 2; }
 
 const char* q6_status_string(int status) {
     switch (status) {
@@ -86,12 +88,6 @@ int q6_dequantize_bf16(const uint32_t* w, const uint16_t* scales, const uint16_t
 
 size_t q6_linear_tc_workspace_bytes(int64_t M, int64_t N, int64_t K) { return q6::tc_workspace_bytes(M, N, K); }
 
-size_t q6_linear_workspace_bytes(int64_t M, int lora_rank) {
-    (void)M;
-    (void)lora_rank;
-    return 0;  // every path (the fused LoRA delta included) works in registers, TMEM and shared memory
-}
-
 int q6_linear_bf16(const uint16_t* x, const uint32_t* w, const uint16_t* scales, const uint16_t* qbiases,
                    const uint16_t* bias, const uint16_t* residual, const uint16_t* gate, const uint16_t* lora_xa,
                    const uint16_t* lora_b, float lora_scale, int lora_rank, uint16_t* y, int64_t M, int64_t N,
@@ -100,7 +96,8 @@ int q6_linear_bf16(const uint16_t* x, const uint32_t* w, const uint16_t* scales,
     int st = check_weights(w, scales, qbiases, N, K, group_size);
     if (st != Q6_OK) return st;
     if (!x || !y || M <= 0) return Q6_ERR_INVALID_ARGUMENT;
-    if ((flags & ~Q6_EPI_GELU) != 0) return Q6_ERR_INVALID_ARGUMENT;
+    if ((flags & ~kEpiFlags) != 0) return Q6_ERR_INVALID_ARGUMENT;
+    if (flags & Q6_EPI_GELU_PRECISE) flags |= Q6_EPI_GELU;  // the precise flag implies GELU
     if ((lora_xa == nullptr) != (lora_b == nullptr)) return Q6_ERR_INVALID_ARGUMENT;
     if (lora_xa && lora_rank <= 0) return Q6_ERR_INVALID_ARGUMENT;
     q6::LinearArgs a{x, w, scales, qbiases, bias, residual, gate, y, M, N, K, group_size, flags};
@@ -121,7 +118,8 @@ int q6_linear_f32(const float* x, const uint32_t* w, const uint16_t* scales, con
     int st = check_weights(w, scales, qbiases, N, K, group_size);
     if (st != Q6_OK) return st;
     if (!x || !y || M <= 0) return Q6_ERR_INVALID_ARGUMENT;
-    if ((flags & ~Q6_EPI_GELU) != 0) return Q6_ERR_INVALID_ARGUMENT;
+    if ((flags & ~kEpiFlags) != 0) return Q6_ERR_INVALID_ARGUMENT;
+    if (flags & Q6_EPI_GELU_PRECISE) flags |= Q6_EPI_GELU;
     if (!simt_aligned(x, K, 4)) return Q6_ERR_ALIGNMENT;
     q6::LinearArgs a{x, w, scales, qbiases, bias, nullptr, nullptr, y, M, N, K, group_size, flags};
     g_last_path = Q6_PATH_SIMT;
@@ -181,6 +179,23 @@ int q6_clear_device_error(void) {
 }
 
 int q6_last_path(void) { return g_last_path; }
+
+int64_t q6_pair_fallback_count(void) { return static_cast<int64_t>(q6::pair_fallbacks()); }
+
+int q6_selftest_bounded_wait(int64_t limit_ns, q6_stream_t stream) {
+    if (limit_ns < 1000 || limit_ns > 1000000000) return Q6_ERR_INVALID_ARGUMENT;
+    return q6::launch_selftest_wait(static_cast<uint64_t>(limit_ns), reinterpret_cast<cudaStream_t>(stream));
+}
+
+int q6_lora_xa_bf16(const uint16_t* x, const uint16_t* a, uint16_t* xa, int64_t M, int64_t K, int r,
+                    q6_stream_t stream) {
+    if (!x || !a || !xa || M <= 0 || K <= 0) return Q6_ERR_INVALID_ARGUMENT;
+    if (r < 32 || r > 256 || r % 32 != 0 || K % 16 != 0) return Q6_ERR_SHAPE;
+    const uintptr_t al = reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(a) |
+                         reinterpret_cast<uintptr_t>(xa);
+    if (al % 16 != 0) return Q6_ERR_ALIGNMENT;
+    return q6::launch_lora_xa(x, a, xa, M, K, r, reinterpret_cast<cudaStream_t>(stream));
+}
 
 int q6_tensor_token_tile(int64_t M, int64_t N) {
     if (M <= 0 || N <= 0) return 0;

@@ -33,6 +33,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 
 #include "q6_dequant.cuh"
 #include "q6_internal.h"
@@ -324,7 +325,7 @@ __global__ void __launch_bounds__(kWarps * 32, 2) gemv_stream_kernel(const Linea
                 const int n = n0 + r;
                 if (m < M && n < N) {
                     if (a.bias) v += bf16f(a.bias[n]);
-                    if (a.flags & Q6_EPI_GELU) v = gelu_ref(v);
+                    if (a.flags & (Q6_EPI_GELU | Q6_EPI_GELU_PRECISE)) v = gelu_ref(v);
                     if (a.gate) v *= bf16f(a.gate[n]);
                     if (a.residual) v += bf16f(a.residual[static_cast<size_t>(m) * N + n]);
                     __nv_bfloat16 h = __float2bfloat16_rn(v);
@@ -346,14 +347,15 @@ size_t gemv_smem_bytes(int64_t K, int gs, int mt) {
 template <int MT, int UPL>
 int launch_gemv_mt(const LinearArgs& a, cudaStream_t stream) {
     const size_t smem = gemv_smem_bytes(a.K, a.group_size, MT);
-    static int attr_set_for_device[64] = {0};
+    static std::atomic<bool> attr_set_for_device[kMaxDevices];
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return Q6_ERR_CUDA;
-    if (dev >= 0 && dev < 64 && !attr_set_for_device[dev]) {
+    if (dev < 0 || dev >= kMaxDevices) return Q6_ERR_UNSUPPORTED;
+    if (!attr_set_for_device[dev].load(std::memory_order_acquire)) {
         if (cudaFuncSetAttribute(gemv_stream_kernel<MT, UPL>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemCap) !=
             cudaSuccess)
             return Q6_ERR_CUDA;
-        attr_set_for_device[dev] = 1;
+        attr_set_for_device[dev].store(true, std::memory_order_release);
     }
     int per_sm = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemv_stream_kernel<MT, UPL>, kWarps * 32, smem) !=

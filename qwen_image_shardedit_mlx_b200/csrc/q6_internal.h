@@ -10,6 +10,10 @@
 
 namespace q6 {
 
+// Device ordinals the per-device host caches cover; calls on a higher ordinal
+// return Q6_ERR_UNSUPPORTED.
+constexpr int kMaxDevices = 64;
+
 // Operands of one q6 linear, y = epilogue(x @ dequant(W)^T).
 struct LinearArgs {
     const void* x;          // [M, K] bf16 (or fp32 for the fp32 path), row-major
@@ -86,6 +90,17 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
     cfg.numAttrs = pdl_enabled() ? 1 : 0;
     return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
+
+// Times a CTA-pair GEMM launch was refused by the device and ran one CTA per
+// tile instead (process-wide).
+long pair_fallbacks();
+
+// Bounded-wait self-test kernel (q6_selftest_bounded_wait).
+int launch_selftest_wait(uint64_t limit_ns, cudaStream_t stream);
+
+// LoRA pre-pass xa = x @ A (q6_lora_xa_bf16).
+int launch_lora_xa(const uint16_t* x, const uint16_t* a, uint16_t* xa, int64_t M, int64_t K, int r,
+                   cudaStream_t stream);
 
 // Per-translation-unit device error words (value, optionally cleared; -1 on
 // a failed copy).

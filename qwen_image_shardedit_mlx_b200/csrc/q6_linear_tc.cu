@@ -42,6 +42,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstdlib>
 #include <mutex>
 
@@ -477,6 +478,7 @@ __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
         const int q = warp & 3;
         const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
         const bool gelu = kEpi == kEpiGelu || (kEpi == kEpiGeneral && (p.flags & Q6_EPI_GELU) != 0);
+        const bool precise = kEpi == kEpiGeneral && (p.flags & Q6_EPI_GELU_PRECISE) != 0;
         // Paired stores: lanes 2i and 2i+1 swap one value so that each writes a
         // 32-bit word holding two adjacent output columns (even lane: token j,
         // odd lane: token j+1).  Needs an even row length and 4-byte aligned y.
@@ -551,7 +553,7 @@ __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
 #pragma unroll
                     for (int j = 0; j < kChunk; j += 2) {
                         float2 val = make_float2(__uint_as_float(v[j]) + bias_n, __uint_as_float(v[j + 1]) + bias_n);
-                        if (gelu) val = gelu_tanh2(val);
+                        if (gelu) val = gelu_tanh2_select(val, precise);
                         const float send = odd ? val.x : val.y;
                         const float recv = __shfl_xor_sync(0xffffffffu, send, 1);
                         const int row = m0 + j + (odd ? 1 : 0);
@@ -571,7 +573,7 @@ __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
                 for (int j = 0; j < kChunk; j += 2) {
                     // tokens m0 + j (x) and m0 + j + 1 (y) of this lane's column n
                     float2 val = make_float2(__uint_as_float(v[j]) + bias_n, __uint_as_float(v[j + 1]) + bias_n);
-                    if (gelu) val = gelu_tanh2(val);
+                    if (gelu) val = gelu_tanh2_select(val, precise);
                     if (kEpi == kEpiGeneral && p.gate) val = __fmul2_rn(val, make_float2(gate_n, gate_n));
                     if (kEpi == kEpiGeneral && p.residual && n_ok) {
                         const size_t off = static_cast<size_t>(m0 + j) * p.N + n;
@@ -900,7 +902,7 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restr
         float v = 0.0f;
         for (int s = 0; s < splits; ++s) v += partial[s * total + i];
         if (bias) v += bf16f(bias[n]);
-        if (flags & Q6_EPI_GELU) v = gelu_tanh(v);
+        if (flags & Q6_EPI_GELU) v = gelu_select(v, (flags & Q6_EPI_GELU_PRECISE) != 0);
         if (gate) v *= bf16f(gate[n]);
         if (residual) v += bf16f(residual[i]);
         y[i] = static_cast<uint16_t>(pack_bf16x2(v, 0.0f) & 0xFFFFu);
@@ -945,8 +947,9 @@ __global__ void __launch_bounds__(256) splitk_reduce8_kernel(const float* __rest
             for (int j = 0; j < 8; ++j) v[j] += t[j];
         }
         if (flags & Q6_EPI_GELU) {
+            const bool precise = (flags & Q6_EPI_GELU_PRECISE) != 0;
 #pragma unroll
-            for (int j = 0; j < 8; ++j) v[j] = gelu_tanh(v[j]);
+            for (int j = 0; j < 8; ++j) v[j] = gelu_select(v[j], precise);
         }
         if (gate) {
             bf16x8_to_f32(*reinterpret_cast<const uint4*>(gate + n), t);
@@ -985,17 +988,31 @@ cudaError_t launch_pair_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, siz
     return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
+// Status of a CTA-pair launch that the device refused before anything ran
+// (cluster size or co-scheduling not available); the caller falls back to
+// one CTA per tile.
+constexpr int kPairRefused = -1;
+
+bool pair_launch_refused(cudaError_t e) {
+    return e == cudaErrorInvalidClusterSize || e == cudaErrorLaunchOutOfResources || e == cudaErrorNotSupported;
+}
+
+std::atomic<long> g_pair_fallbacks{0};
+
 template <int NT, bool kSbTma, int kEpi, bool kPair>
 int launch_tc(const LinearArgs& a, cudaStream_t stream) {
     using C = Cfg<NT, kPair>;
-    static int attr_set_for_device[64] = {0};
+    // Opt-in shared memory size, set once per device (idempotent, so two
+    // threads racing to set it both succeed).
+    static std::atomic<bool> attr_set_for_device[kMaxDevices];
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return Q6_ERR_CUDA;
-    if (dev >= 0 && dev < 64 && !attr_set_for_device[dev]) {
+    if (dev < 0 || dev >= kMaxDevices) return Q6_ERR_UNSUPPORTED;
+    if (!attr_set_for_device[dev].load(std::memory_order_acquire)) {
         if (cudaFuncSetAttribute(q6_linear_tc_kernel<NT, kSbTma, kEpi, kPair>,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes) != cudaSuccess)
             return Q6_ERR_CUDA;
-        attr_set_for_device[dev] = 1;
+        attr_set_for_device[dev].store(true, std::memory_order_release);
     }
     CUtensorMap tmap_x, tmap_w, tmap_s, tmap_b, tmap_xa;
     if (!make_map_2d(&tmap_x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.x, a.K, a.M, a.K * 2, kBoxK, C::kXRows,
@@ -1060,9 +1077,10 @@ int launch_tc(const LinearArgs& a, cudaStream_t stream) {
     p.partial = split ? static_cast<float*>(a.workspace) : nullptr;
     if constexpr (kPair) {
         const int pairs = std::min(p.num_items, device_sm_count() / 2);
-        if (launch_pair_pdl(q6_linear_tc_kernel<NT, kSbTma, kEpi, true>, dim3(2 * pairs), dim3(tc_threads(kDqSets)),
-                            C::kSmemBytes, stream, tmap_x, tmap_w, tmap_s, tmap_b, tmap_xa, p) != cudaSuccess)
-            return Q6_ERR_CUDA;
+        const cudaError_t e = launch_pair_pdl(q6_linear_tc_kernel<NT, kSbTma, kEpi, true>, dim3(2 * pairs),
+                                              dim3(tc_threads(kDqSets)), C::kSmemBytes, stream, tmap_x, tmap_w,
+                                              tmap_s, tmap_b, tmap_xa, p);
+        if (e != cudaSuccess) return pair_launch_refused(e) ? kPairRefused : Q6_ERR_CUDA;
     } else {
         const int grid = std::min(p.num_items, device_sm_count());
         if (launch_pdl(q6_linear_tc_kernel<NT, kSbTma, kEpi, false>, dim3(grid), dim3(tc_threads(kDqSets)),
@@ -1096,7 +1114,7 @@ int launch_tc(const LinearArgs& a, cudaStream_t stream) {
 template <int NT, bool kPair = false>
 int launch_tc_sb(const LinearArgs& a, cudaStream_t stream) {
     if (!sb_tma_ok(a)) return launch_tc<NT, false, kEpiGeneral, kPair>(a, stream);
-    if (a.residual || a.gate) return launch_tc<NT, true, kEpiGeneral, kPair>(a, stream);
+    if (a.residual || a.gate || (a.flags & Q6_EPI_GELU_PRECISE)) return launch_tc<NT, true, kEpiGeneral, kPair>(a, stream);
     if (a.flags & Q6_EPI_GELU) return launch_tc<NT, true, kEpiGelu, kPair>(a, stream);
     return launch_tc<NT, true, kEpiPlain, kPair>(a, stream);
 }
@@ -1114,6 +1132,8 @@ bool pair_mode(const LinearArgs& a, int token_tile) {
 }
 
 }  // namespace
+
+long pair_fallbacks() { return g_pair_fallbacks.load(std::memory_order_relaxed); }
 
 int error_word_tc(bool clear) {
     int v = 0;
@@ -1185,10 +1205,13 @@ int launch_linear_tc(const LinearArgs& a, int token_tile, cudaStream_t stream) {
             case 128: st = launch_tc_sb<128, true>(a, stream); break;
             default: break;
         }
-        if (st == Q6_OK) return st;
+        if (st != kPairRefused) return st;
         // A device or context that cannot co-schedule two-CTA clusters refuses
-        // the launch itself (nothing ran): clear that error and run one CTA per tile.
-        if (st == Q6_ERR_CUDA) (void)cudaGetLastError();
+        // the launch itself (nothing ran): clear that launch error, count the
+        // fallback (q6_pair_fallbacks) and run one CTA per tile.  Any other
+        // launch failure is returned as it is.
+        (void)cudaGetLastError();
+        g_pair_fallbacks.fetch_add(1, std::memory_order_relaxed);
     }
     switch (token_tile) {
         case 256: return launch_tc_sb<256>(a, stream);

@@ -20,6 +20,7 @@
 // hidden element the call later reads.  Two calls whose GPU work overlaps (on
 // different streams, or from different host threads without ordering) race on
 // the array and produce wrong results; order them on one stream.
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <mutex>
@@ -37,19 +38,44 @@ static __device__ __align__(256) unsigned char g_noalloc_hidden[kNoAllocScratchB
 constexpr int kMaxDevices = 64;
 std::mutex g_mu;
 void* g_hidden_addr[kMaxDevices] = {};
+void* g_hidden_ctx[kMaxDevices] = {};  // the context the cached address belongs to
 
-// Device address of g_noalloc_hidden on the current device, looked up once per
-// device (the first call on a device does this set-up; make that first call
-// before any stream capture).
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+
+CtxGetCurrentFn ctx_get_current() {
+    static CtxGetCurrentFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<CtxGetCurrentFn>(ptr);
+    });
+    return fn;
+}
+
+// Device address of g_noalloc_hidden on the current device.  It is looked up
+// once per device and context with cudaGetSymbolAddress (the first call on a
+// device does this set-up; make that first call before any stream capture)
+// and looked up again when the device's context changes (after a
+// cudaDeviceReset the module, and with it the array, is loaded anew).
 int hidden_address(void** out) {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return Q6_ERR_CUDA;
     if (dev < 0 || dev >= kMaxDevices) return Q6_ERR_UNSUPPORTED;
+    // Binding the (already current) device again makes the runtime initialise
+    // its primary context on this thread, so that the driver reports it as current.
+    if (cudaSetDevice(dev) != cudaSuccess) return Q6_ERR_CUDA;
+    CUcontext ctx = nullptr;
+    const CtxGetCurrentFn get = ctx_get_current();
+    if (!get || get(&ctx) != CUDA_SUCCESS) return Q6_ERR_CUDA;
     std::lock_guard<std::mutex> lock(g_mu);
-    if (g_hidden_addr[dev] == nullptr) {
+    if (g_hidden_addr[dev] == nullptr || g_hidden_ctx[dev] != static_cast<void*>(ctx)) {
         void* p = nullptr;
         if (cudaGetSymbolAddress(&p, g_noalloc_hidden) != cudaSuccess || p == nullptr) return Q6_ERR_CUDA;
         g_hidden_addr[dev] = p;
+        g_hidden_ctx[dev] = static_cast<void*>(ctx);
     }
     *out = g_hidden_addr[dev];
     return Q6_OK;

@@ -88,23 +88,28 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parit
 }
 
 // Wait for the phase with the given parity to complete.  Gives up (returns
-// false) when the CTA-wide abort flag is raised or after kWaitLimitNs; in the
+// false) when the CTA-wide abort flag is raised or after limit_ns; in the
 // latter case it raises the abort flag and records `site` in g_device_error.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
-                                          int site) {
+// The clock is checked every 16 suspended tries (each sleeps at most `hint_ns`).
+__device__ __forceinline__ bool mbar_wait_limit(uint32_t bar, uint32_t parity, volatile int* abort_flag, int site,
+                                                uint64_t limit_ns, uint32_t hint_ns = 20000u) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_timer_ns();
     for (uint32_t i = 1;; ++i) {
-        if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
+        if (mbar_try_wait_sleep(bar, parity, hint_ns)) return true;
         if ((i & 15u) == 0) {
             if (*abort_flag) return false;
-            if (global_timer_ns() - t0 > kWaitLimitNs) {
+            if (global_timer_ns() - t0 > limit_ns) {
                 *abort_flag = 1;
                 record_error(site);
                 return false;
             }
         }
     }
+}
+
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int site) {
+    return mbar_wait_limit(bar, parity, abort_flag, site, kWaitLimitNs);
 }
 
 // Bounded wait that ignores the abort flag (used to drain in-flight copies
@@ -381,16 +386,24 @@ __device__ __forceinline__ float tanh_fast(float x) {
 }
 
 // GELU with the tanh approximation, 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))),
-// the formula of mlx nn.gelu_approx used by the reference epilogue.
+// the formula of mlx nn.gelu_approx used by the reference epilogue.  The fast
+// form takes the hardware tanh.approx.f32 (about 2^-11 relative error); the
+// precise form CUDA's tanhf, for callers that ask for the reference kernel's
+// metal::precise::tanh (Q6_EPI_GELU_PRECISE).
 __device__ __forceinline__ float gelu_tanh(float x) {
     const float x3 = x * x * x;
     const float inner = 0.7978845608028654f * (x + 0.044715f * x3);
-#if defined(Q6_PRECISE_GELU)
-    const float t = tanhf(inner);
-#else
-    const float t = tanh_fast(inner);
-#endif
-    return 0.5f * x * (1.0f + t);
+    return 0.5f * x * (1.0f + tanh_fast(inner));
+}
+
+__device__ __forceinline__ float gelu_tanh_precise(float x) {
+    const float x3 = x * x * x;
+    const float inner = 0.7978845608028654f * (x + 0.044715f * x3);
+    return 0.5f * x * (1.0f + tanhf(inner));
+}
+
+__device__ __forceinline__ float gelu_select(float x, bool precise) {
+    return precise ? gelu_tanh_precise(x) : gelu_tanh(x);
 }
 
 // The same GELU on two values with packed fp32x2 arithmetic:
@@ -400,13 +413,14 @@ __device__ __forceinline__ float2 gelu_tanh2(float2 x) {
     constexpr float kc = 0.7978845608028654f * 0.044715f;
     const float2 x2 = __fmul2_rn(x, x);
     const float2 inner = __fmul2_rn(x, __ffma2_rn(make_float2(kc, kc), x2, make_float2(k, k)));
-#if defined(Q6_PRECISE_GELU)
-    const float2 t = make_float2(tanhf(inner.x), tanhf(inner.y));
-#else
     const float2 t = make_float2(tanh_fast(inner.x), tanh_fast(inner.y));
-#endif
     const float2 h = __fmul2_rn(make_float2(0.5f, 0.5f), x);
     return __ffma2_rn(h, t, h);
+}
+
+__device__ __forceinline__ float2 gelu_tanh2_select(float2 x, bool precise) {
+    if (precise) return make_float2(gelu_tanh_precise(x.x), gelu_tanh_precise(x.y));
+    return gelu_tanh2(x);
 }
 
 }  // namespace q6

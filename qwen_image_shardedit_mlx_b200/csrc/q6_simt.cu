@@ -7,9 +7,9 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
-#include <cstdlib>
-
 #include <algorithm>
+#include <atomic>
+#include <cstdlib>
 
 #include "q6_dequant.cuh"
 #include "q6_internal.h"
@@ -128,7 +128,7 @@ __global__ void __launch_bounds__(256) linear_simt_kernel(const LinearArgs a) {
                 if (lane == i) v = acc[i];
             const int64_t m = m0 + lane;
             if (a.bias) v += bf16f(a.bias[n]);
-            if (a.flags & Q6_EPI_GELU) v = gelu_precise(v);
+            if (a.flags & (Q6_EPI_GELU | Q6_EPI_GELU_PRECISE)) v = gelu_precise(v);
             if (a.gate) v *= bf16f(a.gate[n]);
             if (a.residual) v += bf16f(a.residual[m * a.N + n]);
             if constexpr (kF32) {
@@ -141,7 +141,33 @@ __global__ void __launch_bounds__(256) linear_simt_kernel(const LinearArgs a) {
     }
 }
 
+// ------------------------------------------------------------ self-test
+
+// One thread waits on an mbarrier that nothing arrives at, through the same
+// bounded wait the GEMM pipeline uses, so the wait runs out after limit_ns,
+// records Q6_SITE_SELFTEST in the device error word and returns.  No copy is
+// in flight and no tensor memory is held when it gives up.
+__global__ void __launch_bounds__(32) selftest_wait_kernel(uint64_t limit_ns) {
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ int abort_flag;
+    if (threadIdx.x == 0) {
+        mbar_init(smem_u32(&bar), 1);
+        abort_flag = 0;
+        fence_mbar_init();
+    }
+    __syncwarp();
+    if (threadIdx.x == 0) {
+        // phase 0 of a barrier expecting one arrival that never comes
+        (void)mbar_wait_limit(smem_u32(&bar), 0u, &abort_flag, Q6_SITE_SELFTEST, limit_ns, 1000u);
+    }
+}
+
 }  // namespace
+
+int launch_selftest_wait(uint64_t limit_ns, cudaStream_t stream) {
+    selftest_wait_kernel<<<1, 32, 0, stream>>>(limit_ns);
+    return cudaGetLastError() == cudaSuccess ? Q6_OK : Q6_ERR_CUDA;
+}
 
 int error_word_simt(bool clear) {
     int v = 0;
@@ -154,25 +180,27 @@ int error_word_simt(bool clear) {
 }
 
 bool pdl_enabled() {
-    static int v = -1;  // a benign race: every thread computes the same value
-    if (v < 0) {
+    static std::atomic<int> v{-1};  // every thread computes the same value
+    int cur = v.load(std::memory_order_relaxed);
+    if (cur < 0) {
         const char* e = std::getenv("Q6_PDL");
-        v = (e && e[0] == '0') ? 0 : 1;
+        cur = (e && e[0] == '0') ? 0 : 1;
+        v.store(cur, std::memory_order_relaxed);
     }
-    return v == 1;
+    return cur == 1;
 }
 
 int device_sm_count() {
-    static int cached[64] = {0};
+    static std::atomic<int> cached[kMaxDevices];
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return 148;
-    if (dev < 0 || dev >= 64) return 148;
-    if (cached[dev] == 0) {
-        int n = 0;
+    if (dev < 0 || dev >= kMaxDevices) return 148;
+    int n = cached[dev].load(std::memory_order_relaxed);
+    if (n == 0) {
         if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
-        cached[dev] = n;
+        cached[dev].store(n, std::memory_order_relaxed);
     }
-    return cached[dev];
+    return n;
 }
 
 int launch_dequantize(const uint32_t* w, const uint16_t* scales, const uint16_t* qbiases,

@@ -105,13 +105,16 @@ def q6_linear(
     lora: tuple[torch.Tensor, torch.Tensor, float] | None = None,
     path: str = "auto",
     out: torch.Tensor | None = None,
+    precise_gelu: bool = False,
 ) -> torch.Tensor:
     """y = epilogue(x @ dequant(W)^T) for x [..., K]; returns [..., N].
 
     bf16 x runs the tensor-core path (bf16-dequantised weights, fp32
     accumulation) or, for a handful of rows, the CUDA-core path; fp32 x runs
     the CUDA-core path with fp32 weights and returns fp32.
-    Epilogue order: + bias, GELU, then residual + gate * value.
+    Epilogue order: + bias, GELU, then residual + gate * value.  The tensor
+    path's GELU takes the hardware tanh approximation unless ``precise_gelu``
+    asks for the accurate tanh the reference kernel uses.
     """
 
     n, k = check_q6_weights(weight, scales, biases, group_size)
@@ -123,7 +126,9 @@ def q6_linear(
     m = int(flat.shape[0])
     if m == 0:
         return torch.empty(leading + (n,), dtype=x.dtype, device=dev)
-    flags = _lib.Q6_EPI_GELU if apply_gelu else _lib.Q6_EPI_NONE
+    flags = _lib.Q6_EPI_NONE
+    if apply_gelu:
+        flags = _lib.Q6_EPI_GELU | (_lib.Q6_EPI_GELU_PRECISE if precise_gelu else 0)
     sc = scales.to(torch.bfloat16).contiguous()
     qb = biases.to(torch.bfloat16).contiguous()
     bias_t = _bf16_vec(bias, n, "bias")
@@ -160,10 +165,10 @@ def q6_linear(
             raise ValueError(f"LoRA rank {rank} exceeds the fused maximum {MAX_FUSED_RANK}")
         la, lb = pad_lora_rank(la, lb)  # the kernel takes ranks in steps of 32
         rank = int(la.shape[1])
-        # x @ A is a plain bf16 GEMM (fp32 accumulation, bf16 result, as the
-        # reference's LoRA linear computes it); the library fuses s * (xa @ B)
-        # into the q6 product's accumulator.
-        xa = torch.matmul(xb, la).contiguous()
+        # x @ A (fp32 accumulation, bf16 result, as the reference's LoRA
+        # linear computes it) by the library's pre-pass kernel; the q6 kernel
+        # then fuses s * (xa @ B) into its own accumulator.
+        xa = lora_xa(xb, la.contiguous())
     y = out if out is not None else torch.empty((m, n), dtype=torch.bfloat16, device=dev)
     # split-K workspace for the tensor-core path when its tiles alone leave SMs idle
     ws_bytes = int(_lib.lib().q6_linear_tc_workspace_bytes(m, n, k)) if path != "simt" else 0
@@ -175,6 +180,40 @@ def q6_linear(
     )
     _lib.check(st, "q6_linear_bf16")
     return y.reshape(leading + (n,))
+
+
+def lora_xa(x: torch.Tensor, a: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """xa = x @ A for x bf16 [M, K] and A bf16 [K, r] (r a multiple of 32 up
+    to 256): the LoRA pre-pass kernel, fp32 accumulation, bf16 result."""
+
+    dev = _require_cuda(x, a)
+    m, k = int(x.shape[0]), int(x.shape[1])
+    r = int(a.shape[1])
+    if tuple(a.shape) != (k, r):
+        raise ValueError(f"A must be ({k}, r), got {tuple(a.shape)}")
+    xb = x.to(torch.bfloat16).contiguous()
+    ab = a.to(torch.bfloat16).contiguous()
+    y = out if out is not None else torch.empty((m, r), dtype=torch.bfloat16, device=dev)
+    _lib.check(_lib.lib().q6_lora_xa_bf16(xb.data_ptr(), ab.data_ptr(), y.data_ptr(), m, k, r, _stream(dev)),
+               "q6_lora_xa_bf16")
+    return y
+
+
+def selftest_bounded_wait(limit_ns: int = 1_000_000, device: torch.device | str | None = None) -> int:
+    """Run the library's bounded-wait self-test on ``device`` and return the
+    device error word afterwards (Q6_SITE_SELFTEST when the wait gave up as
+    designed).  Clears nothing: call clear_device_error() after reading it."""
+
+    dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    with torch.cuda.device(dev):
+        _lib.check(_lib.lib().q6_selftest_bounded_wait(int(limit_ns), _stream(dev)), "q6_selftest_bounded_wait")
+        return device_error()
+
+
+def pair_fallback_count() -> int:
+    """Tensor-path launches whose CTA-pair cluster the device refused (they ran one CTA per tile)."""
+
+    return int(_lib.lib().q6_pair_fallback_count())
 
 
 def mlp_workspace_bytes(m: int, h: int, d: int | None = None) -> int:

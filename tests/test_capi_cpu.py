@@ -21,7 +21,7 @@ HEADER = Path(__file__).resolve().parents[1] / "include" / "q6_b200.h"
 
 def _declared_symbols() -> list[str]:
     text = HEADER.read_text()
-    return sorted(set(re.findall(r"Q6_API\s+[a-z_ ]+\*?\s*(q6_[a-z0-9_]+)\s*\(", text)))
+    return sorted(set(re.findall(r"Q6_API\s+[a-z0-9_ ]+\*?\s*(q6_[a-z0-9_]+)\s*\(", text)))
 
 
 def test_header_declares_expected_entry_points():
@@ -35,7 +35,7 @@ def test_library_exports_every_declared_symbol():
     lib = _lib.lib()
     for name in _declared_symbols():
         assert hasattr(lib, name), name
-    assert lib.q6_abi_version() == 1
+    assert lib.q6_abi_version() == 2
 
 
 def test_status_strings():
@@ -47,9 +47,7 @@ def test_status_strings():
 def test_workspace_sizes():
     lib = _lib.lib()
     assert lib.q6_mlp_workspace_bytes(3456, 12288) == 3456 * 12288 * 2
-    # The fused LoRA delta takes x @ A from the caller, so no path needs workspace.
-    assert lib.q6_linear_workspace_bytes(3456, 64) == 0
-    assert lib.q6_linear_workspace_bytes(3456, 0) == 0
+    assert lib.q6_mlp_workspace_bytes(0, 12288) == 0
 
 
 def _linear(lib, **kw):
@@ -68,6 +66,7 @@ def test_argument_validation_without_gpu():
     assert _linear(lib, gs=16) == _lib.Q6_ERR_GROUP_SIZE
     assert _linear(lib, K=96, gs=64) == _lib.Q6_ERR_SHAPE
     assert _linear(lib, flags=8) == _lib.Q6_ERR_INVALID_ARGUMENT
+    assert _linear(lib, flags=4) == _lib.Q6_ERR_INVALID_ARGUMENT
     assert _linear(lib, w=258) == _lib.Q6_ERR_ALIGNMENT
     # LoRA: x @ A and B come together, with a positive rank
     assert _linear(lib, lora_xa=256) == _lib.Q6_ERR_INVALID_ARGUMENT
@@ -80,6 +79,22 @@ def test_argument_validation_without_gpu():
     err = ctypes.c_int(0)
     assert lib.q6_get_device_error(None) == _lib.Q6_ERR_INVALID_ARGUMENT
     del err
+    # LoRA pre-pass: rank a multiple of 32 in [32, 256], K a multiple of 16, 16-byte alignment
+    assert lib.q6_lora_xa_bf16(None, 16, 16, 4, 64, 64, None) == _lib.Q6_ERR_INVALID_ARGUMENT
+    assert lib.q6_lora_xa_bf16(16, 16, 16, 4, 64, 48, None) == _lib.Q6_ERR_SHAPE
+    assert lib.q6_lora_xa_bf16(16, 16, 16, 4, 64, 288, None) == _lib.Q6_ERR_SHAPE
+    assert lib.q6_lora_xa_bf16(16, 16, 16, 4, 72, 64, None) == _lib.Q6_ERR_SHAPE
+    assert lib.q6_lora_xa_bf16(18, 16, 16, 4, 64, 64, None) == _lib.Q6_ERR_ALIGNMENT
+    # joint-row add + adaLN modulate
+    add_ln = lib.q6_add_layernorm_modulate_bf16
+    assert add_ln(16, None, 16, 16, 16, 16, 4, 256, 0, 0, 0, 1e-6, None) == _lib.Q6_ERR_INVALID_ARGUMENT  # h_out without add
+    assert add_ln(16, 16, None, 16, 16, 16, 4, 256, 0, 10, 20, 1e-6, None) == _lib.Q6_ERR_INVALID_ARGUMENT  # text_len > seq_len
+    assert add_ln(16, 16, None, 16, 16, 16, 4, 320, 0, 0, 0, 1e-6, None) == _lib.Q6_ERR_SHAPE
+    assert add_ln(16, 24, None, 16, 16, 16, 4, 256, 0, 0, 0, 1e-6, None) == _lib.Q6_ERR_ALIGNMENT
+    # self-test limits: 1 us .. 1 s
+    assert lib.q6_selftest_bounded_wait(10, None) == _lib.Q6_ERR_INVALID_ARGUMENT
+    assert lib.q6_selftest_bounded_wait(2_000_000_000, None) == _lib.Q6_ERR_INVALID_ARGUMENT
+    assert lib.q6_pair_fallback_count() == 0
 
 
 def test_torch_quantizer_matches_oracle_bit_for_bit():

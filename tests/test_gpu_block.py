@@ -112,6 +112,85 @@ def test_block_vs_oracle(dim, heads, img_hw, txt):
     assert_close(f32(t_out[0]), t_ref, what=f"block text stream d{dim}")
 
 
+def _block_pair_gpu(seed: int, dim: int, heads: int, gs: int = 64):
+    """A random block quantised on the GPU (torch quantiser, bit-identical to
+    the oracle's) and the oracle's view of the same weights."""
+
+    from qwen_image_shardedit_mlx_b200.quantize import quantize_affine_q6
+
+    from helpers import to_bits
+
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    lin_o, lin_t = {}, {}
+    for name, (fo, fi) in ob.BLOCK_LINEARS.items():
+        w = torch.randn((fo * dim, fi * dim), generator=g, device="cuda") * 0.02
+        q, s, b = quantize_affine_q6(w, gs)
+        bias = (torch.randn((fo * dim,), generator=g, device="cuda") * 0.01).to(torch.bfloat16)
+        lin_t[name] = QuantizedLinear(q, s, b, bias, group_size=gs)
+        lin_o[name] = oracle.Q6Weights(q.view(torch.int32).cpu().numpy().view(np.uint32), to_bits(s), to_bits(b),
+                                       to_bits(bias), gs)
+    norms_t = {n: (1.0 + 0.1 * torch.randn((128,), generator=g, device="cuda")).to(torch.bfloat16) for n in ob.NORMS}
+    ow = ob.BlockWeights(lin_o, {n: f32(v) for n, v in norms_t.items()}, heads)
+    return ow, QwenTransformerBlock(lin_t, norms_t, heads=heads)
+
+
+def test_full_size_block_vs_oracle_on_sampled_rows():
+    """The Qwen-Image block at its real shape (3072 wide, 24 heads, 3456 image
+    + 256 text tokens): the whole block runs on the GPU; the oracle computes
+    keys and values from every row and the outputs of 16 sampled image rows
+    and 8 sampled text rows."""
+
+    ow, tb = _block_pair_gpu(3072, 3072, 24)
+    rng = np.random.default_rng(3712)
+    s_img, s_txt, d = 3456, 256, 3072
+    hidden = random_bf16(rng, (s_img, d))
+    enc = random_bf16(rng, (s_txt, d))
+    temb = random_bf16(rng, (d,))
+    ia, ta = qwen_rope_angles([(36, 48), (36, 48)], s_txt)
+    rope = rope_tables(ia, ta, "cuda")
+    t_out, i_out = tb(from_bits(hidden)[None], from_bits(enc)[None], from_bits(temb)[None], rope)
+    torch.cuda.synchronize()
+    ir = np.unique(np.concatenate([[0, s_img - 1], rng.choice(s_img, 14, replace=False)]))
+    tr = np.unique(np.concatenate([[0, s_txt - 1], rng.choice(s_txt, 6, replace=False)]))
+    rf = [f32(r) for r in rope]
+    t_ref, i_ref = ob.block_forward_rows(ow, oracle.bf16_bits_to_f32(hidden), oracle.bf16_bits_to_f32(enc),
+                                         oracle.bf16_bits_to_f32(temb), *rf, img_rows=ir, txt_rows=tr)
+    assert_close(f32(i_out[0])[ir], i_ref, what="full-size block, image rows")
+    assert_close(f32(t_out[0])[tr], t_ref, what="full-size block, text rows")
+
+
+def test_block_with_padded_text_mask_vs_oracle():
+    """A padded prompt: the last text tokens are padding (mask 0), so no query
+    may attend to them as keys; image and text outputs follow the masked
+    oracle and differ from the unmasked block."""
+
+    rng = np.random.default_rng(41)
+    dim, heads, img_hw, txt = 768, 6, (10, 20), 40
+    ow, tb = _block_pair(rng, dim, heads)
+    s_img = img_hw[0] * img_hw[1]
+    hidden = random_bf16(rng, (s_img, dim))
+    enc = random_bf16(rng, (txt, dim))
+    temb = random_bf16(rng, (dim,))
+    mask = np.ones(txt, dtype=np.float32)
+    mask[27:] = 0.0
+    ia, ta = qwen_rope_angles([img_hw], txt)
+    rope = rope_tables(ia, ta, "cuda")
+    args = (from_bits(hidden)[None], from_bits(enc)[None], from_bits(temb)[None], rope)
+    t_m, i_m = tb(*args, encoder_mask=torch.from_numpy(mask)[None].cuda())
+    t_u, i_u = tb(*args)
+    torch.cuda.synchronize()
+    rf = [f32(r) for r in rope]
+    t_ref, i_ref = ob.block_forward(ow, oracle.bf16_bits_to_f32(hidden), oracle.bf16_bits_to_f32(enc),
+                                    oracle.bf16_bits_to_f32(temb), *rf, text_mask=mask)
+    assert_close(f32(i_m[0]), i_ref, what="masked block image stream")
+    assert_close(f32(t_m[0]), t_ref, what="masked block text stream")
+    assert float((i_m.float() - i_u.float()).abs().max()) > 1e-2  # the mask changes the image stream
+    # an all-ones mask is the unmasked block
+    t_1, i_1 = tb(*args, encoder_mask=torch.ones((1, txt), device="cuda"))
+    torch.cuda.synchronize()
+    assert_close(f32(i_1[0]), f32(i_u[0]), what="all-ones mask", bf16_output=False)
+
+
 def test_full_size_block_runs():
     g = torch.Generator(device="cuda").manual_seed(5)
     blk = QwenTransformerBlock.random(generator=g)

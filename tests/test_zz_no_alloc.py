@@ -67,6 +67,49 @@ def test_noalloc_residual_gate_epilogue():
     assert_close(f32(y), f32(ref))
 
 
+def test_noalloc_at_the_array_limit():
+    """The largest problem the array holds (M * H * 2 bytes = 32 MiB, 1365
+    tokens at H = 12288), where no split-K space is left over."""
+
+    h, d = 12288, 3072
+    m = SCRATCH_BYTES // (2 * h)
+    rng = np.random.default_rng(1365)
+    fc1 = weights_to_torch(random_weights(rng, h, d, 64))
+    fc2 = weights_to_torch(random_weights(rng, d, h, 64))
+    x = from_bits(random_bf16(rng, (m, d)))
+    ref = ops.q6_mlp(x, fc1, fc2, group_size=64)
+    y = torch.full((m, d), float("nan"), dtype=torch.bfloat16, device="cuda")
+    st = _noalloc(x, fc1, fc2, y, m, d, h)
+    assert st == _lib.Q6_OK, _lib.status_string(st)
+    torch.cuda.synchronize()
+    assert bool(torch.isfinite(y).all())
+    assert_close(f32(y), f32(ref), what="array limit")
+
+
+def test_noalloc_small_m_uses_leftover_space_for_split_k():
+    """64 tokens of the image-FF shapes: the array's space past the hidden
+    activations holds the split-K partials of both linears (checked with the
+    library's own size query), and the result matches the workspace entry
+    point with the same split-K space."""
+
+    h, d, m = 12288, 3072, 64
+    lib = _lib.lib()
+    split = max(lib.q6_linear_tc_workspace_bytes(m, h, d), lib.q6_linear_tc_workspace_bytes(m, d, h))
+    assert split > 0
+    assert (m * h * 2 + 255) // 256 * 256 + split <= SCRATCH_BYTES
+    rng = np.random.default_rng(64)
+    fc1 = weights_to_torch(random_weights(rng, h, d, 64))
+    fc2 = weights_to_torch(random_weights(rng, d, h, 64))
+    for call in range(2):
+        x = from_bits(random_bf16(rng, (m, d)))
+        ref = ops.q6_mlp(x, fc1, fc2, group_size=64)  # its own workspace carries split-K space too
+        y = torch.full((m, d), float("nan"), dtype=torch.bfloat16, device="cuda")
+        assert _noalloc(x, fc1, fc2, y, m, d, h) == _lib.Q6_OK
+        torch.cuda.synchronize()
+        assert bool(torch.isfinite(y).all())
+        assert torch.equal(y, ref), f"call {call}: split-K in the array differs from split-K in a workspace"
+
+
 def test_noalloc_rejects_problems_larger_than_its_array():
     h = 12288
     m_max = SCRATCH_BYTES // (2 * h)  # 1365 tokens
