@@ -55,6 +55,7 @@ def parse_args() -> argparse.Namespace:
     ap.add_argument("--no-gemv", action="store_true", help="skip the skinny-M GEMV side measurement")
     ap.add_argument("--no-block", action="store_true", help="skip the full MMDiT block measurement")
     ap.add_argument("--no-sweep", action="store_true", help="skip the q6 linear shape / M / group-size sweep")
+    ap.add_argument("--no-stack", action="store_true", help="skip the 60-block stack (config 5)")
     return ap.parse_args()
 
 
@@ -325,6 +326,8 @@ def run_ours(args, world: int, rank: int, local: int) -> dict | None:
 
     # ---- one full MMDiT block (3456 image + 256 text tokens), tensor-parallel over the ranks
     block = None if args.no_block else measure_block(dev, world, rank)
+    # ---- config 5: the 60-block stack, 8 steps, batch 2, tensor-parallel over the ranks
+    stack = None if args.no_stack else measure_stack(dev, world, rank)
 
     # ---- skinny-M GEMV side measurement (HBM-bound), rank 0 only
     gemv = None
@@ -390,93 +393,218 @@ def run_ours(args, world: int, rank: int, local: int) -> dict | None:
         line["sweep"] = sweep
     if block is not None:
         line["block"] = block
+    if stack is not None:
+        line["stack"] = stack
     if not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline_port()
     return line
 
 
 BLOCK_IMG, BLOCK_TXT, BLOCK_HEADS = 3456, 256, 24
+STACK_BLOCKS, STACK_STEPS, STACK_BATCH = 60, 8, 2
 
 
-def measure_block(dev, world: int, rank: int, steps: int = 10) -> dict | None:
-    """Device time of one Qwen-Image MMDiT block forward (batch 1, all 14
-    linears q6 gs64, joint attention over 3712 tokens).  With N ranks the
-    block is tensor-parallel (heads and FF columns split, two NCCL
-    all-reduces per block); the time is the slowest rank's."""
+def _graph_ms(run, world: int, steps: int) -> tuple[float, float]:
+    """(graph-replay ms, eager ms) per call of ``run``: device time from CUDA
+    events over ``steps`` calls, max over ranks.  The graph holds the whole
+    call (every launch and collective), captured once after a warm-up."""
 
     import torch
 
-    from qwen_image_shardedit_mlx_b200 import ops
-    from qwen_image_shardedit_mlx_b200.block import (
-        QwenTransformerBlock,
-        TensorParallelQwenBlock,
-        block_flops,
-        qwen_rope_angles,
-        rope_tables,
-    )
-
-    g = torch.Generator(device=dev).manual_seed(2025)  # the same block on every rank
-    full = QwenTransformerBlock.random(DIM, BLOCK_HEADS, generator=g, device=dev)
-    blk = full if world == 1 else TensorParallelQwenBlock(full, world, rank)
-    hidden = torch.randn((1, BLOCK_IMG, DIM), generator=g, device=dev).to(torch.bfloat16)
-    enc = torch.randn((1, BLOCK_TXT, DIM), generator=g, device=dev).to(torch.bfloat16)
-    temb = torch.randn((1, DIM), generator=g, device=dev).to(torch.bfloat16)
-    ia, ta = qwen_rope_angles([(36, 48), (36, 48)], BLOCK_TXT)
-    rope = rope_tables(ia, ta, dev)
-    stream = torch.cuda.current_stream(dev)
+    stream = torch.cuda.current_stream()
     for _ in range(3):
-        blk(hidden, enc, temb, rope)
+        run()
     torch.cuda.synchronize()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
 
-    def timed(run) -> float:
+    def timed(fn) -> float:
         barrier(world)
         torch.cuda.synchronize()
         e0.record(stream)
         for _ in range(steps):
-            run()
+            fn()
         e1.record(stream)
         torch.cuda.synchronize()
         barrier(world)
         return max_over_ranks(e0.elapsed_time(e1) / steps, world)
 
-    eager_ms = timed(lambda: blk(hidden, enc, temb, rope))
-    # the block's ~30 launches (and all-reduces) captured once and replayed: a
-    # serving loop pays no per-launch host cost
-    side = torch.cuda.Stream(dev)
+    eager_ms = timed(run)
+    side = torch.cuda.Stream()
     side.wait_stream(stream)
     with torch.cuda.stream(side):
-        blk(hidden, enc, temb, rope)
+        run()
     stream.wait_stream(side)
     torch.cuda.synchronize()
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph):
-        out = blk(hidden, enc, temb, rope)
+        run()
     graph.replay()
     torch.cuda.synchronize()
     ms = timed(graph.replay)
-    finite = bool(torch.isfinite(out[0]).all()) and bool(torch.isfinite(out[1]).all())
     del graph  # holds NCCL work on N > 1: released before the process group goes
     torch.cuda.synchronize()
-    assert ops.device_error() == 0 and finite, "block benchmark produced a device error or non-finite output"
+    return ms, eager_ms
+
+
+def _block_inputs(dev, batch: int, seed: int):
+    import torch
+
+    from qwen_image_shardedit_mlx_b200.block import joint_rope, qwen_rope_angles, rope_tables
+
+    g = torch.Generator(device=dev).manual_seed(seed)
+    seq = BLOCK_IMG + BLOCK_TXT
+    x = torch.randn((batch * seq, DIM), generator=g, device=dev).to(torch.bfloat16)
+    temb = torch.randn((batch, DIM), generator=g, device=dev).to(torch.bfloat16)
+    ia, ta = qwen_rope_angles([(36, 48), (36, 48)], BLOCK_TXT)
+    return x, temb, joint_rope(rope_tables(ia, ta, dev)), seq
+
+
+def measure_block(dev, world: int, rank: int, steps: int = 10) -> dict | None:
+    """Device time of one Qwen-Image MMDiT block forward (3456 image + 256
+    text tokens, all 14 linears q6 gs64, joint attention over 3712 tokens), at
+    batch 1 (config 3) and batch 2 (the per-block cost of config 5's CFG pair).
+    With N ranks the block is tensor-parallel with sequence-parallel rows
+    (all-gather before each column-parallel GEMM, reduce-scatter after each
+    row-parallel one); rank 0 also times the single-GPU block, so the line
+    carries the strong-scaling efficiency ms_1gpu / (N ms)."""
+
+    import torch
+
+    from qwen_image_shardedit_mlx_b200 import ops
+    from qwen_image_shardedit_mlx_b200.block import QwenTransformerBlock, TensorParallelQwenBlock, block_flops
+
+    g = torch.Generator(device=dev).manual_seed(2025)  # the same block on every rank
+    full = QwenTransformerBlock.random(DIM, BLOCK_HEADS, generator=g, device=dev)
+    tp = TensorParallelQwenBlock(full, world, rank) if world > 1 else None
+    out = {}
+    for batch in (1, 2):
+        x, temb, rope_j, seq = _block_inputs(dev, batch, 7 + batch)
+        y = torch.empty_like(x)
+        rows_local = x.shape[0] // world
+        x_local = x[rank * rows_local:(rank + 1) * rows_local].contiguous()
+        one = lambda: full.forward_joint(x, temb, rope_j, batch, BLOCK_TXT, out=y)  # noqa: E731
+        if tp is None:
+            ms, eager_ms = _graph_ms(one, world, steps)
+            ms_1 = ms
+        else:
+            ms, eager_ms = _graph_ms(lambda: tp.finish(tp.forward_local(x_local, temb, rope_j, batch, seq, BLOCK_TXT)),
+                                     world, steps)
+            ms_1 = None
+            if rank == 0:
+                ms_1, _ = _graph_ms(one, 1, steps)
+            barrier(world)
+        torch.cuda.synchronize()
+        assert ops.device_error() == 0, "block benchmark raised the device error word"
+        flop = batch * block_flops(BLOCK_IMG, BLOCK_TXT, DIM)
+        out[f"b{batch}"] = {
+            "ms": round(ms, 4), "TFLOP/s": round(flop / (ms * 1e-3) / 1e12, 1), "eager_ms": round(eager_ms, 4),
+            "ms_1gpu": None if ms_1 is None else round(ms_1, 4),
+            "efficiency_vs_1gpu": None if ms_1 is None else round(ms_1 / (world * ms), 4),
+            "batch": batch, "flop_per_call": flop,
+        }
     if rank != 0:
         return None
-    flop = block_flops(BLOCK_IMG, BLOCK_TXT, DIM)
-    return {
-        "ms": round(ms, 4),
-        "TFLOP/s": round(flop / (ms * 1e-3) / 1e12, 1),
-        "eager_ms": round(eager_ms, 4),
+    res = dict(out["b1"])
+    res.update({
         "n_gpus": world,
-        "parallelism": "single GPU" if world == 1 else f"tensor-parallel x{world} (heads and FF columns), "
-                                                        "2 NCCL all-reduces per block",
-        "flop_per_block": flop,
+        "batch2": out["b2"],
+        "parallelism": "single GPU" if world == 1 else
+        f"tensor-parallel x{world} (heads and FF columns) with sequence-parallel rows between the GEMMs: "
+        "2 all-gathers + 2 reduce-scatters (NCCL) per block",
         "shape": f"{BLOCK_IMG} image + {BLOCK_TXT} text tokens, hidden {DIM}, {BLOCK_HEADS} heads x 128, "
-                 "FF 4x, all 14 linears q6 gs64, batch 1",
+                 "FF 4x, all 14 linears q6 gs64",
         "steps": steps,
-        "note": "device time per block forward replayed from a CUDA graph (eager_ms: launched from Python "
-                "each time); CUDA events, max over ranks; attention is the library "
-                "scaled_dot_product_attention kernel",
+        "note": "device time per block forward replayed from a CUDA graph (eager_ms: launched from Python each "
+                "time); CUDA events, max over ranks; attention is the library scaled_dot_product_attention kernel; "
+                "ms_1gpu is the same block on one GPU timed on rank 0 in the same run",
+    })
+    return res
+
+
+def measure_stack(dev, world: int, rank: int, blocks: int = STACK_BLOCKS, steps: int = STACK_STEPS) -> dict | None:
+    """Config 5: the 60-block q6 MMDiT stack, batch 2 (CFG cond / uncond),
+    3456 image + 256 text tokens per sample, 8 denoising steps, tensor-parallel
+    over the ranks.  Each rank builds its own shards of 60 random blocks
+    (seeded per block); the joint rows stay sequence-sharded from block to
+    block, the residual add of each block folded into the next block's first
+    modulate.  One denoising step (every block, a new timestep embedding) is
+    captured in a CUDA graph and replayed ``steps`` times; the time is device
+    time, max over ranks.  Only the block stack is timed (the model's input
+    and output projections and the sampler are outside the q6 path)."""
+
+    import torch
+
+    from qwen_image_shardedit_mlx_b200 import ops
+    from qwen_image_shardedit_mlx_b200.block import QwenTransformerBlock, TensorParallelQwenBlock, block_flops
+
+    stack = []
+    for i in range(blocks):
+        g = torch.Generator(device=dev).manual_seed(10_000 + i)
+        full = QwenTransformerBlock.random(DIM, BLOCK_HEADS, generator=g, device=dev)
+        stack.append(TensorParallelQwenBlock(full, world, rank))
+        del full
+    torch.cuda.empty_cache()
+    batch = STACK_BATCH
+    x, _, rope_j, seq = _block_inputs(dev, batch, 99)
+    rows_local = x.shape[0] // world
+    x_local = x[rank * rows_local:(rank + 1) * rows_local].contiguous()
+    g = torch.Generator(device=dev).manual_seed(5)
+    tembs = [torch.randn((batch, DIM), generator=g, device=dev).to(torch.bfloat16) for _ in range(steps)]
+    temb = tembs[0].clone()
+
+    def one_step():
+        pending = stack[0].forward_local(x_local, temb, rope_j, batch, seq, BLOCK_TXT)
+        for blk in stack[1:]:
+            pending = blk.forward_local_pending(pending, temb, rope_j, batch, seq, BLOCK_TXT)
+        return TensorParallelQwenBlock.finish(pending)
+
+    stream = torch.cuda.current_stream()
+    one_step()
+    torch.cuda.synchronize()
+    side = torch.cuda.Stream()
+    side.wait_stream(stream)
+    with torch.cuda.stream(side):
+        one_step()
+    stream.wait_stream(side)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        y = one_step()
+    for i in range(2):  # warm-up replays
+        temb.copy_(tembs[i % steps])
+        graph.replay()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for i in range(steps):
+        temb.copy_(tembs[i])  # the step's timestep embedding (3 KB device copy, part of the step)
+        graph.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    total_ms = max_over_ranks(e0.elapsed_time(e1), world)
+    finite = bool(torch.isfinite(y).all())
+    del graph
+    torch.cuda.synchronize()
+    assert ops.device_error() == 0 and finite, "stack benchmark raised the device error word or non-finite output"
+    del stack
+    torch.cuda.empty_cache()
+    if rank != 0:
+        return None
+    flop = steps * blocks * batch * block_flops(BLOCK_IMG, BLOCK_TXT, DIM)
+    return {
+        "ms_per_step": round(total_ms / steps, 3), "total_ms": round(total_ms, 2), "steps": steps, "blocks": blocks,
+        "batch": batch, "n_gpus": world, "TFLOP/s": round(flop / (total_ms * 1e-3) / 1e12, 1),
+        "parallelism": "single GPU" if world == 1 else
+        f"tensor-parallel x{world} with sequence-parallel rows (NCCL all-gather / reduce-scatter)",
+        "shape": f"{blocks} blocks x batch {batch} x ({BLOCK_IMG} image + {BLOCK_TXT} text tokens), hidden {DIM}, "
+                 "all linears q6 gs64",
+        "note": "one denoising step (all blocks) captured in a CUDA graph and replayed per step with that step's "
+                "timestep embedding; device time, max over ranks; block stack only",
     }
 
 

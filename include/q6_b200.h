@@ -218,6 +218,22 @@ Q6_API int q6_qk_rmsnorm_rope_bf16(uint16_t* qk, int64_t row_stride, int64_t M, 
                                    const uint16_t* weight, const float* cos, const float* sin, float eps,
                                    q6_stream_t stream);
 
+/*
+ * q6_qk_rmsnorm_rope_bf16 over rows of a joint, batched sequence: local row m
+ * is global row g = row0 + m of sequences of seq_len rows whose first
+ * text_len rows are text.  The row takes angle-table row g % seq_len
+ * (cos / sin fp32 [seq_len, 64], text rows first) and the RMSNorm weight
+ * weight_text for text rows (norm_added_q / norm_added_k) or weight_image
+ * for image rows (norm_q / norm_k), so one launch covers the q (or k)
+ * columns of every stream and sample.  seq_len = 0: one sequence of M rows,
+ * weight_image throughout.  Replaces the four norm + `_apply_rope_qwen`
+ * calls of the block (benchmarks/profile_qwen_block.py:203-217).
+ */
+Q6_API int q6_qk_rmsnorm_rope_joint_bf16(uint16_t* qk, int64_t row_stride, int64_t M, int heads, int head_dim,
+                                         const uint16_t* weight_text, const uint16_t* weight_image, const float* cos,
+                                         const float* sin, int64_t row0, int64_t seq_len, int64_t text_len, float eps,
+                                         q6_stream_t stream);
+
 /* Device error word (0 = none, else a q6_error_site code).  Reading it
    synchronises the current device. */
 Q6_API int q6_get_device_error(int* code);

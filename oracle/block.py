@@ -145,7 +145,19 @@ class BlockWeights:
     heads: int
 
 
-def _lin(w: BlockWeights, name: str, x: np.ndarray, **kw) -> np.ndarray:
+FEW_ROWS = 4  # the library's few-row (GEMV) path takes at most this many token rows
+
+
+def _lin(w: BlockWeights, name: str, x: np.ndarray, *, launch_rows: int | None = None, **kw) -> np.ndarray:
+    """One q6 linear with the weight precision of the kernel path that runs it
+    for ``launch_rows`` token rows (default: the rows of ``x``): fp32
+    dequantised weights for a few rows (the modulation linears at M = batch
+    run on the streaming GEMV, which keeps the reference kernel's fp32
+    ``scale * code + qbias``), bf16 weights otherwise (the tensor-core path,
+    MLX qmm semantics).  ``x`` may hold a subset of the launch's rows."""
+
+    rows = np.asarray(x).shape[0] if launch_rows is None else launch_rows
+    kw.setdefault("weight_dtype", "f32" if rows <= FEW_ROWS else "bf16")
     return round_bf16(linear(x, w.linears[name], **kw))
 
 
@@ -193,23 +205,23 @@ def block_forward_rows(w: BlockWeights, hidden: np.ndarray, encoder: np.ndarray,
     v_i = _lin(w, "attn.to_v", img_in)
     v_t = _lin(w, "attn.add_v_proj", txt_in)
     # queries of the selected rows only
-    q_i = round_bf16(qk_rmsnorm_rope(_lin(w, "attn.to_q", img_in[ir]), w.norms["attn.norm_q"], img_cos[ir],
+    q_i = round_bf16(qk_rmsnorm_rope(_lin(w, "attn.to_q", img_in[ir], launch_rows=s_img), w.norms["attn.norm_q"], img_cos[ir],
                                      img_sin[ir], eps))
-    q_t = round_bf16(qk_rmsnorm_rope(_lin(w, "attn.add_q_proj", txt_in[tr]), w.norms["attn.norm_added_q"],
+    q_t = round_bf16(qk_rmsnorm_rope(_lin(w, "attn.add_q_proj", txt_in[tr], launch_rows=s_txt), w.norms["attn.norm_added_q"],
                                      txt_cos[tr], txt_sin[tr], eps))
     key_mask = joint_key_mask(text_mask, s_img)
     keys, vals = np.concatenate([k_t, k_i]), np.concatenate([v_t, v_i])
     att_t = round_bf16(attention(q_t, keys, vals, w.heads, key_mask).astype(np.float32))
     att_i = round_bf16(attention(q_i, keys, vals, w.heads, key_mask).astype(np.float32))
-    img_h = _lin(w, "attn.attn_to_out.0", att_i, residual=hidden[ir], gate=ig1)
-    txt_h = _lin(w, "attn.to_add_out", att_t, residual=encoder[tr], gate=tg1)
+    img_h = _lin(w, "attn.attn_to_out.0", att_i, residual=hidden[ir], gate=ig1, launch_rows=s_img)
+    txt_h = _lin(w, "attn.to_add_out", att_t, residual=encoder[tr], gate=tg1, launch_rows=s_txt)
 
     img_ff_in = round_bf16(layernorm_modulate(img_h, ish2, isc2, eps))
     txt_ff_in = round_bf16(layernorm_modulate(txt_h, tsh2, tsc2, eps))
-    img_mid = _lin(w, "img_ff.mlp_in", img_ff_in, apply_gelu=True)
-    txt_mid = _lin(w, "txt_ff.mlp_in", txt_ff_in, apply_gelu=True)
-    img_out = _lin(w, "img_ff.mlp_out", img_mid, residual=img_h, gate=ig2)
-    txt_out = _lin(w, "txt_ff.mlp_out", txt_mid, residual=txt_h, gate=tg2)
+    img_mid = _lin(w, "img_ff.mlp_in", img_ff_in, apply_gelu=True, launch_rows=s_img)
+    txt_mid = _lin(w, "txt_ff.mlp_in", txt_ff_in, apply_gelu=True, launch_rows=s_txt)
+    img_out = _lin(w, "img_ff.mlp_out", img_mid, residual=img_h, gate=ig2, launch_rows=s_img)
+    txt_out = _lin(w, "txt_ff.mlp_out", txt_mid, residual=txt_h, gate=tg2, launch_rows=s_txt)
     return txt_out, img_out
 
 

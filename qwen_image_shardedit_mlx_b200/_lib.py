@@ -61,6 +61,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "q6_layernorm_modulate_bf16": (_I, [_P, _P, _P, _P, _I64, _I64, _F, _P]),
     "q6_add_layernorm_modulate_bf16": (_I, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _F, _P]),
     "q6_qk_rmsnorm_rope_bf16": (_I, [_P, _I64, _I64, _I, _I, _P, _P, _P, _F, _P]),
+    "q6_qk_rmsnorm_rope_joint_bf16": (_I, [_P, _I64, _I64, _I, _I, _P, _P, _P, _P, _I64, _I64, _I64, _F, _P]),
     "q6_get_device_error": (_I, [ctypes.POINTER(ctypes.c_int)]),
     "q6_clear_device_error": (_I, []),
     "q6_last_path": (_I, []),

@@ -6,16 +6,27 @@ The block the reference profiles stage by stage
 =====================================  =========================================================
 reference stage                         here
 =====================================  =========================================================
-img/txt_mod_linear(silu(temb))         ``q6_linear`` on the few-row streaming GEMV
-_modulate(norm1(x), mod1)              ``q6_layernorm_modulate_bf16`` (one fused kernel)
-to_q/k/v, add_q/k/v_proj               ``q6_linear`` writing straight into the joint
-                                        [text; image] q / k / v buffers
-norm_q/k, norm_added_q/k + rope        ``q6_qk_rmsnorm_rope_bf16`` in place on those buffers
-joint attention (_compute_attention)   torch scaled_dot_product_attention (library kernel)
+img/txt_mod_linear(silu(temb))         ``q6_linear`` on the few-row streaming GEMV (M = batch)
+_modulate(norm1(x), mod1)              ``q6_add_layernorm_modulate_bf16``: one launch over the
+                                        joint rows of every sample and stream
+to_q/k/v, add_q/k/v_proj               one GEMM per (sample, stream) of the concatenated q, k, v
+                                        projections, writing a joint [text; image] qkv buffer
+norm_q/k, norm_added_q/k + rope        ``q6_qk_rmsnorm_rope_joint_bf16`` in place, one launch
+                                        for q and one for k over all rows
+joint attention (_compute_attention)   torch scaled_dot_product_attention over the batch
+                                        (library kernel), text padding masked as keys
 attn_to_out[0] / to_add_out + gate1    ``q6_linear`` with the residual and gate in its epilogue
-_modulate(norm2(x), mod2)              ``q6_layernorm_modulate_bf16``
+_modulate(norm2(x), mod2)              ``q6_add_layernorm_modulate_bf16``
 img_ff / txt_ff + gate2 residual       ``q6_mlp`` with the residual and gate in fc2's epilogue
 =====================================  =========================================================
+
+Rows of a batch live in one joint buffer [B * S, D], each sample's S rows
+text first ([text; image], the order of the reference's joint attention).
+``TensorParallelQwenBlock`` splits the block over the GPUs of a process
+group: heads and feed-forward columns per rank, and the rows between the
+GEMMs (adaLN modulate, residuals) sequence-parallel, with an all-gather
+before each column-parallel GEMM and a reduce-scatter after each
+row-parallel one.
 
 Tensor names follow the reference's checkpoint layout (``img_mod_linear``,
 ``attn.to_q``, ``attn.attn_to_out.0``, ``img_ff.mlp_in``, ``attn.norm_q``
@@ -161,60 +172,28 @@ class QwenTransformerBlock(torch.nn.Module):
         dim = block.linears["attn.to_q"].out_features
         return cls(dict(block.linears), norms, heads=heads or dim // HEAD_DIM)
 
-    def _workspace(self, m: int, device: torch.device) -> torch.Tensor:
-        need = int(ops.mlp_workspace_bytes(m, 4 * self.dim, self.dim))
+    def _workspace(self, m: int, h: int, d: int, device: torch.device) -> torch.Tensor:
+        need = int(ops.mlp_workspace_bytes(m, h, d))
         if self._ws is None or self._ws.numel() < need or self._ws.device != device:
             self._ws = torch.empty(need, dtype=torch.uint8, device=device)
         return self._ws
-
-    def _mlp(self, ff: QwenFeedForward, x: torch.Tensor, residual: torch.Tensor, gate: torch.Tensor) -> torch.Tensor:
-        if ff.mlp_in.lora is not None or ff.mlp_out.lora is not None:
-            mid = ops.q6_linear(x, ff.mlp_in.weight, ff.mlp_in.scales, ff.mlp_in.biases, ff.mlp_in.bias,
-                                group_size=ff.mlp_in.group_size, apply_gelu=True, lora=ff.mlp_in.lora)
-            lo = ff.mlp_out
-            return ops.q6_linear(mid, lo.weight, lo.scales, lo.biases, lo.bias, group_size=lo.group_size,
-                                 residual=residual, gate=gate, lora=lo.lora)
-        w1 = (ff.mlp_in.weight, ff.mlp_in.scales, ff.mlp_in.biases, ff.mlp_in.bias)
-        w2 = (ff.mlp_out.weight, ff.mlp_out.scales, ff.mlp_out.biases, ff.mlp_out.bias)
-        return ops.q6_mlp(x, w1, w2, group_size=ff.mlp_in.group_size, residual=residual, gate=gate,
-                          workspace=self._workspace(x.shape[0], x.device))
 
     def _linear(self, name: str, x: torch.Tensor, **kw) -> torch.Tensor:
         lin = self.linears[name]
         return ops.q6_linear(x, lin.weight, lin.scales, lin.biases, lin.bias, group_size=lin.group_size,
                              lora=lin.lora, **kw)
 
-    def forward_sample(self, hidden: torch.Tensor, encoder: torch.Tensor, mod_img: torch.Tensor,
-                       mod_txt: torch.Tensor, rope: tuple[torch.Tensor, ...],
-                       text_mask: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
-        """One sample: hidden [S_img, D], encoder [S_txt, D], modulation
-        vectors [6, D] per stream, optional text mask [S_txt] (1 = token,
-        0 = padding); returns (text out, image out)."""
-
-        img_cos, img_sin, txt_cos, txt_sin = rope
-        s_img, s_txt, d = hidden.shape[0], encoder.shape[0], self.dim
-        ish1, isc1, ig1, ish2, isc2, ig2 = mod_img
-        tsh1, tsc1, tg1, tsh2, tsc2, tg2 = mod_txt
-        img_in = layernorm_modulate(hidden, ish1, isc1, eps=self.eps)
-        txt_in = layernorm_modulate(encoder, tsh1, tsc1, eps=self.eps)
-        # joint [text; image] projections, written in place
-        s = s_txt + s_img
-        q = torch.empty((s, d), dtype=torch.bfloat16, device=hidden.device)
-        k = torch.empty_like(q)
-        v = torch.empty_like(q)
-        project_qkv(self, txt_in, img_in, q, k, v)
-        qk_rmsnorm_rope_(q[:s_txt], self.norms["attn.norm_added_q"], txt_cos, txt_sin, eps=self.eps)
-        qk_rmsnorm_rope_(q[s_txt:], self.norms["attn.norm_q"], img_cos, img_sin, eps=self.eps)
-        qk_rmsnorm_rope_(k[:s_txt], self.norms["attn.norm_added_k"], txt_cos, txt_sin, eps=self.eps)
-        qk_rmsnorm_rope_(k[s_txt:], self.norms["attn.norm_k"], img_cos, img_sin, eps=self.eps)
-        joint = joint_attention(q, k, v, self.heads, s_txt, text_mask)
-        img_h = self._linear("attn.attn_to_out.0", joint[s_txt:], residual=hidden, gate=ig1)
-        txt_h = self._linear("attn.to_add_out", joint[:s_txt], residual=encoder, gate=tg1)
-        img_ff_in = layernorm_modulate(img_h, ish2, isc2, eps=self.eps)
-        txt_ff_in = layernorm_modulate(txt_h, tsh2, tsc2, eps=self.eps)
-        img_out = self._mlp(self.img_ff, img_ff_in, img_h, ig2)
-        txt_out = self._mlp(self.txt_ff, txt_ff_in, txt_h, tg2)
-        return txt_out, img_out
+    def _mlp(self, prefix: str, x: torch.Tensor, residual: torch.Tensor | None, gate: torch.Tensor,
+             out: torch.Tensor) -> torch.Tensor:
+        l1, l2 = self.linears[f"{prefix}.mlp_in"], self.linears[f"{prefix}.mlp_out"]
+        if l1.lora is not None or l2.lora is not None:
+            mid = ops.q6_linear(x, l1.weight, l1.scales, l1.biases, l1.bias, group_size=l1.group_size,
+                                apply_gelu=True, lora=l1.lora)
+            return ops.q6_linear(mid, l2.weight, l2.scales, l2.biases, l2.bias, group_size=l2.group_size,
+                                 residual=residual, gate=gate, lora=l2.lora, out=out)
+        ws = self._workspace(x.shape[0], l1.out_features, l1.in_features, x.device)
+        return ops.q6_mlp(x, (l1.weight, l1.scales, l1.biases, l1.bias), (l2.weight, l2.scales, l2.biases, l2.bias),
+                          group_size=l1.group_size, residual=residual, gate=gate, workspace=ws, out=out)
 
     def modulation(self, temb: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
         """(img, txt) modulation vectors [B, 6, D] from the timestep embedding [B, D]."""
@@ -224,6 +203,31 @@ class QwenTransformerBlock(torch.nn.Module):
         return (self._linear("img_mod_linear", t).reshape(b, 6, self.dim),
                 self._linear("txt_mod_linear", t).reshape(b, 6, self.dim))
 
+    def forward_joint(self, x: torch.Tensor, temb: torch.Tensor, rope_joint: tuple[torch.Tensor, torch.Tensor],
+                      batch: int, text_len: int, text_mask: torch.Tensor | None = None,
+                      out: torch.Tensor | None = None) -> torch.Tensor:
+        """The block over joint rows ``x`` [B * S, D] (each sample's S rows text
+        first); ``rope_joint`` = (cos, sin) fp32 [S, 64] with the text rows
+        first; ``text_mask`` [B, S_txt] or None.  Returns the joint output rows."""
+
+        rows, d = x.shape
+        seq = rows // batch
+        vec = ModulationVectors(*self.modulation(temb))
+        z = add_layernorm_modulate(x, vec.shift1, vec.scale1, seq_len=seq, text_len=text_len, eps=self.eps)
+        qkv = torch.empty((rows, 3 * d), dtype=torch.bfloat16, device=x.device)
+        project_qkv_joint(self, z, qkv, batch, seq, text_len)
+        rope_qk_joint(self, qkv, d, rope_joint, seq, text_len)
+        att = batched_joint_attention(qkv, d, batch, seq, self.heads, text_len, text_mask)
+        h = torch.empty_like(x)
+        for b, stream, r in segments(batch, seq, text_len):
+            name = "attn.to_add_out" if stream == 0 else "attn.attn_to_out.0"
+            self._linear(name, att[r], residual=x[r], gate=vec.gate1(b, stream), out=h[r])
+        z2 = add_layernorm_modulate(h, vec.shift2, vec.scale2, seq_len=seq, text_len=text_len, eps=self.eps)
+        y = out if out is not None else torch.empty_like(x)
+        for b, stream, r in segments(batch, seq, text_len):
+            self._mlp("txt_ff" if stream == 0 else "img_ff", z2[r], h[r], vec.gate2(b, stream), y[r])
+        return y
+
     def forward(self, hidden: torch.Tensor, encoder: torch.Tensor, temb: torch.Tensor,
                 rope: tuple[torch.Tensor, ...],
                 encoder_mask: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
@@ -232,46 +236,156 @@ class QwenTransformerBlock(torch.nn.Module):
         ``encoder_mask`` [B, S_txt] (1 = text token, 0 = padding; None = no
         padding).  Returns (encoder_out, hidden_out) like the reference block."""
 
-        mod_img, mod_txt = self.modulation(temb)
-        outs = [self.forward_sample(hidden[b], encoder[b], mod_img[b], mod_txt[b], rope,
-                                    None if encoder_mask is None else encoder_mask[b])
-                for b in range(hidden.shape[0])]
-        return torch.stack([o[0] for o in outs]), torch.stack([o[1] for o in outs])
+        x, batch, s_txt = joint_rows(hidden, encoder)
+        y = self.forward_joint(x, temb, joint_rope(rope), batch, s_txt, encoder_mask)
+        return split_joint(y, batch, s_txt)
 
 
-def joint_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, heads: int, s_txt: int,
-                    text_mask: torch.Tensor | None = None) -> torch.Tensor:
-    """Joint [text; image] attention of one sample over rows [S, heads * 128]
-    (torch scaled_dot_product_attention).  ``text_mask`` [S_txt] (1 = token,
-    0 = padding) removes padded text tokens as keys, every image token stays
-    a key: the joint mask the reference builds from
-    ``encoder_hidden_states_mask`` (benchmarks/profile_qwen_block.py:228-248).
-    Without a mask the library's unmasked flash kernel runs."""
+# ------------------------------------------------------------------- joint-row helpers
 
-    s = q.shape[0]
-    shape = (1, s, heads, HEAD_DIM)
+
+class ModulationVectors:
+    """A block's adaLN vectors per (sample, stream), in the [B][text, image][D]
+    layout the joint-row kernels index: shift / scale of the attention half
+    (1) and of the feed-forward half (2), and the gates as [D] views."""
+
+    def __init__(self, mod_img: torch.Tensor, mod_txt: torch.Tensor) -> None:
+        both = torch.stack([mod_txt, mod_img], dim=1)  # [B, 2 streams, 6, D]
+        b, _, _, d = both.shape
+        self.shift1 = both[:, :, 0].reshape(2 * b, d).contiguous()
+        self.scale1 = both[:, :, 1].reshape(2 * b, d).contiguous()
+        self.shift2 = both[:, :, 3].reshape(2 * b, d).contiguous()
+        self.scale2 = both[:, :, 4].reshape(2 * b, d).contiguous()
+        self._both = both
+
+    def gate1(self, b: int, stream: int) -> torch.Tensor:
+        return self._both[b, stream, 2]
+
+    def gate2(self, b: int, stream: int) -> torch.Tensor:
+        return self._both[b, stream, 5]
+
+
+def segments(batch: int, seq: int, text_len: int):
+    """(sample, stream, row slice) of the joint rows: stream 0 text, 1 image."""
+
+    for b in range(batch):
+        if text_len:
+            yield b, 0, slice(b * seq, b * seq + text_len)
+        if seq > text_len:
+            yield b, 1, slice(b * seq + text_len, (b + 1) * seq)
+
+
+def joint_rows(hidden: torch.Tensor, encoder: torch.Tensor) -> tuple[torch.Tensor, int, int]:
+    """[B * S, D] joint rows (each sample's text rows, then its image rows)."""
+
+    batch, s_txt, d = encoder.shape
+    x = torch.cat([encoder.to(torch.bfloat16), hidden.to(torch.bfloat16)], dim=1)
+    return x.reshape(batch * (s_txt + hidden.shape[1]), d).contiguous(), batch, s_txt
+
+
+def split_joint(y: torch.Tensor, batch: int, s_txt: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """(text rows [B, S_txt, D], image rows [B, S_img, D]) views of joint rows."""
+
+    v = y.view(batch, -1, y.shape[-1])
+    return v[:, :s_txt], v[:, s_txt:]
+
+
+def joint_rope(rope: tuple[torch.Tensor, ...]) -> tuple[torch.Tensor, torch.Tensor]:
+    """(cos, sin) [S, 64] of the joint sequence (text rows first) from
+    (img_cos, img_sin, txt_cos, txt_sin)."""
+
+    img_cos, img_sin, txt_cos, txt_sin = rope
+    return torch.cat([txt_cos, img_cos]).contiguous(), torch.cat([txt_sin, img_sin]).contiguous()
+
+
+def add_layernorm_modulate(x: torch.Tensor, shift: torch.Tensor, scale: torch.Tensor, *,
+                           add: torch.Tensor | None = None, h_out: torch.Tensor | None = None,
+                           out: torch.Tensor | None = None, row0: int = 0, seq_len: int = 0, text_len: int = 0,
+                           eps: float = 1e-6) -> torch.Tensor:
+    """y = LayerNorm(x [+ add]) * (1 + scale[v]) + shift[v] over joint rows
+    (q6_add_layernorm_modulate_bf16): row m is row row0 + m of sequences of
+    ``seq_len`` rows whose first ``text_len`` are text; shift / scale hold
+    [samples * 2, D] vectors (text, image per sample).  ``h_out`` receives
+    x + add."""
+
+    d = x.shape[-1]
+    if x.dtype != torch.bfloat16 or not x.is_contiguous():
+        raise ValueError("x must be contiguous bf16 rows")
+    if add is not None and (add.dtype != torch.bfloat16 or not add.is_contiguous() or add.shape != x.shape):
+        raise ValueError("add must match x")
+    y = out if out is not None else torch.empty_like(x)
+    st = _lib.lib().q6_add_layernorm_modulate_bf16(
+        x.data_ptr(), None if add is None else add.data_ptr(), None if h_out is None else h_out.data_ptr(),
+        shift.data_ptr(), scale.data_ptr(), y.data_ptr(), x.shape[0], d, int(row0), int(seq_len), int(text_len),
+        float(eps), ops._stream(x.device))
+    _lib.check(st, "q6_add_layernorm_modulate_bf16")
+    return y
+
+
+def qk_rmsnorm_rope_joint_(qk: torch.Tensor, w_text: torch.Tensor, w_image: torch.Tensor, cos: torch.Tensor,
+                           sin: torch.Tensor, *, row0: int = 0, seq_len: int = 0, text_len: int = 0,
+                           eps: float = 1e-6) -> torch.Tensor:
+    """In place on joint rows [M, H * 128] (row stride may exceed the width):
+    text rows take ``w_text``, image rows ``w_image``; row m uses angle-table
+    row (row0 + m) % seq_len of cos / sin [seq_len, 64]."""
+
+    if qk.dtype != torch.bfloat16 or qk.dim() != 2 or qk.stride(1) != 1:
+        raise ValueError("qk must be a 2-D bf16 view with unit column stride")
+    m, width = qk.shape
+    st = _lib.lib().q6_qk_rmsnorm_rope_joint_bf16(
+        qk.data_ptr(), qk.stride(0), m, width // HEAD_DIM, HEAD_DIM, w_text.data_ptr(), w_image.data_ptr(),
+        cos.data_ptr(), sin.data_ptr(), int(row0), int(seq_len), int(text_len), float(eps), ops._stream(qk.device))
+    _lib.check(st, "q6_qk_rmsnorm_rope_joint_bf16")
+    return qk
+
+
+def rope_qk_joint(owner, qkv: torch.Tensor, width: int, rope_joint: tuple[torch.Tensor, torch.Tensor], seq: int,
+                  text_len: int) -> None:
+    """QK-RMSNorm and rotary embedding on the q and k columns of a joint qkv buffer."""
+
+    cos, sin = rope_joint
+    n = owner.norms
+    qk_rmsnorm_rope_joint_(qkv[:, :width], n["attn.norm_added_q"], n["attn.norm_q"], cos, sin, seq_len=seq,
+                           text_len=text_len, eps=owner.eps)
+    qk_rmsnorm_rope_joint_(qkv[:, width:2 * width], n["attn.norm_added_k"], n["attn.norm_k"], cos, sin,
+                           seq_len=seq, text_len=text_len, eps=owner.eps)
+
+
+def batched_joint_attention(qkv: torch.Tensor, width: int, batch: int, seq: int, heads: int, text_len: int,
+                            text_mask: torch.Tensor | None = None) -> torch.Tensor:
+    """Joint [text; image] attention of every sample from a qkv buffer [B * S,
+    3 * width] (torch scaled_dot_product_attention over [B, heads, S, 128]).
+    ``text_mask`` [B, S_txt] (1 = token, 0 = padding) removes padded text
+    tokens as keys while every image token stays a key: the joint mask the
+    reference builds from ``encoder_hidden_states_mask``
+    (benchmarks/profile_qwen_block.py:228-248).  Without a mask the library's
+    unmasked flash kernel runs.  Returns [B * S, width] rows."""
+
+    def view(j: int) -> torch.Tensor:
+        return qkv[:, j * width:(j + 1) * width].view(batch, seq, heads, HEAD_DIM).transpose(1, 2)
+
     mask = None
     if text_mask is not None:
-        keep = torch.ones(s, dtype=torch.bool, device=q.device)
-        keep[:s_txt] = text_mask.reshape(-1).to(q.device) > 0.5
-        mask = keep.view(1, 1, 1, s)
-    att = F.scaled_dot_product_attention(q.view(shape).transpose(1, 2), k.view(shape).transpose(1, 2),
-                                         v.view(shape).transpose(1, 2), attn_mask=mask,
-                                         scale=1.0 / math.sqrt(HEAD_DIM))
-    return att.transpose(1, 2).reshape(s, heads * HEAD_DIM)
+        keep = torch.ones((batch, seq), dtype=torch.bool, device=qkv.device)
+        keep[:, :text_len] = text_mask.reshape(batch, text_len).to(qkv.device) > 0.5
+        mask = keep.view(batch, 1, 1, seq)
+    att = F.scaled_dot_product_attention(view(0), view(1), view(2), attn_mask=mask, scale=1.0 / math.sqrt(HEAD_DIM))
+    return att.transpose(1, 2).reshape(batch * seq, width)
 
 
 _TXT_QKV = ("attn.add_q_proj", "attn.add_k_proj", "attn.add_v_proj")
+_IMG_QKV = ("attn.to_q", "attn.to_k", "attn.to_v")
 
 
 def fused_rows(owner: torch.nn.Module, names: tuple[str, ...]) -> QuantizedLinear | None:
     """Row concatenation of q6 linears of ``owner.linears`` that read the same
-    input (the text stream's q, k and v projections): one GEMM whose output
-    columns are theirs side by side.  At a few hundred tokens the three
-    3072-row GEMMs each fill a third of the GPU's tiles (and need split-K);
-    their concatenation fills it alone.  The members' tensors are rebound to
-    views of the concatenation, so no weight is held twice.  None when a
-    member carries a LoRA delta or the members differ in input or group size."""
+    input (one stream's q, k and v projections): one GEMM whose output
+    columns are theirs side by side, written straight into the joint qkv
+    buffer.  At a few hundred tokens the three 3072-row GEMMs each fill a
+    third of the GPU's tiles (and need split-K); their concatenation fills it
+    alone.  The members' tensors are rebound to views of the concatenation,
+    so no weight is held twice.  None when a member carries a LoRA delta or
+    the members differ in input or group size."""
 
     lins = [owner.linears[n] for n in names]
     if any(lin.lora is not None for lin in lins):
@@ -299,25 +413,21 @@ def fused_rows(owner: torch.nn.Module, names: tuple[str, ...]) -> QuantizedLinea
     return fused
 
 
-def project_qkv(owner: torch.nn.Module, txt_in: torch.Tensor, img_in: torch.Tensor, q: torch.Tensor,
-                k: torch.Tensor, v: torch.Tensor) -> None:
-    """Joint [text; image] q, k, v projections written in place: the image
-    rows by three GEMMs, the text rows by one GEMM of the concatenated text
-    projections (``fused_rows``) copied into place."""
+def project_qkv_joint(owner: torch.nn.Module, z: torch.Tensor, qkv: torch.Tensor, batch: int, seq: int,
+                      text_len: int) -> None:
+    """q, k, v of every joint row into qkv [B * S, 3 * width]: one GEMM per
+    (sample, stream) of the stream's concatenated projections (``fused_rows``);
+    a stream with a LoRA delta on one of them runs its three GEMMs and copies."""
 
-    s_txt = txt_in.shape[0]
-    fused = fused_rows(owner, _TXT_QKV) if s_txt else None
-    if fused is not None:
-        t = ops.q6_linear(txt_in, fused.weight, fused.scales, fused.biases, fused.bias,
-                          group_size=fused.group_size)
-        width = q.shape[1]
-        for j, buf in enumerate((q, k, v)):
-            buf[:s_txt].copy_(t[:, j * width:(j + 1) * width])
-    for buf, img_name, txt_name in ((q, "attn.to_q", "attn.add_q_proj"), (k, "attn.to_k", "attn.add_k_proj"),
-                                    (v, "attn.to_v", "attn.add_v_proj")):
-        if fused is None:
-            owner._linear(txt_name, txt_in, out=buf[:s_txt])
-        owner._linear(img_name, img_in, out=buf[s_txt:])
+    fused = {0: fused_rows(owner, _TXT_QKV), 1: fused_rows(owner, _IMG_QKV)}
+    width = qkv.shape[1] // 3
+    for _, stream, r in segments(batch, seq, text_len):
+        f = fused[stream]
+        if f is not None:
+            ops.q6_linear(z[r], f.weight, f.scales, f.biases, f.bias, group_size=f.group_size, out=qkv[r])
+            continue
+        for j, name in enumerate(_TXT_QKV if stream == 0 else _IMG_QKV):
+            qkv[r, j * width:(j + 1) * width].copy_(owner._linear(name, z[r]))
 
 
 def block_flops(s_img: int, s_txt: int, dim: int) -> int:
@@ -329,19 +439,23 @@ def block_flops(s_img: int, s_txt: int, dim: int) -> int:
     return 24 * s * dim * dim + 4 * s * s * dim + 24 * dim * dim
 
 
+# ------------------------------------------------------------------- tensor parallel
+
+
 class TensorParallelQwenBlock(torch.nn.Module):
     """The block split over the ranks of a process group (one rank per GPU).
 
     Heads and the feed-forward hidden columns are divided: q / k / v and
     mlp_in are column-parallel (each rank holds its heads' / columns' rows of
     codes, scales and biases), the output projections and mlp_out are
-    row-parallel (each rank holds the matching K slice).  The modulation
-    linears, the norms and the residual streams are replicated.  A
-    row-parallel partial carries the residual and the output bias on rank 0
-    only and the gate on every rank, so that the all-reduce sum of the
-    partials is ``residual + gate * (x W^T + bias)`` exactly as the
-    single-GPU epilogue computes it.  Two all-reduces per block, each over
-    the joint [text; image] rows.
+    row-parallel (each rank holds the matching K slice).  Between the GEMMs
+    the joint rows are sequence-parallel: rank r holds rows [r R, (r + 1) R)
+    of the [B * S, D] joint rows (R = B S / world) and runs the adaLN
+    modulate and the residual adds on them alone.  So each half of the block
+    is all-gather (modulated rows) -> column-parallel GEMM -> local work ->
+    row-parallel GEMM -> reduce-scatter (partial sums, gate and rank-0 bias
+    applied in the epilogue) -> residual add + next modulate on local rows.
+    The modulation linears (M = batch) are replicated.
     """
 
     def __init__(self, full: QwenTransformerBlock, world: int, rank: int, group=None) -> None:
@@ -375,71 +489,100 @@ class TensorParallelQwenBlock(torch.nn.Module):
             self.linears[name] = cols(name)
         self._ws: torch.Tensor | None = None
 
-    def _linear(self, name: str, x: torch.Tensor, **kw) -> torch.Tensor:
-        lin = self.linears[name]
-        return ops.q6_linear(x, lin.weight, lin.scales, lin.biases, lin.bias, group_size=lin.group_size, **kw)
+    _linear = QwenTransformerBlock._linear
+    _workspace = QwenTransformerBlock._workspace
+    _mlp = QwenTransformerBlock._mlp
+    modulation = QwenTransformerBlock.modulation
 
-    def _all_reduce(self, t: torch.Tensor) -> None:
+    # collectives over the rows of the joint buffer
+    def _gather(self, local: torch.Tensor) -> torch.Tensor:
+        if self.world == 1:
+            return local
         import torch.distributed as dist
 
-        if self.world > 1:
-            dist.all_reduce(t, op=dist.ReduceOp.SUM, group=self.group)
+        full = torch.empty((local.shape[0] * self.world, local.shape[1]), dtype=local.dtype, device=local.device)
+        dist.all_gather_into_tensor(full, local, group=self.group)
+        return full
 
-    def _mlp(self, prefix: str, x: torch.Tensor, residual: torch.Tensor | None, gate: torch.Tensor,
-             out: torch.Tensor) -> None:
-        l1, l2 = self.linears[f"{prefix}.mlp_in"], self.linears[f"{prefix}.mlp_out"]
-        need = int(ops.mlp_workspace_bytes(x.shape[0], l1.out_features, l1.in_features))
-        if self._ws is None or self._ws.numel() < need or self._ws.device != x.device:
-            self._ws = torch.empty(need, dtype=torch.uint8, device=x.device)
-        ops.q6_mlp(x, (l1.weight, l1.scales, l1.biases, l1.bias), (l2.weight, l2.scales, l2.biases, l2.bias),
-                   group_size=l1.group_size, residual=residual, gate=gate, workspace=self._ws, out=out)
+    def _reduce_scatter(self, full: torch.Tensor) -> torch.Tensor:
+        if self.world == 1:
+            return full
+        import torch.distributed as dist
 
-    def modulation(self, temb: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
-        t = F.silu(temb.to(torch.bfloat16))
-        b = t.shape[0]
-        return (self._linear("img_mod_linear", t).reshape(b, 6, self.dim),
-                self._linear("txt_mod_linear", t).reshape(b, 6, self.dim))
+        local = torch.empty((full.shape[0] // self.world, full.shape[1]), dtype=full.dtype, device=full.device)
+        dist.reduce_scatter_tensor(local, full, op=dist.ReduceOp.SUM, group=self.group)
+        return local
 
-    def forward_sample(self, hidden: torch.Tensor, encoder: torch.Tensor, mod_img: torch.Tensor,
-                       mod_txt: torch.Tensor, rope: tuple[torch.Tensor, ...],
-                       text_mask: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
-        img_cos, img_sin, txt_cos, txt_sin = rope
-        s_img, s_txt = hidden.shape[0], encoder.shape[0]
-        s, dl, lead = s_txt + s_img, self.heads_local * HEAD_DIM, self.rank == 0
-        ish1, isc1, ig1, ish2, isc2, ig2 = mod_img
-        tsh1, tsc1, tg1, tsh2, tsc2, tg2 = mod_txt
-        img_in = layernorm_modulate(hidden, ish1, isc1, eps=self.eps)
-        txt_in = layernorm_modulate(encoder, tsh1, tsc1, eps=self.eps)
-        q = torch.empty((s, dl), dtype=torch.bfloat16, device=hidden.device)
-        k = torch.empty_like(q)
-        v = torch.empty_like(q)
-        project_qkv(self, txt_in, img_in, q, k, v)
-        qk_rmsnorm_rope_(q[:s_txt], self.norms["attn.norm_added_q"], txt_cos, txt_sin, eps=self.eps)
-        qk_rmsnorm_rope_(q[s_txt:], self.norms["attn.norm_q"], img_cos, img_sin, eps=self.eps)
-        qk_rmsnorm_rope_(k[:s_txt], self.norms["attn.norm_added_k"], txt_cos, txt_sin, eps=self.eps)
-        qk_rmsnorm_rope_(k[s_txt:], self.norms["attn.norm_k"], img_cos, img_sin, eps=self.eps)
-        joint = joint_attention(q, k, v, self.heads_local, s_txt, text_mask)
-        # row-parallel output projections into one joint [text; image] buffer, one all-reduce
-        streams = torch.empty((s, self.dim), dtype=torch.bfloat16, device=hidden.device)
-        self._linear("attn.attn_to_out.0", joint[s_txt:], residual=hidden if lead else None, gate=ig1,
-                     out=streams[s_txt:])
-        self._linear("attn.to_add_out", joint[:s_txt], residual=encoder if lead else None, gate=tg1,
-                     out=streams[:s_txt])
-        self._all_reduce(streams)
-        txt_h, img_h = streams[:s_txt], streams[s_txt:]
-        img_ff_in = layernorm_modulate(img_h, ish2, isc2, eps=self.eps)
-        txt_ff_in = layernorm_modulate(txt_h, tsh2, tsc2, eps=self.eps)
-        outs = torch.empty_like(streams)
-        self._mlp("img_ff", img_ff_in, img_h if lead else None, ig2, outs[s_txt:])
-        self._mlp("txt_ff", txt_ff_in, txt_h if lead else None, tg2, outs[:s_txt])
-        self._all_reduce(outs)
-        return outs[:s_txt], outs[s_txt:]
+    def forward_local(self, x_local: torch.Tensor, temb: torch.Tensor,
+                      rope_joint: tuple[torch.Tensor, torch.Tensor], batch: int, seq: int, text_len: int,
+                      text_mask: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+        """This rank's joint rows through the block: x_local [R, D] are rows
+        [rank R, (rank + 1) R) of the [B * S, D] joint rows.  Returns
+        (h, ff): the block's output rows are h + ff (``finish``); a stack may
+        instead hand the pair to the next block, whose first modulate adds
+        them in the same pass."""
+
+        rows_local, d = x_local.shape
+        row0 = self.rank * rows_local
+        vec = ModulationVectors(*self.modulation(temb))
+        z = self._gather(add_layernorm_modulate(x_local, vec.shift1, vec.scale1, row0=row0, seq_len=seq,
+                                                text_len=text_len, eps=self.eps))
+        return self._rest(x_local, z, vec, rope_joint, batch, seq, text_len, text_mask, row0)
+
+    def forward_local_pending(self, pending: tuple[torch.Tensor, torch.Tensor], temb: torch.Tensor,
+                              rope_joint: tuple[torch.Tensor, torch.Tensor], batch: int, seq: int,
+                              text_len: int, text_mask: torch.Tensor | None = None
+                              ) -> tuple[torch.Tensor, torch.Tensor]:
+        """``forward_local`` of the output (h, ff) of the previous block: its
+        residual add x = h + ff is formed in the same pass as this block's
+        first modulate."""
+
+        h_prev, ff_prev = pending
+        rows_local = h_prev.shape[0]
+        row0 = self.rank * rows_local
+        vec = ModulationVectors(*self.modulation(temb))
+        x_local = torch.empty_like(h_prev)
+        z_local = add_layernorm_modulate(h_prev, vec.shift1, vec.scale1, add=ff_prev, h_out=x_local, row0=row0,
+                                         seq_len=seq, text_len=text_len, eps=self.eps)
+        return self._rest(x_local, self._gather(z_local), vec, rope_joint, batch, seq, text_len, text_mask, row0)
+
+    def _rest(self, x_local, z, vec, rope_joint, batch, seq, text_len, text_mask, row0):
+        d, dl = self.dim, self.heads_local * HEAD_DIM
+        rows = z.shape[0]
+        qkv = torch.empty((rows, 3 * dl), dtype=torch.bfloat16, device=z.device)
+        project_qkv_joint(self, z, qkv, batch, seq, text_len)
+        rope_qk_joint(self, qkv, dl, rope_joint, seq, text_len)
+        att = batched_joint_attention(qkv, dl, batch, seq, self.heads_local, text_len, text_mask)
+        part = torch.empty((rows, d), dtype=torch.bfloat16, device=z.device)
+        for b, stream, r in segments(batch, seq, text_len):
+            name = "attn.to_add_out" if stream == 0 else "attn.attn_to_out.0"
+            self._linear(name, att[r], gate=vec.gate1(b, stream), out=part[r])
+        attn_local = self._reduce_scatter(part)
+        h_local = torch.empty_like(x_local)
+        z2 = self._gather(add_layernorm_modulate(x_local, vec.shift2, vec.scale2, add=attn_local, h_out=h_local,
+                                                 row0=row0, seq_len=seq, text_len=text_len, eps=self.eps))
+        part2 = torch.empty((rows, d), dtype=torch.bfloat16, device=z.device)
+        for b, stream, r in segments(batch, seq, text_len):
+            self._mlp("txt_ff" if stream == 0 else "img_ff", z2[r], None, vec.gate2(b, stream), part2[r])
+        return h_local, self._reduce_scatter(part2)
+
+    @staticmethod
+    def finish(pending: tuple[torch.Tensor, torch.Tensor]) -> torch.Tensor:
+        h, ff = pending
+        return h + ff
 
     def forward(self, hidden: torch.Tensor, encoder: torch.Tensor, temb: torch.Tensor,
                 rope: tuple[torch.Tensor, ...],
                 encoder_mask: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
-        mod_img, mod_txt = self.modulation(temb)
-        outs = [self.forward_sample(hidden[b], encoder[b], mod_img[b], mod_txt[b], rope,
-                                    None if encoder_mask is None else encoder_mask[b])
-                for b in range(hidden.shape[0])]
-        return torch.stack([o[0] for o in outs]), torch.stack([o[1] for o in outs])
+        """Full inputs and outputs on every rank (each rank computes its row
+        shard, then the output rows are all-gathered)."""
+
+        x, batch, s_txt = joint_rows(hidden, encoder)
+        rows = x.shape[0]
+        if rows % self.world:
+            raise ValueError(f"{rows} joint rows do not split over {self.world} ranks")
+        r = rows // self.world
+        x_local = x[self.rank * r:(self.rank + 1) * r].contiguous()
+        seq = rows // batch
+        y_local = self.finish(self.forward_local(x_local, temb, joint_rope(rope), batch, seq, s_txt, encoder_mask))
+        return split_joint(self._gather(y_local), batch, s_txt)

@@ -158,12 +158,17 @@ int dispatch_ln(const LnArgs& a, int64_t D, cudaStream_t s) {
 constexpr int kRopeWarps = 8;
 
 // One warp per (row, head); head_dim 128: lane l holds elements 4l .. 4l+3,
-// i.e. rotary pairs 2l and 2l+1.
+// i.e. rotary pairs 2l and 2l+1.  Row m is row g = row0 + m of sequences of
+// seq_len rows (seq_len 0: g = m, one sequence): it takes angle-table row
+// g % seq_len and the first weight vector for the first text_len rows of a
+// sequence, the second for the rest.
 __global__ void __launch_bounds__(kRopeWarps * 32) qk_rmsnorm_rope_kernel(uint2* __restrict__ qk, int64_t row_stride8,
                                                                          int64_t M, int H,
-                                                                         const uint2* __restrict__ weight,
+                                                                         const uint2* __restrict__ w_text,
+                                                                         const uint2* __restrict__ w_image,
                                                                          const float4* __restrict__ cs,
-                                                                         const float4* __restrict__ sn, float eps) {
+                                                                         const float4* __restrict__ sn, int64_t row0,
+                                                                         int64_t seq_len, int64_t text_len, float eps) {
     pdl_launch_dependents();
     pdl_wait();
     const int lane = threadIdx.x & 31;
@@ -171,6 +176,8 @@ __global__ void __launch_bounds__(kRopeWarps * 32) qk_rmsnorm_rope_kernel(uint2*
     if (item >= M * H) return;
     const int64_t row = item / H;
     const int head = static_cast<int>(item - row * H);
+    const int64_t trow = seq_len > 0 ? (row0 + row) % seq_len : row;
+    const uint2* weight = trow < text_len ? w_text : w_image;
     uint2* p = qk + row * row_stride8 + head * 32 + lane;  // 128 bf16 = 32 uint2 per head
     const uint2 v = *p;
     const float x0 = lo_f(v.x), x1 = hi_f(v.x), x2 = lo_f(v.y), x3 = hi_f(v.y);
@@ -180,8 +187,8 @@ __global__ void __launch_bounds__(kRopeWarps * 32) qk_rmsnorm_rope_kernel(uint2*
     const float a0 = x0 * r * lo_f(w.x), a1 = x1 * r * hi_f(w.x);
     const float a2 = x2 * r * lo_f(w.y), a3 = x3 * r * hi_f(w.y);
     // pairs 2 lane and 2 lane + 1 of this row's 64 angles
-    const float2 c = reinterpret_cast<const float2*>(cs + row * 16)[lane];
-    const float2 s = reinterpret_cast<const float2*>(sn + row * 16)[lane];
+    const float2 c = reinterpret_cast<const float2*>(cs + trow * 16)[lane];
+    const float2 s = reinterpret_cast<const float2*>(sn + trow * 16)[lane];
     const float o0 = a0 * c.x - a1 * s.x, o1 = a0 * s.x + a1 * c.x;
     const float o2 = a2 * c.y - a3 * s.y, o3 = a2 * s.y + a3 * c.y;
     *p = make_uint2(pack2(o0, o1), pack2(o2, o3));
@@ -216,19 +223,30 @@ Q6_API int q6_add_layernorm_modulate_bf16(const uint16_t* x, const uint16_t* add
 Q6_API int q6_qk_rmsnorm_rope_bf16(uint16_t* qk, int64_t row_stride, int64_t M, int heads, int head_dim,
                                    const uint16_t* weight, const float* cos, const float* sin, float eps,
                                    q6_stream_t stream) {
-    if (!qk || !weight || !cos || !sin || M <= 0 || heads <= 0 || !(eps >= 0.0f)) return Q6_ERR_INVALID_ARGUMENT;
+    return q6_qk_rmsnorm_rope_joint_bf16(qk, row_stride, M, heads, head_dim, weight, weight, cos, sin, 0, 0, 0, eps,
+                                         stream);
+}
+
+Q6_API int q6_qk_rmsnorm_rope_joint_bf16(uint16_t* qk, int64_t row_stride, int64_t M, int heads, int head_dim,
+                                         const uint16_t* weight_text, const uint16_t* weight_image, const float* cos,
+                                         const float* sin, int64_t row0, int64_t seq_len, int64_t text_len, float eps,
+                                         q6_stream_t stream) {
+    if (!qk || !weight_text || !weight_image || !cos || !sin || M <= 0 || heads <= 0 || !(eps >= 0.0f))
+        return Q6_ERR_INVALID_ARGUMENT;
+    if (row0 < 0 || seq_len < 0 || text_len < 0 || text_len > seq_len) return Q6_ERR_INVALID_ARGUMENT;
     if (head_dim != 128 || row_stride < static_cast<int64_t>(heads) * head_dim || row_stride % 4 != 0)
         return Q6_ERR_SHAPE;
-    const uintptr_t al = reinterpret_cast<uintptr_t>(qk) | reinterpret_cast<uintptr_t>(weight);
+    const uintptr_t al = reinterpret_cast<uintptr_t>(qk) | reinterpret_cast<uintptr_t>(weight_text) |
+                         reinterpret_cast<uintptr_t>(weight_image);
     if (al % 8 != 0 || (reinterpret_cast<uintptr_t>(cos) | reinterpret_cast<uintptr_t>(sin)) % 16 != 0)
         return Q6_ERR_ALIGNMENT;
     const int64_t items = M * heads;
     const int64_t blocks = (items + q6::kRopeWarps - 1) / q6::kRopeWarps;
-    const cudaError_t e = q6::launch_pdl(q6::qk_rmsnorm_rope_kernel, dim3(static_cast<unsigned>(blocks)),
-                                         dim3(q6::kRopeWarps * 32), 0, reinterpret_cast<cudaStream_t>(stream),
-                                         reinterpret_cast<uint2*>(qk), row_stride / 4, M, heads,
-                                         reinterpret_cast<const uint2*>(weight), reinterpret_cast<const float4*>(cos),
-                                         reinterpret_cast<const float4*>(sin), eps);
+    const cudaError_t e = q6::launch_pdl(
+        q6::qk_rmsnorm_rope_kernel, dim3(static_cast<unsigned>(blocks)), dim3(q6::kRopeWarps * 32), 0,
+        reinterpret_cast<cudaStream_t>(stream), reinterpret_cast<uint2*>(qk), row_stride / 4, M, heads,
+        reinterpret_cast<const uint2*>(weight_text), reinterpret_cast<const uint2*>(weight_image),
+        reinterpret_cast<const float4*>(cos), reinterpret_cast<const float4*>(sin), row0, seq_len, text_len, eps);
     return e == cudaSuccess ? Q6_OK : Q6_ERR_CUDA;
 }
 

@@ -6,17 +6,17 @@
 // [M, K] x [K, r] product with fp32 accumulation and one bf16 rounding, r a
 // multiple of 32 up to 256.  With r far below the ridge point (r FLOP per
 // byte of x) the product is bound by reading x once from HBM, so it is a
-// plain warp-level MMA kernel (mma.sync m16n8k16): each CTA owns 32 token
-// rows and every rank column, and streams K in 32-wide chunks through a
-// two-stage cp.async ring in shared memory.  A (K x r, at most 1.5 MB) is
-// re-read by every CTA from L2.
-//
-// Warps: 2 row groups x 2 column halves; warp (rg, ch) computes rows
-// 16 rg .. 16 rg + 15 and columns ch r/2 .. (ch + 1) r/2 - 1 of the tile.
+// plain warp-level MMA kernel (mma.sync m16n8k16) built for memory-level
+// parallelism: each CTA owns 16 token rows (one MMA row tile) and every rank
+// column, its four warps split the rank columns (r / 4 each), and K streams
+// through a three-stage cp.async ring of 64-wide chunks, so two chunks are in
+// flight while one is multiplied (M = 3456 runs 216 CTAs).  A (K x r, at
+// most 6 MB) is re-read by every CTA from L2.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 
 #include "q6_internal.h"
 #include "q6_ptx.cuh"
@@ -24,10 +24,21 @@
 namespace q6 {
 namespace {
 
-constexpr int kRowsPerCta = 32;
-constexpr int kBK = 32;                    // K per chunk: two K = 16 MMA steps
+constexpr int kRowsPerCta = 16;
+constexpr int kBK = 64;                    // K per chunk: four K = 16 MMA steps
+constexpr int kStages = 3;
 constexpr int kXStride = kBK + 8;          // bf16 per shared x row (16 bytes of padding: no bank conflicts)
 constexpr int kThreads = 128;
+
+template <int R>
+struct LoraCfg {
+    static constexpr int kAStride = R + 8;  // bf16 per shared A row (16 bytes of padding)
+    static constexpr int kXBytes = kRowsPerCta * kXStride * 2;
+    static constexpr int kABytes = kBK * kAStride * 2;
+    static constexpr int kStageBytes = kXBytes + kABytes;
+    static constexpr int kSmemBytes = kStages * kStageBytes;
+    static_assert(kXBytes % 16 == 0 && kStageBytes % 16 == 0, "16-byte aligned stage slices");
+};
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
     const int n = valid ? 16 : 0;  // zero-fill rows past M and columns past K
@@ -61,79 +72,74 @@ __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a
 template <int R>
 __global__ void __launch_bounds__(kThreads) lora_xa_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ a,
                                                           uint16_t* __restrict__ xa, int64_t M, int64_t K) {
-    constexpr int kAStride = R + 8;        // bf16 per shared A row (16 bytes of padding)
-    constexpr int kHalf = R / 2;           // columns per warp
-    constexpr int kTiles = kHalf / 8;      // n8 tiles per warp
-    __shared__ __align__(16) uint16_t xs[2][kRowsPerCta * kXStride];
-    __shared__ __align__(16) uint16_t as[2][kBK * kAStride];
+    using C = LoraCfg<R>;
+    constexpr int kCols = R / 4;           // columns per warp
+    constexpr int kTiles = kCols / 8;      // n8 tiles per warp
+    extern __shared__ __align__(16) uint8_t lora_smem[];
 
     const int tid = threadIdx.x;
     const int warp = tid >> 5;
     const int lane = tid & 31;
-    const int rg = warp & 1;
-    const int ch = warp >> 1;
     const int64_t m0 = static_cast<int64_t>(blockIdx.x) * kRowsPerCta;
     const int chunks = static_cast<int>((K + kBK - 1) / kBK);
+    auto xs = [&](int s) { return reinterpret_cast<uint16_t*>(lora_smem + s * C::kStageBytes); };
+    auto as = [&](int s) { return reinterpret_cast<uint16_t*>(lora_smem + s * C::kStageBytes + C::kXBytes); };
 
     pdl_launch_dependents();
     pdl_wait();  // x may be the previous kernel's output
 
-    auto load_chunk = [&](int c, int buf) {
+    auto load_chunk = [&](int c) {
+        const int s = c % kStages;
         const int64_t k0 = static_cast<int64_t>(c) * kBK;
-        // x: 32 rows x 32 bf16 = 4 x 16-byte pieces per row
-        for (int i = tid; i < kRowsPerCta * 4; i += kThreads) {
-            const int row = i >> 2, piece = i & 3;
+        // x: 16 rows x 64 bf16 = 8 x 16-byte pieces per row
+        for (int i = tid; i < kRowsPerCta * 8; i += kThreads) {
+            const int row = i >> 3, piece = i & 7;
             const int64_t gm = m0 + row, gk = k0 + piece * 8;
             const bool ok = gm < M && gk < K;
-            const uint16_t* src = ok ? x + gm * K + gk : x;
-            cp_async16(smem_u32(&xs[buf][row * kXStride + piece * 8]), src, ok);
+            cp_async16(smem_u32(xs(s) + row * kXStride + piece * 8), ok ? x + gm * K + gk : x, ok);
         }
-        // A: 32 rows of K x R bf16 = R / 8 pieces per row
+        // A: 64 rows of K x R bf16 = R / 8 pieces per row
         for (int i = tid; i < kBK * (R / 8); i += kThreads) {
             const int row = i / (R / 8), piece = i % (R / 8);
             const int64_t gk = k0 + row;
             const bool ok = gk < K;
-            const uint16_t* src = ok ? a + gk * R + piece * 8 : a;
-            cp_async16(smem_u32(&as[buf][row * kAStride + piece * 8]), src, ok);
+            cp_async16(smem_u32(as(s) + row * C::kAStride + piece * 8), ok ? a + gk * R + piece * 8 : a, ok);
         }
-        cp_async_commit();
     };
 
     float acc[kTiles][4];
 #pragma unroll
     for (int t = 0; t < kTiles; ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0.0f;
 
-    load_chunk(0, 0);
+    // Prologue: chunks 0 and 1 in flight (one commit group each; a group past
+    // the last chunk is empty, which keeps the wait counts uniform).
+    for (int c = 0; c < kStages - 1; ++c) {
+        if (c < chunks) load_chunk(c);
+        cp_async_commit();
+    }
     for (int c = 0; c < chunks; ++c) {
-        const int buf = c & 1;
-        if (c + 1 < chunks) {
-            load_chunk(c + 1, buf ^ 1);
-            cp_async_wait<1>();
-        } else {
-            cp_async_wait<0>();
-        }
-        __syncthreads();
+        cp_async_wait<kStages - 2>();  // this thread's copies of chunk c have landed
+        __syncthreads();               // ... and everyone's; the slot of chunk c - 1 is free again
+        if (c + kStages - 1 < chunks) load_chunk(c + kStages - 1);
+        cp_async_commit();
+        const uint16_t* xt = xs(c % kStages);
+        const uint16_t* at = as(c % kStages);
 #pragma unroll
         for (int ks = 0; ks < kBK / 16; ++ks) {
-            // A operand: rows 16 rg .. +15, K columns 16 ks .. +15 of the x tile.
+            // A operand: the 16 rows, K columns 16 ks .. +15 of the x chunk.
             uint32_t af[4];
-            {
-                const int r = 16 * rg + (lane & 15);
-                const int col = 16 * ks + 8 * (lane >> 4);
-                ldmatrix_x4(smem_u32(&xs[buf][r * kXStride + col]), af);
-            }
+            ldmatrix_x4(smem_u32(xt + (lane & 15) * kXStride + 16 * ks + 8 * (lane >> 4)), af);
 #pragma unroll
             for (int t = 0; t < kTiles; ++t) {
                 // B operand: K rows 16 ks .. +15 (row-major [k][n] in shared memory,
-                // transposed by ldmatrix), n columns kHalf ch + 8 t .. +7.
+                // transposed by ldmatrix), n columns warp r/4 + 8 t .. +7.
                 uint32_t bf[2];
-                const int kr = 16 * ks + (lane & 15);
-                ldmatrix_x2_trans(smem_u32(&as[buf][kr * kAStride + kHalf * ch + 8 * t]), bf);
+                ldmatrix_x2_trans(smem_u32(at + (16 * ks + (lane & 15)) * C::kAStride + kCols * warp + 8 * t), bf);
                 mma_bf16_16816(acc[t], af, bf);
             }
         }
-        __syncthreads();  // the buffer is refilled two chunks later
     }
+    cp_async_wait<0>();
 
     // Accumulator layout: thread holds rows g, g + 8 (g = lane / 4) and
     // columns 2 (lane % 4), +1 of each n8 tile.
@@ -141,10 +147,10 @@ __global__ void __launch_bounds__(kThreads) lora_xa_kernel(const uint16_t* __res
     const int cq = 2 * (lane & 3);
 #pragma unroll
     for (int t = 0; t < kTiles; ++t) {
-        const int col = kHalf * ch + 8 * t + cq;
+        const int col = kCols * warp + 8 * t + cq;
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-            const int64_t row = m0 + 16 * rg + g + 8 * h;
+            const int64_t row = m0 + g + 8 * h;
             if (row < M) {
                 const __nv_bfloat162 v = __floats2bfloat162_rn(acc[t][2 * h], acc[t][2 * h + 1]);
                 *reinterpret_cast<__nv_bfloat162*>(xa + row * R + col) = v;
@@ -155,10 +161,21 @@ __global__ void __launch_bounds__(kThreads) lora_xa_kernel(const uint16_t* __res
 
 template <int R>
 int launch_r(const uint16_t* x, const uint16_t* a, uint16_t* xa, int64_t M, int64_t K, cudaStream_t stream) {
+    using C = LoraCfg<R>;
+    static std::atomic<bool> attr_set_for_device[kMaxDevices];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return Q6_ERR_CUDA;
+    if (dev < 0 || dev >= kMaxDevices) return Q6_ERR_UNSUPPORTED;
+    if (!attr_set_for_device[dev].load(std::memory_order_acquire)) {
+        if (cudaFuncSetAttribute(lora_xa_kernel<R>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes) !=
+            cudaSuccess)
+            return Q6_ERR_CUDA;
+        attr_set_for_device[dev].store(true, std::memory_order_release);
+    }
     const int64_t blocks = (M + kRowsPerCta - 1) / kRowsPerCta;
     if (blocks > 0x7fffffff) return Q6_ERR_UNSUPPORTED;
-    const cudaError_t e = launch_pdl(lora_xa_kernel<R>, dim3(static_cast<unsigned>(blocks)), dim3(kThreads), 0,
-                                     stream, x, a, xa, M, K);
+    const cudaError_t e = launch_pdl(lora_xa_kernel<R>, dim3(static_cast<unsigned>(blocks)), dim3(kThreads),
+                                     C::kSmemBytes, stream, x, a, xa, M, K);
     return e == cudaSuccess ? Q6_OK : Q6_ERR_CUDA;
 }
 

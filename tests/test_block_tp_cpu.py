@@ -1,12 +1,16 @@
-"""The tensor-parallel block layout on CPU over a world-size-2 gloo group.
+"""The sequence-parallel tensor-parallel block layout on CPU over gloo groups.
 
 Each rank runs the block's stages with the oracle's linears on its shard of
 the weights (``split_rows`` for q / k / v and mlp_in, ``split_k`` for the
 output projections and mlp_out), in the order ``TensorParallelQwenBlock``
-uses: local heads, row-parallel partials carrying the residual and bias on
-rank 0 and the gate on every rank, an all-reduce after the attention output
-and after the feed-forward.  The summed streams must equal the unsharded
-oracle block (no GPU involved).
+uses: the joint rows [B * S, D] (each sample's text rows, then its image
+rows) split into contiguous row shards; adaLN modulate on the local rows
+with each row's own (sample, stream) vectors; all-gather of the modulated
+rows; local heads; row-parallel partials carrying the gate on every rank and
+the output bias on rank 0; reduce-scatter back to the local rows; residual
+adds on the local rows.  The gathered output must equal the unsharded oracle
+block of every sample (no GPU involved).  Shard boundaries fall inside a
+sample's text / image rows and between samples.
 """
 
 from __future__ import annotations
@@ -37,7 +41,7 @@ def _np(weight, scales, biases, bias, gs):
                             gs)
 
 
-def _setup(seed=31, d=256, heads=2, s_img=24, s_txt=8):
+def _setup(seed=31, d=512, heads=4, s_img=24, s_txt=8, batch=1):
     rng = np.random.default_rng(seed)
     lin = {}
     for name, (fo, fi) in ob.BLOCK_LINEARS.items():
@@ -47,19 +51,26 @@ def _setup(seed=31, d=256, heads=2, s_img=24, s_txt=8):
         lin[name] = oracle.Q6Weights(p, s, b, bias, 64)
     norms = {n: (1 + 0.1 * rng.standard_normal(128)).astype(np.float32) for n in ob.NORMS}
     w = ob.BlockWeights(lin, norms, heads)
-    hidden = rng.standard_normal((s_img, d)).astype(np.float32)
-    enc = rng.standard_normal((s_txt, d)).astype(np.float32)
-    temb = rng.standard_normal(d).astype(np.float32)
+    hidden = rng.standard_normal((batch, s_img, d)).astype(np.float32)
+    enc = rng.standard_normal((batch, s_txt, d)).astype(np.float32)
+    temb = rng.standard_normal((batch, d)).astype(np.float32)
     ia, ta = ob.qwen_rope_angles([(4, 6)], s_txt)
     rope = (np.cos(ia), np.sin(ia), np.cos(ta), np.sin(ta))
     return w, hidden, enc, temb, rope
 
 
 def _tp_block(w, hidden, enc, temb, rope, world, rank):
+    """The sequence-parallel layout on this rank; returns the gathered joint output [B * S, D]."""
+
     import torch.distributed as dist
 
-    d, lead = hidden.shape[1], rank == 0
+    batch, s_img, d = hidden.shape
+    s_txt = enc.shape[1]
+    seq = s_txt + s_img
+    lead = rank == 0
     heads = w.heads // world
+    rows_local = batch * seq // world
+    row0 = rank * rows_local
 
     def rows(name):
         q = w.linears[name]
@@ -70,38 +81,67 @@ def _tp_block(w, hidden, enc, temb, rope, world, rank):
         ws, ss, bs = split_k(_u32(q.weight), _u16(q.scales), _u16(q.biases), 64, world, rank)
         return _np(ws, ss, bs, _u16(q.bias) if lead else None, 64)
 
-    def allreduce(a):
-        t = torch.from_numpy(np.ascontiguousarray(a, dtype=np.float32))
-        dist.all_reduce(t)
-        return t.numpy()
+    def all_gather(local):
+        parts = [torch.zeros_like(torch.from_numpy(local)) for _ in range(world)]
+        dist.all_gather(parts, torch.from_numpy(np.ascontiguousarray(local, dtype=np.float32)))
+        return torch.cat(parts).numpy()
 
-    t = ob.silu(temb).reshape(1, d)
-    im = oracle.linear(t, w.linears["img_mod_linear"]).reshape(6, d)
-    tm = oracle.linear(t, w.linears["txt_mod_linear"]).reshape(6, d)
-    img_in = ob.layernorm_modulate(hidden, im[0], im[1])
-    txt_in = ob.layernorm_modulate(enc, tm[0], tm[1])
+    def reduce_scatter(full):
+        t = torch.from_numpy(np.ascontiguousarray(full, dtype=np.float32))
+        dist.all_reduce(t)  # reduce-scatter's sum, then this rank's rows
+        return t.numpy()[row0:row0 + rows_local]
+
+    mods = []
+    for b in range(batch):
+        t = ob.silu(temb[b]).reshape(1, d)
+        mods.append((oracle.linear(t, w.linears["txt_mod_linear"]).reshape(6, d),
+                     oracle.linear(t, w.linears["img_mod_linear"]).reshape(6, d)))
+
+    def stream_of(g):  # global joint row -> (sample, stream)
+        return g // seq, int(g % seq >= s_txt)
+
+    def modulate(x_local, half):
+        out = np.empty_like(x_local)
+        for i in range(rows_local):
+            b, s = stream_of(row0 + i)
+            m = mods[b][s]
+            out[i] = ob.layernorm_modulate(x_local[i:i + 1], m[3 * half], m[3 * half + 1])[0]
+        return out
+
+    x = np.concatenate([np.concatenate([enc[b], hidden[b]]) for b in range(batch)])
+    x_local = x[row0:row0 + rows_local]
+    z = all_gather(modulate(x_local, 0))
     ic, is_, tc, ts = rope
-    q = np.concatenate([ob.qk_rmsnorm_rope(oracle.linear(txt_in, rows("attn.add_q_proj")), w.norms["attn.norm_added_q"], tc, ts),
-                        ob.qk_rmsnorm_rope(oracle.linear(img_in, rows("attn.to_q")), w.norms["attn.norm_q"], ic, is_)])
-    k = np.concatenate([ob.qk_rmsnorm_rope(oracle.linear(txt_in, rows("attn.add_k_proj")), w.norms["attn.norm_added_k"], tc, ts),
-                        ob.qk_rmsnorm_rope(oracle.linear(img_in, rows("attn.to_k")), w.norms["attn.norm_k"], ic, is_)])
-    v = np.concatenate([oracle.linear(txt_in, rows("attn.add_v_proj")), oracle.linear(img_in, rows("attn.to_v"))])
-    joint = ob.attention(q, k, v, heads).astype(np.float32)
-    s_txt = enc.shape[0]
-    streams = np.concatenate([
-        oracle.linear(joint[:s_txt], cols("attn.to_add_out"), residual=enc if lead else None, gate=tm[2]),
-        oracle.linear(joint[s_txt:], cols("attn.attn_to_out.0"), residual=hidden if lead else None, gate=im[2]),
-    ])
-    streams = allreduce(streams)
-    txt_h, img_h = streams[:s_txt], streams[s_txt:]
-    img_mid = oracle.linear(ob.layernorm_modulate(img_h, im[3], im[4]), rows("img_ff.mlp_in"), apply_gelu=True)
-    txt_mid = oracle.linear(ob.layernorm_modulate(txt_h, tm[3], tm[4]), rows("txt_ff.mlp_in"), apply_gelu=True)
-    outs = np.concatenate([
-        oracle.linear(txt_mid, cols("txt_ff.mlp_out"), residual=txt_h if lead else None, gate=tm[5]),
-        oracle.linear(img_mid, cols("img_ff.mlp_out"), residual=img_h if lead else None, gate=im[5]),
-    ])
-    outs = allreduce(outs)
-    return outs[:s_txt], outs[s_txt:]
+    segs = [(b, s, slice(b * seq, b * seq + s_txt) if s == 0 else slice(b * seq + s_txt, (b + 1) * seq))
+            for b in range(batch) for s in (0, 1)]
+    names = {0: ("attn.add_q_proj", "attn.add_k_proj", "attn.add_v_proj", "attn.norm_added_q", "attn.norm_added_k"),
+             1: ("attn.to_q", "attn.to_k", "attn.to_v", "attn.norm_q", "attn.norm_k")}
+    dl = heads * 128
+    q = np.empty((batch * seq, dl), np.float32)
+    k = np.empty_like(q)
+    v = np.empty_like(q)
+    for b, s, r in segs:
+        nq, nk, nv, wq, wk = names[s]
+        c, sn = (tc, ts) if s == 0 else (ic, is_)
+        q[r] = ob.qk_rmsnorm_rope(oracle.linear(z[r], rows(nq)), w.norms[wq], c, sn)
+        k[r] = ob.qk_rmsnorm_rope(oracle.linear(z[r], rows(nk)), w.norms[wk], c, sn)
+        v[r] = oracle.linear(z[r], rows(nv))
+    att = np.empty_like(q)
+    for b in range(batch):
+        r = slice(b * seq, (b + 1) * seq)
+        att[r] = ob.attention(q[r], k[r], v[r], heads).astype(np.float32)
+    part = np.empty((batch * seq, d), np.float32)
+    for b, s, r in segs:
+        part[r] = oracle.linear(att[r], cols("attn.to_add_out" if s == 0 else "attn.attn_to_out.0"),
+                                gate=mods[b][s][2])
+    h_local = x_local + reduce_scatter(part)
+    z2 = all_gather(modulate(h_local, 1))
+    part2 = np.empty((batch * seq, d), np.float32)
+    for b, s, r in segs:
+        pre = "txt_ff" if s == 0 else "img_ff"
+        mid = oracle.linear(z2[r], rows(f"{pre}.mlp_in"), apply_gelu=True)
+        part2[r] = oracle.linear(mid, cols(f"{pre}.mlp_out"), gate=mods[b][s][5])
+    return all_gather(h_local + reduce_scatter(part2))
 
 
 def _full_block(w, hidden, enc, temb, rope):
@@ -130,22 +170,25 @@ def _full_block(w, hidden, enc, temb, rope):
             oracle.linear(img_mid, lin["img_ff.mlp_out"], residual=img_h, gate=im[5]))
 
 
-def _worker(rank: int, world: int, port: int) -> None:
+def _worker(rank: int, world: int, port: int, batch: int) -> None:
     import torch.distributed as dist
 
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
-        args = _setup()
-        got = _tp_block(*args, world, rank)
-        ref = _full_block(*args)
-        for g, r in zip(got, ref):
-            err = float(np.abs(g - r).max())
-            assert err <= 1e-4 * float(np.abs(r).max()), err
+        w, hidden, enc, temb, rope = _setup(batch=batch)
+        got = _tp_block(w, hidden, enc, temb, rope, world, rank)
+        seq = enc.shape[1] + hidden.shape[1]
+        for b in range(batch):
+            ref_t, ref_i = _full_block(w, hidden[b], enc[b], temb[b], rope)
+            g = got[b * seq:(b + 1) * seq]
+            for part, r in ((g[:enc.shape[1]], ref_t), (g[enc.shape[1]:], ref_i)):
+                err = float(np.abs(part - r).max())
+                assert err <= 1e-4 * float(np.abs(r).max()), err
         # the oracle block with bf16 roundings stays close to the unrounded one
-        rounded = ob.block_forward(*args[:4], *args[4])
-        for g, r in zip(rounded, ref):
+        rounded = ob.block_forward(w, hidden[0], enc[0], temb[0], *rope)
+        for g, r in zip(rounded, _full_block(w, hidden[0], enc[0], temb[0], rope)):
             assert float(np.abs(g - r).max()) <= 3e-2 * float(np.abs(r).max())
     finally:
         dist.destroy_process_group()
@@ -157,5 +200,14 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def test_tensor_parallel_block_gloo_world2():
-    mp.spawn(_worker, args=(2, _free_port()), nprocs=2, join=True)
+def test_sequence_parallel_block_gloo_world2_one_sample():
+    """32 joint rows over 2 ranks: rank 0 holds the 8 text rows and 8 image rows."""
+
+    mp.spawn(_worker, args=(2, _free_port(), 1), nprocs=2, join=True)
+
+
+def test_sequence_parallel_block_gloo_world4_two_samples():
+    """Two samples (CFG cond / uncond) of 32 joint rows over 4 ranks: shards of
+    16 rows, one starting in a sample's text rows, one in its image rows."""
+
+    mp.spawn(_worker, args=(4, _free_port(), 2), nprocs=4, join=True)

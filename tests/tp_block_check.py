@@ -1,6 +1,8 @@
-"""Tensor-parallel MMDiT block over NCCL, one process per GPU (launched by
-tests/test_gpu_block.py through torch.distributed.run): heads and FF columns
-split, two all-reduces per block; checked against the single-GPU block."""
+"""Sequence-parallel tensor-parallel MMDiT block over NCCL, one process per GPU
+(launched by tests/test_gpu_block.py through torch.distributed.run): heads
+and FF columns split, joint rows sharded between the GEMMs (all-gather before
+each column-parallel GEMM, reduce-scatter after each row-parallel one), two
+samples per call; checked against the single-GPU block."""
 
 import datetime
 import os
@@ -24,9 +26,9 @@ dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_i
 g = torch.Generator(device="cuda").manual_seed(11)
 dim, heads = 1024, 8
 full = QwenTransformerBlock.random(dim, heads, generator=g)
-hidden = torch.randn((1, 600, dim), generator=g, device="cuda").to(torch.bfloat16)
-enc = torch.randn((1, 64, dim), generator=g, device="cuda").to(torch.bfloat16)
-temb = torch.randn((1, dim), generator=g, device="cuda").to(torch.bfloat16)
+hidden = torch.randn((2, 600, dim), generator=g, device="cuda").to(torch.bfloat16)
+enc = torch.randn((2, 64, dim), generator=g, device="cuda").to(torch.bfloat16)
+temb = torch.randn((2, dim), generator=g, device="cuda").to(torch.bfloat16)
 ia, ta = qwen_rope_angles([(20, 30)], 64)
 rope = rope_tables(ia, ta, "cuda")
 ref = full(hidden, enc, temb, rope)
