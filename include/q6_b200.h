@@ -58,8 +58,8 @@ enum q6_epilogue {
 /* Site codes a kernel writes into the device error word when one of its
    bounded waits gives up (q6_get_device_error). */
 enum q6_error_site {
-    Q6_SITE_GEMM_MIN = 1,       /* 1..11: tcgen05 GEMM and GEMV pipeline barriers */
-    Q6_SITE_GEMM_MAX = 11,
+    Q6_SITE_GEMM_MIN = 1,       /* 1..12: GEMM, GEMV and few-row MMA pipeline barriers */
+    Q6_SITE_GEMM_MAX = 12,
     Q6_SITE_SELFTEST = 64       /* q6_selftest_bounded_wait */
 };
 
@@ -67,7 +67,9 @@ enum q6_error_site {
 enum q6_path {
     Q6_PATH_AUTO = 0,
     Q6_PATH_SIMT = 1,   /* CUDA-core kernel, fp32 dequantised weights   */
-    Q6_PATH_TENSOR = 2  /* tcgen05 kernel, bf16 dequantised weights     */
+    Q6_PATH_TENSOR = 2, /* tcgen05 kernel, bf16 dequantised weights     */
+    Q6_PATH_SKINNY = 3  /* warp-MMA kernel for 1..32 token rows on the raw codes,
+                           fp32 weight semantics (group size 64 / 128)  */
 };
 
 /*

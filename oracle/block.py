@@ -145,14 +145,14 @@ class BlockWeights:
     heads: int
 
 
-FEW_ROWS = 4  # the library's few-row (GEMV) path takes at most this many token rows
+FEW_ROWS = 32  # the library's few-row paths (streaming GEMV, warp-MMA) take at most this many token rows
 
 
 def _lin(w: BlockWeights, name: str, x: np.ndarray, *, launch_rows: int | None = None, **kw) -> np.ndarray:
     """One q6 linear with the weight precision of the kernel path that runs it
     for ``launch_rows`` token rows (default: the rows of ``x``): fp32
     dequantised weights for a few rows (the modulation linears at M = batch
-    run on the streaming GEMV, which keeps the reference kernel's fp32
+    run on the few-row kernels, which keep the reference kernel's fp32
     ``scale * code + qbias``), bf16 weights otherwise (the tensor-core path,
     MLX qmm semantics).  ``x`` may hold a subset of the launch's rows."""
 

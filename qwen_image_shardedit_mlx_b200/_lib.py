@@ -31,8 +31,9 @@ Q6_SITE_SELFTEST = 64
 Q6_PATH_AUTO = 0
 Q6_PATH_SIMT = 1
 Q6_PATH_TENSOR = 2
+Q6_PATH_SKINNY = 3
 
-PATHS = {"auto": Q6_PATH_AUTO, "simt": Q6_PATH_SIMT, "tensor": Q6_PATH_TENSOR}
+PATHS = {"auto": Q6_PATH_AUTO, "simt": Q6_PATH_SIMT, "tensor": Q6_PATH_TENSOR, "skinny": Q6_PATH_SKINNY}
 
 # Every symbol include/q6_b200.h declares, with its ctypes signature.
 _P = ctypes.c_void_p

@@ -8,6 +8,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <cstdlib>
 
 #include "q6_b200.h"
 #include "q6_internal.h"
@@ -37,10 +38,31 @@ bool simt_aligned(const void* x, int64_t K, int elem_bytes) {
     return aligned(x, 16) && ((K * elem_bytes) % 16 == 0);
 }
 
+// Few-row policy: the warp-MMA kernel runs when asked for by path
+// (Q6_PATH_SKINNY), or for 1..32 token rows when Q6_SKINNY=1; by default the
+// streaming GEMV (M <= 4) and the tensor-core path are faster.
+bool skinny_auto(const q6::LinearArgs& a) {
+    static const int mode = [] {
+        const char* v = std::getenv("Q6_SKINNY");
+        return (v && v[0] == '1') ? 1 : 0;
+    }();
+    return mode && q6::skinny_supported(a);
+}
+
 int run_linear(const q6::LinearArgs& a, int path, cudaStream_t stream) {
     const bool tc_ok = q6::tc_supported(a);
     int chosen = path;
-    if (chosen == Q6_PATH_AUTO) chosen = (tc_ok && (a.M > 4 || a.lora_rank > 0)) ? Q6_PATH_TENSOR : Q6_PATH_SIMT;
+    if (chosen == Q6_PATH_AUTO) {
+        if (skinny_auto(a))
+            chosen = Q6_PATH_SKINNY;
+        else
+            chosen = (tc_ok && (a.M > 4 || a.lora_rank > 0)) ? Q6_PATH_TENSOR : Q6_PATH_SIMT;
+    }
+    if (chosen == Q6_PATH_SKINNY) {
+        if (a.lora_rank > 0 || !q6::skinny_supported(a)) return Q6_ERR_UNSUPPORTED;
+        g_last_path = Q6_PATH_SKINNY;
+        return q6::launch_skinny(a, stream);
+    }
     if (chosen == Q6_PATH_TENSOR) {
         if (!tc_ok) return Q6_ERR_UNSUPPORTED;
         g_last_path = Q6_PATH_TENSOR;
@@ -165,16 +187,21 @@ int q6_mlp_bf16(const uint16_t* x, const uint32_t* w1, const uint16_t* scales1, 
 int q6_get_device_error(int* code) {
     if (!code) return Q6_ERR_INVALID_ARGUMENT;
     if (cudaDeviceSynchronize() != cudaSuccess) return Q6_ERR_CUDA;
-    const int a = q6::error_word_simt(false);
-    const int b = q6::error_word_tc(false);
-    if (a < 0 || b < 0) return Q6_ERR_CUDA;
-    *code = a != 0 ? a : b;
+    const int words[4] = {q6::error_word_simt(false), q6::error_word_tc(false), q6::error_word_gemv(false),
+                          q6::error_word_skinny(false)};
+    *code = 0;
+    for (int w : words) {
+        if (w < 0) return Q6_ERR_CUDA;
+        if (*code == 0) *code = w;
+    }
     return Q6_OK;
 }
 
 int q6_clear_device_error(void) {
     if (cudaDeviceSynchronize() != cudaSuccess) return Q6_ERR_CUDA;
-    if (q6::error_word_simt(true) < 0 || q6::error_word_tc(true) < 0) return Q6_ERR_CUDA;
+    if (q6::error_word_simt(true) < 0 || q6::error_word_tc(true) < 0 || q6::error_word_gemv(true) < 0 ||
+        q6::error_word_skinny(true) < 0)
+        return Q6_ERR_CUDA;
     return Q6_OK;
 }
 

@@ -373,6 +373,16 @@ int launch_gemv_mt(const LinearArgs& a, cudaStream_t stream) {
 
 }  // namespace
 
+int error_word_gemv(bool clear) {
+    int v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_device_error, sizeof(int)) != cudaSuccess) return -1;
+    if (clear && v != 0) {
+        const int zero = 0;
+        if (cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int)) != cudaSuccess) return -1;
+    }
+    return v;
+}
+
 bool gemv_supported(const LinearArgs& a) {
     if (a.M < 1 || a.M > 4 || a.K % 64 != 0) return false;
     if (a.K > (int64_t(1) << 20) || a.N > (int64_t(1) << 30)) return false;

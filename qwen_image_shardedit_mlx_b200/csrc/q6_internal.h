@@ -57,6 +57,12 @@ int launch_linear_simt(const LinearArgs& a, bool f32_io, cudaStream_t stream);
 bool gemv_supported(const LinearArgs& a);
 int launch_gemv(const LinearArgs& a, cudaStream_t stream);
 
+// Warp-level MMA path for 1 <= M <= 32 bf16 rows on the raw codes (fp32
+// weight semantics): group size 64 or 128, K % (8 group_size) == 0, 16-byte
+// aligned x, codes, scales and biases, no LoRA.
+bool skinny_supported(const LinearArgs& a);
+int launch_skinny(const LinearArgs& a, cudaStream_t stream);
+
 // tcgen05 path: bf16 activations, bf16-dequantised weights, fp32 accumulate.
 // Requires K % 64 == 0 and 16-byte aligned x / w rows.
 int launch_linear_tc(const LinearArgs& a, int token_tile, cudaStream_t stream);
@@ -106,5 +112,7 @@ int launch_lora_xa(const uint16_t* x, const uint16_t* a, uint16_t* xa, int64_t M
 // a failed copy).
 int error_word_simt(bool clear);
 int error_word_tc(bool clear);
+int error_word_gemv(bool clear);
+int error_word_skinny(bool clear);
 
 }  // namespace q6

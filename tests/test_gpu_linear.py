@@ -201,6 +201,64 @@ def test_gemv_path_vs_oracle(m, n, k, gs, epi):
     assert_close(f32(got), ref, what=f"gemv {m}x{n}x{k} gs{gs} {epi}")
 
 
+SKINNY_SHAPES = [
+    (12288, 3072, 64),   # the image FF's fc1 shape
+    (3072, 12288, 64),   # fc2 shape: K split across the warps of a row block
+    (18432, 3072, 128),  # modulation-linear shape at group size 128
+    (1001, 1024, 64),    # ragged N: the last row block is partly out of range
+]
+
+
+@pytest.mark.parametrize("m", [1, 2, 3, 8, 16, 17, 32])
+@pytest.mark.parametrize("n,k,gs", SKINNY_SHAPES)
+@pytest.mark.parametrize("epi", ["plain", "bias_gelu", "residual_gate"])
+def test_skinny_path_vs_oracle(m, n, k, gs, epi):
+    """The warp-MMA kernel for 1..32 token rows on the raw codes against the
+    fp32-weight oracle (the reference kernel's weight precision); the output
+    starts as NaN so every element must be written."""
+
+    rng = np.random.default_rng(m * 13 + n + k + gs)
+    w = random_weights(rng, n, k, gs, bias=epi != "plain")
+    x = random_bf16(rng, (m, k))
+    wt, st, bt, bias = weights_to_torch(w)
+    kwargs = {}
+    residual = gate = None
+    if epi == "residual_gate":
+        residual = random_bf16(rng, (m, n))
+        gate = random_bf16(rng, (n,), 0.5)
+        kwargs = dict(residual=from_bits(residual), gate=from_bits(gate))
+    out = torch.full((m, n), float("nan"), dtype=torch.bfloat16, device="cuda")
+    got = ops.q6_linear(from_bits(x), wt, st, bt, bias, group_size=gs, apply_gelu=epi == "bias_gelu",
+                        path="skinny", out=out, **kwargs)
+    torch.cuda.synchronize()
+    assert ops.last_path() == "skinny"
+    assert bool(torch.isfinite(got).all())
+    ref = oracle.linear(
+        oracle.bf16_bits_to_f32(x), w, apply_gelu=epi == "bias_gelu", weight_dtype="f32",
+        residual=None if residual is None else oracle.bf16_bits_to_f32(residual),
+        gate=None if gate is None else oracle.bf16_bits_to_f32(gate),
+    )
+    assert_close(f32(got), ref, what=f"skinny {m}x{n}x{k} gs{gs} {epi}")
+
+
+def test_skinny_split_k_is_reproducible(monkeypatch):
+    """Warps splitting a row block's K sum their partials in a fixed order."""
+
+    rng = np.random.default_rng(6)
+    w = random_weights(rng, 1024, 8192, 64)
+    wt, st, bt, bias = weights_to_torch(w)
+    x = from_bits(random_bf16(rng, (16, 8192)))
+    outs = []
+    for splits in ("4", "4", "1"):
+        monkeypatch.setenv("Q6_SKINNY_SPLITS", splits)
+        outs.append(ops.q6_linear(x, wt, st, bt, bias, group_size=64, path="skinny"))
+    torch.cuda.synchronize()
+    assert torch.equal(outs[0], outs[1])
+    ref = oracle.linear(f32(x), w, weight_dtype="f32")
+    for o in outs:
+        assert_close(f32(o), ref)
+
+
 LORA_CASES = [
     (200, 384, 512, 64, 64, "bias_gelu"),
     (17, 256, 192, 32, 32, "plain"),          # K % 128 == 64 tail before the LoRA stages
