@@ -56,6 +56,8 @@ def parse_args() -> argparse.Namespace:
     ap.add_argument("--no-block", action="store_true", help="skip the full MMDiT block measurement")
     ap.add_argument("--no-sweep", action="store_true", help="skip the q6 linear shape / M / group-size sweep")
     ap.add_argument("--no-stack", action="store_true", help="skip the 60-block stack (config 5)")
+    ap.add_argument("--tp-comm", choices=["peer", "nccl"], default="peer",
+                    help="collectives of the tensor-parallel block: fused peer-memory kernels or NCCL")
     return ap.parse_args()
 
 
@@ -325,9 +327,9 @@ def run_ours(args, world: int, rank: int, local: int) -> dict | None:
     e2e_serial_ms = max_over_ranks(e0.elapsed_time(e1), world)
 
     # ---- one full MMDiT block (3456 image + 256 text tokens), tensor-parallel over the ranks
-    block = None if args.no_block else measure_block(dev, world, rank)
+    block = None if args.no_block else measure_block(dev, world, rank, comm=args.tp_comm)
     # ---- config 5: the 60-block stack, 8 steps, batch 2, tensor-parallel over the ranks
-    stack = None if args.no_stack else measure_stack(dev, world, rank)
+    stack = None if args.no_stack else measure_stack(dev, world, rank, comm=args.tp_comm)
 
     # ---- skinny-M GEMV side measurement (HBM-bound), rank 0 only
     gemv = None
@@ -460,7 +462,7 @@ def _block_inputs(dev, batch: int, seed: int):
     return x, temb, joint_rope(rope_tables(ia, ta, dev)), seq
 
 
-def measure_block(dev, world: int, rank: int, steps: int = 10) -> dict | None:
+def measure_block(dev, world: int, rank: int, steps: int = 10, comm: str = "peer") -> dict | None:
     """Device time of one Qwen-Image MMDiT block forward (3456 image + 256
     text tokens, all 14 linears q6 gs64, joint attention over 3712 tokens), at
     batch 1 (config 3) and batch 2 (the per-block cost of config 5's CFG pair).
@@ -476,7 +478,10 @@ def measure_block(dev, world: int, rank: int, steps: int = 10) -> dict | None:
 
     g = torch.Generator(device=dev).manual_seed(2025)  # the same block on every rank
     full = QwenTransformerBlock.random(DIM, BLOCK_HEADS, generator=g, device=dev)
-    tp = TensorParallelQwenBlock(full, world, rank) if world > 1 else None
+    tp = TensorParallelQwenBlock(full, world, rank, comm=comm) if world > 1 else None
+    tp_other = None
+    if world > 1:
+        tp_other = TensorParallelQwenBlock(full, world, rank, comm="nccl" if comm == "peer" else "peer")
     out = {}
     for batch in (1, 2):
         x, temb, rope_j, seq = _block_inputs(dev, batch, 7 + batch)
@@ -490,6 +495,9 @@ def measure_block(dev, world: int, rank: int, steps: int = 10) -> dict | None:
         else:
             ms, eager_ms = _graph_ms(lambda: tp.finish(tp.forward_local(x_local, temb, rope_j, batch, seq, BLOCK_TXT)),
                                      world, steps)
+            ms_other, _ = _graph_ms(
+                lambda: tp_other.finish(tp_other.forward_local(x_local, temb, rope_j, batch, seq, BLOCK_TXT)),
+                world, steps)
             ms_1 = None
             if rank == 0:
                 ms_1, _ = _graph_ms(one, 1, steps)
@@ -500,6 +508,8 @@ def measure_block(dev, world: int, rank: int, steps: int = 10) -> dict | None:
         out[f"b{batch}"] = {
             "ms": round(ms, 4), "TFLOP/s": round(flop / (ms * 1e-3) / 1e12, 1), "eager_ms": round(eager_ms, 4),
             "ms_1gpu": None if ms_1 is None else round(ms_1, 4),
+            "comm": comm if world > 1 else None,
+            "ms_other_comm": None if world == 1 else round(ms_other, 4),
             "efficiency_vs_1gpu": None if ms_1 is None else round(ms_1 / (world * ms), 4),
             "batch": batch, "flop_per_call": flop,
         }
@@ -510,8 +520,10 @@ def measure_block(dev, world: int, rank: int, steps: int = 10) -> dict | None:
         "n_gpus": world,
         "batch2": out["b2"],
         "parallelism": "single GPU" if world == 1 else
-        f"tensor-parallel x{world} (heads and FF columns) with sequence-parallel rows between the GEMMs: "
-        "2 all-gathers + 2 reduce-scatters (NCCL) per block",
+        f"tensor-parallel x{world} (heads and FF columns) with sequence-parallel rows between the GEMMs; "
+        + ("fused peer-memory reduce + residual + adaLN + gather kernels and 4 barriers per block"
+           if comm == "peer" else "2 all-gathers + 2 reduce-scatters (NCCL) per block")
+        + " (ms_other_comm: the other form, same run)",
         "shape": f"{BLOCK_IMG} image + {BLOCK_TXT} text tokens, hidden {DIM}, {BLOCK_HEADS} heads x 128, "
                  "FF 4x, all 14 linears q6 gs64",
         "steps": steps,
@@ -522,7 +534,8 @@ def measure_block(dev, world: int, rank: int, steps: int = 10) -> dict | None:
     return res
 
 
-def measure_stack(dev, world: int, rank: int, blocks: int = STACK_BLOCKS, steps: int = STACK_STEPS) -> dict | None:
+def measure_stack(dev, world: int, rank: int, blocks: int = STACK_BLOCKS, steps: int = STACK_STEPS,
+                  comm: str = "peer") -> dict | None:
     """Config 5: the 60-block q6 MMDiT stack, batch 2 (CFG cond / uncond),
     3456 image + 256 text tokens per sample, 8 denoising steps, tensor-parallel
     over the ranks.  Each rank builds its own shards of 60 random blocks
@@ -542,7 +555,7 @@ def measure_stack(dev, world: int, rank: int, blocks: int = STACK_BLOCKS, steps:
     for i in range(blocks):
         g = torch.Generator(device=dev).manual_seed(10_000 + i)
         full = QwenTransformerBlock.random(DIM, BLOCK_HEADS, generator=g, device=dev)
-        stack.append(TensorParallelQwenBlock(full, world, rank))
+        stack.append(TensorParallelQwenBlock(full, world, rank, comm=comm if world > 1 else "nccl"))
         del full
     torch.cuda.empty_cache()
     batch = STACK_BATCH
@@ -557,7 +570,7 @@ def measure_stack(dev, world: int, rank: int, blocks: int = STACK_BLOCKS, steps:
         pending = stack[0].forward_local(x_local, temb, rope_j, batch, seq, BLOCK_TXT)
         for blk in stack[1:]:
             pending = blk.forward_local_pending(pending, temb, rope_j, batch, seq, BLOCK_TXT)
-        return TensorParallelQwenBlock.finish(pending)
+        return stack[-1].finish(pending)
 
     stream = torch.cuda.current_stream()
     one_step()
@@ -600,7 +613,8 @@ def measure_stack(dev, world: int, rank: int, blocks: int = STACK_BLOCKS, steps:
         "ms_per_step": round(total_ms / steps, 3), "total_ms": round(total_ms, 2), "steps": steps, "blocks": blocks,
         "batch": batch, "n_gpus": world, "TFLOP/s": round(flop / (total_ms * 1e-3) / 1e12, 1),
         "parallelism": "single GPU" if world == 1 else
-        f"tensor-parallel x{world} with sequence-parallel rows (NCCL all-gather / reduce-scatter)",
+        f"tensor-parallel x{world} with sequence-parallel rows ("
+        + ("fused peer-memory kernels" if comm == "peer" else "NCCL all-gather / reduce-scatter") + ")",
         "shape": f"{blocks} blocks x batch {batch} x ({BLOCK_IMG} image + {BLOCK_TXT} text tokens), hidden {DIM}, "
                  "all linears q6 gs64",
         "note": "one denoising step (all blocks) captured in a CUDA graph and replayed per step with that step's "

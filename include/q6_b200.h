@@ -60,6 +60,7 @@ enum q6_epilogue {
 enum q6_error_site {
     Q6_SITE_GEMM_MIN = 1,       /* 1..12: GEMM, GEMV and few-row MMA pipeline barriers */
     Q6_SITE_GEMM_MAX = 12,
+    Q6_SITE_PEER_BARRIER = 13,  /* q6_sp_barrier: a peer's flag did not arrive in time */
     Q6_SITE_SELFTEST = 64       /* q6_selftest_bounded_wait */
 };
 
@@ -235,6 +236,44 @@ Q6_API int q6_qk_rmsnorm_rope_joint_bf16(uint16_t* qk, int64_t row_stride, int64
                                          const uint16_t* weight_text, const uint16_t* weight_image, const float* cos,
                                          const float* sin, int64_t row0, int64_t seq_len, int64_t text_len, float eps,
                                          q6_stream_t stream);
+
+/*
+ * Sequence-parallel step of the tensor-parallel block over peer memory (one
+ * rank per GPU, `world` <= 8 ranks; pointer tables are HOST arrays of `world`
+ * device pointers, this rank's own at index `rank`, each addressable from this
+ * GPU: CUDA peer mappings of buffers every rank allocated alike).  This rank
+ * owns joint rows [rank R, (rank + 1) R) of [world R, D].  The kernel forms
+ *   h = x_local + sum_r partials[r][own rows]   (rank order, fp32, one bf16 rounding;
+ *                                                h = x_local without partials)
+ * writes h to h_out (nullable), and writes
+ *   y = LayerNorm(h) * (1 + scale[v]) + shift[v]   (v as q6_add_layernorm_modulate_bf16)
+ * into the own-row block of every gathered[r] (gathered null: only h, which
+ * then needs partials and h_out; shift / scale may be null).  It is the reduce-scatter of
+ * the row-parallel GEMM's partial sums, the residual add, the adaLN modulate
+ * and the all-gather the next column-parallel GEMM needs, in one kernel
+ * (benchmarks/profile_qwen_block.py:253-263 with the block split over
+ * GPUs).  Order it between q6_sp_barrier calls: the partials of every rank
+ * complete before it runs, and its stores reach every rank before anyone
+ * reads them.  D in {256, 512, 1024, 3072}.
+ */
+Q6_API int q6_sp_add_layernorm_gather_bf16(const uint16_t* x_local, const uint16_t* const* partials,
+                                           uint16_t* h_out, const uint16_t* shift, const uint16_t* scale,
+                                           uint16_t* const* gathered, int world, int rank, int64_t R, int64_t D,
+                                           int64_t seq_len, int64_t text_len, float eps, q6_stream_t stream);
+
+/*
+ * Barrier of `world` ranks for the kernels above: one thread per peer
+ * publishes this rank's new epoch (system-scope release, after everything
+ * this GPU did before on the stream) into slot `rank` of that peer's signal
+ * array and waits until the peer's epoch is in slot `peer` of this rank's.
+ * signals: host array of `world` device pointers to uint32[world] (zeroed
+ * once, like `epoch`, before the first barrier); epoch: this rank's device
+ * counter, advanced by the barrier itself, so graph replays see new epochs.
+ * A wait longer than timeout_ns (1 us .. 60 s) records
+ * Q6_SITE_PEER_BARRIER in the device error word and gives up.
+ */
+Q6_API int q6_sp_barrier(uint32_t* const* signals, uint32_t* epoch, int world, int rank, int64_t timeout_ns,
+                         q6_stream_t stream);
 
 /* Device error word (0 = none, else a q6_error_site code).  Reading it
    synchronises the current device. */

@@ -26,6 +26,7 @@ Q6_EPI_NONE = 0
 Q6_EPI_GELU = 1
 Q6_EPI_GELU_PRECISE = 2
 
+Q6_SITE_PEER_BARRIER = 13
 Q6_SITE_SELFTEST = 64
 
 Q6_PATH_AUTO = 0
@@ -68,6 +69,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "q6_last_path": (_I, []),
     "q6_tensor_token_tile": (_I, [_I64, _I64]),
     "q6_pair_fallback_count": (_I64, []),
+    "q6_sp_add_layernorm_gather_bf16": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I64, _I64, _I64, _I64, _F, _P]),
+    "q6_sp_barrier": (_I, [_P, _P, _I, _I, _I64, _P]),
     "q6_selftest_bounded_wait": (_I, [_I64, _P]),
     "q6_status_string": (ctypes.c_char_p, [_I]),
     "q6_abi_version": (_I, []),

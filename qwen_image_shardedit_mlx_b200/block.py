@@ -441,6 +441,8 @@ def block_flops(s_img: int, s_txt: int, dim: int) -> int:
 
 # ------------------------------------------------------------------- tensor parallel
 
+_PEER_ROWS: dict = {}
+
 
 class TensorParallelQwenBlock(torch.nn.Module):
     """The block split over the ranks of a process group (one rank per GPU).
@@ -458,9 +460,13 @@ class TensorParallelQwenBlock(torch.nn.Module):
     The modulation linears (M = batch) are replicated.
     """
 
-    def __init__(self, full: QwenTransformerBlock, world: int, rank: int, group=None) -> None:
+    def __init__(self, full: QwenTransformerBlock, world: int, rank: int, group=None, comm: str = "nccl") -> None:
         super().__init__()
         from qwen_image_shardedit_mlx_b200.sharding import split_k, split_rows
+
+        if comm not in ("nccl", "peer"):
+            raise ValueError(f"comm must be 'nccl' or 'peer', got {comm!r}")
+        self.comm = comm
 
         if full.heads % world:
             raise ValueError(f"{full.heads} heads do not split over {world} ranks")
@@ -513,18 +519,37 @@ class TensorParallelQwenBlock(torch.nn.Module):
         dist.reduce_scatter_tensor(local, full, op=dist.ReduceOp.SUM, group=self.group)
         return local
 
+    def _peer(self, rows_total: int, device: torch.device):
+        """The peer-memory row buffers of this group (one set shared by every
+        block of the group with the same shape)."""
+
+        from qwen_image_shardedit_mlx_b200.peer import PeerRows
+
+        key = (id(self.group), int(rows_total), self.dim, str(device))
+        pr = _PEER_ROWS.get(key)
+        if pr is None:
+            pr = PeerRows(rows_total, self.dim, self.group, device)
+            _PEER_ROWS[key] = pr
+        return pr
+
     def forward_local(self, x_local: torch.Tensor, temb: torch.Tensor,
                       rope_joint: tuple[torch.Tensor, torch.Tensor], batch: int, seq: int, text_len: int,
-                      text_mask: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+                      text_mask: torch.Tensor | None = None) -> tuple[torch.Tensor, object]:
         """This rank's joint rows through the block: x_local [R, D] are rows
-        [rank R, (rank + 1) R) of the [B * S, D] joint rows.  Returns
-        (h, ff): the block's output rows are h + ff (``finish``); a stack may
-        instead hand the pair to the next block, whose first modulate adds
-        them in the same pass."""
+        [rank R, (rank + 1) R) of the [B * S, D] joint rows.  Returns a
+        pending pair: the block's output rows are h + ff (``finish``); a stack
+        may instead hand the pair to the next block, whose first modulate
+        adds them in the same pass."""
 
         rows_local, d = x_local.shape
         row0 = self.rank * rows_local
         vec = ModulationVectors(*self.modulation(temb))
+        if self.comm == "peer":
+            pr = self._peer(rows_local * self.world, x_local.device)
+            pr.add_ln_gather(x_local, vec.shift1, vec.scale1, dst="gather1", seq_len=seq, text_len=text_len,
+                             eps=self.eps)
+            pr.barrier()
+            return self._rest_peer(pr, x_local, vec, rope_joint, batch, seq, text_len, text_mask)
         z = self._gather(add_layernorm_modulate(x_local, vec.shift1, vec.scale1, row0=row0, seq_len=seq,
                                                 text_len=text_len, eps=self.eps))
         return self._rest(x_local, z, vec, rope_joint, batch, seq, text_len, text_mask, row0)
@@ -542,9 +567,43 @@ class TensorParallelQwenBlock(torch.nn.Module):
         row0 = self.rank * rows_local
         vec = ModulationVectors(*self.modulation(temb))
         x_local = torch.empty_like(h_prev)
+        if self.comm == "peer":
+            pr = self._peer(rows_local * self.world, h_prev.device)
+            pr.add_ln_gather(h_prev, vec.shift1, vec.scale1, dst="gather1", partials=ff_prev, h_out=x_local,
+                             seq_len=seq, text_len=text_len, eps=self.eps)
+            pr.barrier()
+            return self._rest_peer(pr, x_local, vec, rope_joint, batch, seq, text_len, text_mask)
         z_local = add_layernorm_modulate(h_prev, vec.shift1, vec.scale1, add=ff_prev, h_out=x_local, row0=row0,
                                          seq_len=seq, text_len=text_len, eps=self.eps)
         return self._rest(x_local, self._gather(z_local), vec, rope_joint, batch, seq, text_len, text_mask, row0)
+
+    def _rest_peer(self, pr, x_local, vec, rope_joint, batch, seq, text_len, text_mask):
+        """The block after the first modulate, with the fused peer kernels:
+        partial sums land in this rank's ``part`` buffers, the next kernel
+        reduces them onto their owners and gathers the modulated rows."""
+
+        dl = self.heads_local * HEAD_DIM
+        z = pr.buffers["gather1"]
+        rows = z.shape[0]
+        qkv = torch.empty((rows, 3 * dl), dtype=torch.bfloat16, device=z.device)
+        project_qkv_joint(self, z, qkv, batch, seq, text_len)
+        rope_qk_joint(self, qkv, dl, rope_joint, seq, text_len)
+        att = batched_joint_attention(qkv, dl, batch, seq, self.heads_local, text_len, text_mask)
+        part = pr.buffers["part1"]
+        for b, stream, r in segments(batch, seq, text_len):
+            name = "attn.to_add_out" if stream == 0 else "attn.attn_to_out.0"
+            self._linear(name, att[r], gate=vec.gate1(b, stream), out=part[r])
+        pr.barrier()
+        h_local = torch.empty_like(x_local)
+        pr.add_ln_gather(x_local, vec.shift2, vec.scale2, dst="gather2", partials="part1", h_out=h_local,
+                         seq_len=seq, text_len=text_len, eps=self.eps)
+        pr.barrier()
+        z2 = pr.buffers["gather2"]
+        part2 = pr.buffers["part2"]
+        for b, stream, r in segments(batch, seq, text_len):
+            self._mlp("txt_ff" if stream == 0 else "img_ff", z2[r], None, vec.gate2(b, stream), part2[r])
+        pr.barrier()
+        return h_local, "part2"
 
     def _rest(self, x_local, z, vec, rope_joint, batch, seq, text_len, text_mask, row0):
         d, dl = self.dim, self.heads_local * HEAD_DIM
@@ -566,9 +625,15 @@ class TensorParallelQwenBlock(torch.nn.Module):
             self._mlp("txt_ff" if stream == 0 else "img_ff", z2[r], None, vec.gate2(b, stream), part2[r])
         return h_local, self._reduce_scatter(part2)
 
-    @staticmethod
-    def finish(pending: tuple[torch.Tensor, torch.Tensor]) -> torch.Tensor:
+    def finish(self, pending: tuple[torch.Tensor, object]) -> torch.Tensor:
+        """The output rows h + ff of a pending pair."""
+
         h, ff = pending
+        if isinstance(ff, str):  # peer path: ff is every rank's partial-sum buffer
+            pr = self._peer(h.shape[0] * self.world, h.device)
+            out = torch.empty_like(h)
+            pr.add_ln_gather(h, None, None, dst=None, partials=ff, h_out=out)
+            return out
         return h + ff
 
     def forward(self, hidden: torch.Tensor, encoder: torch.Tensor, temb: torch.Tensor,

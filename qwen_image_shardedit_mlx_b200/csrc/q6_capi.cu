@@ -187,8 +187,8 @@ int q6_mlp_bf16(const uint16_t* x, const uint32_t* w1, const uint16_t* scales1, 
 int q6_get_device_error(int* code) {
     if (!code) return Q6_ERR_INVALID_ARGUMENT;
     if (cudaDeviceSynchronize() != cudaSuccess) return Q6_ERR_CUDA;
-    const int words[4] = {q6::error_word_simt(false), q6::error_word_tc(false), q6::error_word_gemv(false),
-                          q6::error_word_skinny(false)};
+    const int words[5] = {q6::error_word_simt(false), q6::error_word_tc(false), q6::error_word_gemv(false),
+                          q6::error_word_skinny(false), q6::error_word_sp(false)};
     *code = 0;
     for (int w : words) {
         if (w < 0) return Q6_ERR_CUDA;
@@ -200,7 +200,7 @@ int q6_get_device_error(int* code) {
 int q6_clear_device_error(void) {
     if (cudaDeviceSynchronize() != cudaSuccess) return Q6_ERR_CUDA;
     if (q6::error_word_simt(true) < 0 || q6::error_word_tc(true) < 0 || q6::error_word_gemv(true) < 0 ||
-        q6::error_word_skinny(true) < 0)
+        q6::error_word_skinny(true) < 0 || q6::error_word_sp(true) < 0)
         return Q6_ERR_CUDA;
     return Q6_OK;
 }

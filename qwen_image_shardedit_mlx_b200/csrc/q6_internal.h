@@ -114,5 +114,6 @@ int error_word_simt(bool clear);
 int error_word_tc(bool clear);
 int error_word_gemv(bool clear);
 int error_word_skinny(bool clear);
+int error_word_sp(bool clear);
 
 }  // namespace q6

@@ -327,6 +327,52 @@ def test_batched_block_vs_oracle_per_sample():
         assert_close(f32(t_out[b]), t_ref, what=f"batched block text stream, sample {b}")
 
 
+def test_peer_comm_block_world1_matches_nccl_layout():
+    """The peer-memory form of the sequence-parallel block (fused reduce +
+    residual + modulate + gather kernels, barriers) on one rank against the
+    NCCL form: the same rows through the same GEMMs, the residual sums formed
+    by two different kernels (fp32, one bf16 rounding each)."""
+
+    from qwen_image_shardedit_mlx_b200.block import TensorParallelQwenBlock
+
+    rng = np.random.default_rng(78)
+    _, tb = _block_pair(rng, 512, 4)
+    hidden = from_bits(random_bf16(rng, (2, 96, 512)))
+    enc = from_bits(random_bf16(rng, (2, 24, 512)))
+    temb = from_bits(random_bf16(rng, (2, 512)))
+    ia, ta = qwen_rope_angles([(8, 12)], 24)
+    rope = rope_tables(ia, ta, "cuda")
+    a = TensorParallelQwenBlock(tb, 1, 0, comm="nccl")(hidden, enc, temb, rope)
+    b = TensorParallelQwenBlock(tb, 1, 0, comm="peer")(hidden, enc, temb, rope)
+    torch.cuda.synchronize()
+    for x, y in zip(a, b):
+        assert_close(f32(y), f32(x), bf16_output=False, what="peer vs nccl layout, world 1")
+
+
+def test_peer_barrier_gives_up_on_a_missing_peer():
+    """The barrier's bounded wait: a two-rank signal table whose second
+    rank never arrives (both entries are this GPU's memory, and nothing writes
+    the slot this rank waits on) ends after the 2 ms limit with
+    Q6_SITE_PEER_BARRIER in the device error word instead of hanging."""
+
+    import ctypes
+
+    from qwen_image_shardedit_mlx_b200 import ops
+
+    sig = torch.zeros(16, dtype=torch.int32, device="cuda")
+    epoch = torch.zeros(1, dtype=torch.int32, device="cuda")
+    table = (ctypes.c_void_p * 2)(sig.data_ptr(), sig[8:].data_ptr())
+    ops.clear_device_error()
+    try:
+        st = _lib.lib().q6_sp_barrier(table, epoch.data_ptr(), 2, 0, 2_000_000, ops._stream(sig.device))
+        assert st == _lib.Q6_OK
+        assert ops.device_error() == _lib.Q6_SITE_PEER_BARRIER
+    finally:
+        ops.clear_device_error()
+    assert ops.device_error() == 0
+    assert int(epoch.item()) == 1  # the barrier advanced its epoch counter
+
+
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 def test_tensor_parallel_block_over_nccl_world2():
     import os

@@ -32,18 +32,22 @@ temb = torch.randn((2, dim), generator=g, device="cuda").to(torch.bfloat16)
 ia, ta = qwen_rope_angles([(20, 30)], 64)
 rope = rope_tables(ia, ta, "cuda")
 ref = full(hidden, enc, temb, rope)
-tp = TensorParallelQwenBlock(full, world, rank)
-out = tp(hidden, enc, temb, rope)
-torch.cuda.synchronize()
 ok = True
-for name, a, b in (("text", out[0], ref[0]), ("image", out[1], ref[1])):
-    err = (a.float() - b.float()).abs()
-    rel_max = float(err.max() / b.float().abs().max())
-    rel_mean = float(err.mean() / b.float().pow(2).mean().sqrt())
-    good = rel_max < 3e-2 and rel_mean < 3e-3
-    ok = ok and good
-    print(f"rank {rank}: tp{world} {name} stream vs single-GPU block max_rel {rel_max:.2e} mean_rel {rel_mean:.2e}",
-          flush=True)
+for comm in ("nccl", "peer"):
+    tp = TensorParallelQwenBlock(full, world, rank, comm=comm)
+    out = tp(hidden, enc, temb, rope)
+    torch.cuda.synchronize()
+    for name, a, b in (("text", out[0], ref[0]), ("image", out[1], ref[1])):
+        err = (a.float() - b.float()).abs()
+        rel_max = float(err.max() / b.float().abs().max())
+        rel_mean = float(err.mean() / b.float().pow(2).mean().sqrt())
+        good = rel_max < 3e-2 and rel_mean < 3e-3
+        ok = ok and good
+        print(f"rank {rank}: tp{world} {comm} {name} stream vs single-GPU block max_rel {rel_max:.2e} "
+              f"mean_rel {rel_mean:.2e}", flush=True)
+from qwen_image_shardedit_mlx_b200 import ops  # noqa: E402
+
+ok = ok and ops.device_error() == 0
 print(f"rank {rank}: {'OK' if ok else 'FAIL'}", flush=True)
 dist.destroy_process_group()
 sys.exit(0 if ok else 1)
