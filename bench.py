@@ -56,6 +56,8 @@ def parse_args() -> argparse.Namespace:
     ap.add_argument("--no-block", action="store_true", help="skip the full MMDiT block measurement")
     ap.add_argument("--no-sweep", action="store_true", help="skip the q6 linear shape / M / group-size sweep")
     ap.add_argument("--no-stack", action="store_true", help="skip the 60-block stack (config 5)")
+    ap.add_argument("--only", choices=["block", "gemv", "sweep", "stack"], default=None,
+                    help="run one side measurement alone and print its JSON (for profiling runs)")
     ap.add_argument("--tp-comm", choices=["peer", "nccl"], default="peer",
                     help="collectives of the tensor-parallel block: fused peer-memory kernels or NCCL")
     return ap.parse_args()
@@ -269,7 +271,9 @@ def run_ours(args, world: int, rank: int, local: int) -> dict | None:
     torch.cuda.synchronize()
 
     steps = args.steps
-    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(steps)]
+    # Timed region: K steps back to back (each kernel may overlap its
+    # predecessor's tail through programmatic dependent launch), one event
+    # before and one after.
     barrier(world)
     torch.cuda.synchronize()
     with ClockSampler(local) as clocks:
@@ -277,16 +281,24 @@ def run_ours(args, world: int, rank: int, local: int) -> dict | None:
         end = torch.cuda.Event(enable_timing=True)
         start.record(stream)
         for i in range(steps):
-            ev[i][0].record(stream)
             fc1_launch()
-            ev[i][1].record(stream)
             fc2_launch()
-            ev[i][2].record(stream)
         end.record(stream)
         torch.cuda.synchronize()
     barrier(world)
     local_ms = start.elapsed_time(end)
     total_ms = max_over_ranks(local_ms, world)
+    # Per-kernel durations for the roofline: a second pass of K steps with an
+    # event between every pair of launches (which also stops the overlap of
+    # one kernel's start with the previous one's tail).
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(steps)]
+    for i in range(steps):
+        ev[i][0].record(stream)
+        fc1_launch()
+        ev[i][1].record(stream)
+        fc2_launch()
+        ev[i][2].record(stream)
+    torch.cuda.synchronize()
     fc1_ms = statistics.mean(ev[i][0].elapsed_time(ev[i][1]) for i in range(steps))
     fc2_ms = statistics.mean(ev[i][1].elapsed_time(ev[i][2]) for i in range(steps))
     assert ops.device_error() == 0, "device error word raised during the benchmark"
@@ -385,6 +397,8 @@ def run_ours(args, world: int, rank: int, local: int) -> dict | None:
             "serial_api": "QwenFeedForward(x) one call at a time: copy in, ff, copy out on one stream",
         },
         "gpu_launches": 2 * steps,
+        "kernel_timing": "fc1_ms / fc2_ms and roofline.achieved from a second pass of the same steps with an event "
+                         "between launches; value from the timed pass without them",
         "token_tile": int(_lib.lib().q6_tensor_token_tile(TOKENS, HIDDEN)),
         "clocks": clock,
     }
@@ -622,61 +636,54 @@ def measure_stack(dev, world: int, rank: int, blocks: int = STACK_BLOCKS, steps:
     }
 
 
+GEMV_CASES = [
+    # (name, N, K, M): the few-row shapes of the block (q6_linear_profile.py:144-159)
+    ("m1", 12288, 3072, 1),          # 3072 -> 12288 at one token row
+    ("m2", 12288, 3072, 2),          # two rows (a CFG pair)
+    ("m16", 12288, 3072, 16),        # the skinny-M target shape
+    ("m1_k12288", 3072, 12288, 1),   # fc2-shaped (12288 -> 3072) at one row
+    ("mod_m2", 18432, 3072, 2),      # the adaLN modulation linear at batch 2
+]
+
+
 def measure_gemv(dev, peaks) -> dict:
-    """q6 GEMV at M=1 and M=16 (3072 -> 12288, gs64), rotating weight copies > L2."""
+    """q6 linears for a few token rows (GEMV_CASES), rotating weight copies
+    whose total exceeds L2 four times so every launch streams its weights from
+    HBM; device time per launch from a CUDA graph of back-to-back launches,
+    reported as HBM GB/s of the algorithmic bytes (codes, scales, biases, x, y)."""
 
     import torch
 
     from qwen_image_shardedit_mlx_b200 import ops
     from qwen_image_shardedit_mlx_b200.quantize import random_q6
 
-    n, k = 12288, 3072
     g = torch.Generator(device=dev).manual_seed(77)
-    copies = []
-    per_copy = n * k * 6 // 8 + 2 * 2 * n * (k // GROUP)
-    count = max(8, int(4 * L2_BYTES // per_copy) + 1)
-    for _ in range(count):
-        copies.append(random_q6(n, k, group_size=GROUP, generator=g, device=dev))
     out = {}
-    for m in (1, 16):
-        x = torch.randn((m, k), generator=g, device=dev).to(torch.bfloat16)
-        y = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
+    shapes: dict[tuple[int, int], list] = {}
+    for name, n, k, m in GEMV_CASES:
+        shapes.setdefault((n, k), []).append((name, m))
+    for (n, k), cases in shapes.items():
+        per_copy = n * k * 6 // 8 + 2 * 2 * n * (k // GROUP)
+        count = max(8, int(4 * L2_BYTES // per_copy) + 1)
+        w0 = random_q6(n, k, group_size=GROUP, generator=g, device=dev)
+        copies = [w0] + [tuple(t.clone() for t in w0) for _ in range(count - 1)]
+        for name, m in cases:
+            x = torch.randn((m, k), generator=g, device=dev).to(torch.bfloat16)
+            y = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
 
-        def launch(i):
-            w, s, b = copies[i % count]
-            ops.q6_linear(x, w, s, b, group_size=GROUP, out=y)
+            def launch(i, x=x, y=y):
+                w, s, b = copies[i % count]
+                ops.q6_linear(x, w, s, b, group_size=GROUP, out=y)
 
-        for i in range(count):
-            launch(i)
-        torch.cuda.synchronize()
-        # One launch per weight copy, captured in a CUDA graph: replaying it
-        # times the kernels back to back on the device, without the host-side
-        # cost of each Python call (how a decode loop would issue them).
-        side = torch.cuda.Stream()
-        side.wait_stream(torch.cuda.current_stream())
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph, stream=side):
-            for i in range(count):
-                launch(i)
-        torch.cuda.synchronize()
-        for _ in range(3):
-            graph.replay()
-        torch.cuda.synchronize()
-        reps = 8
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(reps):
-            graph.replay()
-        e1.record()
-        torch.cuda.synchronize()
-        us = e0.elapsed_time(e1) * 1e3 / (reps * count)
-        del graph
-        nbytes = per_copy + 2 * m * (k + n)
-        gbs = nbytes / (us * 1e-6) / 1e9
-        out[f"m{m}"] = {"us": round(us, 2), "GB/s": round(gbs, 1), "frac_hbm": round(gbs / peaks["hbm_gbs"], 4),
-                        "path": ops.last_path(), "bytes": nbytes}
-    out["note"] = f"3072->12288 gs64, {count} rotating weight copies ({count * per_copy / 2**20:.0f} MB > L2), one CUDA graph of back-to-back launches, device time"
+            us = _time_launches(launch, count, reps=8)
+            nbytes = per_copy + 2 * m * (k + n)
+            gbs = nbytes / (us * 1e-6) / 1e9
+            out[name] = {"n": n, "k": k, "m": m, "us": round(us, 2), "GB/s": round(gbs, 1),
+                         "frac_hbm": round(gbs / peaks["hbm_gbs"], 4), "path": ops.last_path(), "bytes": nbytes}
+        del copies, w0
+        torch.cuda.empty_cache()
+    out["note"] = ("gs64; weight copies rotating over > 4x L2 per shape, one CUDA graph of back-to-back launches, "
+                   "device time; frac_hbm against the measured copy bandwidth")
     return out
 
 
@@ -822,6 +829,9 @@ def measure_sweep(dev, peaks) -> dict:
 # ------------------------------------------------------------ host baselines
 
 
+# ------------------------------------------------------------ host baselines
+
+
 def cpu_baseline_port(budget_s: float = 12.0) -> dict:
     """The oracle's torch-CPU restatement (dequantise, then matmul) on a token sample."""
 
@@ -881,6 +891,18 @@ def main() -> int:
         return 0
     world, rank, local = dist_setup(args)
     try:
+        if args.only:
+            import torch
+
+            dev = torch.device("cuda", local)
+            fn = {"block": lambda: measure_block(dev, world, rank, comm=args.tp_comm),
+                  "stack": lambda: measure_stack(dev, world, rank, comm=args.tp_comm),
+                  "gemv": lambda: measure_gemv(dev, measured_peaks()) if rank == 0 else None,
+                  "sweep": lambda: measure_sweep(dev, measured_peaks()) if rank == 0 else None}[args.only]
+            res = fn()
+            if rank == 0:
+                print(json.dumps({"only": args.only, args.only: res}), flush=True)
+            return 0
         line = run_ours(args, world, rank, local)
         if line is not None:
             print(json.dumps(line), flush=True)

@@ -34,6 +34,7 @@
 
 #include <algorithm>
 #include <atomic>
+#include <cstdlib>
 
 #include "q6_dequant.cuh"
 #include "q6_internal.h"
@@ -66,9 +67,9 @@ struct GemvLayout {
     int stage_bytes;  // two rows: codes, scales, biases (128-byte multiple)
 };
 
-__host__ __device__ inline GemvLayout gemv_layout(int K, int gs) {
+__host__ __device__ inline GemvLayout gemv_layout(int K, int gs, int max_chunk) {
     GemvLayout L;
-    L.chunk = K < kMaxChunk ? K : kMaxChunk;
+    L.chunk = K < max_chunk ? K : max_chunk;
     L.code_bytes = L.chunk * 6 / 8;
     L.sb_bytes = (L.chunk / gs) * 2;
     L.stage_bytes = (2 * L.code_bytes + 4 * L.sb_bytes + 127) & ~127;
@@ -80,13 +81,13 @@ __host__ __device__ inline GemvLayout gemv_layout(int K, int gs) {
 // loop so that all shared-memory addresses are a per-lane base plus an
 // immediate; UPL = 0 is the generic loop.
 template <int MT, int UPL>
-__global__ void __launch_bounds__(kWarps * 32, 2) gemv_stream_kernel(const LinearArgs a, int gs_shift,
-                                                                  const SpliceExp3 sx) {
+__global__ void __launch_bounds__(kWarps * 32, MT == 1 ? 3 : 2) gemv_stream_kernel(const LinearArgs a, int gs_shift,
+                                                                                const SpliceExp3 sx, int max_chunk) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int K = static_cast<int>(a.K);
     const int N = static_cast<int>(a.N);
     const int M = static_cast<int>(a.M);
-    const GemvLayout L = gemv_layout(K, 1 << gs_shift);
+    const GemvLayout L = gemv_layout(K, 1 << gs_shift, max_chunk);
     const int nchunks = K / L.chunk;
     const int K4 = K / 4;
     const int U16 = K / 16;
@@ -338,8 +339,18 @@ __global__ void __launch_bounds__(kWarps * 32, 2) gemv_stream_kernel(const Linea
     }
 }
 
+// Codes per row per stage: Q6_GEMV_CHUNK (a multiple of 512 up to 4096)
+// overrides the default of 4096.
+int gemv_max_chunk() {
+    if (const char* v = std::getenv("Q6_GEMV_CHUNK")) {
+        const int c = std::atoi(v);
+        if (c >= 512 && c <= kMaxChunk && c % 512 == 0) return c;
+    }
+    return kMaxChunk;
+}
+
 size_t gemv_smem_bytes(int64_t K, int gs, int mt) {
-    const GemvLayout L = gemv_layout(static_cast<int>(K), gs);
+    const GemvLayout L = gemv_layout(static_cast<int>(K), gs, gemv_max_chunk());
     return static_cast<size_t>(kWarps) * kSlots * L.stage_bytes + static_cast<size_t>(mt) * K * 4 +
            static_cast<size_t>(mt) * (K / 16) * 8 + kWarps * kSlots * 8;
 }
@@ -367,7 +378,7 @@ int launch_gemv_mt(const LinearArgs& a, cudaStream_t stream) {
     const int blocks = static_cast<int>(std::min<int64_t>(want, static_cast<int64_t>(device_sm_count()) * per_sm));
     const int gs_shift = a.group_size == 32 ? 5 : (a.group_size == 64 ? 6 : 7);
     const cudaError_t err = launch_pdl(gemv_stream_kernel<MT, UPL>, dim3(blocks), dim3(kWarps * 32), smem, stream, a,
-                                       gs_shift, splice_exp3_host());
+                                       gs_shift, splice_exp3_host(), gemv_max_chunk());
     return err == cudaSuccess ? Q6_OK : Q6_ERR_CUDA;
 }
 
@@ -387,7 +398,8 @@ bool gemv_supported(const LinearArgs& a) {
     if (a.M < 1 || a.M > 4 || a.K % 64 != 0) return false;
     if (a.K > (int64_t(1) << 20) || a.N > (int64_t(1) << 30)) return false;
     if ((a.K / a.group_size) % 8 != 0) return false;
-    if (a.K > kMaxChunk && a.K % kMaxChunk != 0) return false;
+    const int chunk = gemv_max_chunk();
+    if (a.K > chunk && a.K % chunk != 0) return false;
     const uintptr_t align = reinterpret_cast<uintptr_t>(a.x) | reinterpret_cast<uintptr_t>(a.w) |
                             reinterpret_cast<uintptr_t>(a.scales) | reinterpret_cast<uintptr_t>(a.qbiases);
     if (align % 16 != 0) return false;
@@ -397,7 +409,7 @@ bool gemv_supported(const LinearArgs& a) {
 
 template <int MT>
 int launch_gemv_upl(const LinearArgs& a, cudaStream_t stream) {
-    const int64_t chunk = a.K < kMaxChunk ? a.K : kMaxChunk;
+    const int64_t chunk = a.K < gemv_max_chunk() ? a.K : gemv_max_chunk();
     const int upl = chunk % 512 == 0 ? static_cast<int>(chunk / 512) : 0;
     switch (upl) {
         case 1: return launch_gemv_mt<MT, 1>(a, stream);
