@@ -58,6 +58,8 @@ def parse_args() -> argparse.Namespace:
     ap.add_argument("--no-stack", action="store_true", help="skip the 60-block stack (config 5)")
     ap.add_argument("--only", choices=["block", "gemv", "sweep", "stack"], default=None,
                     help="run one side measurement alone and print its JSON (for profiling runs)")
+    ap.add_argument("--gemv-case", default=None,
+                    help="comma-separated GEMV case names to run (default: all of GEMV_CASES)")
     ap.add_argument("--tp-comm", choices=["peer", "nccl"], default="peer",
                     help="collectives of the tensor-parallel block: fused peer-memory kernels or NCCL")
     return ap.parse_args()
@@ -337,20 +339,30 @@ def run_ours(args, world: int, rank: int, local: int) -> dict | None:
     e1.record(stream)
     torch.cuda.synchronize()
     e2e_serial_ms = max_over_ranks(e0.elapsed_time(e1), world)
+    # (c) the module called on host tensors, one call at a time: each call cuts its rows into
+    # chunks whose copies overlap the kernels and returns with the result on the host
+    ff.forward_host(xs[0], out=ys[0])
+    barrier(world)
+    e0.record(stream)
+    for i in range(e2e_steps):
+        ff.forward_host(xs[i], out=ys[i])
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_call_ms = max_over_ranks(e0.elapsed_time(e1), world)
 
     # ---- one full MMDiT block (3456 image + 256 text tokens), tensor-parallel over the ranks
     block = None if args.no_block else measure_block(dev, world, rank, comm=args.tp_comm)
     # ---- config 5: the 60-block stack, 8 steps, batch 2, tensor-parallel over the ranks
     stack = None if args.no_stack else measure_stack(dev, world, rank, comm=args.tp_comm)
 
-    # ---- skinny-M GEMV side measurement (HBM-bound), rank 0 only
+    # ---- skinny-M GEMV side measurement (HBM-bound): a single-GPU figure, taken at N = 1 only
     gemv = None
-    if rank == 0 and not args.no_gemv:
+    if world == 1 and not args.no_gemv:
         gemv = measure_gemv(dev, peaks)
 
-    # ---- config 1 and the shape / M / group-size sweep with the LoRA comparison, rank 0 only
+    # ---- config 1 and the shape / M / group-size sweep with the LoRA comparison: single-GPU, N = 1 only
     sweep = None
-    if rank == 0 and not args.no_sweep:
+    if world == 1 and not args.no_sweep:
         sweep = measure_sweep(dev, peaks)
 
     if rank != 0:
@@ -395,6 +407,10 @@ def run_ours(args, world: int, rank: int, local: int) -> dict | None:
             "api": "QwenFeedForward.forward_host_stream: pinned host batches in and out, uploads and downloads overlapping the kernels",
             "serial_value": round(FLOP_PER_STEP * e2e_steps * world / (e2e_serial_ms * 1e-3) / 1e12, 2),
             "serial_api": "QwenFeedForward(x) one call at a time: copy in, ff, copy out on one stream",
+            "host_call_value": round(FLOP_PER_STEP * e2e_steps * world / (e2e_call_ms * 1e-3) / 1e12, 2),
+            "host_call_api": "QwenFeedForward(x_host) one call at a time on a pinned host tensor: 4 chunks of 864 "
+                             "rows, each chunk's upload / download overlapping the other chunks' kernels; "
+                             "returns with the result on the host",
         },
         "gpu_launches": 2 * steps,
         "kernel_timing": "fc1_ms / fc2_ms and roofline.achieved from a second pass of the same steps with an event "
@@ -411,7 +427,7 @@ def run_ours(args, world: int, rank: int, local: int) -> dict | None:
         line["block"] = block
     if stack is not None:
         line["stack"] = stack
-    if not args.no_cpu_baseline:
+    if world == 1 and not args.no_cpu_baseline:  # the host-core baseline is taken at N = 1 only
         line["cpu_baseline"] = cpu_baseline_port()
     return line
 
@@ -503,9 +519,15 @@ def measure_block(dev, world: int, rank: int, steps: int = 10, comm: str = "peer
         rows_local = x.shape[0] // world
         x_local = x[rank * rows_local:(rank + 1) * rows_local].contiguous()
         one = lambda: full.forward_joint(x, temb, rope_j, batch, BLOCK_TXT, out=y)  # noqa: E731
+        ms_tp1 = None
         if tp is None:
             ms, eager_ms = _graph_ms(one, world, steps)
             ms_1 = ms
+            # the tensor-parallel form on one rank: the cost of its structure alone
+            tp1 = TensorParallelQwenBlock(full, 1, 0, comm=comm)
+            ms_tp1, _ = _graph_ms(lambda: tp1.finish(tp1.forward_local(x, temb, rope_j, batch, seq, BLOCK_TXT)),
+                                  1, steps)
+            del tp1
         else:
             ms, eager_ms = _graph_ms(lambda: tp.finish(tp.forward_local(x_local, temb, rope_j, batch, seq, BLOCK_TXT)),
                                      world, steps)
@@ -524,6 +546,7 @@ def measure_block(dev, world: int, rank: int, steps: int = 10, comm: str = "peer
             "ms_1gpu": None if ms_1 is None else round(ms_1, 4),
             "comm": comm if world > 1 else None,
             "ms_other_comm": None if world == 1 else round(ms_other, 4),
+            "ms_tp_form_1gpu": None if ms_tp1 is None else round(ms_tp1, 4),
             "efficiency_vs_1gpu": None if ms_1 is None else round(ms_1 / (world * ms), 4),
             "batch": batch, "flop_per_call": flop,
         }
@@ -543,7 +566,8 @@ def measure_block(dev, world: int, rank: int, steps: int = 10, comm: str = "peer
         "steps": steps,
         "note": "device time per block forward replayed from a CUDA graph (eager_ms: launched from Python each "
                 "time); CUDA events, max over ranks; attention is the library scaled_dot_product_attention kernel; "
-                "ms_1gpu is the same block on one GPU timed on rank 0 in the same run",
+                "ms_1gpu is the same block on one GPU timed on rank 0 in the same run; ms_tp_form_1gpu (one GPU "
+                "only) is the tensor-parallel form run on a single rank, the cost of its layout and kernels alone",
     })
     return res
 
@@ -646,7 +670,7 @@ GEMV_CASES = [
 ]
 
 
-def measure_gemv(dev, peaks) -> dict:
+def measure_gemv(dev, peaks, only: str | None = None) -> dict:
     """q6 linears for a few token rows (GEMV_CASES), rotating weight copies
     whose total exceeds L2 four times so every launch streams its weights from
     HBM; device time per launch from a CUDA graph of back-to-back launches,
@@ -660,7 +684,13 @@ def measure_gemv(dev, peaks) -> dict:
     g = torch.Generator(device=dev).manual_seed(77)
     out = {}
     shapes: dict[tuple[int, int], list] = {}
+    wanted = None if not only else set(only.split(","))
+    unknown = (wanted or set()) - {c[0] for c in GEMV_CASES}
+    if unknown:
+        raise ValueError(f"unknown GEMV case(s) {sorted(unknown)}")
     for name, n, k, m in GEMV_CASES:
+        if wanted is not None and name not in wanted:
+            continue
         shapes.setdefault((n, k), []).append((name, m))
     for (n, k), cases in shapes.items():
         per_copy = n * k * 6 // 8 + 2 * 2 * n * (k // GROUP)
@@ -829,9 +859,6 @@ def measure_sweep(dev, peaks) -> dict:
 # ------------------------------------------------------------ host baselines
 
 
-# ------------------------------------------------------------ host baselines
-
-
 def cpu_baseline_port(budget_s: float = 12.0) -> dict:
     """The oracle's torch-CPU restatement (dequantise, then matmul) on a token sample."""
 
@@ -897,7 +924,7 @@ def main() -> int:
             dev = torch.device("cuda", local)
             fn = {"block": lambda: measure_block(dev, world, rank, comm=args.tp_comm),
                   "stack": lambda: measure_stack(dev, world, rank, comm=args.tp_comm),
-                  "gemv": lambda: measure_gemv(dev, measured_peaks()) if rank == 0 else None,
+                  "gemv": lambda: measure_gemv(dev, measured_peaks(), args.gemv_case) if rank == 0 else None,
                   "sweep": lambda: measure_sweep(dev, measured_peaks()) if rank == 0 else None}[args.only]
             res = fn()
             if rank == 0:

@@ -205,7 +205,10 @@ Q6_API int q6_layernorm_modulate_bf16(const uint16_t* x, const uint16_t* shift, 
  * where local row m is global row g = row0 + m of sequences of seq_len rows,
  * the first text_len of each from the text stream:
  *   v = (g / seq_len) * 2 + ((g % seq_len) >= text_len ? 1 : 0),
- * i.e. shift / scale hold [samples][text, image][D] vectors.  h_out (nullable)
+ * i.e. shift / scale hold [samples][text, image] vectors of D values, vector
+ * v starting vec_stride elements after vector v - 1 (vec_stride 0 means D;
+ * else a multiple of 8 and >= D, so the vectors can be one chunk of each
+ * [samples][text, image][6][D] modulation output in place).  h_out (nullable)
  * receives h.  With seq_len = text_len = 0 every row takes vector 0 (the
  * plain q6_layernorm_modulate_bf16).  Replaces `x + gate * attn_out` /
  * `x + gate * ff` followed by `_modulate(norm2(x), mod2)` and the next block's
@@ -214,9 +217,9 @@ Q6_API int q6_layernorm_modulate_bf16(const uint16_t* x, const uint16_t* shift, 
  * D and alignment as q6_layernorm_modulate_bf16.
  */
 Q6_API int q6_add_layernorm_modulate_bf16(const uint16_t* x, const uint16_t* add, uint16_t* h_out,
-                                          const uint16_t* shift, const uint16_t* scale, uint16_t* y, int64_t M,
-                                          int64_t D, int64_t row0, int64_t seq_len, int64_t text_len, float eps,
-                                          q6_stream_t stream);
+                                          const uint16_t* shift, const uint16_t* scale, int64_t vec_stride,
+                                          uint16_t* y, int64_t M, int64_t D, int64_t row0, int64_t seq_len,
+                                          int64_t text_len, float eps, q6_stream_t stream);
 Q6_API int q6_qk_rmsnorm_rope_bf16(uint16_t* qk, int64_t row_stride, int64_t M, int heads, int head_dim,
                                    const uint16_t* weight, const float* cos, const float* sin, float eps,
                                    q6_stream_t stream);
@@ -246,7 +249,7 @@ Q6_API int q6_qk_rmsnorm_rope_joint_bf16(uint16_t* qk, int64_t row_stride, int64
  *   h = x_local + sum_r partials[r][own rows]   (rank order, fp32, one bf16 rounding;
  *                                                h = x_local without partials)
  * writes h to h_out (nullable), and writes
- *   y = LayerNorm(h) * (1 + scale[v]) + shift[v]   (v as q6_add_layernorm_modulate_bf16)
+ *   y = LayerNorm(h) * (1 + scale[v]) + shift[v]   (v and vec_stride as q6_add_layernorm_modulate_bf16)
  * into the own-row block of every gathered[r] (gathered null: only h, which
  * then needs partials and h_out; shift / scale may be null).  It is the reduce-scatter of
  * the row-parallel GEMM's partial sums, the residual add, the adaLN modulate
@@ -258,8 +261,9 @@ Q6_API int q6_qk_rmsnorm_rope_joint_bf16(uint16_t* qk, int64_t row_stride, int64
  */
 Q6_API int q6_sp_add_layernorm_gather_bf16(const uint16_t* x_local, const uint16_t* const* partials,
                                            uint16_t* h_out, const uint16_t* shift, const uint16_t* scale,
-                                           uint16_t* const* gathered, int world, int rank, int64_t R, int64_t D,
-                                           int64_t seq_len, int64_t text_len, float eps, q6_stream_t stream);
+                                           int64_t vec_stride, uint16_t* const* gathered, int world, int rank,
+                                           int64_t R, int64_t D, int64_t seq_len, int64_t text_len, float eps,
+                                           q6_stream_t stream);
 
 /*
  * Barrier of `world` ranks for the kernels above: one thread per peer

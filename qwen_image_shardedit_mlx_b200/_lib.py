@@ -61,7 +61,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I, _P],
     ),
     "q6_layernorm_modulate_bf16": (_I, [_P, _P, _P, _P, _I64, _I64, _F, _P]),
-    "q6_add_layernorm_modulate_bf16": (_I, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _F, _P]),
+    "q6_add_layernorm_modulate_bf16": (_I, [_P, _P, _P, _P, _P, _I64, _P, _I64, _I64, _I64, _I64, _I64, _F, _P]),
     "q6_qk_rmsnorm_rope_bf16": (_I, [_P, _I64, _I64, _I, _I, _P, _P, _P, _F, _P]),
     "q6_qk_rmsnorm_rope_joint_bf16": (_I, [_P, _I64, _I64, _I, _I, _P, _P, _P, _P, _I64, _I64, _I64, _F, _P]),
     "q6_get_device_error": (_I, [ctypes.POINTER(ctypes.c_int)]),
@@ -69,7 +69,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "q6_last_path": (_I, []),
     "q6_tensor_token_tile": (_I, [_I64, _I64]),
     "q6_pair_fallback_count": (_I64, []),
-    "q6_sp_add_layernorm_gather_bf16": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I64, _I64, _I64, _I64, _F, _P]),
+    "q6_sp_add_layernorm_gather_bf16": (_I, [_P, _P, _P, _P, _P, _I64, _P, _I, _I, _I64, _I64, _I64, _I64, _F,
+                                             _P]),
     "q6_sp_barrier": (_I, [_P, _P, _I, _I, _I64, _P]),
     "q6_selftest_bounded_wait": (_I, [_I64, _P]),
     "q6_status_string": (ctypes.c_char_p, [_I]),

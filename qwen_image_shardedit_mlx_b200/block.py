@@ -195,13 +195,25 @@ class QwenTransformerBlock(torch.nn.Module):
         return ops.q6_mlp(x, (l1.weight, l1.scales, l1.biases, l1.bias), (l2.weight, l2.scales, l2.biases, l2.bias),
                           group_size=l1.group_size, residual=residual, gate=gate, workspace=ws, out=out)
 
-    def modulation(self, temb: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
-        """(img, txt) modulation vectors [B, 6, D] from the timestep embedding [B, D]."""
+    def modulation_joint(self, temb: torch.Tensor) -> torch.Tensor:
+        """Modulation vectors [B, 2, 6, D] (text stream first) from the
+        timestep embedding [B, D]: txt_mod_linear and img_mod_linear read the
+        same silu(temb), so one GEMV over their row concatenation writes both
+        in the layout the joint-row kernels index (no copies)."""
 
         t = F.silu(temb.to(torch.bfloat16))
         b = t.shape[0]
-        return (self._linear("img_mod_linear", t).reshape(b, 6, self.dim),
-                self._linear("txt_mod_linear", t).reshape(b, 6, self.dim))
+        fused = fused_rows(self, _MOD)
+        if fused is not None:
+            y = ops.q6_linear(t, fused.weight, fused.scales, fused.biases, fused.bias, group_size=fused.group_size)
+            return y.view(b, 2, 6, self.dim)
+        return torch.stack([self._linear(name, t).view(b, 6, self.dim) for name in _MOD], dim=1)
+
+    def modulation(self, temb: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        """(img, txt) modulation vectors [B, 6, D] from the timestep embedding [B, D]."""
+
+        both = self.modulation_joint(temb)
+        return both[:, 1], both[:, 0]
 
     def forward_joint(self, x: torch.Tensor, temb: torch.Tensor, rope_joint: tuple[torch.Tensor, torch.Tensor],
                       batch: int, text_len: int, text_mask: torch.Tensor | None = None,
@@ -212,7 +224,7 @@ class QwenTransformerBlock(torch.nn.Module):
 
         rows, d = x.shape
         seq = rows // batch
-        vec = ModulationVectors(*self.modulation(temb))
+        vec = ModulationVectors(self.modulation_joint(temb))
         z = add_layernorm_modulate(x, vec.shift1, vec.scale1, seq_len=seq, text_len=text_len, eps=self.eps)
         qkv = torch.empty((rows, 3 * d), dtype=torch.bfloat16, device=x.device)
         project_qkv_joint(self, z, qkv, batch, seq, text_len)
@@ -245,18 +257,26 @@ class QwenTransformerBlock(torch.nn.Module):
 
 
 class ModulationVectors:
-    """A block's adaLN vectors per (sample, stream), in the [B][text, image][D]
-    layout the joint-row kernels index: shift / scale of the attention half
-    (1) and of the feed-forward half (2), and the gates as [D] views."""
+    """A block's adaLN vectors per (sample, stream) as views of the
+    [B, 2 streams (text, image), 6, D] modulation output: shift / scale of
+    the attention half (1) and of the feed-forward half (2) as [2 B, D] views
+    whose rows lie 6 D apart (the joint-row kernels take that vector stride),
+    and the gates as [D] views.  Nothing is copied."""
 
-    def __init__(self, mod_img: torch.Tensor, mod_txt: torch.Tensor) -> None:
-        both = torch.stack([mod_txt, mod_img], dim=1)  # [B, 2 streams, 6, D]
-        b, _, _, d = both.shape
-        self.shift1 = both[:, :, 0].reshape(2 * b, d).contiguous()
-        self.scale1 = both[:, :, 1].reshape(2 * b, d).contiguous()
-        self.shift2 = both[:, :, 3].reshape(2 * b, d).contiguous()
-        self.scale2 = both[:, :, 4].reshape(2 * b, d).contiguous()
+    def __init__(self, both: torch.Tensor) -> None:
+        if both.dim() != 4 or both.shape[1:3] != (2, 6) or not both.is_contiguous():
+            raise ValueError("modulation vectors must be a contiguous [B, 2, 6, D] tensor")
+        self.shift1 = both[:, :, 0].flatten(0, 1)
+        self.scale1 = both[:, :, 1].flatten(0, 1)
+        self.shift2 = both[:, :, 3].flatten(0, 1)
+        self.scale2 = both[:, :, 4].flatten(0, 1)
         self._both = both
+
+    @classmethod
+    def from_streams(cls, mod_img: torch.Tensor, mod_txt: torch.Tensor) -> "ModulationVectors":
+        """From separate [B, 6, D] image and text modulation outputs."""
+
+        return cls(torch.stack([mod_txt, mod_img], dim=1).contiguous())
 
     def gate1(self, b: int, stream: int) -> torch.Tensor:
         return self._both[b, stream, 2]
@@ -298,14 +318,29 @@ def joint_rope(rope: tuple[torch.Tensor, ...]) -> tuple[torch.Tensor, torch.Tens
     return torch.cat([txt_cos, img_cos]).contiguous(), torch.cat([txt_sin, img_sin]).contiguous()
 
 
+def vector_stride(shift: torch.Tensor, scale: torch.Tensor, d: int) -> int:
+    """Element stride between the modulation vectors of ``shift`` / ``scale``
+    ([V, D] views with unit column stride, the same row stride; or [D])."""
+
+    for t in (shift, scale):
+        if t.dtype != torch.bfloat16 or t.shape[-1] != d or t.dim() not in (1, 2) or t.stride(-1) != 1:
+            raise ValueError(f"modulation vectors must be bf16 [V, {d}] with unit column stride")
+    if shift.dim() != scale.dim() or (shift.dim() == 2 and (shift.shape[0] != scale.shape[0]
+                                                             or shift.stride(0) != scale.stride(0))):
+        raise ValueError("shift and scale must have the same layout")
+    return d if shift.dim() == 1 or shift.shape[0] == 1 else int(shift.stride(0))
+
+
 def add_layernorm_modulate(x: torch.Tensor, shift: torch.Tensor, scale: torch.Tensor, *,
                            add: torch.Tensor | None = None, h_out: torch.Tensor | None = None,
                            out: torch.Tensor | None = None, row0: int = 0, seq_len: int = 0, text_len: int = 0,
                            eps: float = 1e-6) -> torch.Tensor:
     """y = LayerNorm(x [+ add]) * (1 + scale[v]) + shift[v] over joint rows
     (q6_add_layernorm_modulate_bf16): row m is row row0 + m of sequences of
-    ``seq_len`` rows whose first ``text_len`` are text; shift / scale hold
-    [samples * 2, D] vectors (text, image per sample).  ``h_out`` receives
+    ``seq_len`` rows whose first ``text_len`` are text; shift / scale are
+    [samples * 2, D] vectors (text, image per sample), or [D] for one vector,
+    whose rows may lie any multiple of 8 elements apart (``vector_stride``),
+    e.g. one chunk of the [B, 2, 6, D] modulation output.  ``h_out`` receives
     x + add."""
 
     d = x.shape[-1]
@@ -313,11 +348,12 @@ def add_layernorm_modulate(x: torch.Tensor, shift: torch.Tensor, scale: torch.Te
         raise ValueError("x must be contiguous bf16 rows")
     if add is not None and (add.dtype != torch.bfloat16 or not add.is_contiguous() or add.shape != x.shape):
         raise ValueError("add must match x")
+    vs = vector_stride(shift, scale, d)
     y = out if out is not None else torch.empty_like(x)
     st = _lib.lib().q6_add_layernorm_modulate_bf16(
         x.data_ptr(), None if add is None else add.data_ptr(), None if h_out is None else h_out.data_ptr(),
-        shift.data_ptr(), scale.data_ptr(), y.data_ptr(), x.shape[0], d, int(row0), int(seq_len), int(text_len),
-        float(eps), ops._stream(x.device))
+        shift.data_ptr(), scale.data_ptr(), vs, y.data_ptr(), x.shape[0], d, int(row0), int(seq_len),
+        int(text_len), float(eps), ops._stream(x.device))
     _lib.check(st, "q6_add_layernorm_modulate_bf16")
     return y
 
@@ -373,6 +409,7 @@ def batched_joint_attention(qkv: torch.Tensor, width: int, batch: int, seq: int,
     return att.transpose(1, 2).reshape(batch * seq, width)
 
 
+_MOD = ("txt_mod_linear", "img_mod_linear")  # text first: the [B, 2, 6, D] stream order
 _TXT_QKV = ("attn.add_q_proj", "attn.add_k_proj", "attn.add_v_proj")
 _IMG_QKV = ("attn.to_q", "attn.to_k", "attn.to_v")
 
@@ -392,7 +429,9 @@ def fused_rows(owner: torch.nn.Module, names: tuple[str, ...]) -> QuantizedLinea
         return None
     if len({(lin.in_features, lin.group_size, lin.weight.device) for lin in lins}) != 1:
         return None
-    cache = owner.__dict__.setdefault("_fused_rows", {})
+    # the cache lives on the first member, so every owner sharing the members
+    # (a block and its tensor-parallel form) shares one concatenation
+    cache = lins[0].__dict__.setdefault("_fused_rows", {})
     hit = cache.get(names)
     if hit is not None and all(lin.weight.data_ptr() == ptr for lin, ptr in zip(lins, hit[0])):
         return hit[1]
@@ -499,6 +538,7 @@ class TensorParallelQwenBlock(torch.nn.Module):
     _workspace = QwenTransformerBlock._workspace
     _mlp = QwenTransformerBlock._mlp
     modulation = QwenTransformerBlock.modulation
+    modulation_joint = QwenTransformerBlock.modulation_joint
 
     # collectives over the rows of the joint buffer
     def _gather(self, local: torch.Tensor) -> torch.Tensor:
@@ -543,7 +583,7 @@ class TensorParallelQwenBlock(torch.nn.Module):
 
         rows_local, d = x_local.shape
         row0 = self.rank * rows_local
-        vec = ModulationVectors(*self.modulation(temb))
+        vec = ModulationVectors(self.modulation_joint(temb))
         if self.comm == "peer":
             pr = self._peer(rows_local * self.world, x_local.device)
             pr.add_ln_gather(x_local, vec.shift1, vec.scale1, dst="gather1", seq_len=seq, text_len=text_len,
@@ -565,7 +605,7 @@ class TensorParallelQwenBlock(torch.nn.Module):
         h_prev, ff_prev = pending
         rows_local = h_prev.shape[0]
         row0 = self.rank * rows_local
-        vec = ModulationVectors(*self.modulation(temb))
+        vec = ModulationVectors(self.modulation_joint(temb))
         x_local = torch.empty_like(h_prev)
         if self.comm == "peer":
             pr = self._peer(rows_local * self.world, h_prev.device)

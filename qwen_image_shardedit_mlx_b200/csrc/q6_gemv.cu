@@ -7,10 +7,11 @@
 //   * every warp works through pairs of weight rows (rows 2p, 2p+1), in
 //     K chunks of up to 4096 codes; a stage is one (pair, chunk): both rows'
 //     codes, scales and biases;
-//   * each warp owns a two-slot ring in shared memory; its lane 0 fetches the
-//     next stage with 1-D bulk copies (completing on the slot's mbarrier)
-//     while the warp computes the current one, so one stage per warp is
-//     always in flight;
+//   * each warp owns a two-slot ring in shared memory (three slots when the
+//     shared memory holds one CTA per SM either way); its lane 0 fetches the
+//     next stages with 1-D bulk copies (completing on the slot's mbarrier)
+//     while the warp computes the current one, so one or two stages per warp
+//     are always in flight;
 //   * within a stage, lane l takes the 16-code units j = l, l + 32, ... of
 //     both rows (K = 3072: six units per lane, an even split);
 //   * the reference kernel's sum_k x_k (scale * code_k + qbias)
@@ -44,7 +45,8 @@ namespace q6 {
 namespace {
 
 constexpr int kWarps = 8;          // warps per CTA, each with its own ring
-constexpr int kSlots = 2;          // ring slots per warp
+constexpr int kMinSlots = 2;       // ring slots per warp: 2, or 3 when that keeps the CTAs per SM
+constexpr int kMaxSlots = 3;
 constexpr int kMaxChunk = 4096;    // codes per row per stage
 constexpr int kSmemCap = 220 * 1024;
 
@@ -82,7 +84,8 @@ __host__ __device__ inline GemvLayout gemv_layout(int K, int gs, int max_chunk) 
 // immediate; UPL = 0 is the generic loop.
 template <int MT, int UPL>
 __global__ void __launch_bounds__(kWarps * 32, MT == 1 ? 3 : 2) gemv_stream_kernel(const LinearArgs a, int gs_shift,
-                                                                                const SpliceExp3 sx, int max_chunk) {
+                                                                                const SpliceExp3 sx, int max_chunk,
+                                                                                int slots) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int K = static_cast<int>(a.K);
     const int N = static_cast<int>(a.N);
@@ -94,10 +97,10 @@ __global__ void __launch_bounds__(kWarps * 32, MT == 1 ? 3 : 2) gemv_stream_kern
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    uint8_t* ring = smem + warp * kSlots * L.stage_bytes;
-    float4* xs4 = reinterpret_cast<float4*>(smem + kWarps * kSlots * L.stage_bytes);  // [MT][K/4]
+    uint8_t* ring = smem + warp * slots * L.stage_bytes;
+    float4* xs4 = reinterpret_cast<float4*>(smem + kWarps * slots * L.stage_bytes);  // [MT][K/4]
     float2* xsum = reinterpret_cast<float2*>(xs4 + MT * K4);  // [MT][K/16]: x sums over a unit's even, odd codes
-    uint64_t* full = reinterpret_cast<uint64_t*>(xsum + MT * U16) + warp * kSlots;
+    uint64_t* full = reinterpret_cast<uint64_t*>(xsum + MT * U16) + warp * slots;
 
     const int npairs = (N + 1) / 2;
     const int gw = blockIdx.x * kWarps + warp;
@@ -113,8 +116,8 @@ __global__ void __launch_bounds__(kWarps * 32, MT == 1 ? 3 : 2) gemv_stream_kern
         const int c = t - (t / nchunks) * nchunks;
         const int n0 = 2 * p;
         const bool two = n0 + 1 < N;
-        const uint32_t slot = smem_u32(ring + (t % kSlots) * L.stage_bytes);
-        const uint32_t bar = smem_u32(full + (t % kSlots));
+        const uint32_t slot = smem_u32(ring + (t % slots) * L.stage_bytes);
+        const uint32_t bar = smem_u32(full + (t % slots));
         const uint32_t cb = L.code_bytes, sbb = L.sb_bytes;
         mbar_arrive_expect_tx(bar, (two ? 2u : 1u) * (cb + 2 * sbb));
         const uint8_t* wrow = reinterpret_cast<const uint8_t*>(a.w + static_cast<size_t>(n0) * words_per_row) +
@@ -136,9 +139,9 @@ __global__ void __launch_bounds__(kWarps * 32, MT == 1 ? 3 : 2) gemv_stream_kern
 
     pdl_launch_dependents();
     if (lane == 0) {
-        for (int s = 0; s < kSlots; ++s) mbar_init(smem_u32(full + s), 1);
+        for (int s = 0; s < slots; ++s) mbar_init(smem_u32(full + s), 1);
         fence_mbar_init();
-        for (int t = 0; t < kSlots && t < my_stages; ++t) issue(t);  // weights: before the dependency wait
+        for (int t = 0; t < slots && t < my_stages; ++t) issue(t);  // weights: before the dependency wait
     }
     __syncwarp();
     pdl_wait();  // x, y and the epilogue operands may come from the previous kernel
@@ -180,8 +183,9 @@ __global__ void __launch_bounds__(kWarps * 32, MT == 1 ? 3 : 2) gemv_stream_kern
         const int c = t % nchunks;
         const int p = gw + (t / nchunks) * total_warps;
         const int n0 = 2 * p;
-        const uint8_t* slot = ring + (t % kSlots) * L.stage_bytes;
-        if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(full + (t % kSlots)), static_cast<uint32_t>((t / kSlots) & 1),
+        const int si = t % slots;
+        const uint8_t* slot = ring + si * L.stage_bytes;
+        if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(full + si), static_cast<uint32_t>((t / slots) & 1),
                                                &no_abort, 11)))
             break;
         const uint8_t* codes0 = slot;
@@ -300,11 +304,11 @@ __global__ void __launch_bounds__(kWarps * 32, MT == 1 ? 3 : 2) gemv_stream_kern
                 unit(j, J, (16 * j) >> gs_shift, 4 * J, e_slots);
             }
         }
-        // Hand the slot back to this warp's producer lane for stage t + kSlots.
+        // Hand the slot back to this warp's producer lane for stage t + slots.
         __syncwarp();
-        if (lane == 0 && t + kSlots < my_stages) {
+        if (lane == 0 && t + slots < my_stages) {
             fence_proxy_async_smem();
-            issue(t + kSlots);
+            issue(t + slots);
         }
         if (c == nchunks - 1) {
 #pragma unroll
@@ -349,15 +353,26 @@ int gemv_max_chunk() {
     return kMaxChunk;
 }
 
-size_t gemv_smem_bytes(int64_t K, int gs, int mt) {
+size_t gemv_smem_bytes(int64_t K, int gs, int mt, int slots) {
     const GemvLayout L = gemv_layout(static_cast<int>(K), gs, gemv_max_chunk());
-    return static_cast<size_t>(kWarps) * kSlots * L.stage_bytes + static_cast<size_t>(mt) * K * 4 +
-           static_cast<size_t>(mt) * (K / 16) * 8 + kWarps * kSlots * 8;
+    return static_cast<size_t>(kWarps) * slots * L.stage_bytes + static_cast<size_t>(mt) * K * 4 +
+           static_cast<size_t>(mt) * (K / 16) * 8 + kWarps * slots * 8;
+}
+
+// Ring depth: a third slot (two stages in flight per warp) when it costs no
+// CTA per SM, i.e. when shared memory already holds only one CTA (long K:
+// the fp32 activations take 48 KB at K = 12288).
+int gemv_slots(int64_t K, int gs, int mt) {
+    const size_t two = gemv_smem_bytes(K, gs, mt, kMinSlots), three = gemv_smem_bytes(K, gs, mt, kMaxSlots);
+    if (three > static_cast<size_t>(kSmemCap)) return kMinSlots;
+    const size_t per_sm = 228 * 1024;  // shared memory per SM (each CTA also reserves 1 KB)
+    return (per_sm / (three + 1024)) >= (per_sm / (two + 1024)) ? kMaxSlots : kMinSlots;
 }
 
 template <int MT, int UPL>
 int launch_gemv_mt(const LinearArgs& a, cudaStream_t stream) {
-    const size_t smem = gemv_smem_bytes(a.K, a.group_size, MT);
+    const int slots = gemv_slots(a.K, a.group_size, MT);
+    const size_t smem = gemv_smem_bytes(a.K, a.group_size, MT, slots);
     static std::atomic<bool> attr_set_for_device[kMaxDevices];
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return Q6_ERR_CUDA;
@@ -378,7 +393,7 @@ int launch_gemv_mt(const LinearArgs& a, cudaStream_t stream) {
     const int blocks = static_cast<int>(std::min<int64_t>(want, static_cast<int64_t>(device_sm_count()) * per_sm));
     const int gs_shift = a.group_size == 32 ? 5 : (a.group_size == 64 ? 6 : 7);
     const cudaError_t err = launch_pdl(gemv_stream_kernel<MT, UPL>, dim3(blocks), dim3(kWarps * 32), smem, stream, a,
-                                       gs_shift, splice_exp3_host(), gemv_max_chunk());
+                                       gs_shift, splice_exp3_host(), gemv_max_chunk(), slots);
     return err == cudaSuccess ? Q6_OK : Q6_ERR_CUDA;
 }
 
@@ -404,7 +419,7 @@ bool gemv_supported(const LinearArgs& a) {
                             reinterpret_cast<uintptr_t>(a.scales) | reinterpret_cast<uintptr_t>(a.qbiases);
     if (align % 16 != 0) return false;
     const int mt = a.M == 3 ? 4 : static_cast<int>(a.M);  // token rows of the kernel instantiation
-    return gemv_smem_bytes(a.K, a.group_size, mt) <= static_cast<size_t>(kSmemCap);
+    return gemv_smem_bytes(a.K, a.group_size, mt, kMinSlots) <= static_cast<size_t>(kSmemCap);
 }
 
 template <int MT>

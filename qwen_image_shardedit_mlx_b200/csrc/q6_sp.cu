@@ -58,8 +58,8 @@ __device__ __forceinline__ float warp_sum(float v) {
 template <int NV, bool kParts>
 __global__ void __launch_bounds__(kSpWarps * 32) sp_add_ln_gather_kernel(
     const uint4* __restrict__ x, const PeerIn parts, uint4* h_out, const uint4* __restrict__ shift,
-    const uint4* __restrict__ scale, const PeerOut dst, int world, int64_t R, int64_t row0, int64_t seq_len,
-    int64_t text_len, float eps) {
+    const uint4* __restrict__ scale, int64_t vstride8, const PeerOut dst, int world, int64_t R, int64_t row0,
+    int64_t seq_len, int64_t text_len, float eps) {
     pdl_launch_dependents();
     pdl_wait();
     const int lane = threadIdx.x & 31;
@@ -130,8 +130,8 @@ __global__ void __launch_bounds__(kSpWarps * 32) sp_add_ln_gather_kernel(
     const float rstd = rsqrtf(warp_sum(sq) * (1.0f / (256 * NV)) + eps);
     int64_t vec = 0;
     if (seq_len > 0) vec = (grow / seq_len) * 2 + ((grow % seq_len) >= text_len ? 1 : 0);
-    const uint4* sh = shift + vec * D8;
-    const uint4* sc = scale + vec * D8;
+    const uint4* sh = shift + vec * vstride8;
+    const uint4* sc = scale + vec * vstride8;
 #pragma unroll
     for (int j = 0; j < NV; ++j) {
         const uint4 a = __ldg(sh + lane + 32 * j), b = __ldg(sc + lane + 32 * j);
@@ -145,8 +145,9 @@ __global__ void __launch_bounds__(kSpWarps * 32) sp_add_ln_gather_kernel(
         const uint4 out = make_uint4(o[0], o[1], o[2], o[3]);
         for (int r = 0; r < world; ++r) dst.p[r][grow * D8 + lane + 32 * j] = out;
     }
-    // the peer stores are performed at system scope before this kernel completes
-    __threadfence_system();
+    // No fence here: the peer stores are complete when this grid is, and the
+    // q6_sp_barrier launch that follows on the stream (never a programmatic
+    // dependent) releases them to the peers at system scope.
 }
 
 // Barrier across `world` ranks: thread t releases the new epoch into slot
@@ -182,16 +183,18 @@ __global__ void __launch_bounds__(32) sp_barrier_kernel(const PeerSignals sig, u
 
 template <int NV>
 int launch_sp(const uint4* x, const PeerIn& parts, bool has_parts, uint4* h_out, const uint4* shift,
-              const uint4* scale, const PeerOut& dst, int world, int64_t R, int64_t row0, int64_t seq_len,
-              int64_t text_len, float eps, cudaStream_t stream) {
+              const uint4* scale, int64_t vstride8, const PeerOut& dst, int world, int64_t R, int64_t row0,
+              int64_t seq_len, int64_t text_len, float eps, cudaStream_t stream) {
     const int64_t blocks = (R + kSpWarps - 1) / kSpWarps;
     cudaError_t e;
     if (has_parts)
         e = launch_pdl(sp_add_ln_gather_kernel<NV, true>, dim3(static_cast<unsigned>(blocks)), dim3(kSpWarps * 32), 0,
-                       stream, x, parts, h_out, shift, scale, dst, world, R, row0, seq_len, text_len, eps);
+                       stream, x, parts, h_out, shift, scale, vstride8, dst, world, R, row0, seq_len, text_len,
+                       eps);
     else
         e = launch_pdl(sp_add_ln_gather_kernel<NV, false>, dim3(static_cast<unsigned>(blocks)), dim3(kSpWarps * 32), 0,
-                       stream, x, parts, h_out, shift, scale, dst, world, R, row0, seq_len, text_len, eps);
+                       stream, x, parts, h_out, shift, scale, vstride8, dst, world, R, row0, seq_len, text_len,
+                       eps);
     return e == cudaSuccess ? Q6_OK : Q6_ERR_CUDA;
 }
 
@@ -213,14 +216,18 @@ extern "C" {
 
 Q6_API int q6_sp_add_layernorm_gather_bf16(const uint16_t* x_local, const uint16_t* const* partials,
                                            uint16_t* h_out, const uint16_t* shift, const uint16_t* scale,
-                                           uint16_t* const* gathered, int world, int rank, int64_t R, int64_t D,
-                                           int64_t seq_len, int64_t text_len, float eps, q6_stream_t stream) {
+                                           int64_t vec_stride, uint16_t* const* gathered, int world, int rank,
+                                           int64_t R, int64_t D, int64_t seq_len, int64_t text_len, float eps,
+                                           q6_stream_t stream) {
     if (!x_local || R <= 0 || D <= 0 || !(eps >= 0.0f)) return Q6_ERR_INVALID_ARGUMENT;
     if (world < 1 || world > q6::kMaxRanks || rank < 0 || rank >= world) return Q6_ERR_INVALID_ARGUMENT;
     if (h_out && !partials) return Q6_ERR_INVALID_ARGUMENT;
     if (gathered ? (!shift || !scale) : (!partials || !h_out)) return Q6_ERR_INVALID_ARGUMENT;
     if (seq_len < 0 || text_len < 0 || text_len > seq_len) return Q6_ERR_INVALID_ARGUMENT;
     if (D % 256 != 0) return Q6_ERR_SHAPE;
+    if (vec_stride == 0) vec_stride = D;
+    if (vec_stride < D) return Q6_ERR_INVALID_ARGUMENT;
+    if (vec_stride % 8 != 0) return Q6_ERR_ALIGNMENT;
     uintptr_t al = reinterpret_cast<uintptr_t>(x_local) | reinterpret_cast<uintptr_t>(shift) |
                    reinterpret_cast<uintptr_t>(scale) | reinterpret_cast<uintptr_t>(h_out);
     q6::PeerIn parts{};
@@ -244,11 +251,12 @@ Q6_API int q6_sp_add_layernorm_gather_bf16(const uint16_t* x_local, const uint16
     const int64_t row0 = static_cast<int64_t>(rank) * R;
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     const bool hp = partials != nullptr;
+    const int64_t vs8 = vec_stride / 8;
     switch (D / 256) {
-        case 1: return q6::launch_sp<1>(x, parts, hp, h, sh, sc, dst, world, R, row0, seq_len, text_len, eps, s);
-        case 2: return q6::launch_sp<2>(x, parts, hp, h, sh, sc, dst, world, R, row0, seq_len, text_len, eps, s);
-        case 4: return q6::launch_sp<4>(x, parts, hp, h, sh, sc, dst, world, R, row0, seq_len, text_len, eps, s);
-        case 12: return q6::launch_sp<12>(x, parts, hp, h, sh, sc, dst, world, R, row0, seq_len, text_len, eps, s);
+        case 1: return q6::launch_sp<1>(x, parts, hp, h, sh, sc, vs8, dst, world, R, row0, seq_len, text_len, eps, s);
+        case 2: return q6::launch_sp<2>(x, parts, hp, h, sh, sc, vs8, dst, world, R, row0, seq_len, text_len, eps, s);
+        case 4: return q6::launch_sp<4>(x, parts, hp, h, sh, sc, vs8, dst, world, R, row0, seq_len, text_len, eps, s);
+        case 12: return q6::launch_sp<12>(x, parts, hp, h, sh, sc, vs8, dst, world, R, row0, seq_len, text_len, eps, s);
         default: return Q6_ERR_UNSUPPORTED;
     }
 }

@@ -97,10 +97,13 @@ class PeerRows:
 
         if x_local.shape != (self.rows_local, self.dim) or not x_local.is_contiguous():
             raise ValueError(f"x_local must be contiguous ({self.rows_local}, {self.dim})")
+        from qwen_image_shardedit_mlx_b200.block import vector_stride
+
+        vs = 0 if shift is None else vector_stride(shift, scale, self.dim)
         st = _lib.lib().q6_sp_add_layernorm_gather_bf16(
             x_local.data_ptr(), None if partials is None else self.ptrs[partials],
             None if h_out is None else h_out.data_ptr(), None if shift is None else shift.data_ptr(),
-            None if scale is None else scale.data_ptr(),
+            None if scale is None else scale.data_ptr(), vs,
             None if dst is None else self.ptrs[dst], self.world, self.rank, self.rows_local, self.dim, int(seq_len),
             int(text_len), float(eps), ops._stream(self.device))
         _lib.check(st, "q6_sp_add_layernorm_gather_bf16")

@@ -255,12 +255,51 @@ class QwenFeedForward(torch.nn.Module):
         return cls(make(hidden, dim), make(dim, hidden))
 
     def forward(self, hidden: torch.Tensor) -> torch.Tensor:
+        if hidden.device.type == "cpu" and self.mlp_in.weight.is_cuda:
+            return self.forward_host(hidden)
         if self.mlp_in.lora is not None or self.mlp_out.lora is not None:
             # LoRA-carrying layers: each linear fuses its own delta
             mid = ops.q6_linear(hidden, self.mlp_in.weight, self.mlp_in.scales, self.mlp_in.biases, self.mlp_in.bias,
                                 group_size=self.mlp_in.group_size, apply_gelu=True, lora=self.mlp_in.lora)
             return self.mlp_out(mid)
         return fused_q6_mlp(hidden, quantized_linear_spec(self.mlp_in), quantized_linear_spec(self.mlp_out))
+
+    def forward_host(self, hidden: torch.Tensor, out: torch.Tensor | None = None,
+                     chunks: int | None = None) -> torch.Tensor:
+        """``ff(hidden)`` for activations in host memory, result in host memory
+        (``out``, or a new pinned tensor): the rows are cut into ``chunks``
+        equal batches (default: as many as 4 of at least 512 rows that divide
+        the rows) that run through ``forward_host_stream``, so the upload of
+        one chunk and the download of the previous overlap the kernels of the
+        current one.  Returns once the result is on the host.  Each chunk's
+        rows equal ``ff(chunk.cuda())`` exactly; pinned inputs copy fastest."""
+
+        d = self.mlp_in.in_features
+        x2 = hidden.reshape(-1, d)
+        if x2.dtype != torch.bfloat16:
+            x2 = x2.to(torch.bfloat16)
+        m = int(x2.shape[0])
+        if chunks is None:
+            chunks = max(1, min(4, m // 512))
+            while m % chunks:
+                chunks -= 1
+        if chunks < 1 or m % chunks:
+            raise ValueError(f"{m} rows do not split into {chunks} equal chunks")
+        if out is None:
+            y2 = torch.empty((m, d), dtype=torch.bfloat16, pin_memory=True)
+        else:
+            if out.device.type != "cpu" or out.dtype != torch.bfloat16 or out.numel() != m * d or \
+                    not out.is_contiguous():
+                raise ValueError("out must be a contiguous bf16 host tensor of the input's size")
+            y2 = out.view(m, d)
+        step = m // chunks
+        self.forward_host_stream([x2[i * step:(i + 1) * step] for i in range(chunks)],
+                                 [y2[i * step:(i + 1) * step] for i in range(chunks)])
+        torch.cuda.current_stream(self.mlp_in.weight.device).synchronize()
+        if out is not None:
+            return out
+        y = y2.reshape(*hidden.shape[:-1], d)
+        return y if hidden.dtype == torch.bfloat16 else y.to(hidden.dtype)
 
     def forward_host_stream(self, xs: Sequence[torch.Tensor], ys: Sequence[torch.Tensor]) -> None:
         """Run the MLP over a sequence of batches that live in (pinned) host
@@ -313,8 +352,11 @@ class QwenFeedForward(torch.nn.Module):
                 s_comp.wait_event(loaded)
                 if read_y[slot] is not None:
                     s_comp.wait_event(read_y[slot])
-                ops.q6_mlp(x_dev[slot], w1, w2, group_size=self.mlp_in.group_size, workspace=workspace,
-                           out=y_dev[slot])
+                if self.mlp_in.lora is not None or self.mlp_out.lora is not None:
+                    y_dev[slot].copy_(self.forward(x_dev[slot]))  # each linear fuses its own delta
+                else:
+                    ops.q6_mlp(x_dev[slot], w1, w2, group_size=self.mlp_in.group_size, workspace=workspace,
+                               out=y_dev[slot])
                 computed = torch.cuda.Event()
                 computed.record(s_comp)
                 read_x[slot] = computed

@@ -87,10 +87,19 @@ def test_argument_validation_without_gpu():
     assert lib.q6_lora_xa_bf16(18, 16, 16, 4, 64, 64, None) == _lib.Q6_ERR_ALIGNMENT
     # joint-row add + adaLN modulate
     add_ln = lib.q6_add_layernorm_modulate_bf16
-    assert add_ln(16, None, 16, 16, 16, 16, 4, 256, 0, 0, 0, 1e-6, None) == _lib.Q6_ERR_INVALID_ARGUMENT  # h_out without add
-    assert add_ln(16, 16, None, 16, 16, 16, 4, 256, 0, 10, 20, 1e-6, None) == _lib.Q6_ERR_INVALID_ARGUMENT  # text_len > seq_len
-    assert add_ln(16, 16, None, 16, 16, 16, 4, 320, 0, 0, 0, 1e-6, None) == _lib.Q6_ERR_SHAPE
-    assert add_ln(16, 24, None, 16, 16, 16, 4, 256, 0, 0, 0, 1e-6, None) == _lib.Q6_ERR_ALIGNMENT
+    inval, shape, align = _lib.Q6_ERR_INVALID_ARGUMENT, _lib.Q6_ERR_SHAPE, _lib.Q6_ERR_ALIGNMENT
+    assert add_ln(16, None, 16, 16, 16, 0, 16, 4, 256, 0, 0, 0, 1e-6, None) == inval  # h_out without add
+    assert add_ln(16, 16, None, 16, 16, 0, 16, 4, 256, 0, 10, 20, 1e-6, None) == inval  # text_len > seq_len
+    assert add_ln(16, 16, None, 16, 16, 0, 16, 4, 320, 0, 0, 0, 1e-6, None) == shape
+    assert add_ln(16, 24, None, 16, 16, 0, 16, 4, 256, 0, 0, 0, 1e-6, None) == align
+    assert add_ln(16, 16, None, 16, 16, 128, 16, 4, 256, 0, 0, 0, 1e-6, None) == inval  # vector stride < D
+    assert add_ln(16, 16, None, 16, 16, 260, 16, 4, 256, 0, 0, 0, 1e-6, None) == align  # stride not 8-aligned
+    # sequence-parallel modulate + gather: the same vector-stride rules
+    sp = lib.q6_sp_add_layernorm_gather_bf16
+    one = (ctypes.c_void_p * 1)(16)
+    assert sp(16, None, None, 16, 16, 128, one, 1, 0, 4, 256, 0, 0, 1e-6, None) == inval
+    assert sp(16, None, None, 16, 16, 260, one, 1, 0, 4, 256, 0, 0, 1e-6, None) == align
+    assert sp(16, None, None, 16, 16, 0, one, 2, 2, 4, 256, 0, 0, 1e-6, None) == inval  # rank >= world
     # self-test limits: 1 us .. 1 s
     assert lib.q6_selftest_bounded_wait(10, None) == _lib.Q6_ERR_INVALID_ARGUMENT
     assert lib.q6_selftest_bounded_wait(2_000_000_000, None) == _lib.Q6_ERR_INVALID_ARGUMENT

@@ -59,7 +59,35 @@ def test_layernorm_modulate_rejects_bad_arguments():
         layernorm_modulate(x, v, v)
 
 
-@pytest.mark.parametrize("m,heads,extra", [(1, 2, 0), (45, 6, 64), (3456, 24, 0), (256, 24, 256)])
+def test_add_layernorm_modulate_strided_vectors_match_contiguous():
+    """Modulation vectors read in place from the [B, 2, 6, D] modulation
+    output (rows 6 D apart) give the same bits as contiguous copies."""
+
+    from qwen_image_shardedit_mlx_b200.block import ModulationVectors, add_layernorm_modulate
+
+    g = torch.Generator(device="cuda").manual_seed(5)
+    b, seq, txt, d = 2, 40, 9, 768
+    both = torch.randn((b, 2, 6, d), generator=g, device="cuda").to(torch.bfloat16)
+    x = torch.randn((b * seq, d), generator=g, device="cuda").to(torch.bfloat16)
+    add = torch.randn((b * seq, d), generator=g, device="cuda").to(torch.bfloat16)
+    vec = ModulationVectors(both)
+    assert vec.shift2.stride(0) == 6 * d
+    h1, h2 = torch.empty_like(x), torch.empty_like(x)
+    y1 = add_layernorm_modulate(x, vec.shift2, vec.scale2, add=add, h_out=h1, seq_len=seq, text_len=txt)
+    y2 = add_layernorm_modulate(x, vec.shift2.contiguous(), vec.scale2.contiguous(), add=add, h_out=h2,
+                                seq_len=seq, text_len=txt)
+    torch.cuda.synchronize()
+    assert torch.equal(y1, y2) and torch.equal(h1, h2)
+    # row 0 of sample 1 is a text row: vector 2 (sample 1, text)
+    row = seq
+    hrow = h1[row].float()
+    ln = (hrow - hrow.mean()) / torch.sqrt(hrow.var(unbiased=False) + 1e-6)
+    want = ln * (1 + both[1, 0, 4].float()) + both[1, 0, 3].float()
+    assert torch.allclose(y1[row].float(), want, atol=3e-2, rtol=2e-2)
+
+
+@pytest.mark.parametrize("m,heads,extra", [(1, 2, 0), (45, 6, 64), (3456, 24, 0), (256, 24, 256), (37, 3, 0),
+                                            (100, 5, 8), (9, 1, 0), (7, 11, 128)])
 def test_qk_rmsnorm_rope_vs_oracle(m, heads, extra):
     rng = np.random.default_rng(m * heads + extra)
     width = heads * 128
@@ -177,11 +205,12 @@ def test_full_size_block_vs_oracle_on_sampled_rows():
     # ---- stage by stage, every stage fed the GPU's own input
     x = torch.cat([from_bits(enc), from_bits(hidden)]).contiguous()
     xf = np.concatenate([ef, hf])
-    mod_img, mod_txt = tb.modulation(from_bits(temb)[None])
+    both = tb.modulation_joint(from_bits(temb)[None])  # one GEMV over [txt_mod; img_mod]
+    mod_img, mod_txt = both[:, 1], both[:, 0]
     t = oracle.round_bf16(ob.silu(tf).reshape(1, d))
     assert_close(f32(mod_img[0]).reshape(6 * d), ob._lin(ow, "img_mod_linear", t)[0], what="img modulation")
     mi, mt = f32(mod_img[0]), f32(mod_txt[0])
-    vec = ModulationVectors(mod_img, mod_txt)
+    vec = ModulationVectors(both)  # strided views: vectors 6 D apart
     z = add_layernorm_modulate(x, vec.shift1, vec.scale1, seq_len=seq, text_len=s_txt)
     mod_of = lambda j, k: mt[k] if j < s_txt else mi[k]  # noqa: E731
     ref = np.stack([ob.layernorm_modulate(xf[j], mod_of(j, 0), mod_of(j, 1)) for j in jr])
