@@ -56,7 +56,7 @@ def parse_args() -> argparse.Namespace:
     ap.add_argument("--no-block", action="store_true", help="skip the full MMDiT block measurement")
     ap.add_argument("--no-sweep", action="store_true", help="skip the q6 linear shape / M / group-size sweep")
     ap.add_argument("--no-stack", action="store_true", help="skip the 60-block stack (config 5)")
-    ap.add_argument("--only", choices=["block", "gemv", "sweep", "stack"], default=None,
+    ap.add_argument("--only", choices=["block", "gemv", "sweep", "stack", "kernels"], default=None,
                     help="run one side measurement alone and print its JSON (for profiling runs)")
     ap.add_argument("--gemv-case", default=None,
                     help="comma-separated GEMV case names to run (default: all of GEMV_CASES)")
@@ -360,6 +360,11 @@ def run_ours(args, world: int, rank: int, local: int) -> dict | None:
     if world == 1 and not args.no_gemv:
         gemv = measure_gemv(dev, peaks)
 
+    # ---- the block's memory-bound kernels alone: single-GPU, N = 1 only
+    kernels = None
+    if world == 1 and not args.no_gemv:
+        kernels = measure_kernels(dev, peaks)
+
     # ---- config 1 and the shape / M / group-size sweep with the LoRA comparison: single-GPU, N = 1 only
     sweep = None
     if world == 1 and not args.no_sweep:
@@ -420,6 +425,8 @@ def run_ours(args, world: int, rank: int, local: int) -> dict | None:
     }
     if gemv is not None:
         line["gemv"] = gemv
+    if kernels is not None:
+        line["kernels"] = kernels
     if sweep is not None:
         line["c1"] = sweep.pop("c1")
         line["sweep"] = sweep
@@ -717,6 +724,69 @@ def measure_gemv(dev, peaks, only: str | None = None) -> dict:
     return out
 
 
+def measure_kernels(dev, peaks) -> dict:
+    """The block's memory-bound kernels alone at the block's shapes (3712
+    joint rows of 3072, 24 heads): the residual add + adaLN modulate, the
+    QK-RMSNorm + RoPE (in place on the q columns of a qkv buffer) and the LoRA
+    pre-pass x @ A (3456 x 3072 by rank 64).  Inputs rotate over copies
+    totalling more than L2 so every launch reads HBM; device time per launch
+    from a CUDA graph of back-to-back launches, reported as GB/s of the
+    algorithmic bytes (each element read and written once)."""
+
+    import torch
+
+    from qwen_image_shardedit_mlx_b200 import ops
+    from qwen_image_shardedit_mlx_b200.block import (ModulationVectors, add_layernorm_modulate,
+                                                     qk_rmsnorm_rope_joint_, qwen_rope_angles, rope_tables,
+                                                     joint_rope)
+
+    g = torch.Generator(device=dev).manual_seed(31)
+    rows, seq = BLOCK_IMG + BLOCK_TXT, BLOCK_IMG + BLOCK_TXT
+    out = {}
+
+    def rate(name, us, nbytes, **extra):
+        gbs = nbytes / (us * 1e-6) / 1e9
+        out[name] = {"us": round(us, 2), "GB/s": round(gbs, 1), "frac_hbm": round(gbs / peaks["hbm_gbs"], 4),
+                     "bytes": nbytes, **extra}
+
+    # residual add + adaLN modulate: x + add read, h and y written
+    copies = 3
+    xs = [torch.randn((rows, DIM), generator=g, device=dev).to(torch.bfloat16) for _ in range(copies)]
+    adds = [torch.randn((rows, DIM), generator=g, device=dev).to(torch.bfloat16) for _ in range(copies)]
+    hs = [torch.empty_like(xs[0]) for _ in range(copies)]
+    ys = [torch.empty_like(xs[0]) for _ in range(copies)]
+    vec = ModulationVectors(torch.randn((1, 2, 6, DIM), generator=g, device=dev).to(torch.bfloat16))
+    us = _time_launches(lambda i: add_layernorm_modulate(xs[i % copies], vec.shift2, vec.scale2, add=adds[i % copies],
+                                                         h_out=hs[i % copies], out=ys[i % copies], seq_len=seq,
+                                                         text_len=BLOCK_TXT), copies)
+    rate("add_layernorm_modulate", us, 4 * rows * DIM * 2, rows=rows, dim=DIM)
+    us = _time_launches(lambda i: add_layernorm_modulate(xs[i % copies], vec.shift1, vec.scale1, out=ys[i % copies],
+                                                         seq_len=seq, text_len=BLOCK_TXT), copies)
+    rate("layernorm_modulate", us, 2 * rows * DIM * 2, rows=rows, dim=DIM)
+    del xs, adds, hs, ys
+    # QK-RMSNorm + RoPE on the q columns of a [rows, 3 D] qkv buffer
+    qkvs = [torch.randn((rows, 3 * DIM), generator=g, device=dev).to(torch.bfloat16) for _ in range(copies)]
+    ia, ta = qwen_rope_angles([(36, 48), (36, 48)], BLOCK_TXT)
+    cos, sin = joint_rope(rope_tables(ia, ta, dev))
+    wq = (1.0 + 0.1 * torch.randn((128,), generator=g, device=dev)).to(torch.bfloat16)
+    us = _time_launches(lambda i: qk_rmsnorm_rope_joint_(qkvs[i % copies][:, :DIM], wq, wq, cos, sin, seq_len=seq,
+                                                         text_len=BLOCK_TXT), copies)
+    rate("qk_rmsnorm_rope", us, 2 * rows * DIM * 2, rows=rows, heads=BLOCK_HEADS)
+    del qkvs
+    # LoRA pre-pass: x read once, xa written
+    xs = [torch.randn((TOKENS, DIM), generator=g, device=dev).to(torch.bfloat16) for _ in range(4)]
+    a = (torch.randn((DIM, 64), generator=g, device=dev) * 0.01).to(torch.bfloat16)
+    xa = torch.empty((TOKENS, 64), dtype=torch.bfloat16, device=dev)
+    us = _time_launches(lambda i: ops.lora_xa(xs[i % 4], a, out=xa), 4)
+    rate("lora_xa_rank64", us, TOKENS * DIM * 2 + DIM * 64 * 2 + TOKENS * 64 * 2, rows=TOKENS, rank=64)
+    del xs
+    torch.cuda.empty_cache()
+    assert ops.device_error() == 0, "kernel benchmark raised the device error word"
+    out["note"] = ("device time per launch in a CUDA graph of back-to-back launches over input copies larger than "
+                   "L2; GB/s of the algorithmic bytes against the measured copy bandwidth")
+    return out
+
+
 SWEEP_SHAPES = [(3072, 3072), (12288, 3072), (3072, 12288), (18432, 3072)]  # (N, K): q6_linear_profile.py:144-159
 SWEEP_M = (1, 16, 128, 512, 1728, 3456, 8192)
 SWEEP_GS = (32, 64, 128)
@@ -925,7 +995,8 @@ def main() -> int:
             fn = {"block": lambda: measure_block(dev, world, rank, comm=args.tp_comm),
                   "stack": lambda: measure_stack(dev, world, rank, comm=args.tp_comm),
                   "gemv": lambda: measure_gemv(dev, measured_peaks(), args.gemv_case) if rank == 0 else None,
-                  "sweep": lambda: measure_sweep(dev, measured_peaks()) if rank == 0 else None}[args.only]
+                  "sweep": lambda: measure_sweep(dev, measured_peaks()) if rank == 0 else None,
+                  "kernels": lambda: measure_kernels(dev, measured_peaks()) if rank == 0 else None}[args.only]
             res = fn()
             if rank == 0:
                 print(json.dumps({"only": args.only, args.only: res}), flush=True)

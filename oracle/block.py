@@ -145,7 +145,7 @@ class BlockWeights:
     heads: int
 
 
-FEW_ROWS = 32  # the library's few-row paths (streaming GEMV, warp-MMA) take at most this many token rows
+FEW_ROWS = 2  # launches of at most this many token rows take the library's streaming GEMV (fp32 weights)
 
 
 def _lin(w: BlockWeights, name: str, x: np.ndarray, *, launch_rows: int | None = None, **kw) -> np.ndarray:

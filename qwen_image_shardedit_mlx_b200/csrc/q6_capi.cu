@@ -39,8 +39,7 @@ bool simt_aligned(const void* x, int64_t K, int elem_bytes) {
 }
 
 // Few-row policy: the warp-MMA kernel runs when asked for by path
-// (Q6_PATH_SKINNY), or for 1..32 token rows when Q6_SKINNY=1; by default the
-// streaming GEMV (M <= 4) and the tensor-core path are faster.
+// (Q6_PATH_SKINNY), or for 1..16 token rows when Q6_SKINNY=1.
 bool skinny_auto(const q6::LinearArgs& a) {
     static const int mode = [] {
         const char* v = std::getenv("Q6_SKINNY");
@@ -56,7 +55,10 @@ int run_linear(const q6::LinearArgs& a, int path, cudaStream_t stream) {
         if (skinny_auto(a))
             chosen = Q6_PATH_SKINNY;
         else
-            chosen = (tc_ok && (a.M > 4 || a.lora_rank > 0)) ? Q6_PATH_TENSOR : Q6_PATH_SIMT;
+            // Measured on B200 (rotating weights > 4x L2): the streaming GEMV wins at
+            // 1-2 rows; from 3 rows on the tensor-core path does (at 4 rows
+            // 3072 -> 36864: 35 us against 53 us).
+            chosen = (tc_ok && (a.M > 2 || a.lora_rank > 0)) ? Q6_PATH_TENSOR : Q6_PATH_SIMT;
     }
     if (chosen == Q6_PATH_SKINNY) {
         if (a.lora_rank > 0 || !q6::skinny_supported(a)) return Q6_ERR_UNSUPPORTED;

@@ -9,9 +9,11 @@
 // plain warp-level MMA kernel (mma.sync m16n8k16) built for memory-level
 // parallelism: each CTA owns 16 token rows (one MMA row tile) and every rank
 // column, its four warps split the rank columns (r / 4 each), and K streams
-// through a three-stage cp.async ring of 64-wide chunks, so two chunks are in
-// flight while one is multiplied (M = 3456 runs 216 CTAs).  A (K x r, at
-// most 6 MB) is re-read by every CTA from L2.
+// through a cp.async ring of 64-wide chunks about 150 KB deep (12 stages at
+// rank 64, 4 at rank 256), so that a CTA keeps over 100 KB in flight: each
+// CTA re-reads all of A (K x r, 384 KB at K = 3072, r = 64) from L2 besides
+// its 96 KB of x, and with one CTA per SM the ring depth sets its bandwidth
+// (M = 3456 runs 216 CTAs).
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -26,9 +28,9 @@ namespace {
 
 constexpr int kRowsPerCta = 16;
 constexpr int kBK = 64;                    // K per chunk: four K = 16 MMA steps
-constexpr int kStages = 3;
 constexpr int kXStride = kBK + 8;          // bf16 per shared x row (16 bytes of padding: no bank conflicts)
 constexpr int kThreads = 128;
+constexpr int kRingBytes = 150 * 1024;     // target ring depth in bytes
 
 template <int R>
 struct LoraCfg {
@@ -36,8 +38,11 @@ struct LoraCfg {
     static constexpr int kXBytes = kRowsPerCta * kXStride * 2;
     static constexpr int kABytes = kBK * kAStride * 2;
     static constexpr int kStageBytes = kXBytes + kABytes;
+    static constexpr int kStages =
+        kRingBytes / kStageBytes < 3 ? 3 : (kRingBytes / kStageBytes > 12 ? 12 : kRingBytes / kStageBytes);
     static constexpr int kSmemBytes = kStages * kStageBytes;
     static_assert(kXBytes % 16 == 0 && kStageBytes % 16 == 0, "16-byte aligned stage slices");
+    static_assert(kSmemBytes <= 227 * 1024, "shared memory");
 };
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
@@ -88,6 +93,7 @@ __global__ void __launch_bounds__(kThreads) lora_xa_kernel(const uint16_t* __res
     pdl_launch_dependents();
     pdl_wait();  // x may be the previous kernel's output
 
+    constexpr int kStages = C::kStages;
     auto load_chunk = [&](int c) {
         const int s = c % kStages;
         const int64_t k0 = static_cast<int64_t>(c) * kBK;
@@ -111,8 +117,8 @@ __global__ void __launch_bounds__(kThreads) lora_xa_kernel(const uint16_t* __res
 #pragma unroll
     for (int t = 0; t < kTiles; ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0.0f;
 
-    // Prologue: chunks 0 and 1 in flight (one commit group each; a group past
-    // the last chunk is empty, which keeps the wait counts uniform).
+    // Prologue: chunks 0 .. kStages - 2 in flight (one commit group each; a
+    // group past the last chunk is empty, which keeps the wait counts uniform).
     for (int c = 0; c < kStages - 1; ++c) {
         if (c < chunks) load_chunk(c);
         cp_async_commit();

@@ -1,44 +1,49 @@
-// q6 linear for a few token rows (M <= 32): warp-level MMA on the raw codes.
+// q6 linear for a few token rows (M <= 16): warp-level MMA on the raw codes,
+// K streamed in CTA-wide stages.
 //
 // With a handful of token rows the linear is bound by reading the packed
 // weights (0.8125 bytes per weight at group size 64), so the arithmetic per
-// code must stay a few instructions and the memory pipeline must stay full.
-// The reference's sum_k x_k (scale * code_k + qbias) (shardedit_mlx/
-// q6_metal_mlp.py:42-83) is evaluated per scale group g as
+// code must stay a few instructions and HBM must stay busy.  The reference's
+// sum_k x_k (scale * code_k + qbias) (shardedit_mlx/q6_metal_mlp.py:42-83) is
+// evaluated per 64-code block of one scale group g as
 //
-//     scale_g * sum_{k in g} x_k (128 + code_k) + (qbias_g - 128 scale_g) * sum_{k in g} x_k
+//     scale_g * sum_k x_k (128 + code_k) + (qbias_g - 128 scale_g) * sum_k x_k
 //
 // where 128 + code is exact in bf16 (exponent 2^7, the code in the low
-// mantissa bits), so the two sums are exact-product bf16 MMAs with fp32
-// accumulation (mma.sync m16n8k16): A = the token rows (one or two tiles of
-// 16, zero past M), B = 128 + code for 8 weight rows, and a second B of ones
-// gives the per-token sums of x.  The weights keep the reference kernel's
-// fp32 semantics (no bf16 rounding of scale * code + qbias), like the
-// CUDA-core paths.
+// mantissa bits), so both sums are exact-product bf16 MMAs with fp32
+// accumulation (mma.sync m16n8k16): A = the token rows (one tile of 16, zero
+// past M), B = 128 + code for 8 weight rows, and a B of ones gives the sums
+// of x.  The weights keep the reference kernel's fp32 semantics (no bf16
+// rounding of scale * code + qbias), like the CUDA-core paths.
 //
-// Layout of the MMA K dimension.  Each lane (g = lane / 4, q = lane % 4)
-// owns the 16-code unit q (three packed words) of every 64-code block of its
-// two weight rows g and 8 + g, and MMA K step s of the block takes codes
-// 4s .. 4s + 3 of every lane's unit.  The K order inside the block is
-// permuted, which the sum does not see, and the matching x values of a lane
-// are x[16q + 4s .. 16q + 4s + 3]: eight contiguous bytes, so x fragments
-// are plain 16-byte loads.  A code pair becomes one bf16x2 word with two
-// shifts (one when a code sits on a byte boundary), a byte permute and one
-// logic instruction that masks the codes and sets the exponent bits (a
-// runtime word, so it stays one instruction).
+// Layout of the MMA K dimension.  Lane (g = lane / 4, q = lane % 4) owns the
+// 16-code unit q (three packed words) of every 64-code block of weight row g
+// of a tile, and MMA K step s of the block takes codes 4s .. 4s + 3 of every
+// lane's unit.  The K order inside the block is permuted, which the sum does
+// not see; the matching activations of a lane are x[16q + 4s .. 16q + 4s + 3]
+// of its token rows, eight contiguous bytes.  A code pair becomes one bf16x2
+// word with a shift or two, a byte permute and one logic instruction.
 //
-// Data movement: each warp streams its 16 weight rows through a private
-// two-slot ring in shared memory; its lane 0 loads a stage (16 rows x
-// 8 * group_size codes with their 8 scale and bias groups) with three 2-D
-// TMA copies while the warp works on the other slot.  A CTA of four warps
-// covers 64 / splits rows; `splits` warps share a row block and split its
-// K range, their partial sums meeting in shared memory (fixed order:
-// bitwise reproducible) before one warp applies the epilogue (bias, GELU,
-// gate, residual) and stores bf16.  Every barrier wait is bounded.
+// Work and data movement.  A CTA owns a block of 8 T weight rows (T n8 tiles,
+// T even, at most 16) and streams all of K through a ring of CTA-wide stages
+// of 512 codes.  Each stage arrives by TMA (one [rows x 100 words] code box,
+// 4 words more than the stage's 96 so that the 400-byte shared rows put the
+// eight rows a warp reads in different banks; eight [tokens x 64] activation
+// boxes with the 128-byte swizzle; the stage's scale and bias groups), and the
+// last of the sixteen MMA warps to release a ring slot refills it, so no warp
+// waits to produce.  The warps consume a stage as follows: warp (block b, half h) takes the 64-code block b of the
+// stage for tile half h, so the activations of a block are loaded once per
+// warp and serve all of its tiles.  At the end of a row block the eight block
+// warps of each half hold partial sums over K; they meet in shared memory and
+// are summed in block order (bitwise reproducible) before the epilogue
+// (bias, GELU, gate, residual) stores bf16.  A CTA walks row blocks
+// b, b + gridDim.x, ... with the stage ring running on across them.  Every
+// barrier wait is bounded.
 //
 // Requirements (else another path runs): bf16 activations and output,
-// 1 <= M <= 32, group size 64 or 128, K a multiple of 8 * group_size,
-// 16-byte aligned x, codes, scales and biases, no LoRA delta.
+// 1 <= M <= 16, K a multiple of 512, group size 32, 64 or 128 with
+// K / group_size a multiple of 8, 16-byte aligned x, codes, scales and
+// biases, no LoRA delta.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -48,7 +53,6 @@
 #include <atomic>
 #include <cstdlib>
 #include <mutex>
-#include <type_traits>
 
 #include "q6_dequant.cuh"
 #include "q6_internal.h"
@@ -57,32 +61,58 @@
 namespace q6 {
 namespace {
 
-constexpr int kWarps = 4;         // warps per CTA
-constexpr int kRowsPerWarp = 16;  // weight rows of one warp (two n8 MMA tiles)
-constexpr int kSlots = 2;         // ring slots per warp
-constexpr int kSbGroups = 8;      // scale groups per stage (the 16-byte TMA box minimum)
+constexpr int kBlocks = 8;                  // 64-code blocks per stage
+constexpr int kChunk = 64 * kBlocks;        // codes per row per stage
+constexpr int kHalves = 2;                  // MMA warps per block (tile halves)
+constexpr int kMmaWarps = kBlocks * kHalves;
+constexpr int kThreads = kMmaWarps * 32;
+constexpr int kMaxTiles = 16;               // n8 tiles per row block
+constexpr int kTok = 16;                    // token rows of the A tile
+constexpr int kXBoxStride = kTok * 128;     // shared-memory slot of one [tokens x 64] bf16 activation box
+constexpr int kMaxStages = 4;
+constexpr int kCodeRowWords = 100;         // words per shared code row: the stage's 96 and 4 of padding
+constexpr int kSmemBudget = 227 * 1024 - 1024;  // dynamic shared memory (the kernel's statics stay below 1 KB)
 
-template <int GS>
-struct SkCfg {
-    static constexpr int kStageCodes = kSbGroups * GS;                      // per row
-    static constexpr int kStageWords = kStageCodes * 6 / 32;                // per row
-    static constexpr int kCodeBytes = kRowsPerWarp * kStageWords * 4;       // 6144 (gs64) / 12288 (gs128)
-    static constexpr int kSbBytes = kRowsPerWarp * kSbGroups * 2;           // 256: one array
-    static constexpr int kStageBytes = ((kCodeBytes + 2 * kSbBytes) + 127) & ~127;
-    static constexpr int kSmemBytes = kWarps * kSlots * kStageBytes + kWarps * kSlots * 8 + 128;
-    static_assert(kStageWords <= 256, "TMA box inner extent");
+struct SkGeom {
+    int tiles;          // n8 tiles per row block (even)
+    int rows;           // 8 * tiles
+    int sb_groups;      // scale groups per stage box (>= 8)
+    int code_bytes;     // per stage: rows x 400 bytes
+    int sb_bytes;       // per stage, one of scales / biases
+    int stage_bytes;    // activation boxes first (1024-byte aligned for the swizzle)
+    int scratch_bytes;  // per-warp partial sums of a row block
+    int stages;
+    int smem_bytes;
 };
 
+inline int align_up(int v, int a) { return (v + a - 1) / a * a; }
+
+inline SkGeom sk_geometry(int tiles, int gs) {
+    SkGeom g;
+    g.tiles = tiles;
+    g.rows = 8 * tiles;
+    g.sb_groups = std::max(8, kChunk / gs);
+    g.code_bytes = g.rows * kCodeRowWords * 4;
+    g.sb_bytes = g.rows * g.sb_groups * 2;
+    g.stage_bytes = align_up(kBlocks * kXBoxStride + g.code_bytes + 2 * g.sb_bytes, 1024);
+    g.scratch_bytes = kMmaWarps * (tiles / kHalves) * 4 * 32 * 4;
+    const int fixed = g.scratch_bytes + 1024 /* alignment */ + kMaxStages * 8 /* barriers */;
+    g.stages = std::min(kMaxStages, (kSmemBudget - fixed) / g.stage_bytes);
+    g.smem_bytes = g.stages * g.stage_bytes + fixed;
+    return g;
+}
+
 struct SkParams {
-    const uint16_t* x;
     const uint16_t* bias;
     const uint16_t* gate;
     const uint16_t* residual;
     uint16_t* y;
     int M, N, K, flags;
-    int splits;             // warps per row block (K split), 1, 2 or 4
-    int stages_per_split;   // stages of 8 * gs codes each warp runs
-    uint32_t exp_pair;      // 0x43004300: bf16 exponent of 2^7 in both halves
+    int gs_shift;
+    int rows, sb_groups, code_bytes, sb_bytes, stage_bytes, stages;
+    int row_blocks;
+    uint32_t x_box_bytes;  // M rows x 128 bytes
+    uint32_t exp_pair;     // 0x43004300: bf16 exponent of 2^7 in both halves
 };
 
 __device__ __forceinline__ float bf16f(uint16_t v) { return __uint_as_float(static_cast<uint32_t>(v) << 16); }
@@ -124,220 +154,265 @@ __device__ __forceinline__ void unit_pairs(uint32_t w0, uint32_t w1, uint32_t w2
     }
 }
 
-template <int MTI, int GS>
-__global__ void __launch_bounds__(kWarps * 32) skinny_kernel(const __grid_constant__ CUtensorMap tmap_w,
+// A fragment words of K step S (activation pairs 4S, 4S + 1 and 4S + 2, 4S + 3
+// of the lane's unit) from the lane's 16 activations of a token row.
+template <int S>
+__device__ __forceinline__ void a_words(const uint4 (&r)[2], uint32_t& lo, uint32_t& hi) {
+    const uint4 v = r[S / 2];
+    if constexpr (S % 2 == 0) {
+        lo = v.x;
+        hi = v.y;
+    } else {
+        lo = v.z;
+        hi = v.w;
+    }
+}
+
+// Refill of ring slot s with stage t (one thread): the weights part (codes,
+// scales, biases: never written by a kernel) and the activations part.
+struct SkIssue {
+    const CUtensorMap* tx;
+    const CUtensorMap* tw;
+    const CUtensorMap* ts;
+    const CUtensorMap* tb;
+    uint8_t* ring;
+    uint64_t* full;
+    int stages, stage_bytes, chunks, rows, code_bytes, sb_bytes, groups_per_chunk;
+    uint32_t tx_bytes;
+
+    __device__ __forceinline__ void weights(int t, int rb) const {
+        const int s = t % stages;
+        uint8_t* codes = ring + s * stage_bytes + kBlocks * kXBoxStride;
+        const uint32_t bar = smem_u32(full + s);
+        const int c = t % chunks;
+        const int r0 = rb * rows;
+        mbar_arrive_expect_tx(bar, tx_bytes);
+        tma_load_2d(smem_u32(codes), tw, bar, c * (kChunk * 6 / 32), r0);
+        const int gbox = (c * groups_per_chunk) & ~7;  // 16-byte aligned box start
+        tma_load_2d(smem_u32(codes + code_bytes), ts, bar, gbox, r0);
+        tma_load_2d(smem_u32(codes + code_bytes + sb_bytes), tb, bar, gbox, r0);
+    }
+    __device__ __forceinline__ void activations(int t) const {
+        const int s = t % stages;
+        uint8_t* st = ring + s * stage_bytes;
+        const uint32_t bar = smem_u32(full + s);
+        const int c = t % chunks;
+#pragma unroll 1
+        for (int b = 0; b < kBlocks; ++b)
+            tma_load_2d(smem_u32(st + b * kXBoxStride), tx, bar, c * kChunk + b * 64, 0);
+    }
+};
+
+// GS: group size; TPW: n8 tiles per warp (the row block holds 2 TPW tiles).
+template <int GS, int TPW>
+__global__ void __launch_bounds__(kThreads, 1) skinny_kernel(const __grid_constant__ CUtensorMap tmap_x,
+                                                            const __grid_constant__ CUtensorMap tmap_w,
                                                             const __grid_constant__ CUtensorMap tmap_s,
                                                             const __grid_constant__ CUtensorMap tmap_b,
                                                             const SkParams p) {
-    using C = SkCfg<GS>;
-    extern __shared__ __align__(128) uint8_t sk_smem[];
+    extern __shared__ uint8_t sk_raw[];
+    uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(sk_raw) + 1023) & ~uintptr_t(1023));
+    float* scratch = reinterpret_cast<float*>(ring + p.stages * p.stage_bytes);
+    uint64_t* full = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(scratch) +
+                                                 kMmaWarps * TPW * 4 * 32 * 4);
+    __shared__ int abort_flag;
+    __shared__ uint32_t released[kMaxStages];  // warps done with the slot's current stage
+    __shared__ int issued_total;               // stages whose copies were issued
+
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int g = lane >> 2;
-    const int q = lane & 3;
-    const int rb_per_cta = kWarps / p.splits;
-    const int rb_local = warp / p.splits;
-    const int split = warp - rb_local * p.splits;
-    const int n0 = (blockIdx.x * rb_per_cta + rb_local) * kRowsPerWarp;
-    const bool active = n0 < p.N;  // the same for every warp of a row block
-    uint8_t* ring = sk_smem + warp * kSlots * C::kStageBytes;
-    uint64_t* full = reinterpret_cast<uint64_t*>(sk_smem + kWarps * kSlots * C::kStageBytes) + warp * kSlots;
-    const int st0 = split * p.stages_per_split;
-    const int nst = active ? p.stages_per_split : 0;
+    const int chunks = p.K / kChunk;
+    const int my_blocks =
+        static_cast<int>(blockIdx.x) < p.row_blocks ? (p.row_blocks - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
+    const int total = my_blocks * chunks;  // stages of this CTA
+    const int code_off = kBlocks * kXBoxStride;
+    SkIssue io;
+    io.tx = &tmap_x;
+    io.tw = &tmap_w;
+    io.ts = &tmap_s;
+    io.tb = &tmap_b;
+    io.ring = ring;
+    io.full = full;
+    io.stages = p.stages;
+    io.stage_bytes = p.stage_bytes;
+    io.chunks = chunks;
+    io.rows = p.rows;
+    io.code_bytes = p.code_bytes;
+    io.sb_bytes = p.sb_bytes;
+    io.groups_per_chunk = kChunk / GS;
+    io.tx_bytes = kBlocks * p.x_box_bytes + p.code_bytes + 2 * p.sb_bytes;
+    auto block_of = [&](int t) { return static_cast<int>(blockIdx.x) + (t / chunks) * static_cast<int>(gridDim.x); };
 
-    auto issue = [&](int t) {  // lane 0: stage t of this warp into slot t % kSlots
-        const uint32_t slot = smem_u32(ring + (t % kSlots) * C::kStageBytes);
-        const uint32_t bar = smem_u32(full + (t % kSlots));
-        mbar_arrive_expect_tx(bar, C::kCodeBytes + 2 * C::kSbBytes);
-        const int st = st0 + t;
-        tma_load_2d(slot, &tmap_w, bar, st * C::kStageWords, n0);
-        tma_load_2d(slot + C::kCodeBytes, &tmap_s, bar, st * kSbGroups, n0);
-        tma_load_2d(slot + C::kCodeBytes + C::kSbBytes, &tmap_b, bar, st * kSbGroups, n0);
-    };
-
-    if (lane == 0) {
-        for (int s = 0; s < kSlots; ++s) mbar_init(smem_u32(full + s), 1);
+    const int pre = total < p.stages ? total : p.stages;
+    if (threadIdx.x == 0) {
+        abort_flag = 0;
+        issued_total = pre;
+        for (int s = 0; s < kMaxStages; ++s) released[s] = 0;
+        for (int s = 0; s < p.stages; ++s) mbar_init(smem_u32(full + s), 1);
         fence_mbar_init();
         tma_prefetch_map(&tmap_w);
-        for (int t = 0; t < kSlots && t < nst; ++t) issue(t);  // weights: before the dependency wait
+        tma_prefetch_map(&tmap_x);
+        for (int t = 0; t < pre; ++t) io.weights(t, block_of(t));  // before the dependency wait
     }
-    __syncwarp();
     pdl_launch_dependents();
     pdl_wait();  // x, the epilogue operands and y may belong to the previous kernel
+    if (threadIdx.x == 0)
+        for (int t = 0; t < pre; ++t) io.activations(t);
+    __syncthreads();
 
-    float acc[MTI][2][4];
-#pragma unroll
-    for (int i = 0; i < MTI; ++i)
-#pragma unroll
-        for (int j = 0; j < 2; ++j) acc[i][j][0] = acc[i][j][1] = acc[i][j][2] = acc[i][j][3] = 0.0f;
-
+    const int blk = warp >> 1;         // 64-code block of each stage
+    const int half = warp & 1;         // tile half
+    const int g = lane >> 2;
+    const int q = lane & 3;
+    const int tile0 = half * TPW;      // first tile of this warp in the row block
     const uint32_t e = p.exp_pair;
     const uint32_t ones = 0x3F803F80u;  // bf16 (1, 1)
-    volatile int no_abort = 0;          // the ring is private to the warp
-    const uint16_t* xg = p.x;
-    // token rows of this lane: 16 i + g and 16 i + g + 8
-    bool tok_ok[MTI][2];
-#pragma unroll
-    for (int i = 0; i < MTI; ++i) {
-        tok_ok[i][0] = 16 * i + g < p.M;
-        tok_ok[i][1] = 16 * i + g + 8 < p.M;
-    }
+    const bool row_lo = g < p.M, row_hi = g + 8 < p.M;
+    const int swz = g & 7;              // 128-byte swizzle of token rows g and g + 8
+    const uint32_t mask0 = (GS == 32 && q >= 2) ? 0u : 0xFFFFFFFFu;  // group size 32: lanes of group 0
+    bool ok = true;
 
-    int consumed = 0;  // stages whose copies this warp has waited for
-    for (int t = 0; t < nst; ++t) {
-        const uint8_t* slot = ring + (t % kSlots) * C::kStageBytes;
-        if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(full + (t % kSlots)), static_cast<uint32_t>((t / kSlots) & 1),
-                                               &no_abort, 12)))
-            break;
-        consumed = t + 1;
-        const uint32_t* codes = reinterpret_cast<const uint32_t*>(slot);
-        const uint16_t* scl = reinterpret_cast<const uint16_t*>(slot + C::kCodeBytes);
-        const uint16_t* bia = reinterpret_cast<const uint16_t*>(slot + C::kCodeBytes + C::kSbBytes);
-        const int k_stage = (st0 + t) * C::kStageCodes;
-#pragma unroll 1
-        for (int gi = 0; gi < kSbGroups; ++gi) {
-            // scale and folded bias (qbias - 128 scale) of the accumulator rows 8 j + 2 q + c
-            float2 sv[2], bv[2];
+    for (int rbi = 0; rbi < my_blocks; ++rbi) {
+        const int rb = blockIdx.x + rbi * gridDim.x;
+        float2 acc[TPW][2];  // (token g: rows 2q, 2q + 1), (token g + 8: rows 2q, 2q + 1)
 #pragma unroll
-            for (int j = 0; j < 2; ++j) {
-                const int r = 8 * j + 2 * q;
-                const float s0 = bf16f(scl[r * kSbGroups + gi]), s1 = bf16f(scl[(r + 1) * kSbGroups + gi]);
-                const float c0 = bf16f(bia[r * kSbGroups + gi]), c1 = bf16f(bia[(r + 1) * kSbGroups + gi]);
-                sv[j] = make_float2(s0, s1);
-                bv[j] = make_float2(fmaf(-128.0f, s0, c0), fmaf(-128.0f, s1, c1));
-            }
-            float D[MTI][2][4], X[MTI][4];
-#pragma unroll
-            for (int i = 0; i < MTI; ++i) {
-                X[i][0] = X[i][1] = X[i][2] = X[i][3] = 0.0f;
-#pragma unroll
-                for (int j = 0; j < 2; ++j) D[i][j][0] = D[i][j][1] = D[i][j][2] = D[i][j][3] = 0.0f;
-            }
-#pragma unroll
-            for (int blk = 0; blk < GS / 64; ++blk) {
-                const int kb = gi * GS + blk * 64;            // stage-local K of the 64-code block
-                const int uo = (kb >> 4) * 3 + 3 * q;          // this lane's unit: word offset in a stage row
-                const uint32_t* r0 = codes + g * C::kStageWords + uo;
-                const uint32_t* r1 = codes + (8 + g) * C::kStageWords + uo;
-                const uint32_t u00 = r0[0], u01 = r0[1], u02 = r0[2];
-                const uint32_t u10 = r1[0], u11 = r1[1], u12 = r1[2];
-                // x values of this lane's codes: 16 bf16 per token row = 2 x 16 bytes
-                uint4 xa[MTI][2][2];
-#pragma unroll
-                for (int i = 0; i < MTI; ++i)
-#pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        if (tok_ok[i][h]) {
-                            const uint4* src = reinterpret_cast<const uint4*>(
-                                xg + static_cast<size_t>(16 * i + g + 8 * h) * p.K + k_stage + kb + 16 * q);
-                            xa[i][h][0] = __ldg(src);
-                            xa[i][h][1] = __ldg(src + 1);
-                        } else {
-                            xa[i][h][0] = xa[i][h][1] = make_uint4(0, 0, 0, 0);
-                        }
-                    }
-                auto step = [&](auto S_, uint32_t p0a, uint32_t p0b, uint32_t p1a, uint32_t p1b) {
-                    constexpr int S = decltype(S_)::value;
-#pragma unroll
-                    for (int i = 0; i < MTI; ++i) {
-                        // x words 2S, 2S + 1 of each token row: codes 4S .. 4S + 3 of the lane's unit
-                        const uint32_t* lo = reinterpret_cast<const uint32_t*>(&xa[i][0][S / 2]);
-                        const uint32_t* hi = reinterpret_cast<const uint32_t*>(&xa[i][1][S / 2]);
-                        const uint32_t a0 = lo[2 * (S % 2)], a2 = lo[2 * (S % 2) + 1];
-                        const uint32_t a1 = hi[2 * (S % 2)], a3 = hi[2 * (S % 2) + 1];
-                        mma_bf16_16816(D[i][0], a0, a1, a2, a3, p0a, p0b);
-                        mma_bf16_16816(D[i][1], a0, a1, a2, a3, p1a, p1b);
-                        mma_bf16_16816(X[i], a0, a1, a2, a3, ones, ones);
-                    }
-                };
-                uint32_t b00, b01, b10, b11;
-                unit_pairs<0>(u00, u01, u02, e, b00, b01);
-                unit_pairs<0>(u10, u11, u12, e, b10, b11);
-                step(std::integral_constant<int, 0>{}, b00, b01, b10, b11);
-                unit_pairs<1>(u00, u01, u02, e, b00, b01);
-                unit_pairs<1>(u10, u11, u12, e, b10, b11);
-                step(std::integral_constant<int, 1>{}, b00, b01, b10, b11);
-                unit_pairs<2>(u00, u01, u02, e, b00, b01);
-                unit_pairs<2>(u10, u11, u12, e, b10, b11);
-                step(std::integral_constant<int, 2>{}, b00, b01, b10, b11);
-                unit_pairs<3>(u00, u01, u02, e, b00, b01);
-                unit_pairs<3>(u10, u11, u12, e, b10, b11);
-                step(std::integral_constant<int, 3>{}, b00, b01, b10, b11);
-            }
-            // acc += scale * sum x (128 + code) + (qbias - 128 scale) * sum x, per (token, row) pair
-#pragma unroll
-            for (int i = 0; i < MTI; ++i)
-#pragma unroll
-                for (int j = 0; j < 2; ++j)
-#pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        float2 a = make_float2(acc[i][j][2 * h], acc[i][j][2 * h + 1]);
-                        a = __ffma2_rn(sv[j], make_float2(D[i][j][2 * h], D[i][j][2 * h + 1]), a);
-                        a = __ffma2_rn(bv[j], make_float2(X[i][2 * h], X[i][2 * h + 1]), a);
-                        acc[i][j][2 * h] = a.x;
-                        acc[i][j][2 * h + 1] = a.y;
-                    }
-        }
-        // hand the slot back to this warp's producer lane for stage t + kSlots
-        __syncwarp();
-        if (lane == 0 && t + kSlots < nst) {
-            fence_proxy_async_smem();
-            issue(t + kSlots);
-        }
-    }
-    // After a wait that gave up, copies issued for later stages may still be in
-    // flight: wait for them (bounded) before the ring is reused or the CTA exits.
-    if (lane == 0) {
-        const int issued = nst < consumed + kSlots ? nst : consumed + kSlots;
-        for (int u = consumed; u < issued; ++u)
-            mbar_wait_drain(smem_u32(full + (u % kSlots)), static_cast<uint32_t>((u / kSlots) & 1));
-    }
-    __syncwarp();
-    if (!active) return;  // every warp of an inactive row block leaves together
+        for (int j = 0; j < TPW; ++j) acc[j][0] = acc[j][1] = make_float2(0.0f, 0.0f);
 
-    // K split: the partial sums of warps 1 .. splits - 1 of a row block meet
-    // in shared memory (each warp's own idle ring), summed in split order.
-    if (p.splits > 1) {
-        float* mine = reinterpret_cast<float*>(ring);
-        if (split != 0) {
+        for (int c = 0; c < chunks; ++c) {
+            const int t = rbi * chunks + c;
+            const int s = t % p.stages;
+            const uint8_t* st = ring + s * p.stage_bytes;
+            if (ok && !__all_sync(0xffffffffu, mbar_wait(smem_u32(full + s), static_cast<uint32_t>((t / p.stages) & 1),
+                                                         &abort_flag, Q6_SITE_GEMM_MAX)))
+                ok = false;
+            if (ok) {
+                // activations of this block: token rows g and g + 8, logical 16-byte chunks 2q and 2q + 1
+                uint4 xr[2][2];
+                const uint8_t* xb = st + blk * kXBoxStride;
 #pragma unroll
-            for (int i = 0; i < MTI; ++i)
+                for (int h = 0; h < 2; ++h) {
+                    const bool live = h ? row_hi : row_lo;
+                    const uint8_t* row = xb + (g + 8 * h) * 128;
+                    const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+                    xr[h][0] = live ? *reinterpret_cast<const uint4*>(row + 16 * ((2 * q) ^ swz)) : z;
+                    xr[h][1] = live ? *reinterpret_cast<const uint4*>(row + 16 * ((2 * q + 1) ^ swz)) : z;
+                }
+                uint32_t a[4][4];  // A fragments of the four K steps
+                a_words<0>(xr[0], a[0][0], a[0][2]);
+                a_words<0>(xr[1], a[0][1], a[0][3]);
+                a_words<1>(xr[0], a[1][0], a[1][2]);
+                a_words<1>(xr[1], a[1][1], a[1][3]);
+                a_words<2>(xr[0], a[2][0], a[2][2]);
+                a_words<2>(xr[1], a[2][1], a[2][3]);
+                a_words<3>(xr[0], a[3][0], a[3][2]);
+                a_words<3>(xr[1], a[3][1], a[3][3]);
+                // Sums of x over the block.  Group size 32: codes 0-31 of the block are
+                // the units of lanes q = 0, 1 and codes 32-63 those of q = 2, 3, so each
+                // group's sums take B operands zeroed in the other group's lanes.
+                float X0[4] = {0.0f, 0.0f, 0.0f, 0.0f}, X1[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-                for (int j = 0; j < 2; ++j)
+                for (int ks = 0; ks < 4; ++ks) {
+                    mma_bf16_16816(X0, a[ks][0], a[ks][1], a[ks][2], a[ks][3], ones & mask0, ones & mask0);
+                    if constexpr (GS == 32)
+                        mma_bf16_16816(X1, a[ks][0], a[ks][1], a[ks][2], a[ks][3], ones & ~mask0, ones & ~mask0);
+                }
+                const uint32_t* codes = reinterpret_cast<const uint32_t*>(st + code_off) +
+                                        (8 * tile0 + g) * kCodeRowWords + blk * 12 + 3 * q;
+                const uint16_t* scl = reinterpret_cast<const uint16_t*>(st + code_off + p.code_bytes);
+                const uint16_t* bia = scl + p.sb_bytes / 2;
+                // scale group of this block within the stage's scale box; rows 2q, 2q + 1 of tile 0
+                const int gin = (((c * kChunk) >> p.gs_shift) & 7) + ((blk * 64) >> p.gs_shift);
+                const uint16_t* scl0 = scl + (8 * tile0 + 2 * q) * p.sb_groups + gin;
+                const uint16_t* bia0 = bia + (8 * tile0 + 2 * q) * p.sb_groups + gin;
+                const int tile_sb = 8 * p.sb_groups;  // scale entries per tile
 #pragma unroll
-                    for (int c = 0; c < 4; ++c) mine[((i * 2 + j) * 4 + c) * 32 + lane] = acc[i][j][c];
+                for (int j = 0; j < TPW; ++j) {
+                    const uint32_t* u = codes + j * 8 * kCodeRowWords;
+                    const uint32_t w0 = u[0], w1 = u[1], w2 = u[2];
+                    float D0[4] = {0.0f, 0.0f, 0.0f, 0.0f}, D1[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                    uint32_t b[4][2];
+                    unit_pairs<0>(w0, w1, w2, e, b[0][0], b[0][1]);
+                    unit_pairs<1>(w0, w1, w2, e, b[1][0], b[1][1]);
+                    unit_pairs<2>(w0, w1, w2, e, b[2][0], b[2][1]);
+                    unit_pairs<3>(w0, w1, w2, e, b[3][0], b[3][1]);
+#pragma unroll
+                    for (int ks = 0; ks < 4; ++ks) {
+                        mma_bf16_16816(D0, a[ks][0], a[ks][1], a[ks][2], a[ks][3], b[ks][0] & mask0, b[ks][1] & mask0);
+                        if constexpr (GS == 32)
+                            mma_bf16_16816(D1, a[ks][0], a[ks][1], a[ks][2], a[ks][3], b[ks][0] & ~mask0,
+                                           b[ks][1] & ~mask0);
+                    }
+                    // acc += scale * sum x (128 + code) + (qbias - 128 scale) * sum x, rows 2q and 2q + 1
+                    auto fold = [&](const float (&D)[4], const float (&X)[4], int gi) {
+                        const uint16_t* sp = scl0 + j * tile_sb + gi;
+                        const uint16_t* bp = bia0 + j * tile_sb + gi;
+                        const float2 sv = make_float2(bf16f(sp[0]), bf16f(sp[p.sb_groups]));
+                        const float2 bv = make_float2(bf16f(bp[0]), bf16f(bp[p.sb_groups]));
+                        const float2 cv = __ffma2_rn(make_float2(-128.0f, -128.0f), sv, bv);
+                        acc[j][0] = __ffma2_rn(sv, make_float2(D[0], D[1]), acc[j][0]);
+                        acc[j][0] = __ffma2_rn(cv, make_float2(X[0], X[1]), acc[j][0]);
+                        acc[j][1] = __ffma2_rn(sv, make_float2(D[2], D[3]), acc[j][1]);
+                        acc[j][1] = __ffma2_rn(cv, make_float2(X[2], X[3]), acc[j][1]);
+                    };
+                    fold(D0, X0, 0);
+                    if constexpr (GS == 32) fold(D1, X1, 1);
+                }
+            }
+            // Release the slot; the last warp to release it refills it with stage t + stages.
+            __syncwarp();
+            if (lane == 0) {
+                uint32_t prev;
+                asm volatile("atom.acq_rel.cta.shared::cta.add.u32 %0, [%1], 1;"
+                             : "=r"(prev)
+                             : "r"(smem_u32(&released[s]))
+                             : "memory");
+                if (prev == kMmaWarps - 1) {
+                    released[s] = 0;
+                    const int tn = t + p.stages;
+                    if (tn < total && !abort_flag) {
+                        fence_proxy_async_smem();  // the generic reads of the slot before the copies into it
+                        io.weights(tn, block_of(tn));
+                        io.activations(tn);
+                        atomicMax(&issued_total, tn + 1);
+                    }
+                }
+            }
         }
-        asm volatile("bar.sync %0, %1;" ::"r"(1 + rb_local), "r"(32 * p.splits) : "memory");
-        if (split != 0) return;
-        for (int sp = 1; sp < p.splits; ++sp) {
-            const float* other = reinterpret_cast<const float*>(sk_smem + (warp + sp) * kSlots * C::kStageBytes);
-#pragma unroll
-            for (int i = 0; i < MTI; ++i)
-#pragma unroll
-                for (int j = 0; j < 2; ++j)
-#pragma unroll
-                    for (int c = 0; c < 4; ++c) acc[i][j][c] += other[((i * 2 + j) * 4 + c) * 32 + lane];
-        }
-    }
 
-    // Epilogue: lane holds tokens 16 i + g (+ 8) x rows n0 + 8 j + 2 q (+ 1).
-    const bool gelu = (p.flags & (Q6_EPI_GELU | Q6_EPI_GELU_PRECISE)) != 0;
-    const bool precise = (p.flags & Q6_EPI_GELU_PRECISE) != 0;
+        // The eight block warps of each half meet in shared memory; warp w sums
+        // tile w of the row block over them in block order.
+        float* mine = scratch + warp * (TPW * 4 * 32);
 #pragma unroll
-    for (int j = 0; j < 2; ++j) {
-        const int n = n0 + 8 * j + 2 * q;
-        const bool ok0 = n < p.N, ok1 = n + 1 < p.N;
-        const float b0 = (ok0 && p.bias) ? bf16f(p.bias[n]) : 0.0f;
-        const float b1 = (ok1 && p.bias) ? bf16f(p.bias[n + 1]) : 0.0f;
-        const float g0 = (ok0 && p.gate) ? bf16f(p.gate[n]) : 1.0f;
-        const float g1 = (ok1 && p.gate) ? bf16f(p.gate[n + 1]) : 1.0f;
+        for (int j = 0; j < TPW; ++j) {
+            mine[(j * 4 + 0) * 32 + lane] = acc[j][0].x;
+            mine[(j * 4 + 1) * 32 + lane] = acc[j][0].y;
+            mine[(j * 4 + 2) * 32 + lane] = acc[j][1].x;
+            mine[(j * 4 + 3) * 32 + lane] = acc[j][1].y;
+        }
+        __syncthreads();
+        const int tile = warp;  // 2 TPW <= 16 tiles per row block: at most one per warp
+        if (ok && tile < 2 * TPW) {
+            const int h = tile / TPW, jl = tile - h * TPW;
+            float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            for (int b = 0; b < kBlocks; ++b) {
+                const float* src = scratch + (b * kHalves + h) * (TPW * 4 * 32) + jl * 4 * 32 + lane;
 #pragma unroll
-        for (int i = 0; i < MTI; ++i)
+                for (int k = 0; k < 4; ++k) v[k] += src[k * 32];
+            }
+            // epilogue: tokens g and g + 8 x rows n and n + 1
+            const int n = rb * p.rows + 8 * tile + 2 * q;
+            const bool ok0 = n < p.N, ok1 = n + 1 < p.N;
+            const float bi0 = (ok0 && p.bias) ? bf16f(p.bias[n]) : 0.0f;
+            const float bi1 = (ok1 && p.bias) ? bf16f(p.bias[n + 1]) : 0.0f;
+            const float g0 = (ok0 && p.gate) ? bf16f(p.gate[n]) : 1.0f;
+            const float g1 = (ok1 && p.gate) ? bf16f(p.gate[n + 1]) : 1.0f;
+            const bool gelu = (p.flags & (Q6_EPI_GELU | Q6_EPI_GELU_PRECISE)) != 0;
+            const bool precise = (p.flags & Q6_EPI_GELU_PRECISE) != 0;
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                const int m = 16 * i + g + 8 * h;
-                if (m >= p.M) continue;
-                float v0 = acc[i][j][2 * h] + b0, v1 = acc[i][j][2 * h + 1] + b1;
+            for (int hh = 0; hh < 2; ++hh) {
+                const int m = g + 8 * hh;
+                if (m >= p.M || !ok0) continue;
+                float v0 = v[2 * hh] + bi0, v1 = v[2 * hh + 1] + bi1;
                 if (gelu) {
                     v0 = gelu_select(v0, precise);
                     v1 = gelu_select(v1, precise);
@@ -346,17 +421,25 @@ __global__ void __launch_bounds__(kWarps * 32) skinny_kernel(const __grid_consta
                 v1 *= g1;
                 const size_t off = static_cast<size_t>(m) * p.N + n;
                 if (p.residual) {
-                    if (ok0) v0 += bf16f(p.residual[off]);
+                    v0 += bf16f(p.residual[off]);
                     if (ok1) v1 += bf16f(p.residual[off + 1]);
                 }
                 const uint32_t w = pack_bf16x2(v0, v1);
                 if (ok1 && (reinterpret_cast<uintptr_t>(p.y + off) & 3) == 0) {
                     *reinterpret_cast<uint32_t*>(p.y + off) = w;
                 } else {
-                    if (ok0) p.y[off] = static_cast<uint16_t>(w & 0xFFFFu);
+                    p.y[off] = static_cast<uint16_t>(w & 0xFFFFu);
                     if (ok1) p.y[off + 1] = static_cast<uint16_t>(w >> 16);
                 }
             }
+        }
+        __syncthreads();  // the scratch is free again
+    }
+    // Copies in flight land before the CTA exits (bounded).
+    if (threadIdx.x == 0) {
+        const int issued = issued_total;
+        for (int t = issued > p.stages ? issued - p.stages : 0; t < issued; ++t)
+            mbar_wait_drain(smem_u32(full + t % p.stages), static_cast<uint32_t>((t / p.stages) & 1));
     }
 }
 
@@ -374,7 +457,7 @@ PFN_cuTensorMapEncodeTiled_v12000 sk_encode_fn() {
 }
 
 bool sk_map(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t inner, uint64_t outer,
-            uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer) {
+            uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swizzle) {
     auto fn = sk_encode_fn();
     if (!fn) return false;
     const cuuint64_t dims[2] = {inner, outer};
@@ -382,63 +465,53 @@ bool sk_map(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint6
     const cuuint32_t box[2] = {box_inner, box_outer};
     const cuuint32_t estr[2] = {1, 1};
     return fn(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-              CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+              swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// Warps per row block (K split) for an (N, K) problem: the split whose CTAs,
-// four warps each, best fill the GPU at the resident CTAs per SM that the
-// shared memory allows, fewer splits on a tie.  Q6_SKINNY_SPLITS overrides.
-int plan_splits(int64_t N, int stages, int ctas_per_sm) {
-    if (const char* v = std::getenv("Q6_SKINNY_SPLITS")) {
-        const int s = std::atoi(v);
-        if ((s == 1 || s == 2 || s == 4) && stages % s == 0) return s;
+// n8 tiles per row block, one of 2, 4, 8, 12, 16 (1, 2, 4, 6, 8 per warp):
+// the smallest that spreads the rows over the SMs in one round, 16 at most.
+// Q6_SKINNY_TILES (one of those counts) overrides.
+int plan_tiles(int64_t N) {
+    static const int kChoices[] = {2, 4, 8, 12, 16};
+    if (const char* v = std::getenv("Q6_SKINNY_TILES")) {
+        const int t = std::atoi(v);
+        for (int c : kChoices)
+            if (t == c) return t;
     }
     const int64_t sms = device_sm_count();
-    const int64_t row_blocks = (N + kRowsPerWarp - 1) / kRowsPerWarp;
-    int best = 1;
-    int64_t best_cost = -1;
-    for (int s : {1, 2, 4}) {
-        if (stages % s) continue;
-        const int64_t ctas = (row_blocks + kWarps / s - 1) / (kWarps / s);
-        const int64_t per_sm = (ctas + sms - 1) / sms;                  // CTAs on the busiest SM
-        const int64_t waves = (per_sm + ctas_per_sm - 1) / ctas_per_sm;  // rounds of resident CTAs there
-        const int64_t spw = stages / s;                                  // stages per warp
-        // Busiest SM: its warps' stages over four schedulers at ~0.8 of issue,
-        // but no faster than one warp alone (~0.4 of issue) per round.
-        const int64_t cost = std::max<int64_t>(per_sm * kWarps * spw * 5, waves * spw * 10) * 4 + s;
-        if (best_cost < 0 || cost < best_cost) {
-            best_cost = cost;
-            best = s;
-        }
-    }
-    return best;
+    const int64_t per = ((N + 7) / 8 + sms - 1) / sms;  // tiles per SM for one round
+    for (int c : kChoices)
+        if (c >= per) return c;
+    return kMaxTiles;
 }
 
-template <int MTI, int GS>
+template <int GS, int TPW>
 int launch_skinny_t(const LinearArgs& a, cudaStream_t stream) {
-    using C = SkCfg<GS>;
+    const SkGeom geo = sk_geometry(2 * TPW, GS);
+    if (geo.stages < 2) return Q6_ERR_UNSUPPORTED;
     static std::atomic<bool> attr_set_for_device[kMaxDevices];
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return Q6_ERR_CUDA;
     if (dev < 0 || dev >= kMaxDevices) return Q6_ERR_UNSUPPORTED;
     if (!attr_set_for_device[dev].load(std::memory_order_acquire)) {
-        if (cudaFuncSetAttribute(skinny_kernel<MTI, GS>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes) !=
+        if (cudaFuncSetAttribute(skinny_kernel<GS, TPW>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBudget) !=
             cudaSuccess)
             return Q6_ERR_CUDA;
         attr_set_for_device[dev].store(true, std::memory_order_release);
     }
     const uint64_t words = static_cast<uint64_t>(a.K) * 6 / 32;
     const uint64_t groups = static_cast<uint64_t>(a.K / GS);
-    CUtensorMap tw, ts, tb;
-    if (!sk_map(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT32, a.w, words, a.N, words * 4, C::kStageWords, kRowsPerWarp) ||
-        !sk_map(&ts, CU_TENSOR_MAP_DATA_TYPE_UINT16, a.scales, groups, a.N, groups * 2, kSbGroups, kRowsPerWarp) ||
-        !sk_map(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT16, a.qbiases, groups, a.N, groups * 2, kSbGroups, kRowsPerWarp))
+    const uint32_t m = static_cast<uint32_t>(a.M);
+    CUtensorMap tx, tw, ts, tb;
+    if (!sk_map(&tx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.x, a.K, a.M, a.K * 2, 64, m, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !sk_map(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT32, a.w, words, a.N, words * 4, kCodeRowWords, geo.rows,
+                CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !sk_map(&ts, CU_TENSOR_MAP_DATA_TYPE_UINT16, a.scales, groups, a.N, groups * 2, geo.sb_groups, geo.rows,
+                CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !sk_map(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT16, a.qbiases, groups, a.N, groups * 2, geo.sb_groups, geo.rows,
+                CU_TENSOR_MAP_SWIZZLE_NONE))
         return Q6_ERR_CUDA;
-    const int stages = static_cast<int>(a.K / C::kStageCodes);
-    const int ctas_per_sm = std::max(1, (227 * 1024) / (C::kSmemBytes + 1024));
     SkParams p;
-    p.x = static_cast<const uint16_t*>(a.x);
     p.bias = a.bias;
     p.gate = a.gate;
     p.residual = a.residual;
@@ -447,32 +520,51 @@ int launch_skinny_t(const LinearArgs& a, cudaStream_t stream) {
     p.N = static_cast<int>(a.N);
     p.K = static_cast<int>(a.K);
     p.flags = a.flags;
-    p.splits = plan_splits(a.N, stages, ctas_per_sm);
-    p.stages_per_split = stages / p.splits;
+    p.gs_shift = GS == 32 ? 5 : (GS == 64 ? 6 : 7);
+    p.rows = geo.rows;
+    p.sb_groups = geo.sb_groups;
+    p.code_bytes = geo.code_bytes;
+    p.sb_bytes = geo.sb_bytes;
+    p.stage_bytes = geo.stage_bytes;
+    p.stages = geo.stages;
+    p.row_blocks = static_cast<int>((a.N + geo.rows - 1) / geo.rows);
+    p.x_box_bytes = m * 128u;
     p.exp_pair = 0x43004300u;
-    const int64_t row_blocks = (a.N + kRowsPerWarp - 1) / kRowsPerWarp;
-    const int rb_per_cta = kWarps / p.splits;
-    const int64_t ctas = (row_blocks + rb_per_cta - 1) / rb_per_cta;
-    const cudaError_t err = launch_pdl(skinny_kernel<MTI, GS>, dim3(static_cast<unsigned>(ctas)), dim3(kWarps * 32),
-                                       C::kSmemBytes, stream, tw, ts, tb, p);
+    const int grid = std::min(p.row_blocks, device_sm_count());
+    const cudaError_t err = launch_pdl(skinny_kernel<GS, TPW>, dim3(static_cast<unsigned>(grid)), dim3(kThreads),
+                                       geo.smem_bytes, stream, tx, tw, ts, tb, p);
     return err == cudaSuccess ? Q6_OK : Q6_ERR_CUDA;
+}
+
+template <int GS>
+int launch_skinny_gs(const LinearArgs& a, cudaStream_t stream) {
+    switch (plan_tiles(a.N)) {
+        case 2: return launch_skinny_t<GS, 1>(a, stream);
+        case 4: return launch_skinny_t<GS, 2>(a, stream);
+        case 8: return launch_skinny_t<GS, 4>(a, stream);
+        case 12: return launch_skinny_t<GS, 6>(a, stream);
+        default: return launch_skinny_t<GS, 8>(a, stream);
+    }
 }
 
 }  // namespace
 
 bool skinny_supported(const LinearArgs& a) {
-    if (a.M < 1 || a.M > 32 || a.lora_rank != 0) return false;
-    if (a.group_size != 64 && a.group_size != 128) return false;
-    if (a.K % (kSbGroups * a.group_size) != 0 || a.K > (int64_t(1) << 24) || a.N > (int64_t(1) << 30)) return false;
+    if (a.M < 1 || a.M > kTok || a.lora_rank != 0) return false;
+    if (a.group_size != 32 && a.group_size != 64 && a.group_size != 128) return false;
+    if (a.K % kChunk != 0 || (a.K / a.group_size) % 8 != 0) return false;
+    if (a.K > (int64_t(1) << 24) || a.N > (int64_t(1) << 30)) return false;
     const uintptr_t al = reinterpret_cast<uintptr_t>(a.x) | reinterpret_cast<uintptr_t>(a.w) |
                          reinterpret_cast<uintptr_t>(a.scales) | reinterpret_cast<uintptr_t>(a.qbiases);
     return al % 16 == 0;
 }
 
 int launch_skinny(const LinearArgs& a, cudaStream_t stream) {
-    const bool two = a.M > 16;
-    if (a.group_size == 64) return two ? launch_skinny_t<2, 64>(a, stream) : launch_skinny_t<1, 64>(a, stream);
-    return two ? launch_skinny_t<2, 128>(a, stream) : launch_skinny_t<1, 128>(a, stream);
+    switch (a.group_size) {
+        case 32: return launch_skinny_gs<32>(a, stream);
+        case 64: return launch_skinny_gs<64>(a, stream);
+        default: return launch_skinny_gs<128>(a, stream);
+    }
 }
 
 int error_word_skinny(bool clear) {

@@ -18,7 +18,7 @@ def _bench():
 def test_bench_legs_exist():
     b = _bench()
     for name in ("run_ours", "run_reference", "measure_block", "measure_stack", "measure_gemv", "measure_sweep",
-                 "_time_launches", "_graph_ms", "cpu_baseline_port", "workload_config"):
+                 "measure_kernels", "_time_launches", "_graph_ms", "cpu_baseline_port", "workload_config"):
         assert callable(getattr(b, name)), name
     assert b.FLOP_PER_STEP == 4 * 3456 * 3072 * 12288
 

@@ -203,17 +203,18 @@ def test_gemv_path_vs_oracle(m, n, k, gs, epi):
 
 SKINNY_SHAPES = [
     (12288, 3072, 64),   # the image FF's fc1 shape
-    (3072, 12288, 64),   # fc2 shape: K split across the warps of a row block
+    (3072, 12288, 64),   # fc2 shape: 24 stages of 512 codes
     (18432, 3072, 128),  # modulation-linear shape at group size 128
     (1001, 1024, 64),    # ragged N: the last row block is partly out of range
+    (2048, 1536, 32),    # group size 32: two scale groups per 64-code block, an odd stage count
 ]
 
 
-@pytest.mark.parametrize("m", [1, 2, 3, 8, 16, 17, 32])
+@pytest.mark.parametrize("m", [1, 2, 3, 8, 13, 16])
 @pytest.mark.parametrize("n,k,gs", SKINNY_SHAPES)
 @pytest.mark.parametrize("epi", ["plain", "bias_gelu", "residual_gate"])
 def test_skinny_path_vs_oracle(m, n, k, gs, epi):
-    """The warp-MMA kernel for 1..32 token rows on the raw codes against the
+    """The warp-MMA kernel for 1..16 token rows on the raw codes against the
     fp32-weight oracle (the reference kernel's weight precision); the output
     starts as NaN so every element must be written."""
 
@@ -241,22 +242,33 @@ def test_skinny_path_vs_oracle(m, n, k, gs, epi):
     assert_close(f32(got), ref, what=f"skinny {m}x{n}x{k} gs{gs} {epi}")
 
 
-def test_skinny_split_k_is_reproducible(monkeypatch):
-    """Warps splitting a row block's K sum their partials in a fixed order."""
+def test_skinny_row_blocks_are_reproducible(monkeypatch):
+    """Each output is summed in the same order (stages in K order within a
+    block warp, then the eight block warps in order) whatever the row-block
+    size, so the results are bitwise equal across block sizes, including
+    CTAs that walk several row blocks."""
 
     rng = np.random.default_rng(6)
-    w = random_weights(rng, 1024, 8192, 64)
+    w = random_weights(rng, 4096, 2048, 64)
     wt, st, bt, bias = weights_to_torch(w)
-    x = from_bits(random_bf16(rng, (16, 8192)))
+    x = from_bits(random_bf16(rng, (16, 2048)))
     outs = []
-    for splits in ("4", "4", "1"):
-        monkeypatch.setenv("Q6_SKINNY_SPLITS", splits)
+    for tiles in ("2", "2", "16", "12", "4"):  # 2: 256 row blocks, more than one per CTA
+        monkeypatch.setenv("Q6_SKINNY_TILES", tiles)
         outs.append(ops.q6_linear(x, wt, st, bt, bias, group_size=64, path="skinny"))
     torch.cuda.synchronize()
-    assert torch.equal(outs[0], outs[1])
-    ref = oracle.linear(f32(x), w, weight_dtype="f32")
-    for o in outs:
-        assert_close(f32(o), ref)
+    for o in outs[1:]:
+        assert torch.equal(outs[0], o)
+    assert_close(f32(outs[0]), oracle.linear(f32(x), w, weight_dtype="f32"))
+
+
+def test_skinny_refuses_more_than_16_rows():
+    rng = np.random.default_rng(7)
+    w = random_weights(rng, 256, 1024, 64)
+    wt, st, bt, bias = weights_to_torch(w)
+    x = from_bits(random_bf16(rng, (17, 1024)))
+    with pytest.raises(_lib.Q6Error):
+        ops.q6_linear(x, wt, st, bt, bias, group_size=64, path="skinny")
 
 
 LORA_CASES = [
@@ -327,7 +339,9 @@ def test_auto_path_choice():
     w = random_weights(rng, 256, 128, 64)
     wt, st, bt, bias = weights_to_torch(w)
     ops.q6_linear(from_bits(random_bf16(rng, (2, 128))), wt, st, bt, bias)
-    assert ops.last_path() == "simt"
+    assert ops.last_path() == "simt"  # 1-2 rows: the streaming GEMV
+    ops.q6_linear(from_bits(random_bf16(rng, (3, 128))), wt, st, bt, bias)
+    assert ops.last_path() == "tensor"  # from 3 rows the tensor-core path is faster
     ops.q6_linear(from_bits(random_bf16(rng, (64, 128))), wt, st, bt, bias)
     assert ops.last_path() == "tensor"
     torch.cuda.synchronize()
