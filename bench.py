@@ -594,7 +594,8 @@ def measure_stack(dev, world: int, rank: int, blocks: int = STACK_BLOCKS, steps:
     import torch
 
     from qwen_image_shardedit_mlx_b200 import ops
-    from qwen_image_shardedit_mlx_b200.block import QwenTransformerBlock, TensorParallelQwenBlock, block_flops
+    from qwen_image_shardedit_mlx_b200.block import (QwenTransformerBlock, TensorParallelQwenBlock, block_flops,
+                                                     stack_modulations)
 
     stack = []
     for i in range(blocks):
@@ -612,9 +613,11 @@ def measure_stack(dev, world: int, rank: int, blocks: int = STACK_BLOCKS, steps:
     temb = tembs[0].clone()
 
     def one_step():
-        pending = stack[0].forward_local(x_local, temb, rope_j, batch, seq, BLOCK_TXT)
-        for blk in stack[1:]:
-            pending = blk.forward_local_pending(pending, temb, rope_j, batch, seq, BLOCK_TXT)
+        # every block's modulation vectors first, 1 / N of the GEMVs per rank and one all-gather
+        mods = stack_modulations(stack, temb, world, rank)
+        pending = stack[0].forward_local(x_local, temb, rope_j, batch, seq, BLOCK_TXT, mod=mods[0])
+        for i, blk in enumerate(stack[1:], start=1):
+            pending = blk.forward_local_pending(pending, temb, rope_j, batch, seq, BLOCK_TXT, mod=mods[i])
         return stack[-1].finish(pending)
 
     stream = torch.cuda.current_stream()

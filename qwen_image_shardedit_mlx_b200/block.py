@@ -574,16 +574,18 @@ class TensorParallelQwenBlock(torch.nn.Module):
 
     def forward_local(self, x_local: torch.Tensor, temb: torch.Tensor,
                       rope_joint: tuple[torch.Tensor, torch.Tensor], batch: int, seq: int, text_len: int,
-                      text_mask: torch.Tensor | None = None) -> tuple[torch.Tensor, object]:
+                      text_mask: torch.Tensor | None = None,
+                      mod: torch.Tensor | None = None) -> tuple[torch.Tensor, object]:
         """This rank's joint rows through the block: x_local [R, D] are rows
         [rank R, (rank + 1) R) of the [B * S, D] joint rows.  Returns a
         pending pair: the block's output rows are h + ff (``finish``); a stack
         may instead hand the pair to the next block, whose first modulate
-        adds them in the same pass."""
+        adds them in the same pass.  ``mod``: this block's modulation vectors
+        [B, 2, 6, D] when computed beforehand (``stack_modulations``)."""
 
         rows_local, d = x_local.shape
         row0 = self.rank * rows_local
-        vec = ModulationVectors(self.modulation_joint(temb))
+        vec = ModulationVectors(self.modulation_joint(temb) if mod is None else mod)
         if self.comm == "peer":
             pr = self._peer(rows_local * self.world, x_local.device)
             pr.add_ln_gather(x_local, vec.shift1, vec.scale1, dst="gather1", seq_len=seq, text_len=text_len,
@@ -596,8 +598,8 @@ class TensorParallelQwenBlock(torch.nn.Module):
 
     def forward_local_pending(self, pending: tuple[torch.Tensor, torch.Tensor], temb: torch.Tensor,
                               rope_joint: tuple[torch.Tensor, torch.Tensor], batch: int, seq: int,
-                              text_len: int, text_mask: torch.Tensor | None = None
-                              ) -> tuple[torch.Tensor, torch.Tensor]:
+                              text_len: int, text_mask: torch.Tensor | None = None,
+                              mod: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
         """``forward_local`` of the output (h, ff) of the previous block: its
         residual add x = h + ff is formed in the same pass as this block's
         first modulate."""
@@ -605,7 +607,7 @@ class TensorParallelQwenBlock(torch.nn.Module):
         h_prev, ff_prev = pending
         rows_local = h_prev.shape[0]
         row0 = self.rank * rows_local
-        vec = ModulationVectors(self.modulation_joint(temb))
+        vec = ModulationVectors(self.modulation_joint(temb) if mod is None else mod)
         x_local = torch.empty_like(h_prev)
         if self.comm == "peer":
             pr = self._peer(rows_local * self.world, h_prev.device)
@@ -691,3 +693,29 @@ class TensorParallelQwenBlock(torch.nn.Module):
         seq = rows // batch
         y_local = self.finish(self.forward_local(x_local, temb, joint_rope(rope), batch, seq, s_txt, encoder_mask))
         return split_joint(self._gather(y_local), batch, s_txt)
+
+
+def stack_modulations(blocks, temb: torch.Tensor, world: int = 1, rank: int = 0, group=None) -> torch.Tensor:
+    """Modulation vectors [n, B, 2, 6, D] of every block of a stack for one
+    timestep embedding, the work split over the ranks of a tensor-parallel
+    group: rank r computes a contiguous run of ceil(n / world) blocks and one
+    all-gather shares them.  The modulation linears read only silu(temb), so
+    a denoising step can compute them all before its first block and each
+    block then skips its replicated modulation GEMV."""
+
+    n = len(blocks)
+    per = -(-n // world)
+    b = temb.shape[0]
+    d = blocks[0].dim
+    local = torch.zeros((per, b, 2, 6, d), dtype=torch.bfloat16, device=temb.device)
+    for j in range(per):
+        i = rank * per + j
+        if i < n:
+            local[j].copy_(blocks[i].modulation_joint(temb))
+    if world == 1:
+        return local[:n]
+    import torch.distributed as dist
+
+    everything = torch.empty((per * world, b, 2, 6, d), dtype=torch.bfloat16, device=temb.device)
+    dist.all_gather_into_tensor(everything, local, group=group)
+    return everything[:n]

@@ -763,19 +763,6 @@ __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
                 const uint32_t rs = g % kRing;
                 const int half_r = p.lora_rank / 2;
                 const int j0 = (ks - I.ks1) * half_r;
-                // The stage's B values are loaded before the wait for its A slot,
-                // so their L2 latency overlaps the MMAs still reading the slot.
-                uint32_t a[32];
-#pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    const int k = half * 64 + 2 * i;  // stage-local K of the pair (TMEM column half * 32 + i)
-                    float v0 = 0.0f, v1 = 0.0f;
-                    if (n_ok && k < half_r)
-                        v0 = p.lora_scale * bf16f(p.lora_b[static_cast<size_t>(j0 + k) * p.N + n]);
-                    if (n_ok && k + 1 < half_r)
-                        v1 = p.lora_scale * bf16f(p.lora_b[static_cast<size_t>(j0 + k + 1) * p.N + n]);
-                    a[i] = pack_bf16x2(v0, v1);
-                }
                 if (g >= static_cast<uint32_t>(C::kAStages)) {
                     const uint32_t prev = g - C::kAStages;
                     if (!warp_wait(smem_u32(done + prev % kRing), (prev / kRing) & 1u, abort_flag, 7)) {
@@ -784,8 +771,26 @@ __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
                     }
                 }
                 tc_fence_after();
-                tmem_st_32x32b_x32(
-                    tmem_base + lane_base + static_cast<uint32_t>(C::kAccCols + as * kAColsPerStage + half * 32), a);
+                // 16 columns (32 rank values) at a time: a register budget the
+                // q6 stages of the same kernel can afford (one array of 32 here
+                // made every variant spill in its dequant loop)
+#pragma unroll 1
+                for (int hh = 0; hh < 2; ++hh) {
+                    uint32_t a[16];
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        const int k = half * 64 + hh * 32 + 2 * i;  // stage-local K of the pair
+                        float v0 = 0.0f, v1 = 0.0f;
+                        if (n_ok && k < half_r)
+                            v0 = p.lora_scale * bf16f(p.lora_b[static_cast<size_t>(j0 + k) * p.N + n]);
+                        if (n_ok && k + 1 < half_r)
+                            v1 = p.lora_scale * bf16f(p.lora_b[static_cast<size_t>(j0 + k + 1) * p.N + n]);
+                        a[i] = pack_bf16x2(v0, v1);
+                    }
+                    tmem_st_32x32b_x16(tmem_base + lane_base +
+                                           static_cast<uint32_t>(C::kAccCols + as * kAColsPerStage + half * 32 + hh * 16),
+                                       a);
+                }
                 tmem_wait_st();
                 tc_fence_before();
                 __syncwarp();

@@ -5,20 +5,27 @@
 // s * (xa @ B) into its own tile; this kernel produces xa = x @ A, a bf16
 // [M, K] x [K, r] product with fp32 accumulation and one bf16 rounding, r a
 // multiple of 32 up to 256.  With r far below the ridge point (r FLOP per
-// byte of x) the product is bound by reading x once from HBM, so it is a
-// plain warp-level MMA kernel (mma.sync m16n8k16) built for memory-level
-// parallelism: each CTA owns 16 token rows (one MMA row tile) and every rank
-// column, its four warps split the rank columns (r / 4 each), and K streams
-// through a cp.async ring of 64-wide chunks about 150 KB deep (12 stages at
-// rank 64, 4 at rank 256), so that a CTA keeps over 100 KB in flight: each
-// CTA re-reads all of A (K x r, 384 KB at K = 3072, r = 64) from L2 besides
-// its 96 KB of x, and with one CTA per SM the ring depth sets its bandwidth
-// (M = 3456 runs 216 CTAs).
+// byte of x) the product is bound by moving bytes, so it is a plain
+// warp-level MMA kernel (mma.sync m16n8k16) built around its data movement:
+// each CTA owns 16 token rows (one MMA row tile) and every rank column, its
+// four warps split the rank columns (r / 4 each), and K streams in 64-wide
+// chunks through a ring of TMA stages: one [16 rows x 64] box of x and
+// r / 64 [64 x 64] boxes of A with the 128-byte swizzle (a rank that is an odd
+// multiple of 32 adds one [64 x 32] box with the 64-byte swizzle), which
+// keeps the ldmatrix reads conflict-free.  Every CTA reads all of A (384 KB at
+// K = 3072, r = 64) from L2 besides its own 96 KB of x; TMA moves it without
+// occupying the warps' load slots, which bounded the earlier cp.async form.
+// The last warp to release a ring slot refills it, and each CTA starts its
+// K loop at a different chunk (the sum order stays fixed per row tile).
+// Every wait is bounded.
+#include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
+#include <cudaTypedefs.h>
 
 #include <algorithm>
 #include <atomic>
+#include <mutex>
 
 #include "q6_internal.h"
 #include "q6_ptx.cuh"
@@ -27,33 +34,25 @@ namespace q6 {
 namespace {
 
 constexpr int kRowsPerCta = 16;
-constexpr int kBK = 64;                    // K per chunk: four K = 16 MMA steps
-constexpr int kXStride = kBK + 8;          // bf16 per shared x row (16 bytes of padding: no bank conflicts)
-constexpr int kThreads = 128;
-constexpr int kRingBytes = 150 * 1024;     // target ring depth in bytes
+constexpr int kBK = 64;                  // K per chunk: four K = 16 MMA steps
+constexpr int kWarps = 4;
+constexpr int kThreads = kWarps * 32;
+constexpr int kXBoxBytes = kRowsPerCta * 128;  // [16 rows x 64 bf16], 128-byte swizzled
+constexpr int kABoxBytes = kBK * 128;          // [64 k x 64 rank columns], 128-byte swizzled
+constexpr int kATailBytes = kBK * 64;          // [64 k x 32 rank columns], 64-byte swizzled
+constexpr int kRingBytes = 100 * 1024;         // two CTAs per SM
 
 template <int R>
 struct LoraCfg {
-    static constexpr int kAStride = R + 8;  // bf16 per shared A row (16 bytes of padding)
-    static constexpr int kXBytes = kRowsPerCta * kXStride * 2;
-    static constexpr int kABytes = kBK * kAStride * 2;
-    static constexpr int kStageBytes = kXBytes + kABytes;
-    static constexpr int kStages =
-        kRingBytes / kStageBytes < 3 ? 3 : (kRingBytes / kStageBytes > 12 ? 12 : kRingBytes / kStageBytes);
-    static constexpr int kSmemBytes = kStages * kStageBytes;
-    static_assert(kXBytes % 16 == 0 && kStageBytes % 16 == 0, "16-byte aligned stage slices");
+    static constexpr int kABoxes = R / 64;          // full 64-column boxes
+    static constexpr bool kTail = R % 64 != 0;      // one 32-column box
+    static constexpr int kStageBytes = kXBoxBytes + kABoxes * kABoxBytes + (kTail ? kATailBytes : 0);
+    static constexpr int kStages = kRingBytes / kStageBytes < 2 ? 2 : (kRingBytes / kStageBytes > 16 ? 16
+                                                                                                  : kRingBytes / kStageBytes);
+    static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /* alignment */;
+    static_assert(kStageBytes % 1024 == 0, "swizzled boxes need 1024-byte alignment");
     static_assert(kSmemBytes <= 227 * 1024, "shared memory");
 };
-
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
-    const int n = valid ? 16 : 0;  // zero-fill rows past M and columns past K
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(n) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
 
 __device__ __forceinline__ void ldmatrix_x4(uint32_t addr, uint32_t (&r)[4]) {
     asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
@@ -73,96 +72,184 @@ __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
 }
 
+// Byte offset of 16-byte chunk c of row `row` in a 128-byte-swizzled box
+// (128-byte rows: chunk bits 4-6 XOR address bits 7-9) and in a
+// 64-byte-swizzled box (64-byte rows: chunk bits 4-5 XOR address bits 7-8).
+__device__ __forceinline__ uint32_t swz(int row, int c) { return static_cast<uint32_t>(row * 128 + ((c ^ (row & 7)) << 4)); }
+__device__ __forceinline__ uint32_t swz64(int row, int c) {
+    return static_cast<uint32_t>(row * 64 + ((c ^ ((row >> 1) & 3)) << 4));
+}
+
 // R = rank (compile-time, multiple of 32, <= 256).
 template <int R>
-__global__ void __launch_bounds__(kThreads) lora_xa_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ a,
-                                                          uint16_t* __restrict__ xa, int64_t M, int64_t K) {
+__global__ void __launch_bounds__(kThreads) lora_xa_kernel(const __grid_constant__ CUtensorMap tmap_x,
+                                                          const __grid_constant__ CUtensorMap tmap_a,
+                                                          const __grid_constant__ CUtensorMap tmap_a_tail,
+                                                          uint16_t* __restrict__ xa, int64_t M, int64_t K,
+                                                          uint32_t x_box_bytes) {
     using C = LoraCfg<R>;
+    constexpr int kStages = C::kStages;
     constexpr int kCols = R / 4;           // columns per warp
     constexpr int kTiles = kCols / 8;      // n8 tiles per warp
-    extern __shared__ __align__(16) uint8_t lora_smem[];
+    extern __shared__ uint8_t lora_raw[];
+    uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(lora_raw) + 1023) & ~uintptr_t(1023));
+    __shared__ __align__(8) uint64_t full[kStages];
+    __shared__ uint32_t released[kStages];
+    __shared__ int abort_flag;
+    __shared__ int issued_total;
 
-    const int tid = threadIdx.x;
-    const int warp = tid >> 5;
-    const int lane = tid & 31;
-    const int64_t m0 = static_cast<int64_t>(blockIdx.x) * kRowsPerCta;
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int m0 = static_cast<int>(blockIdx.x) * kRowsPerCta;
     const int chunks = static_cast<int>((K + kBK - 1) / kBK);
-    auto xs = [&](int s) { return reinterpret_cast<uint16_t*>(lora_smem + s * C::kStageBytes); };
-    auto as = [&](int s) { return reinterpret_cast<uint16_t*>(lora_smem + s * C::kStageBytes + C::kXBytes); };
+    const uint32_t tx = x_box_bytes + C::kABoxes * kABoxBytes + (C::kTail ? kATailBytes : 0);
+    // Ring position c holds K chunk (c + k_first) mod chunks: the CTAs start at
+    // different chunks, so they do not all read the same few kilobytes of A
+    // from the same L2 slices at the same moment.
+    const int k_first = static_cast<int>((blockIdx.x * 7u) % static_cast<unsigned>(chunks));
+    auto kchunk = [&](int c) { return (c + k_first) % chunks; };
 
+    auto issue_a = [&](int c) {  // A: a weight, never written by a kernel
+        const int s = c % kStages;
+        uint8_t* st = ring + s * C::kStageBytes;
+        const uint32_t bar = smem_u32(&full[s]);
+        mbar_arrive_expect_tx(bar, tx);
+#pragma unroll
+        for (int b = 0; b < C::kABoxes; ++b)
+            tma_load_2d(smem_u32(st + kXBoxBytes + b * kABoxBytes), &tmap_a, bar, 64 * b, kchunk(c) * kBK);
+        if constexpr (C::kTail)
+            tma_load_2d(smem_u32(st + kXBoxBytes + C::kABoxes * kABoxBytes), &tmap_a_tail, bar, 64 * C::kABoxes,
+                        kchunk(c) * kBK);
+    };
+    auto issue_x = [&](int c) {
+        const int s = c % kStages;
+        tma_load_2d(smem_u32(ring + s * C::kStageBytes), &tmap_x, smem_u32(&full[s]), kchunk(c) * kBK, m0);
+    };
+
+    const int pre = chunks < kStages ? chunks : kStages;
+    if (threadIdx.x == 0) {
+        abort_flag = 0;
+        issued_total = pre;
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(smem_u32(&full[s]), 1);
+            released[s] = 0;
+        }
+        fence_mbar_init();
+        for (int c = 0; c < pre; ++c) issue_a(c);
+    }
     pdl_launch_dependents();
     pdl_wait();  // x may be the previous kernel's output
-
-    constexpr int kStages = C::kStages;
-    auto load_chunk = [&](int c) {
-        const int s = c % kStages;
-        const int64_t k0 = static_cast<int64_t>(c) * kBK;
-        // x: 16 rows x 64 bf16 = 8 x 16-byte pieces per row
-        for (int i = tid; i < kRowsPerCta * 8; i += kThreads) {
-            const int row = i >> 3, piece = i & 7;
-            const int64_t gm = m0 + row, gk = k0 + piece * 8;
-            const bool ok = gm < M && gk < K;
-            cp_async16(smem_u32(xs(s) + row * kXStride + piece * 8), ok ? x + gm * K + gk : x, ok);
-        }
-        // A: 64 rows of K x R bf16 = R / 8 pieces per row
-        for (int i = tid; i < kBK * (R / 8); i += kThreads) {
-            const int row = i / (R / 8), piece = i % (R / 8);
-            const int64_t gk = k0 + row;
-            const bool ok = gk < K;
-            cp_async16(smem_u32(as(s) + row * C::kAStride + piece * 8), ok ? a + gk * R + piece * 8 : a, ok);
-        }
-    };
+    if (threadIdx.x == 0)
+        for (int c = 0; c < pre; ++c) issue_x(c);
+    __syncthreads();
 
     float acc[kTiles][4];
 #pragma unroll
     for (int t = 0; t < kTiles; ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0.0f;
-
-    // Prologue: chunks 0 .. kStages - 2 in flight (one commit group each; a
-    // group past the last chunk is empty, which keeps the wait counts uniform).
-    for (int c = 0; c < kStages - 1; ++c) {
-        if (c < chunks) load_chunk(c);
-        cp_async_commit();
-    }
+    bool ok = true;
     for (int c = 0; c < chunks; ++c) {
-        cp_async_wait<kStages - 2>();  // this thread's copies of chunk c have landed
-        __syncthreads();               // ... and everyone's; the slot of chunk c - 1 is free again
-        if (c + kStages - 1 < chunks) load_chunk(c + kStages - 1);
-        cp_async_commit();
-        const uint16_t* xt = xs(c % kStages);
-        const uint16_t* at = as(c % kStages);
+        const int s = c % kStages;
+        const uint8_t* st = ring + s * C::kStageBytes;
+        if (ok && !__all_sync(0xffffffffu, mbar_wait(smem_u32(&full[s]), static_cast<uint32_t>((c / kStages) & 1),
+                                                     &abort_flag, Q6_SITE_GEMM_MAX)))
+            ok = false;
+        if (ok) {
+            const uint32_t xs = smem_u32(st);
+            const uint32_t as = smem_u32(st + kXBoxBytes);
 #pragma unroll
-        for (int ks = 0; ks < kBK / 16; ++ks) {
-            // A operand: the 16 rows, K columns 16 ks .. +15 of the x chunk.
-            uint32_t af[4];
-            ldmatrix_x4(smem_u32(xt + (lane & 15) * kXStride + 16 * ks + 8 * (lane >> 4)), af);
+            for (int ks = 0; ks < kBK / 16; ++ks) {
+                // A operand: the 16 rows, K columns 16 ks .. +15 of the x chunk
+                uint32_t af[4];
+                ldmatrix_x4(xs + swz(lane & 15, 2 * ks + (lane >> 4)), af);
 #pragma unroll
-            for (int t = 0; t < kTiles; ++t) {
-                // B operand: K rows 16 ks .. +15 (row-major [k][n] in shared memory,
-                // transposed by ldmatrix), n columns warp r/4 + 8 t .. +7.
-                uint32_t bf[2];
-                ldmatrix_x2_trans(smem_u32(at + (16 * ks + (lane & 15)) * C::kAStride + kCols * warp + 8 * t), bf);
-                mma_bf16_16816(acc[t], af, bf);
+                for (int t = 0; t < kTiles; ++t) {
+                    // B operand: K rows 16 ks .. +15 of A, rank columns kCols warp + 8 t .. +7
+                    const int col = kCols * warp + 8 * t;
+                    const int krow = 16 * ks + (lane & 15);
+                    uint32_t bf[2];
+                    if (col / 64 < C::kABoxes)
+                        ldmatrix_x2_trans(as + (col / 64) * kABoxBytes + swz(krow, (col % 64) / 8), bf);
+                    else
+                        ldmatrix_x2_trans(as + C::kABoxes * kABoxBytes + swz64(krow, (col % 64) / 8), bf);
+                    mma_bf16_16816(acc[t], af, bf);
+                }
+            }
+        }
+        // Release the slot; the last warp to release it refills it with chunk c + kStages.
+        __syncwarp();
+        if (lane == 0) {
+            uint32_t prev;
+            asm volatile("atom.acq_rel.cta.shared::cta.add.u32 %0, [%1], 1;"
+                         : "=r"(prev)
+                         : "r"(smem_u32(&released[s]))
+                         : "memory");
+            if (prev == kWarps - 1) {
+                released[s] = 0;
+                const int cn = c + kStages;
+                if (cn < chunks && !abort_flag) {
+                    fence_proxy_async_smem();  // the generic reads of the slot before the copies into it
+                    issue_a(cn);
+                    issue_x(cn);
+                    atomicMax(&issued_total, cn + 1);
+                }
             }
         }
     }
-    cp_async_wait<0>();
 
     // Accumulator layout: thread holds rows g, g + 8 (g = lane / 4) and
     // columns 2 (lane % 4), +1 of each n8 tile.
     const int g = lane >> 2;
     const int cq = 2 * (lane & 3);
+    if (ok) {
 #pragma unroll
-    for (int t = 0; t < kTiles; ++t) {
-        const int col = kCols * warp + 8 * t + cq;
+        for (int t = 0; t < kTiles; ++t) {
+            const int col = kCols * warp + 8 * t + cq;
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            const int64_t row = m0 + g + 8 * h;
-            if (row < M) {
-                const __nv_bfloat162 v = __floats2bfloat162_rn(acc[t][2 * h], acc[t][2 * h + 1]);
-                *reinterpret_cast<__nv_bfloat162*>(xa + row * R + col) = v;
+            for (int h = 0; h < 2; ++h) {
+                const int64_t row = m0 + g + 8 * h;
+                if (row < M) {
+                    const __nv_bfloat162 v = __floats2bfloat162_rn(acc[t][2 * h], acc[t][2 * h + 1]);
+                    *reinterpret_cast<__nv_bfloat162*>(xa + row * R + col) = v;
+                }
             }
         }
     }
+    // Copies in flight land before the CTA exits (bounded).
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const int issued = issued_total;
+        for (int c = issued > kStages ? issued - kStages : 0; c < issued; ++c)
+            mbar_wait_drain(smem_u32(&full[c % kStages]), static_cast<uint32_t>((c / kStages) & 1));
+    }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 lora_encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult qr{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &qr) == cudaSuccess &&
+            qr == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    });
+    return fn;
+}
+
+// 2-D bf16 tensor map [outer][inner] with a [box_outer][box_inner] box
+// (box_inner 64 with the 128-byte swizzle, 32 with the 64-byte swizzle).
+bool lora_map(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint32_t box_inner,
+              uint32_t box_outer) {
+    auto fn = lora_encode_fn();
+    if (!fn) return false;
+    const cuuint64_t dims[2] = {inner, outer};
+    const cuuint64_t strides[1] = {inner * 2};
+    const cuuint32_t box[2] = {box_inner, box_outer};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUtensorMapSwizzle sw = box_inner == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 template <int R>
@@ -179,9 +266,19 @@ int launch_r(const uint16_t* x, const uint16_t* a, uint16_t* xa, int64_t M, int6
         attr_set_for_device[dev].store(true, std::memory_order_release);
     }
     const int64_t blocks = (M + kRowsPerCta - 1) / kRowsPerCta;
-    if (blocks > 0x7fffffff) return Q6_ERR_UNSUPPORTED;
+    if (blocks > 0x7fffffff || M > 0x7fffffff) return Q6_ERR_UNSUPPORTED;
+    // boxes no larger than the tensor: x rows past M stay unwritten (their
+    // products land in accumulator rows that are never stored)
+    const uint32_t x_rows = static_cast<uint32_t>(M < kRowsPerCta ? M : kRowsPerCta);
+    CUtensorMap tx, ta, tt;
+    if (!lora_map(&tx, x, static_cast<uint64_t>(K), static_cast<uint64_t>(M), 64, x_rows) ||
+        (C::kABoxes > 0 && !lora_map(&ta, a, static_cast<uint64_t>(R), static_cast<uint64_t>(K), 64, kBK)) ||
+        (C::kTail && !lora_map(&tt, a, static_cast<uint64_t>(R), static_cast<uint64_t>(K), 32, kBK)))
+        return Q6_ERR_CUDA;
+    if (C::kABoxes == 0) ta = tt;
+    if (!C::kTail) tt = ta;
     const cudaError_t e = launch_pdl(lora_xa_kernel<R>, dim3(static_cast<unsigned>(blocks)), dim3(kThreads),
-                                     C::kSmemBytes, stream, x, a, xa, M, K);
+                                     C::kSmemBytes, stream, tx, ta, tt, xa, M, K, x_rows * 128u);
     return e == cudaSuccess ? Q6_OK : Q6_ERR_CUDA;
 }
 

@@ -211,3 +211,42 @@ def test_sequence_parallel_block_gloo_world4_two_samples():
     16 rows, one starting in a sample's text rows, one in its image rows."""
 
     mp.spawn(_worker, args=(4, _free_port(), 2), nprocs=4, join=True)
+
+
+class _StubBlock:
+    """A block whose modulation vectors are a known function of its index."""
+
+    def __init__(self, i: int, d: int) -> None:
+        self.i, self.dim = i, d
+
+    def modulation_joint(self, temb: torch.Tensor) -> torch.Tensor:
+        b = temb.shape[0]
+        base = torch.arange(b * 2 * 6 * self.dim, dtype=torch.float32).reshape(b, 2, 6, self.dim)
+        return (base * 0.001 + self.i + temb.float().sum()).to(torch.bfloat16)
+
+
+def _mod_worker(rank: int, world: int, port: int, n: int) -> None:
+    import torch.distributed as dist
+
+    from qwen_image_shardedit_mlx_b200.block import stack_modulations
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        d = 16
+        blocks = [_StubBlock(i, d) for i in range(n)]
+        temb = torch.full((2, d), 0.25, dtype=torch.bfloat16)
+        got = stack_modulations(blocks, temb, world, rank)
+        assert got.shape == (n, 2, 2, 6, d)
+        for i, blk in enumerate(blocks):
+            assert torch.equal(got[i], blk.modulation_joint(temb)), (rank, i)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_stack_modulations_split_over_ranks_gloo():
+    """Every rank ends with every block's modulation vectors, each computed
+    once somewhere (7 blocks over 4 ranks leave the last rank a short run)."""
+
+    mp.spawn(_mod_worker, args=(4, _free_port(), 7), nprocs=4, join=True)

@@ -104,15 +104,17 @@ def test_config1_gemv_rows_and_tensor_rows_agree():
 
     rng = np.random.default_rng(17)
     w, ow = _gpu_weights(1717, 12288, 3072, 64, bias=False)
-    for m in (1, 2, 4):
+    for m in (1, 2, 4):  # the auto path: the GEMV for 1-2 rows, the tensor core from 3
         x = random_bf16(rng, (m, 3072))
         got = ops.q6_linear(from_bits(x), *w, group_size=64)
         torch.cuda.synchronize()
-        ref = oracle.linear(oracle.bf16_bits_to_f32(x), ow, weight_dtype="f32")
+        assert ops.last_path() == ("simt" if m <= 2 else "tensor")
+        ref = oracle.linear(oracle.bf16_bits_to_f32(x), ow, weight_dtype="f32" if m <= 2 else "bf16")
         assert_close(f32(got), ref, what=f"config-1 weight, {m} rows")
 
 
-@pytest.mark.parametrize("m,k,r", [(3456, 3072, 64), (37, 256, 32), (130, 12288, 256), (1000, 1040, 96)])
+@pytest.mark.parametrize("m,k,r", [(3456, 3072, 64), (37, 256, 32), (130, 12288, 256), (1000, 1040, 96),
+                                   (5, 192, 128), (16, 64, 160)])
 def test_lora_prepass_kernel(m, k, r):
     """xa = x @ A by the library's pre-pass kernel against float64, rounded to
     bf16 once (fp32 accumulation: a few bf16 units at most)."""
