@@ -526,10 +526,14 @@ def measure_block(dev, world: int, rank: int, steps: int = 10, comm: str = "peer
         rows_local = x.shape[0] // world
         x_local = x[rank * rows_local:(rank + 1) * rows_local].contiguous()
         one = lambda: full.forward_joint(x, temb, rope_j, batch, BLOCK_TXT, out=y)  # noqa: E731
-        ms_tp1 = None
+        ms_tp1 = ms_one_stream = None
         if tp is None:
             ms, eager_ms = _graph_ms(one, world, steps)
             ms_1 = ms
+            # both streams' GEMMs in order on one CUDA stream (no fork / join)
+            full.overlap_streams = False
+            ms_one_stream, _ = _graph_ms(one, 1, steps)
+            full.overlap_streams = True
             # the tensor-parallel form on one rank: the cost of its structure alone
             tp1 = TensorParallelQwenBlock(full, 1, 0, comm=comm)
             ms_tp1, _ = _graph_ms(lambda: tp1.finish(tp1.forward_local(x, temb, rope_j, batch, seq, BLOCK_TXT)),
@@ -554,6 +558,7 @@ def measure_block(dev, world: int, rank: int, steps: int = 10, comm: str = "peer
             "comm": comm if world > 1 else None,
             "ms_other_comm": None if world == 1 else round(ms_other, 4),
             "ms_tp_form_1gpu": None if ms_tp1 is None else round(ms_tp1, 4),
+            "ms_one_stream_1gpu": None if ms_one_stream is None else round(ms_one_stream, 4),
             "efficiency_vs_1gpu": None if ms_1 is None else round(ms_1 / (world * ms), 4),
             "batch": batch, "flop_per_call": flop,
         }
@@ -574,7 +579,9 @@ def measure_block(dev, world: int, rank: int, steps: int = 10, comm: str = "peer
         "note": "device time per block forward replayed from a CUDA graph (eager_ms: launched from Python each "
                 "time); CUDA events, max over ranks; attention is the library scaled_dot_product_attention kernel; "
                 "ms_1gpu is the same block on one GPU timed on rank 0 in the same run; ms_tp_form_1gpu (one GPU "
-                "only) is the tensor-parallel form run on a single rank, the cost of its layout and kernels alone",
+                "only) is the tensor-parallel form run on a single rank, the cost of its layout and kernels alone; "
+                "ms_one_stream_1gpu runs the text- and image-stream GEMMs in order on one CUDA stream instead of "
+                "overlapping them on two",
     })
     return res
 
@@ -901,8 +908,11 @@ def measure_sweep(dev, peaks) -> dict:
             else:
                 y.add_(bias)
 
-        def fused(i, x=x, w=w, s=s, b=b, bias=bias, y=y, gelu=gelu, a_l=a_l, b_l=b_l):
-            ops.q6_linear(x, w, s, b, bias, group_size=64, apply_gelu=gelu, lora=(a_l, b_l, 1.0), out=y)
+        b_t = b_l.t().contiguous()  # what QuantizedLinear.set_lora keeps beside B: [N, r]
+
+        def fused(i, x=x, w=w, s=s, b=b, bias=bias, y=y, gelu=gelu, a_l=a_l, b_l=b_l, b_t=b_t):
+            ops.q6_linear(x, w, s, b, bias, group_size=64, apply_gelu=gelu, lora=(a_l, b_l, 1.0), lora_b_nmajor=b_t,
+                          out=y)
 
         t_plain = _time_launches(plain, 8)
         t_unf = _time_launches(unfused, 8)

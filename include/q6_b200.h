@@ -47,12 +47,15 @@ enum q6_status {
     Q6_ERR_WORKSPACE = 8         /* workspace missing or too small            */
 };
 
-/* Epilogue flags (bit set). */
+/* Epilogue and operand flags (bit set). */
 enum q6_epilogue {
     Q6_EPI_NONE = 0,
-    Q6_EPI_GELU = 1,        /* GELU-tanh after the bias (mlx nn.gelu_approx), hardware tanh.approx */
-    Q6_EPI_GELU_PRECISE = 2 /* the same GELU with the IEEE-accurate tanhf the reference kernel
-                               calls (metal::precise::tanh, q6_metal_mlp.py:21-26); implies GELU */
+    Q6_EPI_GELU = 1,         /* GELU-tanh after the bias (mlx nn.gelu_approx), hardware tanh.approx */
+    Q6_EPI_GELU_PRECISE = 2, /* the same GELU with the IEEE-accurate tanhf the reference kernel
+                                calls (metal::precise::tanh, q6_metal_mlp.py:21-26); implies GELU */
+    Q6_LORA_B_NMAJOR = 4     /* q6_linear_bf16 only: lora_b is laid out [N, r] (B transposed, each
+                                output row's r values contiguous, 16-byte aligned), which the
+                                fused LoRA stages read with 16-byte loads */
 };
 
 /* Site codes a kernel writes into the device error word when one of its
@@ -86,8 +89,9 @@ Q6_API int q6_dequantize_bf16(const uint32_t* w, const uint16_t* scales, const u
  * epi: + bias[n] (if bias), GELU (if flags & Q6_EPI_GELU, or with an accurate tanh if
  *      flags & Q6_EPI_GELU_PRECISE), then
  *      y = residual[m,n] + gate[n] * value  (each term only if its pointer is non-null).
- * LoRA (lora_xa bf16 [M, r] = x @ A computed by the caller, lora_b bf16 [r, N],
- *      both non-null, r a multiple of 32 in [32, 256]): the value gains
+ * LoRA (lora_xa bf16 [M, r] = x @ A computed by the caller, lora_b bf16 [r, N], or
+ *      [N, r] with flags & Q6_LORA_B_NMAJOR, both non-null, r a multiple of 32 in
+ *      [32, 256]): the value gains
  *      lora_scale * (lora_xa @ lora_b) before the bias, accumulated in the same
  *      fp32 tile as the q6 product (tensor-core path; Q6_PATH_SIMT returns
  *      Q6_ERR_UNSUPPORTED).

@@ -25,6 +25,7 @@ Q6_ERR_WORKSPACE = 8
 Q6_EPI_NONE = 0
 Q6_EPI_GELU = 1
 Q6_EPI_GELU_PRECISE = 2
+Q6_LORA_B_NMAJOR = 4
 
 Q6_SITE_PEER_BARRIER = 13
 Q6_SITE_SELFTEST = 64

@@ -133,6 +133,8 @@ def rope_tables(img_angles: torch.Tensor, txt_angles: torch.Tensor, device: torc
 class QwenTransformerBlock(torch.nn.Module):
     """Dual-stream MMDiT block: q6 linears by reference name, bf16 norm weights."""
 
+    overlap_streams = True  # text- and image-stream GEMMs on two CUDA streams (both_streams)
+
     def __init__(self, linears: dict[str, QuantizedLinear], norms: dict[str, torch.Tensor], *,
                  heads: int, eps: float = 1e-6) -> None:
         super().__init__()
@@ -172,26 +174,32 @@ class QwenTransformerBlock(torch.nn.Module):
         dim = block.linears["attn.to_q"].out_features
         return cls(dict(block.linears), norms, heads=heads or dim // HEAD_DIM)
 
-    def _workspace(self, m: int, h: int, d: int, device: torch.device) -> torch.Tensor:
+    def _workspace(self, m: int, h: int, d: int, device: torch.device, slot: int = 0) -> torch.Tensor:
+        """MLP workspace; one per stream that runs MLPs concurrently (``slot``)."""
+
         need = int(ops.mlp_workspace_bytes(m, h, d))
-        if self._ws is None or self._ws.numel() < need or self._ws.device != device:
-            self._ws = torch.empty(need, dtype=torch.uint8, device=device)
-        return self._ws
+        slots = self.__dict__.setdefault("_ws_slots", {})
+        ws = slots.get(slot)
+        if ws is None or ws.numel() < need or ws.device != device:
+            ws = torch.empty(need, dtype=torch.uint8, device=device)
+            slots[slot] = ws
+        return ws
 
     def _linear(self, name: str, x: torch.Tensor, **kw) -> torch.Tensor:
         lin = self.linears[name]
         return ops.q6_linear(x, lin.weight, lin.scales, lin.biases, lin.bias, group_size=lin.group_size,
-                             lora=lin.lora, **kw)
+                             lora=lin.lora, lora_b_nmajor=getattr(lin, "lora_b_nmajor", None), **kw)
 
     def _mlp(self, prefix: str, x: torch.Tensor, residual: torch.Tensor | None, gate: torch.Tensor,
-             out: torch.Tensor) -> torch.Tensor:
+             out: torch.Tensor, slot: int = 0) -> torch.Tensor:
         l1, l2 = self.linears[f"{prefix}.mlp_in"], self.linears[f"{prefix}.mlp_out"]
         if l1.lora is not None or l2.lora is not None:
             mid = ops.q6_linear(x, l1.weight, l1.scales, l1.biases, l1.bias, group_size=l1.group_size,
-                                apply_gelu=True, lora=l1.lora)
+                                apply_gelu=True, lora=l1.lora, lora_b_nmajor=getattr(l1, "lora_b_nmajor", None))
             return ops.q6_linear(mid, l2.weight, l2.scales, l2.biases, l2.bias, group_size=l2.group_size,
-                                 residual=residual, gate=gate, lora=l2.lora, out=out)
-        ws = self._workspace(x.shape[0], l1.out_features, l1.in_features, x.device)
+                                 residual=residual, gate=gate, lora=l2.lora, out=out,
+                                 lora_b_nmajor=getattr(l2, "lora_b_nmajor", None))
+        ws = self._workspace(x.shape[0], l1.out_features, l1.in_features, x.device, slot)
         return ops.q6_mlp(x, (l1.weight, l1.scales, l1.biases, l1.bias), (l2.weight, l2.scales, l2.biases, l2.bias),
                           group_size=l1.group_size, residual=residual, gate=gate, workspace=ws, out=out)
 
@@ -227,17 +235,30 @@ class QwenTransformerBlock(torch.nn.Module):
         vec = ModulationVectors(self.modulation_joint(temb))
         z = add_layernorm_modulate(x, vec.shift1, vec.scale1, seq_len=seq, text_len=text_len, eps=self.eps)
         qkv = torch.empty((rows, 3 * d), dtype=torch.bfloat16, device=x.device)
-        project_qkv_joint(self, z, qkv, batch, seq, text_len)
+        both_streams(self, x.device,
+                     lambda: project_qkv_joint(self, z, qkv, batch, seq, text_len, which=0),
+                     lambda: project_qkv_joint(self, z, qkv, batch, seq, text_len, which=1))
         rope_qk_joint(self, qkv, d, rope_joint, seq, text_len)
         att = batched_joint_attention(qkv, d, batch, seq, self.heads, text_len, text_mask)
         h = torch.empty_like(x)
-        for b, stream, r in segments(batch, seq, text_len):
-            name = "attn.to_add_out" if stream == 0 else "attn.attn_to_out.0"
-            self._linear(name, att[r], residual=x[r], gate=vec.gate1(b, stream), out=h[r])
+
+        def out_proj(which: int) -> None:
+            for b, stream, r in segments(batch, seq, text_len):
+                if stream == which:
+                    name = "attn.to_add_out" if stream == 0 else "attn.attn_to_out.0"
+                    self._linear(name, att[r], residual=x[r], gate=vec.gate1(b, stream), out=h[r])
+
+        both_streams(self, x.device, lambda: out_proj(0), lambda: out_proj(1))
         z2 = add_layernorm_modulate(h, vec.shift2, vec.scale2, seq_len=seq, text_len=text_len, eps=self.eps)
         y = out if out is not None else torch.empty_like(x)
-        for b, stream, r in segments(batch, seq, text_len):
-            self._mlp("txt_ff" if stream == 0 else "img_ff", z2[r], h[r], vec.gate2(b, stream), y[r])
+
+        def ff(which: int) -> None:
+            for b, stream, r in segments(batch, seq, text_len):
+                if stream == which:
+                    self._mlp("txt_ff" if stream == 0 else "img_ff", z2[r], h[r], vec.gate2(b, stream), y[r],
+                              slot=stream)
+
+        both_streams(self, x.device, lambda: ff(0), lambda: ff(1))
         return y
 
     def forward(self, hidden: torch.Tensor, encoder: torch.Tensor, temb: torch.Tensor,
@@ -452,15 +473,44 @@ def fused_rows(owner: torch.nn.Module, names: tuple[str, ...]) -> QuantizedLinea
     return fused
 
 
+def both_streams(owner, device: torch.device, text_fn, image_fn) -> None:
+    """Run a stage's text-stream launches (``text_fn``) and image-stream
+    launches (``image_fn``), which touch disjoint rows and weights, on two CUDA
+    streams: the text work on a side stream that first waits for everything
+    queued so far, the image work on the caller's stream, which then waits
+    for the side stream.  The small text GEMMs (256 rows) fill SMs that the
+    image GEMM's last wave leaves idle.  With ``owner.overlap_streams`` False
+    both run in order on the caller's stream.  CUDA graph capture records the
+    fork and the join."""
+
+    if not getattr(owner, "overlap_streams", True):
+        text_fn()
+        image_fn()
+        return
+    side = owner.__dict__.get("_side_stream")
+    if side is None or side.device != device:
+        side = torch.cuda.Stream(device)
+        owner.__dict__["_side_stream"] = side
+    main = torch.cuda.current_stream(device)
+    side.wait_stream(main)
+    with torch.cuda.stream(side):
+        text_fn()
+    image_fn()
+    main.wait_stream(side)
+
+
 def project_qkv_joint(owner: torch.nn.Module, z: torch.Tensor, qkv: torch.Tensor, batch: int, seq: int,
-                      text_len: int) -> None:
+                      text_len: int, which: int | None = None) -> None:
     """q, k, v of every joint row into qkv [B * S, 3 * width]: one GEMM per
     (sample, stream) of the stream's concatenated projections (``fused_rows``);
-    a stream with a LoRA delta on one of them runs its three GEMMs and copies."""
+    a stream with a LoRA delta on one of them runs its three GEMMs and copies.
+    ``which`` (0 text, 1 image) limits the launches to one stream."""
 
     fused = {0: fused_rows(owner, _TXT_QKV), 1: fused_rows(owner, _IMG_QKV)}
     width = qkv.shape[1] // 3
     for _, stream, r in segments(batch, seq, text_len):
+        if which is not None and stream != which:
+            continue
         f = fused[stream]
         if f is not None:
             ops.q6_linear(z[r], f.weight, f.scales, f.biases, f.bias, group_size=f.group_size, out=qkv[r])
@@ -534,6 +584,7 @@ class TensorParallelQwenBlock(torch.nn.Module):
             self.linears[name] = cols(name)
         self._ws: torch.Tensor | None = None
 
+    overlap_streams = True  # text- and image-stream GEMMs on two CUDA streams (both_streams)
     _linear = QwenTransformerBlock._linear
     _workspace = QwenTransformerBlock._workspace
     _mlp = QwenTransformerBlock._mlp
@@ -628,13 +679,20 @@ class TensorParallelQwenBlock(torch.nn.Module):
         z = pr.buffers["gather1"]
         rows = z.shape[0]
         qkv = torch.empty((rows, 3 * dl), dtype=torch.bfloat16, device=z.device)
-        project_qkv_joint(self, z, qkv, batch, seq, text_len)
+        both_streams(self, z.device,
+                     lambda: project_qkv_joint(self, z, qkv, batch, seq, text_len, which=0),
+                     lambda: project_qkv_joint(self, z, qkv, batch, seq, text_len, which=1))
         rope_qk_joint(self, qkv, dl, rope_joint, seq, text_len)
         att = batched_joint_attention(qkv, dl, batch, seq, self.heads_local, text_len, text_mask)
         part = pr.buffers["part1"]
-        for b, stream, r in segments(batch, seq, text_len):
-            name = "attn.to_add_out" if stream == 0 else "attn.attn_to_out.0"
-            self._linear(name, att[r], gate=vec.gate1(b, stream), out=part[r])
+
+        def out_proj(which: int) -> None:
+            for b, stream, r in segments(batch, seq, text_len):
+                if stream == which:
+                    name = "attn.to_add_out" if stream == 0 else "attn.attn_to_out.0"
+                    self._linear(name, att[r], gate=vec.gate1(b, stream), out=part[r])
+
+        both_streams(self, z.device, lambda: out_proj(0), lambda: out_proj(1))
         pr.barrier()
         h_local = torch.empty_like(x_local)
         pr.add_ln_gather(x_local, vec.shift2, vec.scale2, dst="gather2", partials="part1", h_out=h_local,
@@ -642,8 +700,14 @@ class TensorParallelQwenBlock(torch.nn.Module):
         pr.barrier()
         z2 = pr.buffers["gather2"]
         part2 = pr.buffers["part2"]
-        for b, stream, r in segments(batch, seq, text_len):
-            self._mlp("txt_ff" if stream == 0 else "img_ff", z2[r], None, vec.gate2(b, stream), part2[r])
+
+        def ff(which: int) -> None:
+            for b, stream, r in segments(batch, seq, text_len):
+                if stream == which:
+                    self._mlp("txt_ff" if stream == 0 else "img_ff", z2[r], None, vec.gate2(b, stream), part2[r],
+                              slot=stream)
+
+        both_streams(self, z2.device, lambda: ff(0), lambda: ff(1))
         pr.barrier()
         return h_local, "part2"
 

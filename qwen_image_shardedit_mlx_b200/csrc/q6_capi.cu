@@ -120,10 +120,11 @@ int q6_linear_bf16(const uint16_t* x, const uint32_t* w, const uint16_t* scales,
     int st = check_weights(w, scales, qbiases, N, K, group_size);
     if (st != Q6_OK) return st;
     if (!x || !y || M <= 0) return Q6_ERR_INVALID_ARGUMENT;
-    if ((flags & ~kEpiFlags) != 0) return Q6_ERR_INVALID_ARGUMENT;
+    if ((flags & ~(kEpiFlags | Q6_LORA_B_NMAJOR)) != 0) return Q6_ERR_INVALID_ARGUMENT;
     if (flags & Q6_EPI_GELU_PRECISE) flags |= Q6_EPI_GELU;  // the precise flag implies GELU
     if ((lora_xa == nullptr) != (lora_b == nullptr)) return Q6_ERR_INVALID_ARGUMENT;
     if (lora_xa && lora_rank <= 0) return Q6_ERR_INVALID_ARGUMENT;
+    if ((flags & Q6_LORA_B_NMAJOR) && (!lora_b || !aligned(lora_b, 16))) return Q6_ERR_INVALID_ARGUMENT;
     q6::LinearArgs a{x, w, scales, qbiases, bias, residual, gate, y, M, N, K, group_size, flags};
     if (lora_xa) {
         a.lora_xa = lora_xa;

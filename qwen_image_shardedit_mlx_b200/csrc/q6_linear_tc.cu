@@ -149,6 +149,7 @@ struct TcParams {
     const uint16_t* lora_b;
     float lora_scale;
     int lora_rank, lora_stages, lora_ksteps;
+    int lora_b_nmajor;  // lora_b is [N, r]: 16-byte loads of an output row's rank values
     SpliceExp3 sexp;  // splice exponent words, runtime values so each splice is one instruction
     // Split-K: work item it covers tile it / ksplit and the q6 stages
     // [s * ks_per, min((s + 1) * ks_per, k_stages)) of split s = it % ksplit
@@ -777,15 +778,34 @@ __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
 #pragma unroll 1
                 for (int hh = 0; hh < 2; ++hh) {
                     uint32_t a[16];
+                    if (p.lora_b_nmajor) {
+                        // B^T row n: the 32 rank values of this slice are contiguous (four
+                        // 16-byte loads); half_r is a multiple of 16, so an 8-value chunk
+                        // lies wholly inside or outside the stage's rank range
+                        const uint16_t* src =
+                            p.lora_b + static_cast<size_t>(n_ok ? n : 0) * p.lora_rank + j0 + half * 64 + hh * 32;
 #pragma unroll
-                    for (int i = 0; i < 16; ++i) {
-                        const int k = half * 64 + hh * 32 + 2 * i;  // stage-local K of the pair
-                        float v0 = 0.0f, v1 = 0.0f;
-                        if (n_ok && k < half_r)
-                            v0 = p.lora_scale * bf16f(p.lora_b[static_cast<size_t>(j0 + k) * p.N + n]);
-                        if (n_ok && k + 1 < half_r)
-                            v1 = p.lora_scale * bf16f(p.lora_b[static_cast<size_t>(j0 + k + 1) * p.N + n]);
-                        a[i] = pack_bf16x2(v0, v1);
+                        for (int c8 = 0; c8 < 4; ++c8) {
+                            const int k = half * 64 + hh * 32 + 8 * c8;
+                            uint4 v = make_uint4(0u, 0u, 0u, 0u);
+                            if (n_ok && k < half_r) v = __ldg(reinterpret_cast<const uint4*>(src + 8 * c8));
+                            const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                            for (int i = 0; i < 4; ++i)
+                                a[4 * c8 + i] = pack_bf16x2(p.lora_scale * bf16f(static_cast<uint16_t>(w[i] & 0xFFFFu)),
+                                                            p.lora_scale * bf16f(static_cast<uint16_t>(w[i] >> 16)));
+                        }
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) {
+                            const int k = half * 64 + hh * 32 + 2 * i;  // stage-local K of the pair
+                            float v0 = 0.0f, v1 = 0.0f;
+                            if (n_ok && k < half_r)
+                                v0 = p.lora_scale * bf16f(p.lora_b[static_cast<size_t>(j0 + k) * p.N + n]);
+                            if (n_ok && k + 1 < half_r)
+                                v1 = p.lora_scale * bf16f(p.lora_b[static_cast<size_t>(j0 + k + 1) * p.N + n]);
+                            a[i] = pack_bf16x2(v0, v1);
+                        }
                     }
                     tmem_st_32x32b_x16(tmem_base + lane_base +
                                            static_cast<uint32_t>(C::kAccCols + as * kAColsPerStage + half * 32 + hh * 16),
@@ -1069,6 +1089,7 @@ int launch_tc(const LinearArgs& a, cudaStream_t stream) {
     p.lora_rank = a.lora_rank;
     p.lora_stages = a.lora_rank > 0 ? 2 : 0;
     p.lora_ksteps = a.lora_rank / 32;
+    p.lora_b_nmajor = (a.flags & Q6_LORA_B_NMAJOR) ? 1 : 0;
     p.sexp = splice_exp3_host();
     const KSplit ksp = kPair ? KSplit{1, p.k_stages} : plan_ksplit(a.M, a.N, a.K, NT, kSbTma ? (1 << p.sb_shift) : 1);
     const size_t need = static_cast<size_t>(ksp.splits) * a.M * a.N * sizeof(float);

@@ -106,6 +106,7 @@ def q6_linear(
     path: str = "auto",
     out: torch.Tensor | None = None,
     precise_gelu: bool = False,
+    lora_b_nmajor: torch.Tensor | None = None,
 ) -> torch.Tensor:
     """y = epilogue(x @ dequant(W)^T) for x [..., K]; returns [..., N].
 
@@ -114,7 +115,10 @@ def q6_linear(
     the CUDA-core path with fp32 weights and returns fp32.
     Epilogue order: + bias, GELU, then residual + gate * value.  The tensor
     path's GELU takes the hardware tanh approximation unless ``precise_gelu``
-    asks for the accurate tanh the reference kernel uses.
+    asks for the accurate tanh the reference kernel uses.  ``lora_b_nmajor``
+    (optional) is the LoRA B transposed to [N, r_padded] (``lora_b_nmajor``
+    of a ``QuantizedLinear``), which the fused LoRA stages read with 16-byte
+    loads.
     """
 
     n, k = check_q6_weights(weight, scales, biases, group_size)
@@ -165,6 +169,11 @@ def q6_linear(
             raise ValueError(f"LoRA rank {rank} exceeds the fused maximum {MAX_FUSED_RANK}")
         la, lb = pad_lora_rank(la, lb)  # the kernel takes ranks in steps of 32
         rank = int(la.shape[1])
+        if (lora_b_nmajor is not None and tuple(lora_b_nmajor.shape) == (n, rank)
+                and lora_b_nmajor.dtype == torch.bfloat16 and lora_b_nmajor.is_contiguous()
+                and lora_b_nmajor.device == lb.device and lora_b_nmajor.data_ptr() % 16 == 0):
+            lb = lora_b_nmajor
+            flags |= _lib.Q6_LORA_B_NMAJOR
         # x @ A (fp32 accumulation, bf16 result, as the reference's LoRA
         # linear computes it) by the library's pre-pass kernel; the q6 kernel
         # then fuses s * (xa @ B) into its own accumulator.

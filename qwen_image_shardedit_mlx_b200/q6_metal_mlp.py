@@ -35,7 +35,7 @@ import torch
 import torch.nn.functional as F
 
 from qwen_image_shardedit_mlx_b200 import ops
-from qwen_image_shardedit_mlx_b200.lora import LoRAAdapter, fold_lora_adapters
+from qwen_image_shardedit_mlx_b200.lora import LoRAAdapter, fold_lora_adapters, pad_lora_rank
 from qwen_image_shardedit_mlx_b200.quantize import quantize_affine_q6
 
 
@@ -76,6 +76,7 @@ class QuantizedLinear(torch.nn.Module):
         self.mode = "affine"
         self.loras: list[LoRAAdapter] = []
         self.lora: tuple[torch.Tensor, torch.Tensor, float] | None = None  # the fused delta of ``loras``
+        self.lora_b_nmajor: torch.Tensor | None = None  # its B transposed, [N, r padded to 32]
 
     @classmethod
     def from_linear(cls, linear: torch.nn.Linear, *, bits: int = 6, group_size: int = 64) -> "QuantizedLinear":
@@ -104,6 +105,7 @@ class QuantizedLinear(torch.nn.Module):
         if a is None:
             self.loras = []
             self.lora = None
+            self.lora_b_nmajor = None
             return
         if b is None:
             raise ValueError("LoRA needs both A and B")
@@ -119,10 +121,13 @@ class QuantizedLinear(torch.nn.Module):
         adapters = [*self.loras, ad]
         self.lora = fold_lora_adapters(adapters, in_features=self.in_features, out_features=self.out_features)
         self.loras = adapters
+        # the fused kernel reads B one output row at a time: keep it transposed too
+        _, b_pad = pad_lora_rank(self.lora[0], self.lora[1])
+        self.lora_b_nmajor = b_pad.t().contiguous()
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         return ops.q6_linear(x, self.weight, self.scales, self.biases, self.bias, group_size=self.group_size,
-                             lora=self.lora)
+                             lora=self.lora, lora_b_nmajor=self.lora_b_nmajor)
 
 
 def quantized_linear_spec(layer: torch.nn.Module) -> Q6LinearSpec:
@@ -260,7 +265,8 @@ class QwenFeedForward(torch.nn.Module):
         if self.mlp_in.lora is not None or self.mlp_out.lora is not None:
             # LoRA-carrying layers: each linear fuses its own delta
             mid = ops.q6_linear(hidden, self.mlp_in.weight, self.mlp_in.scales, self.mlp_in.biases, self.mlp_in.bias,
-                                group_size=self.mlp_in.group_size, apply_gelu=True, lora=self.mlp_in.lora)
+                                group_size=self.mlp_in.group_size, apply_gelu=True, lora=self.mlp_in.lora,
+                                lora_b_nmajor=self.mlp_in.lora_b_nmajor)
             return self.mlp_out(mid)
         return fused_q6_mlp(hidden, quantized_linear_spec(self.mlp_in), quantized_linear_spec(self.mlp_out))
 

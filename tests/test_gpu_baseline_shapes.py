@@ -139,10 +139,32 @@ def test_lora_rank64_image_ff_width():
     b_bits = random_bf16(rng, (r, n), 0.01)
     got = ops.q6_linear(from_bits(x), *w, group_size=64, apply_gelu=True,
                         lora=(from_bits(a_bits), from_bits(b_bits), 1.0))
+    # B also given transposed ([N, r]: the fused stages' 16-byte row loads): the same bits
+    got_t = ops.q6_linear(from_bits(x), *w, group_size=64, apply_gelu=True,
+                          lora=(from_bits(a_bits), from_bits(b_bits), 1.0),
+                          lora_b_nmajor=from_bits(b_bits).t().contiguous())
     torch.cuda.synchronize()
+    assert torch.equal(got, got_t)
     rows = _sample_rows(rng, m, 24)
     lora = (oracle.bf16_bits_to_f32(a_bits), oracle.bf16_bits_to_f32(b_bits), 1.0)
     _check_rows(got, x, ow, rows, apply_gelu=True, lora=lora)
+
+
+@pytest.mark.parametrize("r,scale", [(32, 0.5), (96, 2.0), (256, 1.0)])
+def test_lora_nmajor_b_matches_row_major(r, scale):
+    """The [N, r] LoRA B layout (Q6_LORA_B_NMAJOR) against the [r, N] one: same
+    bits, including ranks whose second LoRA stage is partly padding."""
+
+    rng = np.random.default_rng(r)
+    m, n, k = 300, 1000, 512
+    w, _ = _gpu_weights(r + 1, n, k, 64, bias=True)
+    x = from_bits(random_bf16(rng, (m, k)))
+    a = from_bits(random_bf16(rng, (k, r), 0.05))
+    b = from_bits(random_bf16(rng, (r, n), 0.05))
+    want = ops.q6_linear(x, *w, group_size=64, lora=(a, b, scale))
+    got = ops.q6_linear(x, *w, group_size=64, lora=(a, b, scale), lora_b_nmajor=b.t().contiguous())
+    torch.cuda.synchronize()
+    assert torch.equal(got, want)
 
 
 @pytest.mark.parametrize("path,m", [("tensor", 16), ("tensor", 64), ("simt", 1), ("simt", 3)])

@@ -420,3 +420,38 @@ def test_tensor_parallel_block_over_nccl_world2():
     r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=300)
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
     assert r.stdout.count("OK") == 2
+
+
+def test_two_stream_block_matches_one_stream():
+    """The text- and image-stream launches on two CUDA streams give the same
+    bits as both in order on one stream (batch 2, so each stage forks four
+    GEMMs over two streams), eagerly and replayed from a CUDA graph."""
+
+    from qwen_image_shardedit_mlx_b200.block import QwenTransformerBlock, joint_rope
+
+    g = torch.Generator(device="cuda").manual_seed(44)
+    blk = QwenTransformerBlock.random(512, 4, generator=g)
+    x = torch.randn((2 * (96 + 24), 512), generator=g, device="cuda").to(torch.bfloat16)
+    temb = torch.randn((2, 512), generator=g, device="cuda").to(torch.bfloat16)
+    ia, ta = qwen_rope_angles([(8, 12)], 24)
+    rope = joint_rope(rope_tables(ia, ta, "cuda"))
+    blk.overlap_streams = False
+    ref = blk.forward_joint(x, temb, rope, 2, 24)
+    blk.overlap_streams = True
+    got = blk.forward_joint(x, temb, rope, 2, 24)
+    torch.cuda.synchronize()
+    assert torch.equal(got, ref)
+    out = torch.empty_like(x)
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        blk.forward_joint(x, temb, rope, 2, 24, out=out)
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        blk.forward_joint(x, temb, rope, 2, 24, out=out)
+    out.zero_()
+    graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(out, ref)
+    del graph
