@@ -66,7 +66,9 @@ def test_argument_validation_without_gpu():
     assert _linear(lib, gs=16) == _lib.Q6_ERR_GROUP_SIZE
     assert _linear(lib, K=96, gs=64) == _lib.Q6_ERR_SHAPE
     assert _linear(lib, flags=8) == _lib.Q6_ERR_INVALID_ARGUMENT
-    assert _linear(lib, flags=4) == _lib.Q6_ERR_INVALID_ARGUMENT
+    assert _linear(lib, flags=4) == _lib.Q6_ERR_INVALID_ARGUMENT  # transposed LoRA B without a LoRA
+    assert _linear(lib, flags=16) == _lib.Q6_ERR_INVALID_ARGUMENT
+    assert _linear(lib, flags=4, lora_xa=256, lora_b=264, rank=64) == _lib.Q6_ERR_INVALID_ARGUMENT  # B not 16-aligned
     assert _linear(lib, w=258) == _lib.Q6_ERR_ALIGNMENT
     # LoRA: x @ A and B come together, with a positive rank
     assert _linear(lib, lora_xa=256) == _lib.Q6_ERR_INVALID_ARGUMENT
