@@ -197,7 +197,7 @@ __global__ void __launch_bounds__(tc_threads(kDqSets), 1)
                         const __grid_constant__ CUtensorMap tmap_xa, const TcParams p) {
     using C = Cfg<NT, kPair>;
     extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* smem = smem_align_up<1024>(smem_raw);
     uint8_t* x_smem = smem;
     uint8_t* c_smem = smem + C::kXStages * C::kXStageBytes;
     uint8_t* sb_smem = c_smem + C::kCStages * kCodeStageBytes;

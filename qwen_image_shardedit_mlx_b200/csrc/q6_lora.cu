@@ -92,7 +92,7 @@ __global__ void __launch_bounds__(kThreads) lora_xa_kernel(const __grid_constant
     constexpr int kCols = R / 4;           // columns per warp
     constexpr int kTiles = kCols / 8;      // n8 tiles per warp
     extern __shared__ uint8_t lora_raw[];
-    uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(lora_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* ring = smem_align_up<1024>(lora_raw);
     __shared__ __align__(8) uint64_t full[kStages];
     __shared__ uint32_t released[kStages];
     __shared__ int abort_flag;

@@ -22,6 +22,15 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+// Rounds a dynamic shared-memory pointer up to kAlign bytes by pointer
+// arithmetic on the shared array itself, so that the compiler keeps every
+// pointer derived from it in the shared address space (a round trip through
+// an integer makes each access through it a generic one).
+template <uint32_t kAlign>
+__device__ __forceinline__ uint8_t* smem_align_up(uint8_t* p) {
+    return p + ((kAlign - (smem_u32(p) & (kAlign - 1u))) & (kAlign - 1u));
+}
+
 __device__ __forceinline__ uint64_t global_timer_ns() {
     uint64_t t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));

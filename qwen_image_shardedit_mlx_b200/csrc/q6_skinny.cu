@@ -211,7 +211,7 @@ __global__ void __launch_bounds__(kThreads, 1) skinny_kernel(const __grid_consta
                                                             const __grid_constant__ CUtensorMap tmap_b,
                                                             const SkParams p) {
     extern __shared__ uint8_t sk_raw[];
-    uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(sk_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* ring = smem_align_up<1024>(sk_raw);
     float* scratch = reinterpret_cast<float*>(ring + p.stages * p.stage_bytes);
     uint64_t* full = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(scratch) +
                                                  kMmaWarps * TPW * 4 * 32 * 4);
