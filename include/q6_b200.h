@@ -72,8 +72,9 @@ enum q6_path {
     Q6_PATH_AUTO = 0,
     Q6_PATH_SIMT = 1,   /* CUDA-core kernel, fp32 dequantised weights   */
     Q6_PATH_TENSOR = 2, /* tcgen05 kernel, bf16 dequantised weights     */
-    Q6_PATH_SKINNY = 3  /* warp-MMA kernel for 1..32 token rows on the raw codes,
-                           fp32 weight semantics (group size 64 / 128)  */
+    Q6_PATH_SKINNY = 3  /* warp-MMA kernel for 1..16 token rows on the raw codes,
+                           fp32 weight semantics, K a multiple of 512, group size
+                           32 / 64 / 128; K split over a thread-block cluster */
 };
 
 /*
@@ -305,6 +306,13 @@ Q6_API int q6_last_path(void);
 
 /* Token tile (MMA N) the tensor path would use for an M x N problem. */
 Q6_API int q6_tensor_token_tile(int64_t M, int64_t N);
+
+/* Plan the few-row path (Q6_PATH_SKINNY) would launch for an M x N x K problem at
+   this group size on the current device: *tpw 16-row weight tiles per warp (row
+   blocks of 32 * tpw rows), *split CTAs per thread-block cluster sharing K, and
+   *clusters clusters.  Q6_ERR_UNSUPPORTED when the shape is outside the path. */
+Q6_API int q6_skinny_plan(int64_t M, int64_t N, int64_t K, int group_size, int* tpw, int* split,
+                          int* clusters);
 
 /* How many tensor-path launches in this process asked for CTA pairs (two-CTA
    clusters sharing one cta_group::2 MMA), were refused by the device before

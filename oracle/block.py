@@ -145,19 +145,31 @@ class BlockWeights:
     heads: int
 
 
-FEW_ROWS = 2  # launches of at most this many token rows take the library's streaming GEMV (fp32 weights)
+def kernel_weight_dtype(rows: int, n: int, k: int, group_size: int) -> str:
+    """Weight precision of the library kernel that runs a linear launch of
+    ``rows`` token rows on an n x k weight: fp32 dequantised weights on the
+    few-row kernels (the streaming GEMV for 1-2 rows; the warp-MMA kernel for
+    2-16 rows when the weight holds at least 2^24 codes, K is a multiple of
+    512 and, at group size 32, for at most 8 rows), bf16 on the tensor-core
+    path (MLX qmm semantics).  Mirrors the library's auto-path policy."""
+
+    if rows <= 2:
+        return "f32"
+    warp_mma = (rows <= 16 and n * k >= 1 << 24 and k % 512 == 0 and (k // group_size) % 8 == 0
+                and (group_size != 32 or rows <= 8))
+    return "f32" if warp_mma else "bf16"
 
 
 def _lin(w: BlockWeights, name: str, x: np.ndarray, *, launch_rows: int | None = None, **kw) -> np.ndarray:
     """One q6 linear with the weight precision of the kernel path that runs it
-    for ``launch_rows`` token rows (default: the rows of ``x``): fp32
-    dequantised weights for a few rows (the modulation linears at M = batch
-    run on the few-row kernels, which keep the reference kernel's fp32
-    ``scale * code + qbias``), bf16 weights otherwise (the tensor-core path,
-    MLX qmm semantics).  ``x`` may hold a subset of the launch's rows."""
+    for ``launch_rows`` token rows (default: the rows of ``x``;
+    kernel_weight_dtype): the modulation linears at M = batch run on the
+    few-row kernels, which keep the reference kernel's fp32
+    ``scale * code + qbias``.  ``x`` may hold a subset of the launch's rows."""
 
     rows = np.asarray(x).shape[0] if launch_rows is None else launch_rows
-    kw.setdefault("weight_dtype", "f32" if rows <= FEW_ROWS else "bf16")
+    lin = w.linears[name]
+    kw.setdefault("weight_dtype", kernel_weight_dtype(rows, lin.out_features, lin.in_features, lin.group_size))
     return round_bf16(linear(x, w.linears[name], **kw))
 
 

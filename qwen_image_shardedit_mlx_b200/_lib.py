@@ -69,6 +69,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "q6_clear_device_error": (_I, []),
     "q6_last_path": (_I, []),
     "q6_tensor_token_tile": (_I, [_I64, _I64]),
+    "q6_skinny_plan": (_I, [_I64, _I64, _I64, _I, _P, _P, _P]),
     "q6_pair_fallback_count": (_I64, []),
     "q6_sp_add_layernorm_gather_bf16": (_I, [_P, _P, _P, _P, _P, _I64, _P, _I, _I, _I64, _I64, _I64, _I64, _F,
                                              _P]),

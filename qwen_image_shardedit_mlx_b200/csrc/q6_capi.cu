@@ -38,14 +38,23 @@ bool simt_aligned(const void* x, int64_t K, int elem_bytes) {
     return aligned(x, 16) && ((K * elem_bytes) % 16 == 0);
 }
 
-// Few-row policy: the warp-MMA kernel runs when asked for by path
-// (Q6_PATH_SKINNY), or for 1..16 token rows when Q6_SKINNY=1.
+// Few-row policy of the auto path, from B200 measurements with rotating weights
+// larger than 4x L2 (3072 <-> 12288, 3072 -> 18432 / 36864, group sizes
+// 32 / 64 / 128): the warp-MMA kernel for 2..16 token rows when the weights hold
+// at least 2^24 codes (3072 -> 12288: 12.1-14.2 us against the tensor path's
+// 16.8 us; 3072 -> 36864 at 2 rows: 26.1 us against the GEMV's 32.9 us), except
+// group size 32 past 8 rows; the streaming GEMV for one row (10.4 us against
+// 12.1 us) and for small weights.  Q6_SKINNY=1 takes the warp-MMA kernel for
+// every 1..16-row shape it supports, Q6_SKINNY=0 never (read once per process).
 bool skinny_auto(const q6::LinearArgs& a) {
     static const int mode = [] {
         const char* v = std::getenv("Q6_SKINNY");
-        return (v && v[0] == '1') ? 1 : 0;
+        if (!v || !v[0]) return -1;
+        return v[0] == '1' ? 1 : 0;
     }();
-    return mode && q6::skinny_supported(a);
+    if (mode == 0 || a.lora_rank > 0 || !q6::skinny_supported(a)) return false;
+    if (mode == 1) return true;
+    return a.M >= 2 && a.N * a.K >= (int64_t(1) << 24) && (a.group_size != 32 || a.M <= 8);
 }
 
 int run_linear(const q6::LinearArgs& a, int path, cudaStream_t stream) {
@@ -55,9 +64,8 @@ int run_linear(const q6::LinearArgs& a, int path, cudaStream_t stream) {
         if (skinny_auto(a))
             chosen = Q6_PATH_SKINNY;
         else
-            // Measured on B200 (rotating weights > 4x L2): the streaming GEMV wins at
-            // 1-2 rows; from 3 rows on the tensor-core path does (at 4 rows
-            // 3072 -> 36864: 35 us against 53 us).
+            // The streaming GEMV at 1-2 rows; from 3 rows the tensor-core path
+            // (at 4 rows 3072 -> 3072: 6.5 us against 7.9 us).
             chosen = (tc_ok && (a.M > 2 || a.lora_rank > 0)) ? Q6_PATH_TENSOR : Q6_PATH_SIMT;
     }
     if (chosen == Q6_PATH_SKINNY) {
@@ -230,6 +238,17 @@ int q6_lora_xa_bf16(const uint16_t* x, const uint16_t* a, uint16_t* xa, int64_t 
 int q6_tensor_token_tile(int64_t M, int64_t N) {
     if (M <= 0 || N <= 0) return 0;
     return q6::choose_token_tile(M, N);
+}
+
+int q6_skinny_plan(int64_t M, int64_t N, int64_t K, int group_size, int* tpw, int* split, int* clusters) {
+    if (!tpw || !split || !clusters) return Q6_ERR_INVALID_ARGUMENT;
+    q6::LinearArgs a{};
+    a.M = M;
+    a.N = N;
+    a.K = K;
+    a.group_size = group_size;
+    if (M <= 0 || N <= 0 || K <= 0 || !q6::skinny_supported(a)) return Q6_ERR_UNSUPPORTED;
+    return q6::skinny_plan(a, tpw, split, clusters);
 }
 
 }  // extern "C"

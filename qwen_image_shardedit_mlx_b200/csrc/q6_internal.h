@@ -57,11 +57,14 @@ int launch_linear_simt(const LinearArgs& a, bool f32_io, cudaStream_t stream);
 bool gemv_supported(const LinearArgs& a);
 int launch_gemv(const LinearArgs& a, cudaStream_t stream);
 
-// Warp-level MMA path for 1 <= M <= 32 bf16 rows on the raw codes (fp32
-// weight semantics): group size 64 or 128, K % (8 group_size) == 0, 16-byte
-// aligned x, codes, scales and biases, no LoRA.
+// Warp-level MMA path for 1 <= M <= 16 bf16 rows on the raw codes (fp32
+// weight semantics): group size 32, 64 or 128, K % 512 == 0,
+// (K / group_size) % 8 == 0, 16-byte aligned x, codes, scales and biases,
+// no LoRA.  K is split over the CTAs of a cluster where that balances the SMs.
 bool skinny_supported(const LinearArgs& a);
 int launch_skinny(const LinearArgs& a, cudaStream_t stream);
+// The few-row path's plan for a shape (tiles per warp, K split, clusters).
+int skinny_plan(const LinearArgs& a, int* tpw, int* split, int* clusters);
 
 // tcgen05 path: bf16 activations, bf16-dequantised weights, fp32 accumulate.
 // Requires K % 64 == 0 and 16-byte aligned x / w rows.

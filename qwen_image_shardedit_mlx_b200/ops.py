@@ -285,6 +285,16 @@ def q6_mlp(
     return y.reshape(leading + (d,))
 
 
+def skinny_plan(m: int, n: int, k: int, group_size: int = 64) -> dict:
+    """The plan the few-row path would launch for an m x n x k linear on the
+    current device: 16-row weight tiles per warp, CTAs per cluster sharing K,
+    clusters."""
+    tpw, split, clusters = ctypes.c_int(0), ctypes.c_int(0), ctypes.c_int(0)
+    _lib.check(_lib.lib().q6_skinny_plan(m, n, k, group_size, ctypes.byref(tpw), ctypes.byref(split),
+                                         ctypes.byref(clusters)), "q6_skinny_plan")
+    return {"tpw": tpw.value, "rows": 32 * tpw.value, "split": split.value, "clusters": clusters.value}
+
+
 def last_path() -> str:
     code = _lib.lib().q6_last_path()
     return {v: k for k, v in _lib.PATHS.items()}.get(code, "none")

@@ -99,17 +99,23 @@ def test_tensor_path_production_shapes(m, n, k, gs, epi):
 
 
 def test_config1_gemv_rows_and_tensor_rows_agree():
-    """The few-row path (fp32 weights) and the tensor path (bf16 weights) on
-    the config-1 weight: both within tolerance of their oracles."""
+    """The few-row paths (fp32 weights) and the tensor path (bf16 weights) on
+    the config-1 weight, as the auto path picks them: the streaming GEMV for
+    one row, the warp-MMA kernel for 2-16 rows, the tensor core past that;
+    each within tolerance of its oracle."""
+
+    from oracle.block import kernel_weight_dtype
 
     rng = np.random.default_rng(17)
     w, ow = _gpu_weights(1717, 12288, 3072, 64, bias=False)
-    for m in (1, 2, 4):  # the auto path: the GEMV for 1-2 rows, the tensor core from 3
+    for m, path in ((1, "simt"), (2, "skinny"), (4, "skinny"), (16, "skinny"), (17, "tensor")):
         x = random_bf16(rng, (m, 3072))
         got = ops.q6_linear(from_bits(x), *w, group_size=64)
         torch.cuda.synchronize()
-        assert ops.last_path() == ("simt" if m <= 2 else "tensor")
-        ref = oracle.linear(oracle.bf16_bits_to_f32(x), ow, weight_dtype="f32" if m <= 2 else "bf16")
+        assert ops.last_path() == path
+        dtype = kernel_weight_dtype(m, 12288, 3072, 64)
+        assert dtype == ("bf16" if path == "tensor" else "f32")
+        ref = oracle.linear(oracle.bf16_bits_to_f32(x), ow, weight_dtype=dtype)
         assert_close(f32(got), ref, what=f"config-1 weight, {m} rows")
 
 

@@ -242,24 +242,49 @@ def test_skinny_path_vs_oracle(m, n, k, gs, epi):
     assert_close(f32(got), ref, what=f"skinny {m}x{n}x{k} gs{gs} {epi}")
 
 
-def test_skinny_row_blocks_are_reproducible(monkeypatch):
-    """Each output is summed in the same order (stages in K order within a
-    block warp, then the eight block warps in order) whatever the row-block
-    size, so the results are bitwise equal across block sizes, including
-    CTAs that walk several row blocks."""
+@pytest.mark.parametrize("m", [5, 16])
+def test_skinny_plans_are_reproducible(monkeypatch, m):
+    """For a given K split, each output is summed in the same order (the
+    CTA's stages in K order within a block warp, the eight block warps in
+    order, the cluster's CTAs in rank order) whatever the row-block size and
+    the number of clusters, so the results are bitwise equal across those,
+    including clusters that walk several row blocks; other splits agree with
+    the oracle."""
 
-    rng = np.random.default_rng(6)
-    w = random_weights(rng, 4096, 2048, 64)
+    rng = np.random.default_rng(6 + m)
+    w = random_weights(rng, 4096, 2048, 64)  # four 512-code stages
     wt, st, bt, bias = weights_to_torch(w)
-    x = from_bits(random_bf16(rng, (16, 2048)))
-    outs = []
-    for tiles in ("2", "2", "16", "12", "4"):  # 2: 256 row blocks, more than one per CTA
-        monkeypatch.setenv("Q6_SKINNY_TILES", tiles)
-        outs.append(ops.q6_linear(x, wt, st, bt, bias, group_size=64, path="skinny"))
+    x = from_bits(random_bf16(rng, (m, 2048)))
+    ref = oracle.linear(f32(x), w, weight_dtype="f32")
+    by_split = {}
+    # tpw 1: 128 row blocks of 32 rows, more than one per cluster at splits 2-4
+    for plan in ("1,1", "1,1", "4,1", "2,1", "1,2", "4,2", "2,2", "1,3", "4,3", "4,4", "1,4"):
+        monkeypatch.setenv("Q6_SKINNY_PLAN", plan)
+        out = ops.q6_linear(x, wt, st, bt, bias, group_size=64, path="skinny")
+        by_split.setdefault(plan.split(",")[1], []).append(out)
     torch.cuda.synchronize()
-    for o in outs[1:]:
-        assert torch.equal(outs[0], o)
-    assert_close(f32(outs[0]), oracle.linear(f32(x), w, weight_dtype="f32"))
+    for split, outs in by_split.items():
+        for o in outs[1:]:
+            assert torch.equal(outs[0], o), f"split {split}"
+        assert_close(f32(outs[0]), ref, what=f"skinny split {split}")
+
+
+def test_skinny_plan_query(monkeypatch):
+    """q6_skinny_plan reports the plan the path launches: the override when
+    Q6_SKINNY_PLAN is set, otherwise row blocks that spread the weights over
+    the SMs (at least 96 clusters x split CTAs for the image FF's shapes)."""
+
+    monkeypatch.setenv("Q6_SKINNY_PLAN", "3,2")
+    plan = ops.skinny_plan(4, 12288, 3072)
+    assert (plan["tpw"], plan["rows"], plan["split"]) == (3, 96, 2) and plan["clusters"] >= 1
+    monkeypatch.delenv("Q6_SKINNY_PLAN")
+    for m in (1, 16):
+        for n, k in ((12288, 3072), (3072, 12288)):
+            plan = ops.skinny_plan(m, n, k)
+            assert 1 <= plan["tpw"] <= 4 and 1 <= plan["split"] <= 4
+            assert plan["clusters"] * plan["split"] >= 96, (m, n, k, plan)
+    with pytest.raises(_lib.Q6Error):
+        ops.skinny_plan(17, 12288, 3072)
 
 
 def test_skinny_refuses_more_than_16_rows():
@@ -339,11 +364,20 @@ def test_auto_path_choice():
     w = random_weights(rng, 256, 128, 64)
     wt, st, bt, bias = weights_to_torch(w)
     ops.q6_linear(from_bits(random_bf16(rng, (2, 128))), wt, st, bt, bias)
-    assert ops.last_path() == "simt"  # 1-2 rows: the streaming GEMV
+    assert ops.last_path() == "simt"  # small weights, 1-2 rows: the streaming GEMV
     ops.q6_linear(from_bits(random_bf16(rng, (3, 128))), wt, st, bt, bias)
-    assert ops.last_path() == "tensor"  # from 3 rows the tensor-core path is faster
+    assert ops.last_path() == "tensor"  # small weights from 3 rows: the tensor-core path
     ops.q6_linear(from_bits(random_bf16(rng, (64, 128))), wt, st, bt, bias)
     assert ops.last_path() == "tensor"
+    # weights of 2^24 codes and more: the warp-MMA kernel for 2-16 rows (8 at group size 32)
+    for gs, cases in ((64, ((1, "simt"), (2, "skinny"), (16, "skinny"), (17, "tensor"))),
+                      (32, ((8, "skinny"), (9, "tensor")))):
+        wb = [torch.zeros((4096, 4096 * 6 // 32), dtype=torch.int32, device="cuda"),
+              torch.ones((4096, 4096 // gs), dtype=torch.bfloat16, device="cuda"),
+              torch.zeros((4096, 4096 // gs), dtype=torch.bfloat16, device="cuda")]
+        for m, path in cases:
+            ops.q6_linear(torch.ones((m, 4096), dtype=torch.bfloat16, device="cuda"), *wb, group_size=gs)
+            assert ops.last_path() == path, (gs, m)
     torch.cuda.synchronize()
 
 
