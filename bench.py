@@ -60,8 +60,10 @@ def parse_args() -> argparse.Namespace:
                     help="run one side measurement alone and print its JSON (for profiling runs)")
     ap.add_argument("--gemv-case", default=None,
                     help="comma-separated GEMV case names to run (default: all of GEMV_CASES)")
-    ap.add_argument("--tp-comm", choices=["peer", "nccl"], default="peer",
-                    help="collectives of the tensor-parallel block: fused peer-memory kernels or NCCL")
+    ap.add_argument("--block-form", choices=list(BLOCK_FORMS), default="cp",
+                    help="multi-GPU form of the block and the stack: context-parallel rows with all-gathered keys "
+                         "and values (cp), or tensor-parallel heads / FF columns with fused peer-memory (tp-peer) or "
+                         "NCCL (tp-nccl) collectives")
     return ap.parse_args()
 
 
@@ -351,9 +353,9 @@ def run_ours(args, world: int, rank: int, local: int) -> dict | None:
     e2e_call_ms = max_over_ranks(e0.elapsed_time(e1), world)
 
     # ---- one full MMDiT block (3456 image + 256 text tokens), tensor-parallel over the ranks
-    block = None if args.no_block else measure_block(dev, world, rank, comm=args.tp_comm)
+    block = None if args.no_block else measure_block(dev, world, rank, form=args.block_form)
     # ---- config 5: the 60-block stack, 8 steps, batch 2, tensor-parallel over the ranks
-    stack = None if args.no_stack else measure_stack(dev, world, rank, comm=args.tp_comm)
+    stack = None if args.no_stack else measure_stack(dev, world, rank, form=args.block_form)
 
     # ---- skinny-M GEMV side measurement (HBM-bound): a single-GPU figure, taken at N = 1 only
     gemv = None
@@ -499,14 +501,39 @@ def _block_inputs(dev, batch: int, seed: int):
     return x, temb, joint_rope(rope_tables(ia, ta, dev)), seq
 
 
-def measure_block(dev, world: int, rank: int, steps: int = 10, comm: str = "peer") -> dict | None:
+BLOCK_FORMS = {
+    "cp": "context-parallel: every rank the full weights and 1 / N of each sample's joint rows through the whole "
+          "block, keys and values all-gathered (NCCL) for the attention",
+    "tp-peer": "tensor-parallel heads and FF columns with sequence-parallel rows between the GEMMs; fused "
+               "peer-memory reduce + residual + adaLN + gather kernels and 4 barriers per block",
+    "tp-nccl": "tensor-parallel heads and FF columns with sequence-parallel rows between the GEMMs; 2 all-gathers "
+               "+ 2 reduce-scatters (NCCL) per block",
+}
+
+
+def _block_runner(form: str, full, world: int, rank: int, x, temb, rope_j, batch: int, seq: int):
+    """A per-rank forward of one multi-GPU block form over this rank's rows of x."""
+
+    from qwen_image_shardedit_mlx_b200.block import ContextParallelQwenBlock, TensorParallelQwenBlock
+
+    if form == "cp":
+        blk = ContextParallelQwenBlock(full, world, rank)
+        x_local = blk.local_rows(x, batch, seq)
+        return lambda: blk.forward_local(x_local, temb, rope_j, batch, seq, BLOCK_TXT)
+    blk = TensorParallelQwenBlock(full, world, rank, comm=form[3:])
+    rows_local = x.shape[0] // world
+    x_local = x[rank * rows_local:(rank + 1) * rows_local].contiguous()
+    return lambda: blk.finish(blk.forward_local(x_local, temb, rope_j, batch, seq, BLOCK_TXT))
+
+
+def measure_block(dev, world: int, rank: int, steps: int = 10, form: str = "cp") -> dict | None:
     """Device time of one Qwen-Image MMDiT block forward (3456 image + 256
     text tokens, all 14 linears q6 gs64, joint attention over 3712 tokens), at
     batch 1 (config 3) and batch 2 (the per-block cost of config 5's CFG pair).
-    With N ranks the block is tensor-parallel with sequence-parallel rows
-    (all-gather before each column-parallel GEMM, reduce-scatter after each
-    row-parallel one); rank 0 also times the single-GPU block, so the line
-    carries the strong-scaling efficiency ms_1gpu / (N ms)."""
+    With N ranks every multi-GPU form is timed in the same run (``forms_ms``)
+    and ``ms`` is the one ``form`` names (BLOCK_FORMS); rank 0 also times the
+    single-GPU block, so the line carries the strong-scaling efficiency
+    ms_1gpu / (N ms)."""
 
     import torch
 
@@ -515,19 +542,14 @@ def measure_block(dev, world: int, rank: int, steps: int = 10, comm: str = "peer
 
     g = torch.Generator(device=dev).manual_seed(2025)  # the same block on every rank
     full = QwenTransformerBlock.random(DIM, BLOCK_HEADS, generator=g, device=dev)
-    tp = TensorParallelQwenBlock(full, world, rank, comm=comm) if world > 1 else None
-    tp_other = None
-    if world > 1:
-        tp_other = TensorParallelQwenBlock(full, world, rank, comm="nccl" if comm == "peer" else "peer")
     out = {}
     for batch in (1, 2):
         x, temb, rope_j, seq = _block_inputs(dev, batch, 7 + batch)
         y = torch.empty_like(x)
-        rows_local = x.shape[0] // world
-        x_local = x[rank * rows_local:(rank + 1) * rows_local].contiguous()
         one = lambda: full.forward_joint(x, temb, rope_j, batch, BLOCK_TXT, out=y)  # noqa: E731
         ms_tp1 = ms_one_stream = None
-        if tp is None:
+        forms_ms = None
+        if world == 1:
             ms, eager_ms = _graph_ms(one, world, steps)
             ms_1 = ms
             # both streams' GEMMs in order on one CUDA stream (no fork / join)
@@ -535,16 +557,21 @@ def measure_block(dev, world: int, rank: int, steps: int = 10, comm: str = "peer
             ms_one_stream, _ = _graph_ms(one, 1, steps)
             full.overlap_streams = True
             # the tensor-parallel form on one rank: the cost of its structure alone
-            tp1 = TensorParallelQwenBlock(full, 1, 0, comm=comm)
+            tp1 = TensorParallelQwenBlock(full, 1, 0, comm="peer")
             ms_tp1, _ = _graph_ms(lambda: tp1.finish(tp1.forward_local(x, temb, rope_j, batch, seq, BLOCK_TXT)),
                                   1, steps)
             del tp1
         else:
-            ms, eager_ms = _graph_ms(lambda: tp.finish(tp.forward_local(x_local, temb, rope_j, batch, seq, BLOCK_TXT)),
-                                     world, steps)
-            ms_other, _ = _graph_ms(
-                lambda: tp_other.finish(tp_other.forward_local(x_local, temb, rope_j, batch, seq, BLOCK_TXT)),
-                world, steps)
+            forms_ms = {}
+            eager_ms = None
+            for f in BLOCK_FORMS:  # every rank takes the same forms in the same order
+                run = _block_runner(f, full, world, rank, x, temb, rope_j, batch, seq)
+                f_ms, f_eager = _graph_ms(run, world, steps)
+                forms_ms[f] = round(f_ms, 4)
+                if f == form:
+                    ms, eager_ms = f_ms, f_eager
+                del run
+                torch.cuda.empty_cache()
             ms_1 = None
             if rank == 0:
                 ms_1, _ = _graph_ms(one, 1, steps)
@@ -555,8 +582,8 @@ def measure_block(dev, world: int, rank: int, steps: int = 10, comm: str = "peer
         out[f"b{batch}"] = {
             "ms": round(ms, 4), "TFLOP/s": round(flop / (ms * 1e-3) / 1e12, 1), "eager_ms": round(eager_ms, 4),
             "ms_1gpu": None if ms_1 is None else round(ms_1, 4),
-            "comm": comm if world > 1 else None,
-            "ms_other_comm": None if world == 1 else round(ms_other, 4),
+            "form": form if world > 1 else None,
+            "forms_ms": forms_ms,
             "ms_tp_form_1gpu": None if ms_tp1 is None else round(ms_tp1, 4),
             "ms_one_stream_1gpu": None if ms_one_stream is None else round(ms_one_stream, 4),
             "efficiency_vs_1gpu": None if ms_1 is None else round(ms_1 / (world * ms), 4),
@@ -569,10 +596,7 @@ def measure_block(dev, world: int, rank: int, steps: int = 10, comm: str = "peer
         "n_gpus": world,
         "batch2": out["b2"],
         "parallelism": "single GPU" if world == 1 else
-        f"tensor-parallel x{world} (heads and FF columns) with sequence-parallel rows between the GEMMs; "
-        + ("fused peer-memory reduce + residual + adaLN + gather kernels and 4 barriers per block"
-           if comm == "peer" else "2 all-gathers + 2 reduce-scatters (NCCL) per block")
-        + " (ms_other_comm: the other form, same run)",
+        f"{BLOCK_FORMS[form]} (x{world}; forms_ms: every form, same run)",
         "shape": f"{BLOCK_IMG} image + {BLOCK_TXT} text tokens, hidden {DIM}, {BLOCK_HEADS} heads x 128, "
                  "FF 4x, all 14 linears q6 gs64",
         "steps": steps,
@@ -587,13 +611,16 @@ def measure_block(dev, world: int, rank: int, steps: int = 10, comm: str = "peer
 
 
 def measure_stack(dev, world: int, rank: int, blocks: int = STACK_BLOCKS, steps: int = STACK_STEPS,
-                  comm: str = "peer") -> dict | None:
+                  form: str = "cp") -> dict | None:
     """Config 5: the 60-block q6 MMDiT stack, batch 2 (CFG cond / uncond),
-    3456 image + 256 text tokens per sample, 8 denoising steps, tensor-parallel
-    over the ranks.  Each rank builds its own shards of 60 random blocks
-    (seeded per block); the joint rows stay sequence-sharded from block to
-    block, the residual add of each block folded into the next block's first
-    modulate.  One denoising step (every block, a new timestep embedding) is
+    3456 image + 256 text tokens per sample, 8 denoising steps, over the
+    ranks in the multi-GPU ``form`` (BLOCK_FORMS).  Each rank builds 60 random
+    blocks (seeded per block; the full weights for the context-parallel form,
+    its shards for the tensor-parallel ones) and keeps its rows sharded from
+    block to block (the tensor-parallel forms fold each block's residual add
+    into the next block's first modulate; on one GPU that form runs).  Every
+    block's modulation vectors come first, 1 / N of the GEMVs per rank and one
+    all-gather.  One denoising step (every block, a new timestep embedding) is
     captured in a CUDA graph and replayed ``steps`` times; the time is device
     time, max over ranks.  Only the block stack is timed (the model's input
     and output projections and the sampler are outside the q6 path)."""
@@ -601,20 +628,27 @@ def measure_stack(dev, world: int, rank: int, blocks: int = STACK_BLOCKS, steps:
     import torch
 
     from qwen_image_shardedit_mlx_b200 import ops
-    from qwen_image_shardedit_mlx_b200.block import (QwenTransformerBlock, TensorParallelQwenBlock, block_flops,
-                                                     stack_modulations)
+    from qwen_image_shardedit_mlx_b200.block import (ContextParallelQwenBlock, QwenTransformerBlock,
+                                                     TensorParallelQwenBlock, block_flops, stack_modulations)
 
+    cp = form == "cp" and world > 1
     stack = []
     for i in range(blocks):
         g = torch.Generator(device=dev).manual_seed(10_000 + i)
         full = QwenTransformerBlock.random(DIM, BLOCK_HEADS, generator=g, device=dev)
-        stack.append(TensorParallelQwenBlock(full, world, rank, comm=comm if world > 1 else "nccl"))
+        if cp:
+            stack.append(ContextParallelQwenBlock(full, world, rank))
+        else:
+            stack.append(TensorParallelQwenBlock(full, world, rank, comm=form[3:] if world > 1 else "nccl"))
         del full
     torch.cuda.empty_cache()
     batch = STACK_BATCH
     x, _, rope_j, seq = _block_inputs(dev, batch, 99)
-    rows_local = x.shape[0] // world
-    x_local = x[rank * rows_local:(rank + 1) * rows_local].contiguous()
+    if cp:
+        x_local = stack[0].local_rows(x, batch, seq)
+    else:
+        rows_local = x.shape[0] // world
+        x_local = x[rank * rows_local:(rank + 1) * rows_local].contiguous()
     g = torch.Generator(device=dev).manual_seed(5)
     tembs = [torch.randn((batch, DIM), generator=g, device=dev).to(torch.bfloat16) for _ in range(steps)]
     temb = tembs[0].clone()
@@ -622,6 +656,11 @@ def measure_stack(dev, world: int, rank: int, blocks: int = STACK_BLOCKS, steps:
     def one_step():
         # every block's modulation vectors first, 1 / N of the GEMVs per rank and one all-gather
         mods = stack_modulations(stack, temb, world, rank)
+        if cp:
+            y = x_local
+            for i, blk in enumerate(stack):
+                y = blk.forward_local(y, temb, rope_j, batch, seq, BLOCK_TXT, mod=mods[i])
+            return y
         pending = stack[0].forward_local(x_local, temb, rope_j, batch, seq, BLOCK_TXT, mod=mods[0])
         for i, blk in enumerate(stack[1:], start=1):
             pending = blk.forward_local_pending(pending, temb, rope_j, batch, seq, BLOCK_TXT, mod=mods[i])
@@ -667,9 +706,8 @@ def measure_stack(dev, world: int, rank: int, blocks: int = STACK_BLOCKS, steps:
     return {
         "ms_per_step": round(total_ms / steps, 3), "total_ms": round(total_ms, 2), "steps": steps, "blocks": blocks,
         "batch": batch, "n_gpus": world, "TFLOP/s": round(flop / (total_ms * 1e-3) / 1e12, 1),
-        "parallelism": "single GPU" if world == 1 else
-        f"tensor-parallel x{world} with sequence-parallel rows ("
-        + ("fused peer-memory kernels" if comm == "peer" else "NCCL all-gather / reduce-scatter") + ")",
+        "parallelism": "single GPU" if world == 1 else f"{BLOCK_FORMS[form]} (x{world})",
+        "form": form if world > 1 else None,
         "shape": f"{blocks} blocks x batch {batch} x ({BLOCK_IMG} image + {BLOCK_TXT} text tokens), hidden {DIM}, "
                  "all linears q6 gs64",
         "note": "one denoising step (all blocks) captured in a CUDA graph and replayed per step with that step's "
@@ -1005,8 +1043,8 @@ def main() -> int:
             import torch
 
             dev = torch.device("cuda", local)
-            fn = {"block": lambda: measure_block(dev, world, rank, comm=args.tp_comm),
-                  "stack": lambda: measure_stack(dev, world, rank, comm=args.tp_comm),
+            fn = {"block": lambda: measure_block(dev, world, rank, form=args.block_form),
+                  "stack": lambda: measure_stack(dev, world, rank, form=args.block_form),
                   "gemv": lambda: measure_gemv(dev, measured_peaks(), args.gemv_case) if rank == 0 else None,
                   "sweep": lambda: measure_sweep(dev, measured_peaks()) if rank == 0 else None,
                   "kernels": lambda: measure_kernels(dev, measured_peaks()) if rank == 0 else None}[args.only]

@@ -500,15 +500,16 @@ def both_streams(owner, device: torch.device, text_fn, image_fn) -> None:
 
 
 def project_qkv_joint(owner: torch.nn.Module, z: torch.Tensor, qkv: torch.Tensor, batch: int, seq: int,
-                      text_len: int, which: int | None = None) -> None:
+                      text_len: int, which: int | None = None, segs=None) -> None:
     """q, k, v of every joint row into qkv [B * S, 3 * width]: one GEMM per
     (sample, stream) of the stream's concatenated projections (``fused_rows``);
     a stream with a LoRA delta on one of them runs its three GEMMs and copies.
-    ``which`` (0 text, 1 image) limits the launches to one stream."""
+    ``which`` (0 text, 1 image) limits the launches to one stream; ``segs``
+    ((sample, stream, row slice) triples) replaces the joint rows' segments."""
 
     fused = {0: fused_rows(owner, _TXT_QKV), 1: fused_rows(owner, _IMG_QKV)}
     width = qkv.shape[1] // 3
-    for _, stream, r in segments(batch, seq, text_len):
+    for _, stream, r in (segments(batch, seq, text_len) if segs is None else segs):
         if which is not None and stream != which:
             continue
         f = fused[stream]
@@ -757,6 +758,160 @@ class TensorParallelQwenBlock(torch.nn.Module):
         seq = rows // batch
         y_local = self.finish(self.forward_local(x_local, temb, joint_rope(rope), batch, seq, s_txt, encoder_mask))
         return split_joint(self._gather(y_local), batch, s_txt)
+
+
+
+class ContextParallelQwenBlock(torch.nn.Module):
+    """The block with its joint rows split over the ranks (context
+    parallelism): rank r of W keeps rows [r S / W, (r + 1) S / W) of every
+    sample's joint sequence (S rows, text first) through the whole block and
+    holds every weight (the full block, replicated), and only keys and values
+    cross GPUs: one all-gather per sample before the joint attention, whose
+    queries are the rank's rows.  Every GEMM keeps all its output columns and
+    all of K, so at 8 GPUs the image GEMMs run on 464 rows at the tensor
+    path's full tile widths, where the tensor-parallel form's out-projection
+    (K = 384) and q / k / v (1152 columns) leave most SMs idle.  A stack keeps
+    the rows sharded from block to block.  The per-rank weights are the whole
+    model's (16.6 GB for 60 blocks).  Requires S divisible by W."""
+
+    overlap_streams = True  # text- and image-stream GEMMs on two CUDA streams (both_streams)
+
+    def __init__(self, full: QwenTransformerBlock, world: int, rank: int, group=None) -> None:
+        super().__init__()
+        self.full = full
+        self.world, self.rank, self.group = int(world), int(rank), group
+        self.dim, self.heads, self.eps = full.dim, full.heads, full.eps
+
+    def modulation_joint(self, temb: torch.Tensor) -> torch.Tensor:
+        return self.full.modulation_joint(temb)
+
+    def rows_per_rank(self, seq: int) -> int:
+        if seq % self.world:
+            raise ValueError(f"{seq} joint rows per sample do not split over {self.world} ranks")
+        return seq // self.world
+
+    def local_rows(self, x: torch.Tensor, batch: int, seq: int) -> torch.Tensor:
+        """This rank's rows [B * R, D] of joint rows x [B * S, D]."""
+
+        r = self.rows_per_rank(seq)
+        return x.view(batch, seq, -1)[:, self.rank * r:(self.rank + 1) * r].reshape(batch * r, -1).contiguous()
+
+    def local_segments(self, batch: int, seq: int, text_len: int):
+        """(sample, stream, local row slice) of this rank's rows: stream 0 text, 1 image."""
+
+        r = self.rows_per_rank(seq)
+        t = min(max(text_len - self.rank * r, 0), r)
+        out = []
+        for b in range(batch):
+            if t:
+                out.append((b, 0, slice(b * r, b * r + t)))
+            if t < r:
+                out.append((b, 1, slice(b * r + t, (b + 1) * r)))
+        return out
+
+    def _gather_kv(self, kv_local: torch.Tensor, batch: int, seq: int) -> torch.Tensor:
+        """Keys and values of every row of every sample, [B, S, 2D], from this
+        rank's [B * R, 2D] (one all-gather per sample)."""
+
+        if self.world == 1:
+            return kv_local.view(batch, seq, -1)
+        import torch.distributed as dist
+
+        r = seq // self.world
+        full = torch.empty((batch, seq, kv_local.shape[1]), dtype=kv_local.dtype, device=kv_local.device)
+        for b in range(batch):
+            dist.all_gather_into_tensor(full[b], kv_local[b * r:(b + 1) * r], group=self.group)
+        return full
+
+    def forward_local(self, x_local: torch.Tensor, temb: torch.Tensor, rope_joint: tuple[torch.Tensor, torch.Tensor],
+                      batch: int, seq: int, text_len: int, text_mask: torch.Tensor | None = None,
+                      mod: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+        """This rank's output rows [B * R, D] from its input rows ``x_local``
+        (``local_rows`` of the joint rows); ``rope_joint`` covers the whole
+        sequence; ``mod`` = the block's [B, 2, 6, D] modulation vectors when
+        precomputed (``stack_modulations``)."""
+
+        full, d = self.full, self.dim
+        r = self.rows_per_rank(seq)
+        r0 = self.rank * r
+        dev = x_local.device
+        vec = ModulationVectors(full.modulation_joint(temb) if mod is None else mod)
+        segs = self.local_segments(batch, seq, text_len)
+        cos, sin = rope_joint
+        n = full.norms
+
+        def modulate(src: torch.Tensor, shift, scale, dst: torch.Tensor) -> None:
+            for b in range(batch):  # row0 places each sample's rows in its sequence
+                rows = slice(b * r, (b + 1) * r)
+                add_layernorm_modulate(src[rows], shift, scale, out=dst[rows], row0=b * seq + r0, seq_len=seq,
+                                       text_len=text_len, eps=self.eps)
+
+        z = torch.empty_like(x_local)
+        modulate(x_local, vec.shift1, vec.scale1, z)
+        qkv = torch.empty((batch * r, 3 * d), dtype=torch.bfloat16, device=dev)
+        both_streams(self, dev,
+                     lambda: project_qkv_joint(full, z, qkv, batch, seq, text_len, which=0, segs=segs),
+                     lambda: project_qkv_joint(full, z, qkv, batch, seq, text_len, which=1, segs=segs))
+        for b in range(batch):
+            rows = slice(b * r, (b + 1) * r)
+            for j, (w_txt, w_img) in enumerate((("attn.norm_added_q", "attn.norm_q"),
+                                                ("attn.norm_added_k", "attn.norm_k"))):
+                qk_rmsnorm_rope_joint_(qkv[rows, j * d:(j + 1) * d], n[w_txt], n[w_img], cos, sin, row0=b * seq + r0,
+                                       seq_len=seq, text_len=text_len, eps=self.eps)
+        kv = self._gather_kv(qkv[:, d:].contiguous(), batch, seq)
+        q = qkv[:, :d].view(batch, r, self.heads, HEAD_DIM).transpose(1, 2)
+        k = kv[..., :d].view(batch, seq, self.heads, HEAD_DIM).transpose(1, 2)
+        v = kv[..., d:].view(batch, seq, self.heads, HEAD_DIM).transpose(1, 2)
+        mask = None
+        if text_mask is not None:
+            keep = torch.ones((batch, seq), dtype=torch.bool, device=dev)
+            keep[:, :text_len] = text_mask.reshape(batch, text_len).to(dev) > 0.5
+            mask = keep.view(batch, 1, 1, seq)
+        att = F.scaled_dot_product_attention(q, k, v, attn_mask=mask, scale=1.0 / math.sqrt(HEAD_DIM))
+        att = att.transpose(1, 2).reshape(batch * r, d)
+        h = torch.empty_like(x_local)
+
+        def out_proj(which: int) -> None:
+            for b, stream, rows in segs:
+                if stream == which:
+                    name = "attn.to_add_out" if stream == 0 else "attn.attn_to_out.0"
+                    full._linear(name, att[rows], residual=x_local[rows], gate=vec.gate1(b, stream), out=h[rows])
+
+        both_streams(self, dev, lambda: out_proj(0), lambda: out_proj(1))
+        z2 = torch.empty_like(x_local)
+        modulate(h, vec.shift2, vec.scale2, z2)
+        y = out if out is not None else torch.empty_like(x_local)
+
+        def ff(which: int) -> None:
+            for b, stream, rows in segs:
+                if stream == which:
+                    full._mlp("txt_ff" if stream == 0 else "img_ff", z2[rows], h[rows], vec.gate2(b, stream), y[rows],
+                              slot=stream)
+
+        both_streams(self, dev, lambda: ff(0), lambda: ff(1))
+        return y
+
+    def forward(self, hidden: torch.Tensor, encoder: torch.Tensor, temb: torch.Tensor,
+                rope: tuple[torch.Tensor, ...],
+                encoder_mask: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+        """Every rank passes the full inputs (as the reference block takes them)
+        and gets the full (encoder_out, hidden_out): local rows in, one
+        all-gather of the output rows at the end."""
+
+        x, batch, s_txt = joint_rows(hidden, encoder)
+        seq = x.shape[0] // batch
+        y_local = self.forward_local(self.local_rows(x, batch, seq), temb, joint_rope(rope), batch, seq, s_txt,
+                                     encoder_mask)
+        if self.world == 1:
+            y = y_local
+        else:
+            import torch.distributed as dist
+
+            r = seq // self.world
+            parts = torch.empty((self.world * batch * r, self.dim), dtype=y_local.dtype, device=y_local.device)
+            dist.all_gather_into_tensor(parts, y_local, group=self.group)
+            y = parts.view(self.world, batch, r, self.dim).transpose(0, 1).reshape(batch * seq, self.dim)
+        return split_joint(y, batch, s_txt)
 
 
 def stack_modulations(blocks, temb: torch.Tensor, world: int = 1, rank: int = 0, group=None) -> torch.Tensor:

@@ -285,6 +285,39 @@ def q6_mlp(
     return y.reshape(leading + (d,))
 
 
+class MlpCall:
+    """A prepared ``q6_mlp`` for fixed weights, row count and workspace: the
+    checks, dtype views and pointer lookups run once, and each call passes
+    only the activation and output pointers and the stream to the C ABI.  For
+    loops that launch the same MLP on rotating device buffers (the streamed
+    host-batch path), where the per-call Python work of ``q6_mlp`` would
+    otherwise pace the GPU.  The weight and workspace tensors are kept alive
+    by the object; they must not be reallocated while it is in use."""
+
+    def __init__(self, w1, w2, m: int, group_size: int, workspace: torch.Tensor):
+        h, d = check_q6_weights(w1[0], w1[1], w1[2], group_size)
+        d2, h2 = check_q6_weights(w2[0], w2[1], w2[2], group_size)
+        if (d2, h2) != (d, h):
+            raise ValueError(f"fc2 must map {h} -> {d}, got {h2} -> {d2}")
+        dev = _require_cuda(*w1[:3], *w2[:3], workspace)
+        if workspace.numel() * workspace.element_size() < mlp_workspace_bytes(m, h):
+            raise ValueError("workspace smaller than mlp_workspace_bytes(m, h)")
+        self.m, self.d, self.h, self.group_size, self.device = int(m), d, h, group_size, dev
+        self._keep = [w1[0].contiguous(), w1[1].to(torch.bfloat16).contiguous(), w1[2].to(torch.bfloat16).contiguous(),
+                      _bf16_vec(w1[3], h, "fc1 bias"),
+                      w2[0].contiguous(), w2[1].to(torch.bfloat16).contiguous(), w2[2].to(torch.bfloat16).contiguous(),
+                      _bf16_vec(w2[3], d, "fc2 bias"), workspace]
+        k = self._keep
+        self._w = (k[0].data_ptr(), k[1].data_ptr(), k[2].data_ptr(), _ptr(k[3]),
+                   k[4].data_ptr(), k[5].data_ptr(), k[6].data_ptr(), _ptr(k[7]))
+        self._tail = (self.m, d, h, group_size, workspace.data_ptr(), workspace.numel() * workspace.element_size())
+        self._fn = _lib.lib().q6_mlp_bf16
+
+    def __call__(self, x_ptr: int, y_ptr: int, stream: int) -> None:
+        """y = fc2(gelu(fc1(x))) for bf16 [m, d] device buffers given by pointer, on ``stream`` (a raw handle)."""
+        _lib.check(self._fn(x_ptr, *self._w, None, None, y_ptr, *self._tail, stream), "q6_mlp_bf16")
+
+
 def skinny_plan(m: int, n: int, k: int, group_size: int = 64) -> dict:
     """The plan the few-row path would launch for an m x n x k linear on the
     current device: 16-row weight tiles per warp, CTAs per cluster sharing K,

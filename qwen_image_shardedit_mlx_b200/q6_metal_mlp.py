@@ -327,49 +327,47 @@ class QwenFeedForward(torch.nn.Module):
         dev = self.mlp_in.weight.device
         d, h = self.mlp_in.in_features, self.mlp_in.out_features
         m = int(xs[0].reshape(-1, d).shape[0])
-        key = (m, d, h, str(dev))
+        lora = self.mlp_in.lora is not None or self.mlp_out.lora is not None
+        w1 = (self.mlp_in.weight, self.mlp_in.scales, self.mlp_in.biases, self.mlp_in.bias)
+        w2 = (self.mlp_out.weight, self.mlp_out.scales, self.mlp_out.biases, self.mlp_out.bias)
+        key = (m, d, h, str(dev), lora, tuple(0 if t is None else t.data_ptr() for t in (*w1, *w2)))
         if getattr(self, "_stream_key", None) != key:
-            self._stream_bufs = (
-                [torch.empty((m, d), dtype=torch.bfloat16, device=dev) for _ in range(2)],
-                [torch.empty((m, d), dtype=torch.bfloat16, device=dev) for _ in range(2)],
-                torch.empty(int(ops.mlp_workspace_bytes(m, h, d)), dtype=torch.uint8, device=dev),
-                [torch.cuda.Stream(dev) for _ in range(3)],
-            )
+            x_dev = [torch.empty((m, d), dtype=torch.bfloat16, device=dev) for _ in range(2)]
+            y_dev = [torch.empty((m, d), dtype=torch.bfloat16, device=dev) for _ in range(2)]
+            workspace = torch.empty(int(ops.mlp_workspace_bytes(m, h, d)), dtype=torch.uint8, device=dev)
+            # One prepared MLP call per slot (fixed pointers): the loop's host work
+            # per batch stays far below the kernels' time.
+            call = None if lora else ops.MlpCall(w1, w2, m, self.mlp_in.group_size, workspace)
+            events = [[torch.cuda.Event() for _ in range(2)] for _ in range(3)]  # loaded, computed, done
+            self._stream_bufs = (x_dev, y_dev, workspace, [torch.cuda.Stream(dev) for _ in range(3)], call, events)
             self._stream_key = key
-        x_dev, y_dev, workspace, (s_in, s_comp, s_out) = self._stream_bufs
+        x_dev, y_dev, workspace, (s_in, s_comp, s_out), call, (loaded, computed, done) = self._stream_bufs
         caller = torch.cuda.current_stream(dev)
         for s in (s_in, s_comp, s_out):
             s.wait_stream(caller)
-        w1 = (self.mlp_in.weight, self.mlp_in.scales, self.mlp_in.biases, self.mlp_in.bias)
-        w2 = (self.mlp_out.weight, self.mlp_out.scales, self.mlp_out.biases, self.mlp_out.bias)
-        read_x = [None, None]   # compute of the batch that last read x_dev[slot]
-        read_y = [None, None]   # download of the batch that last read y_dev[slot]
+        comp_handle = s_comp.cuda_stream
+        # A wait on an event takes its latest record at the time of the wait, so
+        # the per-slot events recorded again two batches later stay correct.
         for i, (xh, yh) in enumerate(zip(xs, ys)):
             slot = i % 2
             if xh.reshape(-1, d).shape[0] != m or yh.numel() != m * d:
                 raise ValueError("all batches must have the first batch's shape")
+            if i >= 2:
+                s_in.wait_event(computed[slot])  # the compute of batch i - 2 has read x_dev[slot]
             with torch.cuda.stream(s_in):
-                if read_x[slot] is not None:
-                    s_in.wait_event(read_x[slot])
                 x_dev[slot].copy_(xh.reshape(m, d), non_blocking=True)
-                loaded = torch.cuda.Event()
-                loaded.record(s_in)
-            with torch.cuda.stream(s_comp):
-                s_comp.wait_event(loaded)
-                if read_y[slot] is not None:
-                    s_comp.wait_event(read_y[slot])
-                if self.mlp_in.lora is not None or self.mlp_out.lora is not None:
+            loaded[slot].record(s_in)
+            s_comp.wait_event(loaded[slot])
+            if i >= 2:
+                s_comp.wait_event(done[slot])  # the download of batch i - 2 has read y_dev[slot]
+            if call is not None:
+                call(x_dev[slot].data_ptr(), y_dev[slot].data_ptr(), comp_handle)
+            else:
+                with torch.cuda.stream(s_comp):
                     y_dev[slot].copy_(self.forward(x_dev[slot]))  # each linear fuses its own delta
-                else:
-                    ops.q6_mlp(x_dev[slot], w1, w2, group_size=self.mlp_in.group_size, workspace=workspace,
-                               out=y_dev[slot])
-                computed = torch.cuda.Event()
-                computed.record(s_comp)
-                read_x[slot] = computed
+            computed[slot].record(s_comp)
+            s_out.wait_event(computed[slot])
             with torch.cuda.stream(s_out):
-                s_out.wait_event(computed)
                 yh.reshape(m, d).copy_(y_dev[slot], non_blocking=True)
-                done = torch.cuda.Event()
-                done.record(s_out)
-                read_y[slot] = done
+            done[slot].record(s_out)
         caller.wait_stream(s_out)

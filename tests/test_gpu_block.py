@@ -332,6 +332,31 @@ def test_tensor_parallel_block_world1_matches_the_block():
         assert_close(f32(y), f32(x), bf16_output=False, what="tp world 1")
 
 
+def test_context_parallel_block_world1_matches_the_block():
+    """One rank holds every row: the context-parallel block (per-sample adaLN
+    and QK-norm launches placed by row0, keys and values copied out for the
+    attention) agrees with the single-GPU block, batch 2 with a padded text
+    mask."""
+
+    from qwen_image_shardedit_mlx_b200.block import ContextParallelQwenBlock
+
+    rng = np.random.default_rng(78)
+    _, tb = _block_pair(rng, 512, 4)
+    cp = ContextParallelQwenBlock(tb, 1, 0)
+    hidden = from_bits(random_bf16(rng, (2, 96, 512)))
+    enc = from_bits(random_bf16(rng, (2, 24, 512)))
+    temb = from_bits(random_bf16(rng, (2, 512)))
+    mask = torch.ones((2, 24), device="cuda")
+    mask[1, 20:] = 0
+    ia, ta = qwen_rope_angles([(8, 12)], 24)
+    rope = rope_tables(ia, ta, "cuda")
+    a = tb(hidden, enc, temb, rope, encoder_mask=mask)
+    b = cp(hidden, enc, temb, rope, encoder_mask=mask)
+    torch.cuda.synchronize()
+    for x, y in zip(a, b):
+        assert_close(f32(y), f32(x), bf16_output=False, what="cp world 1")
+
+
 def test_batched_block_vs_oracle_per_sample():
     """Two samples (CFG cond / uncond) through one block call: the joint rows
     of both go through each batched kernel, and every sample matches the

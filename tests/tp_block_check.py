@@ -1,8 +1,11 @@
-"""Sequence-parallel tensor-parallel MMDiT block over NCCL, one process per GPU
-(launched by tests/test_gpu_block.py through torch.distributed.run): heads
-and FF columns split, joint rows sharded between the GEMMs (all-gather before
-each column-parallel GEMM, reduce-scatter after each row-parallel one), two
-samples per call; checked against the single-GPU block."""
+"""Multi-GPU MMDiT block forms, one process per GPU (launched by
+tests/test_gpu_block.py through torch.distributed.run), two samples per call,
+each checked against the single-GPU block: the sequence-parallel
+tensor-parallel block over NCCL and over peer memory (heads and FF columns
+split, joint rows sharded between the GEMMs: all-gather before each
+column-parallel GEMM, reduce-scatter after each row-parallel one), and the
+context-parallel block (every rank the full weights and 1 / N of each
+sample's rows, keys and values all-gathered for the attention)."""
 
 import datetime
 import os
@@ -14,6 +17,7 @@ import torch.distributed as dist
 
 sys.path.insert(0, str(Path(__file__).resolve().parents[1]))
 from qwen_image_shardedit_mlx_b200.block import (  # noqa: E402
+    ContextParallelQwenBlock,
     QwenTransformerBlock,
     TensorParallelQwenBlock,
     qwen_rope_angles,
@@ -33,8 +37,9 @@ ia, ta = qwen_rope_angles([(20, 30)], 64)
 rope = rope_tables(ia, ta, "cuda")
 ref = full(hidden, enc, temb, rope)
 ok = True
-for comm in ("nccl", "peer"):
-    tp = TensorParallelQwenBlock(full, world, rank, comm=comm)
+for comm in ("nccl", "peer", "cp"):
+    tp = ContextParallelQwenBlock(full, world, rank) if comm == "cp" else TensorParallelQwenBlock(full, world, rank,
+                                                                                                   comm=comm)
     out = tp(hidden, enc, temb, rope)
     torch.cuda.synchronize()
     for name, a, b in (("text", out[0], ref[0]), ("image", out[1], ref[1])):
