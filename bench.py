@@ -60,10 +60,11 @@ def parse_args() -> argparse.Namespace:
                     help="run one side measurement alone and print its JSON (for profiling runs)")
     ap.add_argument("--gemv-case", default=None,
                     help="comma-separated GEMV case names to run (default: all of GEMV_CASES)")
-    ap.add_argument("--block-form", choices=list(BLOCK_FORMS), default="cp",
+    ap.add_argument("--block-form", choices=["auto", *BLOCK_FORMS], default="auto",
                     help="multi-GPU form of the block and the stack: context-parallel rows with all-gathered keys "
                          "and values (cp), or tensor-parallel heads / FF columns with fused peer-memory (tp-peer) or "
-                         "NCCL (tp-nccl) collectives")
+                         "NCCL (tp-nccl) collectives; auto: the measured faster one at that GPU count (tp-peer at "
+                         "2, cp from 4)")
     return ap.parse_args()
 
 
@@ -353,9 +354,9 @@ def run_ours(args, world: int, rank: int, local: int) -> dict | None:
     e2e_call_ms = max_over_ranks(e0.elapsed_time(e1), world)
 
     # ---- one full MMDiT block (3456 image + 256 text tokens), tensor-parallel over the ranks
-    block = None if args.no_block else measure_block(dev, world, rank, form=args.block_form)
+    block = None if args.no_block else measure_block(dev, world, rank, form=block_form(args.block_form, world))
     # ---- config 5: the 60-block stack, 8 steps, batch 2, tensor-parallel over the ranks
-    stack = None if args.no_stack else measure_stack(dev, world, rank, form=args.block_form)
+    stack = None if args.no_stack else measure_stack(dev, world, rank, form=block_form(args.block_form, world))
 
     # ---- skinny-M GEMV side measurement (HBM-bound): a single-GPU figure, taken at N = 1 only
     gemv = None
@@ -509,6 +510,18 @@ BLOCK_FORMS = {
     "tp-nccl": "tensor-parallel heads and FF columns with sequence-parallel rows between the GEMMs; 2 all-gathers "
                "+ 2 reduce-scatters (NCCL) per block",
 }
+
+
+def block_form(choice: str, world: int) -> str:
+    """The multi-GPU block form for ``--block-form``: ``auto`` takes the form
+    measured faster at that GPU count on B200 (block at batch 1 / 2: tp-peer
+    0.679 / 1.220 ms against cp 0.718 / 1.294 ms at 2 GPUs; at 8 GPUs the
+    tensor-parallel GEMMs shrink to K = 384 and 1152 columns, 0.573 ms, while
+    cp keeps full-width GEMMs on 464 rows)."""
+
+    if choice != "auto":
+        return choice
+    return "tp-peer" if world <= 2 else "cp"
 
 
 def _block_runner(form: str, full, world: int, rank: int, x, temb, rope_j, batch: int, seq: int):
@@ -1043,8 +1056,8 @@ def main() -> int:
             import torch
 
             dev = torch.device("cuda", local)
-            fn = {"block": lambda: measure_block(dev, world, rank, form=args.block_form),
-                  "stack": lambda: measure_stack(dev, world, rank, form=args.block_form),
+            fn = {"block": lambda: measure_block(dev, world, rank, form=block_form(args.block_form, world)),
+                  "stack": lambda: measure_stack(dev, world, rank, form=block_form(args.block_form, world)),
                   "gemv": lambda: measure_gemv(dev, measured_peaks(), args.gemv_case) if rank == 0 else None,
                   "sweep": lambda: measure_sweep(dev, measured_peaks()) if rank == 0 else None,
                   "kernels": lambda: measure_kernels(dev, measured_peaks()) if rank == 0 else None}[args.only]

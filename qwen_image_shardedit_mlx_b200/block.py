@@ -809,6 +809,13 @@ class ContextParallelQwenBlock(torch.nn.Module):
                 out.append((b, 1, slice(b * r + t, (b + 1) * r)))
         return out
 
+    def _comm_stream(self, device: torch.device) -> torch.cuda.Stream:
+        side = self.__dict__.get("_comm")
+        if side is None or side.device != device:
+            side = torch.cuda.Stream(device)
+            self.__dict__["_comm"] = side
+        return side
+
     def _gather_kv(self, kv_local: torch.Tensor, batch: int, seq: int) -> torch.Tensor:
         """Keys and values of every row of every sample, [B, S, 2D], from this
         rank's [B * R, 2D] (one all-gather per sample)."""
@@ -849,26 +856,50 @@ class ContextParallelQwenBlock(torch.nn.Module):
         z = torch.empty_like(x_local)
         modulate(x_local, vec.shift1, vec.scale1, z)
         qkv = torch.empty((batch * r, 3 * d), dtype=torch.bfloat16, device=dev)
-        both_streams(self, dev,
-                     lambda: project_qkv_joint(full, z, qkv, batch, seq, text_len, which=0, segs=segs),
-                     lambda: project_qkv_joint(full, z, qkv, batch, seq, text_len, which=1, segs=segs))
+        kv_src = torch.empty((batch * r, 2 * d), dtype=torch.bfloat16, device=dev)
+        kv = torch.empty((batch, seq, 2 * d), dtype=torch.bfloat16, device=dev) if self.world > 1 else None
+        main = torch.cuda.current_stream(dev)
+        comm = self._comm_stream(dev) if self.world > 1 else None
+        landed = []
+        # Sample by sample: q / k / v, QK-norm + RoPE, then its keys and values
+        # leave on the communication stream while the next sample's GEMMs run.
         for b in range(batch):
             rows = slice(b * r, (b + 1) * r)
+            mine = [sg for sg in segs if sg[0] == b]
+            both_streams(self, dev,
+                         lambda: project_qkv_joint(full, z, qkv, batch, seq, text_len, which=0, segs=mine),
+                         lambda: project_qkv_joint(full, z, qkv, batch, seq, text_len, which=1, segs=mine))
             for j, (w_txt, w_img) in enumerate((("attn.norm_added_q", "attn.norm_q"),
                                                 ("attn.norm_added_k", "attn.norm_k"))):
                 qk_rmsnorm_rope_joint_(qkv[rows, j * d:(j + 1) * d], n[w_txt], n[w_img], cos, sin, row0=b * seq + r0,
                                        seq_len=seq, text_len=text_len, eps=self.eps)
-        kv = self._gather_kv(qkv[:, d:].contiguous(), batch, seq)
-        q = qkv[:, :d].view(batch, r, self.heads, HEAD_DIM).transpose(1, 2)
-        k = kv[..., :d].view(batch, seq, self.heads, HEAD_DIM).transpose(1, 2)
-        v = kv[..., d:].view(batch, seq, self.heads, HEAD_DIM).transpose(1, 2)
-        mask = None
+            kv_src[rows].copy_(qkv[rows, d:])
+            if comm is not None:
+                import torch.distributed as dist
+
+                comm.wait_stream(main)
+                with torch.cuda.stream(comm):
+                    dist.all_gather_into_tensor(kv[b], kv_src[rows], group=self.group)
+                    ev = torch.cuda.Event()
+                    ev.record(comm)
+                landed.append(ev)
+        if kv is None:
+            kv = kv_src.view(batch, seq, 2 * d)
+        att = torch.empty((batch * r, d), dtype=torch.bfloat16, device=dev)
+        keep = None
         if text_mask is not None:
             keep = torch.ones((batch, seq), dtype=torch.bool, device=dev)
             keep[:, :text_len] = text_mask.reshape(batch, text_len).to(dev) > 0.5
-            mask = keep.view(batch, 1, 1, seq)
-        att = F.scaled_dot_product_attention(q, k, v, attn_mask=mask, scale=1.0 / math.sqrt(HEAD_DIM))
-        att = att.transpose(1, 2).reshape(batch * r, d)
+        for b in range(batch):  # each sample's attention as soon as its keys and values are in
+            if landed:
+                main.wait_event(landed[b])
+            rows = slice(b * r, (b + 1) * r)
+            q = qkv[rows, :d].view(1, r, self.heads, HEAD_DIM).transpose(1, 2)
+            k = kv[b:b + 1, :, :d].view(1, seq, self.heads, HEAD_DIM).transpose(1, 2)
+            v = kv[b:b + 1, :, d:].view(1, seq, self.heads, HEAD_DIM).transpose(1, 2)
+            mask = None if keep is None else keep[b].view(1, 1, 1, seq)
+            o = F.scaled_dot_product_attention(q, k, v, attn_mask=mask, scale=1.0 / math.sqrt(HEAD_DIM))
+            att[rows].copy_(o.transpose(1, 2).reshape(r, d))
         h = torch.empty_like(x_local)
 
         def out_proj(which: int) -> None:
