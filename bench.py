@@ -14,9 +14,10 @@ rank runs its own 3456-token batch with replicated weights and no collective
 on the data path (weak scaling); the job value is all ranks' FLOPs over the
 slowest rank's device time.  Rank 0 prints one JSON line.
 
-Beside the headline, the line carries the skinny-M GEMV (``gemv``) and one
+Beside the headline, the line carries the few-row linears (``gemv``), one
 full Qwen-Image MMDiT block (``block``: 3456 image + 256 text tokens, all 14
-linears q6, joint attention), tensor-parallel over the ranks when N > 1.
+linears q6, joint attention) and the 60-block stack (``stack``), split over the
+ranks when N > 1 in every multi-GPU form (BLOCK_FORMS, ``--block-form``).
 
 --impl reference times the reference's own q6 kernel source
 (shardedit_mlx/q6_metal_mlp.py SOURCE_QMM_T, compiled for the host by
@@ -62,9 +63,10 @@ def parse_args() -> argparse.Namespace:
                     help="comma-separated GEMV case names to run (default: all of GEMV_CASES)")
     ap.add_argument("--block-form", choices=["auto", *BLOCK_FORMS], default="auto",
                     help="multi-GPU form of the block and the stack: context-parallel rows with all-gathered keys "
-                         "and values (cp), or tensor-parallel heads / FF columns with fused peer-memory (tp-peer) or "
-                         "NCCL (tp-nccl) collectives; auto: the measured faster one at that GPU count (tp-peer at "
-                         "2, cp from 4)")
+                         "and values, a batch first split over rank groups (cp), or tensor-parallel heads / FF "
+                         "columns with fused peer-memory (tp-peer) or NCCL (tp-nccl) collectives; auto: the measured "
+                         "faster one (cp for a batch that splits over the GPUs; for one sample tp-peer at 2 GPUs, cp "
+                         "from 4)")
     return ap.parse_args()
 
 
@@ -356,9 +358,10 @@ def run_ours(args, world: int, rank: int, local: int) -> dict | None:
     e2e_call_ms = max_over_ranks(e0.elapsed_time(e1), world)
 
     # ---- one full MMDiT block (3456 image + 256 text tokens), tensor-parallel over the ranks
-    block = None if args.no_block else measure_block(dev, world, rank, form=block_form(args.block_form, world))
+    block = None if args.no_block else measure_block(dev, world, rank, form=args.block_form)
     # ---- config 5: the 60-block stack, 8 steps, batch 2, tensor-parallel over the ranks
-    stack = None if args.no_stack else measure_stack(dev, world, rank, form=block_form(args.block_form, world))
+    stack = None if args.no_stack else measure_stack(dev, world, rank,
+                                                     form=block_form(args.block_form, world, STACK_BATCH))
 
     # ---- skinny-M GEMV side measurement (HBM-bound): a single-GPU figure, taken at N = 1 only
     gemv = None
@@ -505,8 +508,10 @@ def _block_inputs(dev, batch: int, seed: int):
 
 
 BLOCK_FORMS = {
-    "cp": "context-parallel: every rank the full weights and 1 / N of each sample's joint rows through the whole "
-          "block, keys and values all-gathered (NCCL) for the attention",
+    "cp": "context-parallel: every rank the full weights; a batch's samples first split over rank groups "
+          "(gcd(N, batch) groups, e.g. one sample of the CFG pair per half of the GPUs), then each sample's joint "
+          "rows split over its group's ranks through the whole block, keys and values all-gathered (NCCL) within "
+          "the group for the attention",
     "tp-peer": "tensor-parallel heads and FF columns with sequence-parallel rows between the GEMMs; fused "
                "peer-memory reduce + residual + adaLN + gather kernels and 4 barriers per block",
     "tp-nccl": "tensor-parallel heads and FF columns with sequence-parallel rows between the GEMMs; 2 all-gathers "
@@ -514,34 +519,43 @@ BLOCK_FORMS = {
 }
 
 
-def block_form(choice: str, world: int) -> str:
+def block_form(choice: str, world: int, batch: int) -> str:
     """The multi-GPU block form for ``--block-form``: ``auto`` takes the form
-    measured faster at that GPU count on B200 (block at batch 1 / 2: tp-peer
-    0.679 / 1.220 ms against cp 0.718 / 1.294 ms at 2 GPUs; at 8 GPUs the
-    tensor-parallel GEMMs shrink to K = 384 and 1152 columns, 0.573 ms, while
-    cp keeps full-width GEMMs on 464 rows)."""
+    measured faster on B200.  A batch that splits over the GPUs (the CFG
+    pair on an even count) runs context-parallel with one sample per group of
+    ranks (no communication at 2 GPUs).  One sample runs tensor-parallel with
+    peer-memory collectives at 2 GPUs (block 0.679 ms against cp's 0.718 ms)
+    and context-parallel from 4, where the tensor-parallel GEMMs shrink to
+    K = 384 and 1152 columns (8 GPUs: 0.579 ms against cp's 0.408 ms)."""
 
     if choice != "auto":
         return choice
+    import math
+
+    if batch > 1 and math.gcd(world, batch) > 1:
+        return "cp"
     return "tp-peer" if world <= 2 else "cp"
 
 
 def _block_runner(form: str, full, world: int, rank: int, x, temb, rope_j, batch: int, seq: int):
     """A per-rank forward of one multi-GPU block form over this rank's rows of x."""
 
-    from qwen_image_shardedit_mlx_b200.block import ContextParallelQwenBlock, TensorParallelQwenBlock
+    from qwen_image_shardedit_mlx_b200.block import ContextParallelQwenBlock, TensorParallelQwenBlock, sample_groups
 
     if form == "cp":
-        blk = ContextParallelQwenBlock(full, world, rank)
-        x_local = blk.local_rows(x, batch, seq)
-        return lambda: blk.forward_local(x_local, temb, rope_j, batch, seq, BLOCK_TXT)
+        samples, size, r_in, grp = sample_groups(world, rank, batch)
+        nb = samples.stop - samples.start
+        blk = ContextParallelQwenBlock(full, size, r_in, group=grp)
+        x_local = blk.local_rows(x.view(batch, seq, -1)[samples].reshape(nb * seq, -1), nb, seq)
+        t = temb[samples]
+        return lambda: blk.forward_local(x_local, t, rope_j, nb, seq, BLOCK_TXT)
     blk = TensorParallelQwenBlock(full, world, rank, comm=form[3:])
     rows_local = x.shape[0] // world
     x_local = x[rank * rows_local:(rank + 1) * rows_local].contiguous()
     return lambda: blk.finish(blk.forward_local(x_local, temb, rope_j, batch, seq, BLOCK_TXT))
 
 
-def measure_block(dev, world: int, rank: int, steps: int = 10, form: str = "cp") -> dict | None:
+def measure_block(dev, world: int, rank: int, steps: int = 10, form: str = "auto") -> dict | None:
     """Device time of one Qwen-Image MMDiT block forward (3456 image + 256
     text tokens, all 14 linears q6 gs64, joint attention over 3712 tokens), at
     batch 1 (config 3) and batch 2 (the per-block cost of config 5's CFG pair).
@@ -558,7 +572,9 @@ def measure_block(dev, world: int, rank: int, steps: int = 10, form: str = "cp")
     g = torch.Generator(device=dev).manual_seed(2025)  # the same block on every rank
     full = QwenTransformerBlock.random(DIM, BLOCK_HEADS, generator=g, device=dev)
     out = {}
+    choice = form
     for batch in (1, 2):
+        form = block_form(choice, world, batch)
         x, temb, rope_j, seq = _block_inputs(dev, batch, 7 + batch)
         y = torch.empty_like(x)
         one = lambda: full.forward_joint(x, temb, rope_j, batch, BLOCK_TXT, out=y)  # noqa: E731
@@ -611,7 +627,8 @@ def measure_block(dev, world: int, rank: int, steps: int = 10, form: str = "cp")
         "n_gpus": world,
         "batch2": out["b2"],
         "parallelism": "single GPU" if world == 1 else
-        f"{BLOCK_FORMS[form]} (x{world}; forms_ms: every form, same run)",
+        f"batch 1: {BLOCK_FORMS[out['b1']['form']]}; batch 2: {BLOCK_FORMS[out['b2']['form']]} "
+        f"(x{world}; forms_ms: every form, same run)",
         "shape": f"{BLOCK_IMG} image + {BLOCK_TXT} text tokens, hidden {DIM}, {BLOCK_HEADS} heads x 128, "
                  "FF 4x, all 14 linears q6 gs64",
         "steps": steps,
@@ -644,23 +661,26 @@ def measure_stack(dev, world: int, rank: int, blocks: int = STACK_BLOCKS, steps:
 
     from qwen_image_shardedit_mlx_b200 import ops
     from qwen_image_shardedit_mlx_b200.block import (ContextParallelQwenBlock, QwenTransformerBlock,
-                                                     TensorParallelQwenBlock, block_flops, stack_modulations)
+                                                     TensorParallelQwenBlock, block_flops, sample_groups,
+                                                     stack_modulations)
 
     cp = form == "cp" and world > 1
+    batch = STACK_BATCH
+    samples, size, r_in, grp = sample_groups(world, rank, batch) if cp else (slice(0, batch), world, rank, None)
+    nb = samples.stop - samples.start
     stack = []
     for i in range(blocks):
         g = torch.Generator(device=dev).manual_seed(10_000 + i)
         full = QwenTransformerBlock.random(DIM, BLOCK_HEADS, generator=g, device=dev)
         if cp:
-            stack.append(ContextParallelQwenBlock(full, world, rank))
+            stack.append(ContextParallelQwenBlock(full, size, r_in, group=grp))
         else:
             stack.append(TensorParallelQwenBlock(full, world, rank, comm=form[3:] if world > 1 else "nccl"))
         del full
     torch.cuda.empty_cache()
-    batch = STACK_BATCH
     x, _, rope_j, seq = _block_inputs(dev, batch, 99)
     if cp:
-        x_local = stack[0].local_rows(x, batch, seq)
+        x_local = stack[0].local_rows(x.view(batch, seq, -1)[samples].reshape(nb * seq, -1), nb, seq)
     else:
         rows_local = x.shape[0] // world
         x_local = x[rank * rows_local:(rank + 1) * rows_local].contiguous()
@@ -669,13 +689,17 @@ def measure_stack(dev, world: int, rank: int, blocks: int = STACK_BLOCKS, steps:
     temb = tembs[0].clone()
 
     def one_step():
-        # every block's modulation vectors first, 1 / N of the GEMVs per rank and one all-gather
-        mods = stack_modulations(stack, temb, world, rank)
         if cp:
+            # this group's samples: every block's modulation vectors first, the GEMVs split
+            # over the group's ranks and one all-gather
+            t = temb[samples]
+            mods = stack_modulations(stack, t, size, r_in, group=grp)
             y = x_local
             for i, blk in enumerate(stack):
-                y = blk.forward_local(y, temb, rope_j, batch, seq, BLOCK_TXT, mod=mods[i])
+                y = blk.forward_local(y, t, rope_j, nb, seq, BLOCK_TXT, mod=mods[i])
             return y
+        # every block's modulation vectors first, 1 / N of the GEMVs per rank and one all-gather
+        mods = stack_modulations(stack, temb, world, rank)
         pending = stack[0].forward_local(x_local, temb, rope_j, batch, seq, BLOCK_TXT, mod=mods[0])
         for i, blk in enumerate(stack[1:], start=1):
             pending = blk.forward_local_pending(pending, temb, rope_j, batch, seq, BLOCK_TXT, mod=mods[i])
@@ -1058,8 +1082,9 @@ def main() -> int:
             import torch
 
             dev = torch.device("cuda", local)
-            fn = {"block": lambda: measure_block(dev, world, rank, form=block_form(args.block_form, world)),
-                  "stack": lambda: measure_stack(dev, world, rank, form=block_form(args.block_form, world)),
+            fn = {"block": lambda: measure_block(dev, world, rank, form=args.block_form),
+                  "stack": lambda: measure_stack(dev, world, rank,
+                                                 form=block_form(args.block_form, world, STACK_BATCH)),
                   "gemv": lambda: measure_gemv(dev, measured_peaks(), args.gemv_case) if rank == 0 else None,
                   "sweep": lambda: measure_sweep(dev, measured_peaks()) if rank == 0 else None,
                   "kernels": lambda: measure_kernels(dev, measured_peaks()) if rank == 0 else None}[args.only]

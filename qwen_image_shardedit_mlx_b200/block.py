@@ -945,6 +945,35 @@ class ContextParallelQwenBlock(torch.nn.Module):
         return split_joint(y, batch, s_txt)
 
 
+_SAMPLE_GROUPS: dict = {}
+
+
+def sample_groups(world: int, rank: int, batch: int):
+    """Split a batch of independent samples (the CFG cond / uncond pair run
+    through the same blocks) over the ranks before splitting rows: with
+    g = gcd(world, batch) groups, group i takes samples [i B / g, (i + 1) B / g)
+    on ranks [i W / g, (i + 1) W / g), and a ContextParallelQwenBlock over the
+    group's ranks splits those samples' rows.  Two GPUs then run one sample
+    each with no communication; eight run each sample context-parallel over
+    four.  Returns (sample slice, group size, rank in group, process group or
+    None).  Every rank must call it with the same arguments (the groups are
+    created collectively, once per (world, g))."""
+
+    g = math.gcd(world, batch)
+    size = world // g
+    i = rank // size
+    group = None
+    if g > 1 and size > 1:
+        import torch.distributed as dist
+
+        key = (world, g)
+        if key not in _SAMPLE_GROUPS:
+            _SAMPLE_GROUPS[key] = [dist.new_group(list(range(j * size, (j + 1) * size))) for j in range(g)]
+        group = _SAMPLE_GROUPS[key][i]
+    per = batch // g
+    return slice(i * per, (i + 1) * per), size, rank % size, group
+
+
 def stack_modulations(blocks, temb: torch.Tensor, world: int = 1, rank: int = 0, group=None) -> torch.Tensor:
     """Modulation vectors [n, B, 2, 6, D] of every block of a stack for one
     timestep embedding, the work split over the ranks of a tensor-parallel

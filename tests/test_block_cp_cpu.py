@@ -144,3 +144,40 @@ def test_context_parallel_segments():
         pass
     else:
         raise AssertionError("36 rows over 5 ranks must be refused")
+
+
+def _groups_worker(rank: int, world: int, port: int, batch: int) -> None:
+    import math
+
+    import torch.distributed as dist
+
+    from qwen_image_shardedit_mlx_b200.block import sample_groups
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        samples, size, r_in, group = sample_groups(world, rank, batch)
+        g = math.gcd(world, batch)
+        assert size == world // g and r_in == rank % size
+        per = batch // g
+        assert samples == slice((rank // size) * per, (rank // size + 1) * per)
+        if size > 1 and g > 1:
+            got = torch.empty(size, dtype=torch.float32)
+            dist.all_gather_into_tensor(got, torch.tensor([float(rank)]), group=group)
+            first = (rank // size) * size
+            assert got.tolist() == [float(first + j) for j in range(size)]
+        else:
+            assert group is None
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sample_groups_split_the_batch_then_the_rows():
+    """4 ranks, a batch of 2: two groups of 2 ranks, one sample each, whose
+    collectives stay inside the group; 2 ranks, a batch of 2: one sample per
+    rank and no group; 4 ranks, one sample: every rank in one group."""
+
+    mp.spawn(_groups_worker, args=(4, _free_port(), 2), nprocs=4, join=True)
+    mp.spawn(_groups_worker, args=(2, _free_port(), 2), nprocs=2, join=True)
+    mp.spawn(_groups_worker, args=(4, _free_port(), 1), nprocs=4, join=True)

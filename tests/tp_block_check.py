@@ -5,7 +5,8 @@ tensor-parallel block over NCCL and over peer memory (heads and FF columns
 split, joint rows sharded between the GEMMs: all-gather before each
 column-parallel GEMM, reduce-scatter after each row-parallel one), and the
 context-parallel block (every rank the full weights and 1 / N of each
-sample's rows, keys and values all-gathered for the attention)."""
+sample's rows, keys and values all-gathered for the attention), also with the
+two samples first split over rank groups (``sample_groups``)."""
 
 import datetime
 import os
@@ -22,6 +23,7 @@ from qwen_image_shardedit_mlx_b200.block import (  # noqa: E402
     TensorParallelQwenBlock,
     qwen_rope_angles,
     rope_tables,
+    sample_groups,
 )
 
 rank = int(os.environ["RANK"]); world = int(os.environ["WORLD_SIZE"]); local = int(os.environ["LOCAL_RANK"])
@@ -37,12 +39,19 @@ ia, ta = qwen_rope_angles([(20, 30)], 64)
 rope = rope_tables(ia, ta, "cuda")
 ref = full(hidden, enc, temb, rope)
 ok = True
-for comm in ("nccl", "peer", "cp"):
-    tp = ContextParallelQwenBlock(full, world, rank) if comm == "cp" else TensorParallelQwenBlock(full, world, rank,
-                                                                                                   comm=comm)
-    out = tp(hidden, enc, temb, rope)
+for comm in ("nccl", "peer", "cp", "cp-sp"):
+    want = ref
+    if comm == "cp-sp":  # the two samples split over rank groups, rows split within each group
+        samples, size, r_in, grp = sample_groups(world, rank, 2)
+        out = ContextParallelQwenBlock(full, size, r_in, group=grp)(hidden[samples], enc[samples], temb[samples],
+                                                                    rope)
+        want = (ref[0][samples], ref[1][samples])
+    elif comm == "cp":
+        out = ContextParallelQwenBlock(full, world, rank)(hidden, enc, temb, rope)
+    else:
+        out = TensorParallelQwenBlock(full, world, rank, comm=comm)(hidden, enc, temb, rope)
     torch.cuda.synchronize()
-    for name, a, b in (("text", out[0], ref[0]), ("image", out[1], ref[1])):
+    for name, a, b in (("text", out[0], want[0]), ("image", out[1], want[1])):
         err = (a.float() - b.float()).abs()
         rel_max = float(err.max() / b.float().abs().max())
         rel_mean = float(err.mean() / b.float().pow(2).mean().sqrt())
