@@ -6,18 +6,23 @@
 // [M, K] x [K, r] product with fp32 accumulation and one bf16 rounding, r a
 // multiple of 32 up to 256.  With r far below the ridge point (r FLOP per
 // byte of x) the product is bound by moving bytes, so it is a plain
-// warp-level MMA kernel (mma.sync m16n8k16) built around its data movement:
-// each CTA owns 16 token rows (one MMA row tile) and every rank column, its
-// four warps split the rank columns (r / 4 each), and K streams in 64-wide
-// chunks through a ring of TMA stages: one [16 rows x 64] box of x and
+// warp-level MMA kernel (mma.sync m16n8k16) built around its data movement
+// and its latencies.  Each CTA owns 32 token rows (two MMA row tiles) and
+// every rank column.  K streams in 64-wide chunks through a ring of TMA stages
+// (one CTA per SM, up to 16 stages in flight): one [32 rows x 64] box of x and
 // r / 64 [64 x 64] boxes of A with the 128-byte swizzle (a rank that is an odd
 // multiple of 32 adds one [64 x 32] box with the 64-byte swizzle), which
-// keeps the ldmatrix reads conflict-free.  Every CTA reads all of A (384 KB at
-// K = 3072, r = 64) from L2 besides its own 96 KB of x; TMA moves it without
-// occupying the warps' load slots, which bounded the earlier cp.async form.
-// The last warp to release a ring slot refills it, and each CTA starts its
-// K loop at a different chunk (the sum order stays fixed per row tile).
-// Every wait is bounded.
+// keeps the ldmatrix reads conflict-free.  The eight warps split the chunks,
+// not the output: warp (K group kg, column group cg) takes the chunks
+// c = kg, kg + G, ... (G K groups) for all 32 rows and its r / (8 / G) rank
+// columns, so a warp waits on one chunk in G and keeps 2 x (its n8 tiles)
+// independent MMA chains (16 at r = 64).  With every warp on every chunk, a
+// chunk cost each warp ~100 dependent instructions at ~10 cycles each, and the
+// kernel took chunks x 0.55 us whatever its grid.  At the end the K groups'
+// partial sums meet in the drained ring and are added in K-group order.  The
+// last warp to release a ring slot refills it, and each CTA starts its K loop
+// at a different chunk; every sum runs in a fixed order per CTA.  Every wait
+// is bounded.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -33,14 +38,15 @@
 namespace q6 {
 namespace {
 
-constexpr int kRowsPerCta = 16;
-constexpr int kBK = 64;                  // K per chunk: four K = 16 MMA steps
-constexpr int kWarps = 4;
+constexpr int kRowsPerCta = 32;
+constexpr int kRowTiles = kRowsPerCta / 16;    // MMA row tiles per CTA
+constexpr int kBK = 64;                        // K per chunk: four K = 16 MMA steps
+constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
-constexpr int kXBoxBytes = kRowsPerCta * 128;  // [16 rows x 64 bf16], 128-byte swizzled
+constexpr int kXBoxBytes = kRowsPerCta * 128;  // [32 rows x 64 bf16], 128-byte swizzled
 constexpr int kABoxBytes = kBK * 128;          // [64 k x 64 rank columns], 128-byte swizzled
 constexpr int kATailBytes = kBK * 64;          // [64 k x 32 rank columns], 64-byte swizzled
-constexpr int kRingBytes = 100 * 1024;         // two CTAs per SM
+constexpr int kRingBytes = 200 * 1024;         // one CTA per SM
 
 template <int R>
 struct LoraCfg {
@@ -50,8 +56,15 @@ struct LoraCfg {
     static constexpr int kStages = kRingBytes / kStageBytes < 2 ? 2 : (kRingBytes / kStageBytes > 16 ? 16
                                                                                                   : kRingBytes / kStageBytes);
     static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /* alignment */;
+    // Column groups: the fewest (1, 2 or 4) that leave a warp at most eight n8 tiles.
+    static constexpr int kColGroups = R / 8 <= 8 ? 1 : (R / 8 <= 16 ? 2 : 4);
+    static constexpr int kKGroups = kWarps / kColGroups;
+    static constexpr int kTilesW = R / 8 / kColGroups;  // n8 tiles per warp
+    static constexpr int kFrag = kRowTiles * kTilesW * 4;  // accumulator floats per lane
+    static_assert((R / 8) % kColGroups == 0, "column groups must split the n8 tiles evenly");
     static_assert(kStageBytes % 1024 == 0, "swizzled boxes need 1024-byte alignment");
     static_assert(kSmemBytes <= 227 * 1024, "shared memory");
+    static_assert(kWarps * kFrag * 32 * 4 <= kStages * kStageBytes, "partial sums fit the drained ring");
 };
 
 __device__ __forceinline__ void ldmatrix_x4(uint32_t addr, uint32_t (&r)[4]) {
@@ -89,8 +102,9 @@ __global__ void __launch_bounds__(kThreads) lora_xa_kernel(const __grid_constant
                                                           uint32_t x_box_bytes) {
     using C = LoraCfg<R>;
     constexpr int kStages = C::kStages;
-    constexpr int kCols = R / 4;           // columns per warp
-    constexpr int kTiles = kCols / 8;      // n8 tiles per warp
+    constexpr int kTilesW = C::kTilesW;
+    constexpr int kKGroups = C::kKGroups;
+    constexpr int kColGroups = C::kColGroups;
     extern __shared__ uint8_t lora_raw[];
     uint8_t* ring = smem_align_up<1024>(lora_raw);
     __shared__ __align__(8) uint64_t full[kStages];
@@ -100,6 +114,8 @@ __global__ void __launch_bounds__(kThreads) lora_xa_kernel(const __grid_constant
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
+    const int kg = warp / kColGroups;  // this warp's K group: chunks kg, kg + kKGroups, ...
+    const int cg = warp % kColGroups;  // and its rank columns [cg R / kColGroups, +R / kColGroups)
     const int m0 = static_cast<int>(blockIdx.x) * kRowsPerCta;
     const int chunks = static_cast<int>((K + kBK - 1) / kBK);
     const uint32_t tx = x_box_bytes + C::kABoxes * kABoxBytes + (C::kTail ? kATailBytes : 0);
@@ -143,11 +159,14 @@ __global__ void __launch_bounds__(kThreads) lora_xa_kernel(const __grid_constant
         for (int c = 0; c < pre; ++c) issue_x(c);
     __syncthreads();
 
-    float acc[kTiles][4];
+    // acc[rt][t]: row tile rt, n8 tile t (rank columns cg R / kColGroups + 8 t .. +7)
+    float acc[kRowTiles][kTilesW][4];
 #pragma unroll
-    for (int t = 0; t < kTiles; ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0.0f;
+    for (int i = 0; i < kRowTiles; ++i)
+#pragma unroll
+        for (int t = 0; t < kTilesW; ++t) acc[i][t][0] = acc[i][t][1] = acc[i][t][2] = acc[i][t][3] = 0.0f;
     bool ok = true;
-    for (int c = 0; c < chunks; ++c) {
+    for (int c = kg; c < chunks; c += kKGroups) {
         const int s = c % kStages;
         const uint8_t* st = ring + s * C::kStageBytes;
         if (ok && !__all_sync(0xffffffffu, mbar_wait(smem_u32(&full[s]), static_cast<uint32_t>((c / kStages) & 1),
@@ -158,24 +177,26 @@ __global__ void __launch_bounds__(kThreads) lora_xa_kernel(const __grid_constant
             const uint32_t as = smem_u32(st + kXBoxBytes);
 #pragma unroll
             for (int ks = 0; ks < kBK / 16; ++ks) {
-                // A operand: the 16 rows, K columns 16 ks .. +15 of the x chunk
-                uint32_t af[4];
-                ldmatrix_x4(xs + swz(lane & 15, 2 * ks + (lane >> 4)), af);
+                // A operands: both row tiles' 16 rows, K columns 16 ks .. +15 of the x chunk
+                uint32_t af[kRowTiles][4];
 #pragma unroll
-                for (int t = 0; t < kTiles; ++t) {
-                    // B operand: K rows 16 ks .. +15 of A, rank columns kCols warp + 8 t .. +7
-                    const int col = kCols * warp + 8 * t;
+                for (int i = 0; i < kRowTiles; ++i) ldmatrix_x4(xs + swz(16 * i + (lane & 15), 2 * ks + (lane >> 4)), af[i]);
+#pragma unroll
+                for (int t = 0; t < kTilesW; ++t) {
+                    // B operand: K rows 16 ks .. +15 of A, 8 rank columns
+                    const int col = (R / kColGroups) * cg + 8 * t;
                     const int krow = 16 * ks + (lane & 15);
                     uint32_t bf[2];
                     if (col / 64 < C::kABoxes)
                         ldmatrix_x2_trans(as + (col / 64) * kABoxBytes + swz(krow, (col % 64) / 8), bf);
                     else
                         ldmatrix_x2_trans(as + C::kABoxes * kABoxBytes + swz64(krow, (col % 64) / 8), bf);
-                    mma_bf16_16816(acc[t], af, bf);
+#pragma unroll
+                    for (int i = 0; i < kRowTiles; ++i) mma_bf16_16816(acc[i][t], af[i], bf);
                 }
             }
         }
-        // Release the slot; the last warp to release it refills it with chunk c + kStages.
+        // Release the slot; the last of the chunk's kColGroups warps refills it with chunk c + kStages.
         __syncwarp();
         if (lane == 0) {
             uint32_t prev;
@@ -183,7 +204,7 @@ __global__ void __launch_bounds__(kThreads) lora_xa_kernel(const __grid_constant
                          : "=r"(prev)
                          : "r"(smem_u32(&released[s]))
                          : "memory");
-            if (prev == kWarps - 1) {
+            if (prev == kColGroups - 1) {
                 released[s] = 0;
                 const int cn = c + kStages;
                 if (cn < chunks && !abort_flag) {
@@ -196,30 +217,52 @@ __global__ void __launch_bounds__(kThreads) lora_xa_kernel(const __grid_constant
         }
     }
 
-    // Accumulator layout: thread holds rows g, g + 8 (g = lane / 4) and
-    // columns 2 (lane % 4), +1 of each n8 tile.
-    const int g = lane >> 2;
-    const int cq = 2 * (lane & 3);
-    if (ok) {
-#pragma unroll
-        for (int t = 0; t < kTiles; ++t) {
-            const int col = kCols * warp + 8 * t + cq;
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                const int64_t row = m0 + g + 8 * h;
-                if (row < M) {
-                    const __nv_bfloat162 v = __floats2bfloat162_rn(acc[t][2 * h], acc[t][2 * h + 1]);
-                    *reinterpret_cast<__nv_bfloat162*>(xa + row * R + col) = v;
-                }
-            }
-        }
-    }
-    // Copies in flight land before the CTA exits (bounded).
+    // Copies in flight land before the ring holds the partial sums (bounded;
+    // with every chunk consumed there are none).
     __syncthreads();
     if (threadIdx.x == 0) {
         const int issued = issued_total;
         for (int c = issued > kStages ? issued - kStages : 0; c < issued; ++c)
             mbar_wait_drain(smem_u32(&full[c % kStages]), static_cast<uint32_t>((c / kStages) & 1));
+    }
+    __syncthreads();
+    // K groups 1.. store their partial sums (fragment order, lane-contiguous);
+    // K group 0 adds them in K-group order and stores bf16.
+    float* part = reinterpret_cast<float*>(ring);
+    if (kg > 0) {
+        float* mine = part + warp * (C::kFrag * 32) + lane;
+#pragma unroll
+        for (int i = 0; i < kRowTiles; ++i)
+#pragma unroll
+            for (int t = 0; t < kTilesW; ++t)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) mine[((i * kTilesW + t) * 4 + e) * 32] = acc[i][t][e];
+    }
+    __syncthreads();
+    if (kg == 0 && ok && !abort_flag) {
+        // Accumulator layout: thread holds rows g, g + 8 (g = lane / 4) of each
+        // row tile and columns 2 (lane % 4), +1 of each n8 tile.
+        const int g = lane >> 2;
+        const int cq = 2 * (lane & 3);
+#pragma unroll
+        for (int i = 0; i < kRowTiles; ++i)
+#pragma unroll
+            for (int t = 0; t < kTilesW; ++t) {
+                float v[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    v[e] = acc[i][t][e];
+                    for (int q = 1; q < kKGroups; ++q)
+                        v[e] += part[(q * kColGroups + cg) * (C::kFrag * 32) + ((i * kTilesW + t) * 4 + e) * 32 + lane];
+                }
+                const int col = (R / kColGroups) * cg + 8 * t + cq;
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const int64_t row = m0 + 16 * i + g + 8 * h;
+                    if (row < M)
+                        *reinterpret_cast<__nv_bfloat162*>(xa + row * R + col) = __floats2bfloat162_rn(v[2 * h], v[2 * h + 1]);
+                }
+            }
     }
 }
 

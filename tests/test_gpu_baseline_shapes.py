@@ -120,7 +120,7 @@ def test_config1_gemv_rows_and_tensor_rows_agree():
 
 
 @pytest.mark.parametrize("m,k,r", [(3456, 3072, 64), (37, 256, 32), (130, 12288, 256), (1000, 1040, 96),
-                                   (5, 192, 128), (16, 64, 160)])
+                                   (5, 192, 128), (16, 64, 160), (20, 512, 64)])
 def test_lora_prepass_kernel(m, k, r):
     """xa = x @ A by the library's pre-pass kernel against float64, rounded to
     bf16 once (fp32 accumulation: a few bf16 units at most)."""
