@@ -28,8 +28,10 @@ from oracle import block as ob
 from tests.test_block_tp_cpu import _free_port, _full_block, _setup
 
 
-def _cp_block(w, hidden, enc, temb, rope, world, rank):
-    """This rank's share of the context-parallel block; returns the gathered joint output [B * S, D]."""
+def _cp_block(w, hidden, enc, temb, rope, world, rank, group=None):
+    """This rank's share of the context-parallel block over the ``world``
+    ranks of ``group`` (the default group when None); returns the gathered
+    joint output [B * S, D]."""
 
     import torch.distributed as dist
 
@@ -38,7 +40,7 @@ def _cp_block(w, hidden, enc, temb, rope, world, rank):
     batch, s_img, d = hidden.shape
     s_txt = enc.shape[1]
     seq = s_txt + s_img
-    cp = ContextParallelQwenBlock(types.SimpleNamespace(dim=d, heads=w.heads, eps=1e-6), world, rank)
+    cp = ContextParallelQwenBlock(types.SimpleNamespace(dim=d, heads=w.heads, eps=1e-6), world, rank, group=group)
     r = cp.rows_per_rank(seq)
     r0 = rank * r
     x = np.concatenate([np.concatenate([enc[b], hidden[b]]) for b in range(batch)]).astype(np.float32)
@@ -90,7 +92,7 @@ def _cp_block(w, hidden, enc, temb, rope, world, rank):
         mid = oracle.linear(z2[rows], lin[f"{pre}.mlp_in"], apply_gelu=True)
         y[rows] = oracle.linear(mid, lin[f"{pre}.mlp_out"], residual=h[rows], gate=mods[b][s][5])
     parts = torch.empty((world * batch * r, d))
-    dist.all_gather_into_tensor(parts, torch.from_numpy(y))
+    dist.all_gather_into_tensor(parts, torch.from_numpy(y), group=group)
     return parts.view(world, batch, r, d).transpose(0, 1).reshape(batch * seq, d).numpy()
 
 
@@ -181,3 +183,35 @@ def test_sample_groups_split_the_batch_then_the_rows():
     mp.spawn(_groups_worker, args=(4, _free_port(), 2), nprocs=4, join=True)
     mp.spawn(_groups_worker, args=(2, _free_port(), 2), nprocs=2, join=True)
     mp.spawn(_groups_worker, args=(4, _free_port(), 1), nprocs=4, join=True)
+
+
+def _groups_block_worker(rank: int, world: int, port: int, batch: int, s_txt: int) -> None:
+    import torch.distributed as dist
+
+    from qwen_image_shardedit_mlx_b200.block import sample_groups
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        w, hidden, enc, temb, rope = _setup(batch=batch, s_txt=s_txt)
+        samples, size, r_in, group = sample_groups(world, rank, batch)
+        got = _cp_block(w, hidden[samples], enc[samples], temb[samples], rope, size, r_in, group=group)
+        seq = enc.shape[1] + hidden.shape[1]
+        for i, b in enumerate(range(batch)[samples]):
+            ref_t, ref_i = _full_block(w, hidden[b], enc[b], temb[b], rope)
+            g = got[i * seq:(i + 1) * seq]
+            for part, ref in ((g[:s_txt], ref_t), (g[s_txt:], ref_i)):
+                err = float(np.abs(part - ref).max())
+                assert err <= 1e-4 * float(np.abs(ref).max()), err
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sample_groups_block_gloo_world8_cfg_pair():
+    """The 8-GPU layout of the CFG pair: two groups of four ranks, one sample
+    each, every sample's 36 joint rows (12 text) split 9 per rank inside its
+    group, keys and values gathered over the group only.  Every rank's sample
+    must equal the unsharded oracle block."""
+
+    mp.spawn(_groups_block_worker, args=(8, _free_port(), 2, 12), nprocs=8, join=True)
